@@ -1,0 +1,361 @@
+#!/usr/bin/env python
+"""MoE-layer tokens/s on B200 for DiskMule's routed-expert path.
+
+Default workload (N=1): the Qwen3.5-shaped MoE block of the benchmark table
+(hidden 2048, 512 experts, top-10, intermediate 512, Q4_K gate/up, Q6_K down,
+shared expert with a sigmoid gate), prefill of T=512 tokens per step. Weights
+(1.06 GB) exceed the 126 MB L2, so every step streams them from HBM. Decode (T=1)
+is reported beside it. One JSON line on rank 0.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+`--impl reference` times the CPU restatement of the reference path (the oracle)
+on this host's cores over a bounded token sample per step. Under torchrun each
+rank runs an independent replica on its own GPU (the GGUF block does not shard);
+the timed region is bracketed by barriers and the max over ranks is reported.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--config", default="qwen35")
+    p.add_argument("--tokens", type=int, default=512)
+    p.add_argument("--decode-steps", type=int, default=200)
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    return p.parse_args()
+
+
+CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={CLOCK_QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        for line in (self.out or "").splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(REASONS, f[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        d = json.load(f)
+    return d.get(f"{kernel}@{workload}")
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the CPU restatement of the reference path (the oracle)
+# ---------------------------------------------------------------------------
+
+def cpu_tokens_per_second(cfg_name: str, seconds: float, threads: int, seed: int = 1,
+                          sample: int | None = None):
+    from diskmule_b200.synthetic import CONFIGS, SyntheticLayer, input_spec, layer_specs, vectors
+    from oracle import oracle as O
+    cfg = dict(CONFIGS[cfg_name])
+    sl = SyntheticLayer(cfg_name, cfg, seed, None, layer_specs(cfg, seed), vectors(cfg, seed))
+    w = sl.host_weights()
+    fn = {"gemma4": O.gemma_moe, "qwen35": O.qwen_moe, "glm52": O.glm_moe}[cfg["family"]]
+    n = sample or max(threads, 8)
+    spec = input_spec(cfg, n, 21)
+    raw = spec.host()
+    x = raw.view(np.float32).reshape(n, -1)
+    fn(w, x[:1], threads=threads)  # touch the weights once
+    done, t0 = 0, time.perf_counter()
+    while True:
+        rc, _, _, _ = fn(w, x, threads=threads)
+        assert rc == O.OK
+        done += n
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return done / el, n, el
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    per_step = []
+    sample = max(threads, 8)
+    for i in range(args.warmup + args.steps):
+        tps, n, el = cpu_tokens_per_second(args.config, 0.0, threads, sample=sample)
+        if i >= args.warmup:
+            per_step.append(n / tps)
+    total_tokens = sample * args.steps
+    secs = sum(per_step)
+    value = total_tokens / secs
+    line = {
+        "impl": "reference", "metric": f"MoE-layer tokens/s ({args.config}, CPU reference path)",
+        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.config} MoE block, {sample}-token sample per step",
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample} tokens per step of the {args.config} block "
+                                   "(tokens are independent in the reference)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def stage_bytes(sl, T, counts):
+    """Algorithmic bytes per stage (weights once per distinct expert touched)."""
+    cfg = sl.cfg
+    H, I, E, k = cfg["hidden"], cfg["intermediate"], cfg["experts"], cfg["top_k"]
+    sp = sl.specs
+    active = int((counts > 0).sum())
+    shared = 1 if cfg.get("shared") else 0
+    P = T * k + shared * T
+    xb = 2 if cfg["family"] == "glm52" else 4
+    up_w = sp["gate"].expert_bytes + (sp["up"].expert_bytes if "up" in sp else 0)
+    up = (active + shared) * up_w + T * H * xb + P * I * 4
+    down = (active + shared) * sp["down"].expert_bytes + P * I * 4 + P * H * 4
+    router = sp["router"].nbytes + T * H * xb + T * (E + 1) * 4
+    return {"expert_up": up, "expert_down": down, "router": router}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    from diskmule_b200 import _native as N
+    from diskmule_b200.moe import CudaContext
+    from diskmule_b200.synthetic import build_layer, input_spec
+
+    ctx = CudaContext(local)
+    sl = build_layer(ctx, args.config, seed=1)
+    cfg = sl.cfg
+    T, H, k = args.tokens, cfg["hidden"], cfg["top_k"]
+    xdt = torch.bfloat16 if cfg["family"] == "glm52" else torch.float32
+    x = torch.empty((T, H), dtype=xdt, device="cuda")
+    y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    xs = input_spec(cfg, T, 21 + rank)
+    xs.device_fill(x.data_ptr())
+    ctx.synchronize()
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+
+    def step(tokens, xp, yp):
+        sl.layer.forward(xp, yp, tokens, stream=sptr)
+
+    # ---- prefill: the headline value ----
+    for _ in range(args.warmup):
+        step(T, x.data_ptr(), y.data_ptr())
+    torch.cuda.synchronize()
+    launches = sl.layer.last_launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            step(T, x.data_ptr(), y.data_ptr())
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(end))
+    value = world * T * args.steps / (ms / 1e3)
+
+    # ---- per-stage times (same workload, profiled pass) for the roofline ----
+    counts, _, _, _ = sl.layer.last_dispatch(T)
+    sl.layer.set_profiling(True)
+    totals = {}
+    for _ in range(args.steps):
+        step(T, x.data_ptr(), y.data_ptr())
+        for name, t in sl.layer.stage_times().items():
+            totals[name] = totals.get(name, 0.0) + t
+    sl.layer.set_profiling(False)
+    avg = {n: v / args.steps for n, v in totals.items()}
+    nbytes = stage_bytes(sl, T, counts)
+    dominant = max(("expert_up", "expert_down"), key=lambda n: avg[n])
+    peak, peak_src = measured_peaks()
+    achieved = nbytes[dominant] / (avg[dominant] / 1e3) / 1e9
+    workload = f"{args.config}-T{T}"
+    traffic = ncu_traffic(dominant, workload)
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": traffic, "kernel": dominant,
+                "algorithmic_bytes": nbytes[dominant], "peak_source": peak_src,
+                "stage_ms": {n: round(v, 4) for n, v in avg.items()}}
+
+    # ---- decode (T=1) ----
+    x1 = torch.empty((1, H), dtype=xdt, device="cuda")
+    input_spec(cfg, 1, 33 + rank).device_fill(x1.data_ptr())
+    y1 = torch.empty((1, H), dtype=torch.float32, device="cuda")
+    ctx.synchronize()
+    for _ in range(args.warmup):
+        step(1, x1.data_ptr(), y1.data_ptr())
+    barrier()
+    torch.cuda.synchronize()
+    s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s1.record(stream)
+    for _ in range(args.decode_steps):
+        step(1, x1.data_ptr(), y1.data_ptr())
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    dms = max_over_ranks(s1.elapsed_time(e1))
+    decode_tps = world * args.decode_steps / (dms / 1e3)
+    c1, _, _, _ = sl.layer.last_dispatch(1)
+    b1 = stage_bytes(sl, 1, c1)
+    dec_bytes = b1["expert_up"] + b1["expert_down"] + b1["router"]
+    decode = {"tokens_per_s": decode_tps, "us_per_token": 1e3 * dms / args.decode_steps,
+              "algorithmic_bytes_per_token": dec_bytes,
+              "hbm_frac": dec_bytes / (dms / args.decode_steps / 1e3) / 1e9 / peak}
+
+    # ---- end to end through the public host API (pinned host buffers) ----
+    xh = torch.empty((T, H), dtype=xdt, pin_memory=True)
+    xh.copy_(x.cpu())
+    xnp = xh.view(torch.int16).numpy() if xdt == torch.bfloat16 else xh.numpy()
+    for _ in range(2):
+        sl.layer.forward_host(xnp)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        sl.layer.forward_host(xnp)
+    el = max_over_ranks(time.perf_counter() - t0)
+    e2e = {"value": world * T * args.steps / el, "unit": "tokens/s",
+           "h2d_bytes_per_step": int(T * H * (2 if xdt == torch.bfloat16 else 4)),
+           "d2h_bytes_per_step": int(T * H * 4 + T * k * 8)}
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            threads = os.cpu_count() or 1
+            tps, n, secs = cpu_tokens_per_second(args.config, args.cpu_seconds, threads)
+            cpu = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+                   "sample": f"{n}-token batches of the {args.config} block for {secs:.1f} s"}
+        line = {
+            "metric": f"MoE-layer tokens/s ({args.config} prefill T={T})",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.config} MoE block, prefill T={T} per GPU",
+                       "tokens_per_step": T, "hidden": H, "experts": cfg["experts"],
+                       "top_k": k, "intermediate": cfg["intermediate"],
+                       "formats": "Q4_K gate/up, Q6_K down" if args.config.startswith("qwen") else None,
+                       "parallelism": f"replicas x{world}",
+                       "l2": "weights (1.06 GB) larger than L2; no flush needed"},
+            "roofline": roofline, "decode": decode, "e2e": e2e,
+            "gpu_launches": launches * args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    sl.close()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,765 @@
+// dm_api.cu -- the extern "C" boundary (include/diskmule_cuda.h).
+//
+// The host side mirrors MetalContext (src/metal.rs:179-1604): validation before
+// any launch, in the reference's error order, then stream-ordered kernels.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "../../include/diskmule_cuda.h"
+#include "dm_kernels.cuh"
+
+namespace {
+
+thread_local char g_message[512] = "";
+
+int32_t fail(int32_t status, const char *fmt, ...) {
+  va_list args;
+  va_start(args, fmt);
+  vsnprintf(g_message, sizeof g_message, fmt, args);
+  va_end(args);
+  return status;
+}
+
+int32_t cuda_fail(cudaError_t err, const char *what) {
+  return fail(DM_ERR_COMMAND, "%s: %s", what, cudaGetErrorString(err));
+}
+
+#define DM_CUDA(call, what)                        \
+  do {                                             \
+    cudaError_t err__ = (call);                    \
+    if (err__ != cudaSuccess) return cuda_fail(err__, what); \
+  } while (0)
+
+}  // namespace
+
+struct dm_cuda_context {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  char name[256] = {0};
+  // operator scratch (grown on demand)
+  void *scratch = nullptr;
+  size_t scratch_bytes = 0;
+  int32_t *status = nullptr;
+
+  int32_t ensure_scratch(size_t bytes) {
+    if (bytes <= scratch_bytes) return DM_OK;
+    if (scratch) cudaFree(scratch);
+    scratch = nullptr;
+    scratch_bytes = 0;
+    size_t want = std::max(bytes, (size_t)1 << 20);
+    cudaError_t err = cudaMalloc(&scratch, want);
+    if (err != cudaSuccess)
+      return fail(DM_ERR_ALLOCATION, "could not allocate a %zu-byte device buffer", want);
+    scratch_bytes = want;
+    return DM_OK;
+  }
+};
+
+struct dm_buffer {
+  dm_cuda_context *ctx = nullptr;
+  void *device = nullptr;
+  size_t length = 0;
+  bool read_only = false;
+};
+
+extern "C" {
+
+const char *dm_status_string(int32_t status) {
+  switch (status) {
+    case DM_OK: return "ok";
+    case DM_ERR_NO_DEVICE: return "no CUDA device is available";
+    case DM_ERR_ALLOCATION: return "device allocation failed";
+    case DM_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case DM_ERR_UNSUPPORTED_TENSOR_TYPE: return "unsupported tensor type";
+    case DM_ERR_ELEMENT_COUNT: return "element count is not a whole number of blocks";
+    case DM_ERR_BYTE_LENGTH: return "encoded byte length does not match the shape";
+    case DM_ERR_INPUT_LENGTH: return "matvec input length does not match the columns";
+    case DM_ERR_OUTPUT_LENGTH: return "matvec output length does not match the rows";
+    case DM_ERR_EMPTY_INPUT: return "empty input";
+    case DM_ERR_NON_FINITE: return "non-finite value";
+    case DM_ERR_TOP_K: return "top-k count out of range";
+    case DM_ERR_MAPPED_RANGE: return "range exceeds the mapped buffer";
+    case DM_ERR_OVERFLOW: return "size overflow";
+    case DM_ERR_COMMAND: return "CUDA command failed";
+    case DM_ERR_INVALID_EXPERT: return "invalid expert";
+    case DM_ERR_INVALID_LAYER: return "invalid layer";
+    case DM_ERR_ALL_SLOTS_PINNED: return "all expert slots are pinned";
+    case DM_ERR_CANCELLED: return "cancelled";
+    case DM_ERR_NO_SLOTS: return "expert cache requires at least one slot";
+    case DM_ERR_VECTOR_LENGTH: return "vector length mismatch";
+    case DM_ERR_POSITIVE_PARAMETER: return "parameter must be finite and positive";
+    case DM_ERR_TIMEOUT: return "a bounded wait ran out";
+    case DM_ERR_NOT_BUILT: return "component not built";
+    case DM_ERR_COMMUNICATOR: return "expert-parallel exchange failed";
+    default: return "unknown status";
+  }
+}
+
+const char *dm_last_error_message(void) { return g_message; }
+
+int32_t dm_cuda_create(int32_t device_ordinal, dm_cuda_context **out) {
+  if (!out) return fail(DM_ERR_INVALID_ARGUMENT, "null output handle");
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)
+    return fail(DM_ERR_NO_DEVICE, "no CUDA device is available");
+  if (device_ordinal < 0 || device_ordinal >= count)
+    return fail(DM_ERR_NO_DEVICE, "device %d is outside the %d visible devices", device_ordinal,
+                count);
+  DM_CUDA(cudaSetDevice(device_ordinal), "cudaSetDevice");
+  auto *ctx = new (std::nothrow) dm_cuda_context();
+  if (!ctx) return fail(DM_ERR_ALLOCATION, "host allocation failed");
+  ctx->device = device_ordinal;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device_ordinal) == cudaSuccess)
+    snprintf(ctx->name, sizeof ctx->name, "%s", prop.name);
+  cudaError_t err = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+  if (err == cudaSuccess) err = cudaMalloc(&ctx->status, 256);
+  if (err != cudaSuccess) {
+    delete ctx;
+    return cuda_fail(err, "context set-up");
+  }
+  *out = ctx;
+  return DM_OK;
+}
+
+void dm_cuda_destroy(dm_cuda_context *ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->scratch) cudaFree(ctx->scratch);
+  if (ctx->status) cudaFree(ctx->status);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+int32_t dm_cuda_device_name(const dm_cuda_context *ctx, char *name, size_t capacity) {
+  if (!ctx || !name || capacity == 0) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  snprintf(name, capacity, "%s", ctx->name);
+  return DM_OK;
+}
+
+int32_t dm_cuda_synchronize(dm_cuda_context *ctx) {
+  if (!ctx) return fail(DM_ERR_INVALID_ARGUMENT, "null context");
+  cudaSetDevice(ctx->device);
+  DM_CUDA(cudaDeviceSynchronize(), "device synchronize");
+  return DM_OK;
+}
+
+// ---- buffers ----
+
+static int32_t new_buffer(dm_cuda_context *ctx, size_t length, bool read_only, dm_buffer **out) {
+  if (!ctx || !out) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  if (length == 0) return fail(DM_ERR_ALLOCATION, "could not allocate a 0-byte buffer");
+  cudaSetDevice(ctx->device);
+  void *p = nullptr;
+  if (cudaMalloc(&p, length) != cudaSuccess)
+    return fail(DM_ERR_ALLOCATION, "could not allocate a %zu-byte device buffer", length);
+  auto *b = new (std::nothrow) dm_buffer();
+  if (!b) {
+    cudaFree(p);
+    return fail(DM_ERR_ALLOCATION, "host allocation failed");
+  }
+  b->ctx = ctx;
+  b->device = p;
+  b->length = length;
+  b->read_only = read_only;
+  *out = b;
+  return DM_OK;
+}
+
+int32_t dm_cuda_map_read_only(dm_cuda_context *ctx, const void *host, size_t length,
+                              dm_buffer **out) {
+  if (!host) return fail(DM_ERR_INVALID_ARGUMENT, "null host mapping");
+  int32_t rc = new_buffer(ctx, length, true, out);
+  if (rc != DM_OK) return rc;
+  cudaError_t err = cudaMemcpy((*out)->device, host, length, cudaMemcpyHostToDevice);
+  if (err != cudaSuccess) {
+    dm_buffer_free(*out);
+    *out = nullptr;
+    return cuda_fail(err, "upload of a read-only mapping");
+  }
+  return DM_OK;
+}
+
+int32_t dm_cuda_new_owned_buffer(dm_cuda_context *ctx, size_t length, dm_buffer **out) {
+  int32_t rc = new_buffer(ctx, length, false, out);
+  if (rc != DM_OK) return rc;
+  DM_CUDA(cudaMemset((*out)->device, 0, length), "zero a new buffer");
+  return DM_OK;
+}
+
+static int32_t check_range(const dm_buffer *b, size_t offset, size_t length) {
+  if (!b) return fail(DM_ERR_INVALID_ARGUMENT, "null buffer");
+  size_t end = offset + length;
+  if (end < offset) return fail(DM_ERR_OVERFLOW, "range overflows");
+  if (end > b->length)
+    return fail(DM_ERR_MAPPED_RANGE, "range %zu..%zu exceeds its %zu-byte buffer", offset, end,
+                b->length);
+  return DM_OK;
+}
+
+int32_t dm_buffer_write(dm_buffer *b, size_t offset, const void *source, size_t length) {
+  int32_t rc = check_range(b, offset, length);
+  if (rc != DM_OK) return rc;
+  if (b->read_only) return fail(DM_ERR_INVALID_ARGUMENT, "buffer is read-only");
+  if (length == 0) return DM_OK;
+  cudaSetDevice(b->ctx->device);
+  DM_CUDA(cudaMemcpy((uint8_t *)b->device + offset, source, length, cudaMemcpyHostToDevice),
+          "buffer write");
+  return DM_OK;
+}
+
+int32_t dm_buffer_read(const dm_buffer *b, size_t offset, void *destination, size_t length) {
+  int32_t rc = check_range(b, offset, length);
+  if (rc != DM_OK) return rc;
+  if (length == 0) return DM_OK;
+  cudaSetDevice(b->ctx->device);
+  DM_CUDA(cudaMemcpy(destination, (const uint8_t *)b->device + offset, length,
+                     cudaMemcpyDeviceToHost),
+          "buffer read");
+  return DM_OK;
+}
+
+size_t dm_buffer_length(const dm_buffer *b) { return b ? b->length : 0; }
+void *dm_buffer_device_pointer(const dm_buffer *b) { return b ? b->device : nullptr; }
+
+void dm_buffer_free(dm_buffer *b) {
+  if (!b) return;
+  cudaSetDevice(b->ctx->device);
+  cudaFree(b->device);
+  delete b;
+}
+
+// ---- operators ----
+
+static bool supported_matvec_type(int32_t kind) {
+  switch (kind) {
+    case DM_F32: case DM_F16: case DM_BF16: case DM_Q5_0: case DM_Q8_0: case DM_Q4_K:
+    case DM_Q6_K:
+      return true;
+    default:
+      return false;
+  }
+}
+
+// prepare_matvec (src/metal.rs:1513-1560): lengths, type, element count, bytes.
+static int32_t prepare_matvec(int32_t kind, size_t rows, size_t columns, size_t encoded_length,
+                              size_t input_length, size_t output_length, uint64_t *row_bytes) {
+  if (input_length != columns)
+    return fail(DM_ERR_INPUT_LENGTH, "matvec input has %zu columns; expected %zu", input_length,
+                columns);
+  if (output_length != rows)
+    return fail(DM_ERR_OUTPUT_LENGTH, "matvec output has %zu rows; expected %zu", output_length,
+                rows);
+  if (!supported_matvec_type(kind))
+    return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "matrix-vector multiplication does not support type %d", kind);
+  uint64_t rb = dm::row_bytes(kind, columns);
+  if (rb == 0 && columns != 0)
+    return fail(DM_ERR_ELEMENT_COUNT, "output length %zu is not a whole number of blocks", columns);
+  if (rb != 0 && rows > UINT64_MAX / rb) return fail(DM_ERR_OVERFLOW, "matrix size overflows");
+  if ((uint64_t)encoded_length != rows * rb)
+    return fail(DM_ERR_BYTE_LENGTH, "requires %llu encoded bytes, got %zu",
+                (unsigned long long)(rows * rb), encoded_length);
+  *row_bytes = rb;
+  return DM_OK;
+}
+
+static int32_t run_matvec(dm_cuda_context *ctx, int32_t kind, size_t rows, size_t columns,
+                          const uint8_t *device_matrix, const float *input, float *output) {
+  if (rows > INT32_MAX || columns > INT32_MAX) return fail(DM_ERR_OVERFLOW, "shape too large");
+  size_t in_bytes = (columns * 4 + 255) & ~size_t(255);
+  size_t out_bytes = (rows * 4 + 255) & ~size_t(255);
+  int32_t rc = ctx->ensure_scratch(in_bytes + out_bytes);
+  if (rc != DM_OK) return rc;
+  float *x = (float *)ctx->scratch;
+  float *y = (float *)((uint8_t *)ctx->scratch + in_bytes);
+  DM_CUDA(cudaMemcpyAsync(x, input, columns * 4, cudaMemcpyHostToDevice, ctx->stream), "input copy");
+  if (dm::launch_gemv(kind, device_matrix, (int)rows, (int)columns, x, y, ctx->stream) < 0)
+    return fail(DM_ERR_INVALID_ARGUMENT, "matrix rows are not 16-byte aligned");
+  DM_CUDA(cudaGetLastError(), "matvec launch");
+  DM_CUDA(cudaMemcpyAsync(output, y, rows * 4, cudaMemcpyDeviceToHost, ctx->stream), "output copy");
+  DM_CUDA(cudaStreamSynchronize(ctx->stream), "matvec");
+  return DM_OK;
+}
+
+int32_t dm_cuda_matvec(dm_cuda_context *ctx, int32_t kind, size_t rows, size_t columns,
+                       const uint8_t *encoded, size_t encoded_length, const float *input,
+                       size_t input_length, float *output, size_t output_length) {
+  if (!ctx) return fail(DM_ERR_INVALID_ARGUMENT, "null context");
+  uint64_t rb = 0;
+  int32_t rc = prepare_matvec(kind, rows, columns, encoded_length, input_length, output_length, &rb);
+  if (rc != DM_OK) return rc;
+  if (rows == 0) return DM_OK;
+  if (input_length == 0) return fail(DM_ERR_EMPTY_INPUT, "matvec requires a non-empty input");
+  cudaSetDevice(ctx->device);
+  void *matrix = nullptr;
+  if (cudaMalloc(&matrix, encoded_length) != cudaSuccess)
+    return fail(DM_ERR_ALLOCATION, "could not allocate a %zu-byte device buffer", encoded_length);
+  cudaError_t err = cudaMemcpy(matrix, encoded, encoded_length, cudaMemcpyHostToDevice);
+  if (err != cudaSuccess) {
+    cudaFree(matrix);
+    return cuda_fail(err, "matrix upload");
+  }
+  rc = run_matvec(ctx, kind, rows, columns, (const uint8_t *)matrix, input, output);
+  cudaFree(matrix);
+  return rc;
+}
+
+int32_t dm_cuda_matvec_mapped(dm_cuda_context *ctx, int32_t kind, size_t rows, size_t columns,
+                              const dm_buffer *mapped, size_t offset, size_t encoded_length,
+                              const float *input, size_t input_length, float *output,
+                              size_t output_length) {
+  if (!ctx || !mapped) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  uint64_t rb = 0;
+  int32_t rc = prepare_matvec(kind, rows, columns, encoded_length, input_length, output_length, &rb);
+  if (rc != DM_OK) return rc;
+  rc = check_range(mapped, offset, encoded_length);
+  if (rc != DM_OK) return rc;
+  if (rows == 0) return DM_OK;
+  if (input_length == 0) return fail(DM_ERR_EMPTY_INPUT, "matvec requires a non-empty input");
+  cudaSetDevice(ctx->device);
+  return run_matvec(ctx, kind, rows, columns, (const uint8_t *)mapped->device + offset, input,
+                    output);
+}
+
+int32_t dm_cuda_top_k_softmax(dm_cuda_context *ctx, const float *logits, size_t length, size_t k,
+                              uint32_t *indices, float *probabilities) {
+  if (!ctx) return fail(DM_ERR_INVALID_ARGUMENT, "null context");
+  if (k == 0 || k > length) return fail(DM_ERR_TOP_K, "top-k count %zu is outside 1..=%zu", k, length);
+  if (k > 32) return fail(DM_ERR_TOP_K, "top-k count %zu exceeds the kernel limit of 32", k);
+  for (size_t i = 0; i < length; i++)
+    if (!std::isfinite(logits[i])) return fail(DM_ERR_NON_FINITE, "top-k softmax received a non-finite value");
+  if (length > INT32_MAX) return fail(DM_ERR_OVERFLOW, "input too large");
+  cudaSetDevice(ctx->device);
+  size_t in_bytes = (length * 4 + 255) & ~size_t(255);
+  int32_t rc = ctx->ensure_scratch(in_bytes + 512);
+  if (rc != DM_OK) return rc;
+  float *lg = (float *)ctx->scratch;
+  uint32_t *idx = (uint32_t *)((uint8_t *)ctx->scratch + in_bytes);
+  float *prob = (float *)(idx + 64);
+  DM_CUDA(cudaMemcpyAsync(lg, logits, length * 4, cudaMemcpyHostToDevice, ctx->stream), "copy");
+  DM_CUDA(cudaMemsetAsync(ctx->status, 0, 4, ctx->stream), "status reset");
+  dm::launch_topk_softmax(lg, (int)length, (int)k, idx, prob, ctx->status, ctx->stream);
+  DM_CUDA(cudaGetLastError(), "top-k launch");
+  DM_CUDA(cudaMemcpyAsync(indices, idx, k * 4, cudaMemcpyDeviceToHost, ctx->stream), "copy");
+  DM_CUDA(cudaMemcpyAsync(probabilities, prob, k * 4, cudaMemcpyDeviceToHost, ctx->stream), "copy");
+  DM_CUDA(cudaStreamSynchronize(ctx->stream), "top-k softmax");
+  return DM_OK;
+}
+
+static int32_t run_elementwise(dm_cuda_context *ctx, int op, const char *name, const float *gate,
+                               const float *up, float *output, size_t length) {
+  if (!ctx) return fail(DM_ERR_INVALID_ARGUMENT, "null context");
+  if (length == 0) return fail(DM_ERR_EMPTY_INPUT, "%s requires a non-empty input", name);
+  if (length > INT32_MAX) return fail(DM_ERR_OVERFLOW, "input too large");
+  cudaSetDevice(ctx->device);
+  size_t bytes = (length * 4 + 255) & ~size_t(255);
+  int32_t rc = ctx->ensure_scratch(3 * bytes);
+  if (rc != DM_OK) return rc;
+  float *g = (float *)ctx->scratch;
+  float *u = (float *)((uint8_t *)ctx->scratch + bytes);
+  float *o = (float *)((uint8_t *)ctx->scratch + 2 * bytes);
+  DM_CUDA(cudaMemcpyAsync(g, gate, length * 4, cudaMemcpyHostToDevice, ctx->stream), "copy");
+  DM_CUDA(cudaMemcpyAsync(u, up, length * 4, cudaMemcpyHostToDevice, ctx->stream), "copy");
+  dm::launch_elementwise(op, g, u, o, (int)length, 0.0f, ctx->stream);
+  DM_CUDA(cudaGetLastError(), "elementwise launch");
+  DM_CUDA(cudaMemcpyAsync(output, o, length * 4, cudaMemcpyDeviceToHost, ctx->stream), "copy");
+  DM_CUDA(cudaStreamSynchronize(ctx->stream), name);
+  return DM_OK;
+}
+
+int32_t dm_cuda_gelu_mul(dm_cuda_context *ctx, const float *gate, const float *up, float *output,
+                         size_t length) {
+  return run_elementwise(ctx, dm::kOpGeluMul, "GELU multiply", gate, up, output, length);
+}
+
+int32_t dm_cuda_silu_mul(dm_cuda_context *ctx, const float *gate, const float *up, float *output,
+                         size_t length) {
+  return run_elementwise(ctx, dm::kOpSiluMul, "SiLU multiply", gate, up, output, length);
+}
+
+// MetalContext::rms_norm (src/metal.rs:435-476) validation; CPU arithmetic (bit-exact).
+int32_t dm_cuda_rms_norm(dm_cuda_context *ctx, const float *input, const float *weight,
+                         size_t length, float epsilon, float *output) {
+  if (!ctx) return fail(DM_ERR_INVALID_ARGUMENT, "null context");
+  if (length == 0) return fail(DM_ERR_EMPTY_INPUT, "RMSNorm requires a non-empty input");
+  if (!std::isfinite(epsilon) || epsilon <= 0.0f)
+    return fail(DM_ERR_POSITIVE_PARAMETER, "RMSNorm epsilon requires a finite positive parameter");
+  for (size_t i = 0; i < length; i++)
+    if (!std::isfinite(input[i])) return fail(DM_ERR_NON_FINITE, "RMSNorm received a non-finite value");
+  if (length > INT32_MAX) return fail(DM_ERR_OVERFLOW, "input too large");
+  cudaSetDevice(ctx->device);
+  size_t bytes = (length * 4 + 255) & ~size_t(255);
+  int32_t rc = ctx->ensure_scratch(3 * bytes);
+  if (rc != DM_OK) return rc;
+  float *x = (float *)ctx->scratch;
+  float *w = (float *)((uint8_t *)ctx->scratch + bytes);
+  float *o = (float *)((uint8_t *)ctx->scratch + 2 * bytes);
+  DM_CUDA(cudaMemcpyAsync(x, input, length * 4, cudaMemcpyHostToDevice, ctx->stream), "copy");
+  if (weight)
+    DM_CUDA(cudaMemcpyAsync(w, weight, length * 4, cudaMemcpyHostToDevice, ctx->stream), "copy");
+  DM_CUDA(cudaMemsetAsync(ctx->status, 0, 4, ctx->stream), "status reset");
+  dm::launch_rms_norm(x, weight ? w : nullptr, o, (int)length, epsilon, ctx->status, ctx->stream);
+  DM_CUDA(cudaGetLastError(), "rms_norm launch");
+  int32_t status = 0;
+  DM_CUDA(cudaMemcpyAsync(output, o, length * 4, cudaMemcpyDeviceToHost, ctx->stream), "copy");
+  DM_CUDA(cudaMemcpyAsync(&status, ctx->status, 4, cudaMemcpyDeviceToHost, ctx->stream), "copy");
+  DM_CUDA(cudaStreamSynchronize(ctx->stream), "rms_norm");
+  if (status) return fail(DM_ERR_NON_FINITE, "RMSNorm received a non-finite value");
+  return DM_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// MoE layer
+// ---------------------------------------------------------------------------
+
+struct dm_moe_layer {
+  dm_cuda_context *ctx = nullptr;
+  dm_moe_desc desc{};
+  int E1 = 0;
+  bool shared = false;
+  void *router_t = nullptr;  // transposed router [H][E1]
+  uint64_t gate_stride = 0, up_stride = 0, down_stride = 0;
+  const uint8_t *up_base = nullptr;
+  // scratch
+  void *scratch = nullptr;
+  size_t scratch_bytes = 0;
+  int capacity = 0;
+  dm::ForwardArgs args{};
+  int last_tokens = 0;
+  int last_launches = 0;
+  // host-call staging
+  void *io = nullptr;
+  size_t io_bytes = 0;
+  // per-stage device timers (GenerationProfile analog)
+  bool profiling = false;
+  cudaEvent_t events[dm::kStageCount + 1] = {};
+};
+
+namespace {
+
+int32_t validate_desc(const dm_moe_desc *d) {
+  if (!d) return fail(DM_ERR_INVALID_ARGUMENT, "null descriptor");
+  if (d->family != DM_FAMILY_GEMMA4 && d->family != DM_FAMILY_QWEN35_MOE &&
+      d->family != DM_FAMILY_GLM52)
+    return fail(DM_ERR_INVALID_ARGUMENT, "unknown family %d", d->family);
+  if (d->hidden <= 0 || d->intermediate <= 0 || d->experts <= 0)
+    return fail(DM_ERR_INVALID_ARGUMENT, "hidden, intermediate and experts must be positive");
+  if (d->hidden % 32 || d->intermediate % 32)
+    return fail(DM_ERR_ELEMENT_COUNT, "hidden and intermediate must be multiples of 32");
+  if (d->top_k <= 0 || d->top_k > d->experts || d->top_k > 32)
+    return fail(DM_ERR_TOP_K, "top-k count %d is outside 1..=%d", d->top_k, std::min(d->experts, 32));
+  if (d->experts > 1024) return fail(DM_ERR_INVALID_ARGUMENT, "at most 1024 experts");
+  if (!d->router || !d->gate || !d->down) return fail(DM_ERR_INVALID_ARGUMENT, "null weight pointer");
+  int types[3] = {d->gate_type, d->up_type, d->down_type};
+  for (int i = 0; i < 3; i++) {
+    if (i == 1 && d->family == DM_FAMILY_GEMMA4) continue;
+    if (!supported_matvec_type(types[i]))
+      return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "unsupported expert tensor type %d", types[i]);
+  }
+  if (d->family != DM_FAMILY_GEMMA4 && d->gate_type != d->up_type)
+    return fail(DM_ERR_INVALID_ARGUMENT, "gate and up must share a type");
+  if (dm::row_bytes(d->gate_type, d->hidden) == 0 || dm::row_bytes(d->down_type, d->intermediate) == 0)
+    return fail(DM_ERR_ELEMENT_COUNT, "expert rows are not a whole number of blocks");
+  if (d->family == DM_FAMILY_GEMMA4) {
+    if (!d->router_scale || !d->routed_pre_norm || !d->expert_scale)
+      return fail(DM_ERR_INVALID_ARGUMENT, "Gemma needs router_scale, routed_pre_norm, expert_scale");
+    if (!std::isfinite(d->epsilon) || d->epsilon <= 0.0f)
+      return fail(DM_ERR_POSITIVE_PARAMETER, "RMSNorm epsilon requires a finite positive parameter");
+    if (d->router_type != DM_F32 || d->input_type != DM_F32)
+      return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "Gemma router and input are f32");
+  } else {
+    if (!d->up) return fail(DM_ERR_INVALID_ARGUMENT, "null up pointer");
+  }
+  if (d->family == DM_FAMILY_QWEN35_MOE) {
+    if (d->router_type != DM_F32 || d->input_type != DM_F32)
+      return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "Qwen router and input are f32");
+    if (d->shared_intermediate > 0 && !d->shared_gate_vector)
+      return fail(DM_ERR_INVALID_ARGUMENT, "Qwen shared expert needs shared_gate_vector");
+  }
+  if (d->family == DM_FAMILY_GLM52) {
+    if (!d->correction_bias) return fail(DM_ERR_INVALID_ARGUMENT, "GLM needs correction_bias");
+    if (d->router_type != DM_BF16 && d->router_type != DM_F32)
+      return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "GLM router must be bf16 or f32");
+    if (d->input_type != DM_BF16 && d->input_type != DM_F32)
+      return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "GLM input must be bf16 or f32");
+    int g = d->n_groups <= 0 ? 1 : d->n_groups, kg = d->topk_groups <= 0 ? 1 : d->topk_groups;
+    if (d->experts % g || kg > g || g > 32 || (g > 1 && d->experts / g < 2))
+      return fail(DM_ERR_INVALID_ARGUMENT, "invalid expert groups %d/%d", g, kg);
+    if (d->top_k > kg * (d->experts / g)) return fail(DM_ERR_TOP_K, "top-k exceeds the kept groups");
+  }
+  if (d->shared_intermediate > 0) {
+    if (d->shared_intermediate != d->intermediate)
+      return fail(DM_ERR_INVALID_ARGUMENT, "shared intermediate must equal the routed intermediate");
+    if (!d->shared_gate || !d->shared_up || !d->shared_down)
+      return fail(DM_ERR_INVALID_ARGUMENT, "null shared expert pointer");
+    if (d->family == DM_FAMILY_GEMMA4)
+      return fail(DM_ERR_INVALID_ARGUMENT, "Gemma's shared FFN is outside the routed branch");
+  }
+  // vector loads need 16-byte aligned rows for the block formats that use them
+  auto aligned = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+  if ((d->gate_type == DM_Q4_K || d->gate_type == DM_BF16 || d->gate_type == DM_F32) &&
+      (!aligned(d->gate) || (d->up && !aligned(d->up)) ||
+       (d->shared_gate && (!aligned(d->shared_gate) || !aligned(d->shared_up)))))
+    return fail(DM_ERR_INVALID_ARGUMENT, "gate/up weights must be 16-byte aligned");
+  if ((d->down_type == DM_Q4_K || d->down_type == DM_BF16 || d->down_type == DM_F32) &&
+      (!aligned(d->down) || (d->shared_down && !aligned(d->shared_down))))
+    return fail(DM_ERR_INVALID_ARGUMENT, "down weights must be 16-byte aligned");
+  return DM_OK;
+}
+
+int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
+  if (tokens <= L->capacity) return DM_OK;
+  const dm_moe_desc &d = L->desc;
+  size_t T = (size_t)std::max(tokens, 1), H = d.hidden, I = d.intermediate, E = d.experts,
+         k = d.top_k;
+  size_t pairs = T * k + (L->shared ? T : 0);
+  auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+  size_t bytes = 0;
+  if (d.family == DM_FAMILY_GEMMA4) bytes += 2 * al(T * H * 4);
+  bytes += al(T * L->E1 * 4) + 2 * al(T * k * 4);
+  bytes += al((E + 1) * 4) + al((E + 2) * 4) + 2 * al(pairs * 4) + al((E + 1) * 4) + 2 * al(4);
+  bytes += al(pairs * I * 4) + al(pairs * H * 4);
+  if (L->scratch) cudaFree(L->scratch);
+  L->scratch = nullptr;
+  L->capacity = 0;
+  if (cudaMalloc(&L->scratch, bytes) != cudaSuccess)
+    return fail(DM_ERR_ALLOCATION, "could not allocate %zu bytes of layer scratch", bytes);
+  L->scratch_bytes = bytes;
+  dm::Arena arena{(uint8_t *)L->scratch, 0, bytes};
+  dm::ForwardArgs &a = L->args;
+  a.router_in = d.family == DM_FAMILY_GEMMA4 ? arena.take<float>(T * H) : nullptr;
+  a.expert_in = d.family == DM_FAMILY_GEMMA4 ? arena.take<float>(T * H) : nullptr;
+  a.logits = arena.take<float>(T * L->E1);
+  a.sel_idx = arena.take<uint32_t>(T * k);
+  a.sel_w = arena.take<float>(T * k);
+  a.counts = arena.take<int32_t>(E + 1);
+  a.offsets = arena.take<int32_t>(E + 2);
+  a.sorted = arena.take<int32_t>(pairs);
+  a.inverse = arena.take<int32_t>(pairs);
+  a.active = arena.take<int32_t>(E + 1);
+  a.n_active = arena.take<int32_t>(1);
+  a.status = arena.take<int32_t>(1);
+  a.h = arena.take<float>(pairs * I);
+  a.ysorted = arena.take<float>(pairs * H);
+  L->capacity = tokens;
+  return DM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t dm_moe_layer_create(dm_cuda_context *ctx, const dm_moe_desc *desc, dm_moe_layer **out) {
+  if (!ctx || !out) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  int32_t rc = validate_desc(desc);
+  if (rc != DM_OK) return rc;
+  cudaSetDevice(ctx->device);
+  auto *L = new (std::nothrow) dm_moe_layer();
+  if (!L) return fail(DM_ERR_ALLOCATION, "host allocation failed");
+  L->ctx = ctx;
+  L->desc = *desc;
+  dm_moe_desc &d = L->desc;
+  if (d.n_groups <= 0) d.n_groups = 1;
+  if (d.topk_groups <= 0) d.topk_groups = 1;
+  L->shared = d.shared_intermediate > 0;
+  const bool qwen_gate = d.family == DM_FAMILY_QWEN35_MOE && L->shared;
+  L->E1 = d.experts + (qwen_gate ? 1 : 0);
+  const uint64_t H = d.hidden, I = d.intermediate;
+  const bool fused = d.family == DM_FAMILY_GEMMA4;
+  L->gate_stride = (fused ? 2 * I : I) * dm::row_bytes(d.gate_type, H);
+  L->up_stride = L->gate_stride;
+  L->up_base = fused ? (const uint8_t *)d.gate + I * dm::row_bytes(d.gate_type, H)
+                     : (const uint8_t *)d.up;
+  L->down_stride = H * dm::row_bytes(d.down_type, I);
+  const int wbytes = d.router_type == DM_BF16 ? 2 : 4;
+  if (cudaMalloc(&L->router_t, (size_t)H * L->E1 * wbytes) != cudaSuccess) {
+    delete L;
+    return fail(DM_ERR_ALLOCATION, "could not allocate the transposed router");
+  }
+  dm::launch_transpose_router(d.router, d.router_type == DM_BF16, d.experts, d.hidden,
+                              qwen_gate ? d.shared_gate_vector : nullptr, L->router_t,
+                              ctx->stream);
+  cudaError_t err = cudaStreamSynchronize(ctx->stream);
+  if (err == cudaSuccess) err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    cudaFree(L->router_t);
+    delete L;
+    return cuda_fail(err, "router transpose");
+  }
+  *out = L;
+  return DM_OK;
+}
+
+void dm_moe_layer_destroy(dm_moe_layer *L) {
+  if (!L) return;
+  cudaSetDevice(L->ctx->device);
+  cudaStreamSynchronize(L->ctx->stream);
+  if (L->router_t) cudaFree(L->router_t);
+  if (L->scratch) cudaFree(L->scratch);
+  if (L->io) cudaFree(L->io);
+  for (auto &e : L->events)
+    if (e) cudaEventDestroy(e);
+  delete L;
+}
+
+int32_t dm_moe_set_profiling(dm_moe_layer *L, int32_t enable) {
+  if (!L) return fail(DM_ERR_INVALID_ARGUMENT, "null layer");
+  cudaSetDevice(L->ctx->device);
+  if (enable && !L->events[0]) {
+    for (auto &e : L->events) DM_CUDA(cudaEventCreate(&e), "event create");
+  }
+  L->profiling = enable != 0;
+  return DM_OK;
+}
+
+int32_t dm_moe_stage_times(dm_moe_layer *L, float *milliseconds, int32_t capacity) {
+  if (!L || !milliseconds) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  if (!L->profiling || !L->events[0]) return fail(DM_ERR_INVALID_ARGUMENT, "profiling is off");
+  cudaSetDevice(L->ctx->device);
+  DM_CUDA(cudaEventSynchronize(L->events[dm::kStageCount]), "event sync");
+  int n = std::min<int>(capacity, dm::kStageCount);
+  for (int i = 0; i < n; i++)
+    DM_CUDA(cudaEventElapsedTime(&milliseconds[i], L->events[i], L->events[i + 1]), "elapsed");
+  return n;
+}
+
+const char *dm_moe_stage_name(int32_t stage) {
+  static const char *names[dm::kStageCount] = {"prep", "router", "topk", "dispatch",
+                                              "expert_up", "expert_down", "combine"};
+  return stage >= 0 && stage < dm::kStageCount ? names[stage] : "";
+}
+
+int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
+                       uint32_t *sel_idx, float *sel_weight, void *stream) {
+  if (!L || !x || !y) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  if (tokens < 0) return fail(DM_ERR_INVALID_ARGUMENT, "negative token count");
+  if (tokens == 0) return DM_OK;
+  if ((int64_t)tokens * L->desc.top_k > INT32_MAX / 2 || tokens > (1 << 22))
+    return fail(DM_ERR_OVERFLOW, "too many tokens in one call (limit 4194304)");
+  cudaSetDevice(L->ctx->device);
+  int32_t rc = ensure_layer_scratch(L, tokens);
+  if (rc != DM_OK) return rc;
+  const dm_moe_desc &d = L->desc;
+  dm::ForwardArgs a = L->args;
+  a.family = d.family;
+  a.T = tokens;
+  a.H = d.hidden;
+  a.I = d.intermediate;
+  a.E = d.experts;
+  a.k = d.top_k;
+  a.E1 = L->E1;
+  a.shared = L->shared;
+  a.n_groups = d.n_groups;
+  a.topk_groups = d.topk_groups;
+  a.normalize = d.normalize_topk;
+  a.routed_scale = d.routed_scale;
+  a.epsilon = d.epsilon;
+  a.inv_sqrt_hidden = 1.0f / std::sqrt((float)d.hidden);
+  a.input_bf16 = d.input_type == DM_BF16;
+  a.x = x;
+  a.y = y;
+  a.router_bf16 = d.router_type == DM_BF16;
+  a.router_t = L->router_t;
+  a.bias = d.correction_bias;
+  a.router_scale = d.router_scale;
+  a.routed_pre_norm = d.routed_pre_norm;
+  a.expert_scale = d.expert_scale;
+  a.logit_bias = d.family == DM_FAMILY_GLM52 ? nullptr : d.router_logit_bias;
+  a.gate_type = d.gate_type;
+  a.up_type = d.family == DM_FAMILY_GEMMA4 ? d.gate_type : d.up_type;
+  a.down_type = d.down_type;
+  a.gate = (const uint8_t *)d.gate;
+  a.up = L->up_base;
+  a.down = (const uint8_t *)d.down;
+  a.gate_stride = L->gate_stride;
+  a.up_stride = L->up_stride;
+  a.down_stride = L->down_stride;
+  a.sh_gate = (const uint8_t *)d.shared_gate;
+  a.sh_up = (const uint8_t *)d.shared_up;
+  a.sh_down = (const uint8_t *)d.shared_down;
+  if (sel_idx) a.sel_idx = sel_idx;
+  if (sel_weight) a.sel_w = sel_weight;
+  cudaStream_t s = (cudaStream_t)stream;
+  DM_CUDA(cudaMemsetAsync(a.status, 0, 4, s), "status reset");
+  int launches = dm::launch_forward(a, s, L->profiling ? L->events : nullptr);
+  DM_CUDA(cudaGetLastError(), "MoE forward launch");
+  L->last_tokens = tokens;
+  L->last_launches = launches;
+  // keep where the dispatch of this call lives for dm_moe_last_dispatch
+  L->args.sel_idx = L->args.sel_idx;
+  return DM_OK;
+}
+
+int32_t dm_moe_forward_host(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
+                            uint32_t *sel_idx, float *sel_weight) {
+  if (!L || !x || !y) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  if (tokens < 0) return fail(DM_ERR_INVALID_ARGUMENT, "negative token count");
+  if (tokens == 0) return DM_OK;
+  cudaSetDevice(L->ctx->device);
+  const dm_moe_desc &d = L->desc;
+  size_t xb = (size_t)tokens * d.hidden * (d.input_type == DM_BF16 ? 2 : 4);
+  size_t yb = (size_t)tokens * d.hidden * 4;
+  size_t need = ((xb + 255) & ~size_t(255)) + yb;
+  if (need > L->io_bytes) {
+    if (L->io) cudaFree(L->io);
+    L->io = nullptr;
+    L->io_bytes = 0;
+    if (cudaMalloc(&L->io, need) != cudaSuccess)
+      return fail(DM_ERR_ALLOCATION, "could not allocate %zu bytes of staging", need);
+    L->io_bytes = need;
+  }
+  void *xd = L->io;
+  float *yd = (float *)((uint8_t *)L->io + ((xb + 255) & ~size_t(255)));
+  cudaStream_t s = L->ctx->stream;
+  DM_CUDA(cudaMemcpyAsync(xd, x, xb, cudaMemcpyHostToDevice, s), "input copy");
+  int32_t rc = dm_moe_forward(L, xd, yd, tokens, nullptr, nullptr, s);
+  if (rc != DM_OK) return rc;
+  int32_t status = 0;
+  DM_CUDA(cudaMemcpyAsync(y, yd, yb, cudaMemcpyDeviceToHost, s), "output copy");
+  if (sel_idx)
+    DM_CUDA(cudaMemcpyAsync(sel_idx, L->args.sel_idx, (size_t)tokens * d.top_k * 4,
+                            cudaMemcpyDeviceToHost, s), "selection copy");
+  if (sel_weight)
+    DM_CUDA(cudaMemcpyAsync(sel_weight, L->args.sel_w, (size_t)tokens * d.top_k * 4,
+                            cudaMemcpyDeviceToHost, s), "weight copy");
+  DM_CUDA(cudaMemcpyAsync(&status, L->args.status, 4, cudaMemcpyDeviceToHost, s), "status copy");
+  DM_CUDA(cudaStreamSynchronize(s), "MoE forward");
+  if (status == dm::kStatusNonFiniteRouter)
+    return fail(DM_ERR_NON_FINITE, "router produced a non-finite score");
+  if (status == dm::kStatusNonFiniteNorm)
+    return fail(DM_ERR_NON_FINITE, "RMSNorm received a non-finite value");
+  return DM_OK;
+}
+
+int32_t dm_moe_last_dispatch(dm_moe_layer *L, int32_t *counts, int32_t *offsets,
+                             int32_t *sorted_pairs, int32_t *inverse) {
+  if (!L) return fail(DM_ERR_INVALID_ARGUMENT, "null layer");
+  if (L->last_tokens == 0) return DM_OK;
+  cudaSetDevice(L->ctx->device);
+  const int E = L->desc.experts;
+  const size_t P = (size_t)L->last_tokens * L->desc.top_k;
+  DM_CUDA(cudaDeviceSynchronize(), "dispatch sync");
+  if (counts) DM_CUDA(cudaMemcpy(counts, L->args.counts, E * 4, cudaMemcpyDeviceToHost), "copy");
+  if (offsets) DM_CUDA(cudaMemcpy(offsets, L->args.offsets, (E + 1) * 4, cudaMemcpyDeviceToHost), "copy");
+  if (sorted_pairs) DM_CUDA(cudaMemcpy(sorted_pairs, L->args.sorted, P * 4, cudaMemcpyDeviceToHost), "copy");
+  if (inverse) DM_CUDA(cudaMemcpy(inverse, L->args.inverse, P * 4, cudaMemcpyDeviceToHost), "copy");
+  return DM_OK;
+}
+
+int32_t dm_moe_last_launch_count(const dm_moe_layer *L) { return L ? L->last_launches : 0; }
+
+}  // extern "C"

@@ -1,0 +1,858 @@
+// dm_kernels.cu -- sm_100a kernels of the routed-expert path (router -> top-k ->
+// dispatch -> expert gate/up -> expert down -> combine) and the Metal-style
+// operators (matvec, top-k softmax, gelu/silu multiply, rms_norm).
+//
+// Bit-exactness rules (the parts the reference's selection depends on):
+//   * router logits are one sequential chain per (token, expert) in column order:
+//     fma for the GGUF path (src/cpu.rs:389-397), multiply-then-add for GLM
+//     (src/glm52/cpu.rs:1177-1185); every op uses an explicit _rn intrinsic so
+//     nothing is contracted or reassociated;
+//   * Gemma's router input reproduces src/cpu.rs:99-143 and src/gemma4/cpu.rs:562-573;
+//   * top-k orders by (value desc, index asc) under the IEEE total order.
+// Expert products accumulate in f32 in a different order than the reference and
+// are held to the relative-L2 tolerance instead.
+#include "dm_kernels.cuh"
+
+#include <algorithm>
+
+namespace dm {
+
+// ---------------------------------------------------------------------------
+// small helpers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long other = __shfl_xor_sync(0xffffffffu, v, o);
+    v = other > v ? other : v;
+  }
+  return v;
+}
+
+__device__ __forceinline__ float load_as_f32(const void *p, size_t i, bool bf16) {
+  if (bf16) return bf16_bits_to_f32(reinterpret_cast<const uint16_t *>(p)[i]);
+  return reinterpret_cast<const float *>(p)[i];
+}
+
+template <typename F>
+static void set_smem(F *kernel, size_t bytes) {
+  if (bytes > 48 * 1024)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+// ---------------------------------------------------------------------------
+// router transpose (layer set-up): [E][H] -> [H][E1], optional extra column E
+// ---------------------------------------------------------------------------
+
+__global__ void transpose_router_kernel(const void *src, int bf16, int E, int H,
+                                        const float *extra, void *dst, int E1) {
+  size_t n = (size_t)H * E1;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    int h = (int)(idx / E1), e = (int)(idx % E1);
+    if (bf16) {
+      uint16_t v = e < E ? reinterpret_cast<const uint16_t *>(src)[(size_t)e * H + h] : 0;
+      reinterpret_cast<uint16_t *>(dst)[idx] = v;
+    } else {
+      float v = e < E ? reinterpret_cast<const float *>(src)[(size_t)e * H + h] : extra[h];
+      reinterpret_cast<float *>(dst)[idx] = v;
+    }
+  }
+}
+
+int launch_transpose_router(const void *src, int src_bf16, int E, int H, const float *extra_col,
+                            void *dst, cudaStream_t stream) {
+  int E1 = E + (extra_col ? 1 : 0);
+  size_t n = (size_t)H * E1;
+  int blocks = (int)std::min<size_t>((n + 255) / 256, 4096);
+  transpose_router_kernel<<<blocks, 256, 0, stream>>>(src, src_bf16, E, H, extra_col, dst, E1);
+  return 1;
+}
+
+// ---------------------------------------------------------------------------
+// Gemma router / expert input (src/gemma4/cpu.rs:559-573, rms_norm src/cpu.rs:99-143)
+// ---------------------------------------------------------------------------
+
+constexpr int kPrepTokens = 8;
+
+__global__ void __launch_bounds__(256) gemma_prep_kernel(ForwardArgs a) {
+  extern __shared__ float xs[];  // [kPrepTokens][H + 1]
+  __shared__ float inv_s[kPrepTokens];
+  const int H = a.H, HP = H + 1;
+  const int t0 = blockIdx.x * kPrepTokens;
+  const int nt = min(kPrepTokens, a.T - t0);
+  const float *x = reinterpret_cast<const float *>(a.x);
+  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
+    int tt = idx / H, i = idx - tt * H;
+    xs[tt * HP + i] = x[(size_t)(t0 + tt) * H + i];
+  }
+  __syncthreads();
+  if (threadIdx.x < nt) {
+    const float *row = xs + threadIdx.x * HP;
+    float s = 0.0f;
+    for (int i = 0; i < H; i++) s = __fmaf_rn(row[i], row[i], s);
+    float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)H), a.epsilon)));
+    if (!isfinite(inv)) atomicExch(a.status, kStatusNonFiniteNorm);
+    inv_s[threadIdx.x] = inv;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
+    int tt = idx / H, i = idx - tt * H;
+    float v = xs[tt * HP + i], inv = inv_s[tt];
+    size_t o = (size_t)(t0 + tt) * H + i;
+    a.router_in[o] = __fmul_rn(__fmul_rn(v, inv), __fmul_rn(a.router_scale[i], a.inv_sqrt_hidden));
+    a.expert_in[o] = __fmul_rn(__fmul_rn(v, a.routed_pre_norm[i]), inv);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// router logits: one sequential chain per (token, expert)
+// ---------------------------------------------------------------------------
+
+template <bool GLM>
+__device__ __forceinline__ float chain_step(float w, float x, float s) {
+  if (GLM) return __fadd_rn(s, __fmul_rn(w, x));
+  return __fmaf_rn(w, x, s);
+}
+
+// Few tokens: a CTA stages the [H][8] column tile of the transposed router and
+// up to RT token rows in shared memory, then 8*RT threads run the chains.
+constexpr int kSmallExperts = 8;
+
+template <bool GLM, bool WBF16, bool XBF16>
+__global__ void __launch_bounds__(256) router_small_kernel(const void *wt, const void *x, int T,
+                                                          int H, int E1, int RT,
+                                                          const float *lbias, int E,
+                                                          float *logits) {
+  extern __shared__ float smem[];
+  float *xs = smem;                                         // [RT][H + 1]
+  uint16_t *ws16 = reinterpret_cast<uint16_t *>(xs + RT * (H + 1));
+  float *ws32 = reinterpret_cast<float *>(ws16);            // [H][8]
+  const int e0 = blockIdx.x * kSmallExperts, t0 = blockIdx.y * RT;
+  const int nt = min(RT, T - t0), HP = H + 1;
+  for (int idx = threadIdx.x; idx < H * kSmallExperts; idx += blockDim.x) {
+    int h = idx / kSmallExperts, e = e0 + idx % kSmallExperts;
+    if (WBF16)
+      ws16[idx] = e < E1 ? reinterpret_cast<const uint16_t *>(wt)[(size_t)h * E1 + e] : 0;
+    else
+      ws32[idx] = e < E1 ? reinterpret_cast<const float *>(wt)[(size_t)h * E1 + e] : 0.0f;
+  }
+  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
+    int tt = idx / H, i = idx - tt * H;
+    xs[tt * HP + i] = load_as_f32(x, (size_t)(t0 + tt) * H + i, XBF16);
+  }
+  __syncthreads();
+  int el = threadIdx.x % kSmallExperts, tl = threadIdx.x / kSmallExperts;
+  if (tl < nt && e0 + el < E1) {
+    const float *xr = xs + tl * HP;
+    float s = GLM ? -0.0f : 0.0f;
+#pragma unroll 8
+    for (int h = 0; h < H; h++) {
+      float w = WBF16 ? bf16_bits_to_f32(ws16[h * kSmallExperts + el]) : ws32[h * kSmallExperts + el];
+      s = chain_step<GLM>(w, xr[h], s);
+    }
+    if (lbias && e0 + el < E) s = __fadd_rn(s, lbias[e0 + el]);
+    logits[(size_t)(t0 + tl) * E1 + e0 + el] = s;
+  }
+}
+
+// Many tokens: thread = token, 16 experts per thread (16 independent chains),
+// column chunks of 32 staged through shared memory.
+constexpr int kTiledTokens = 64, kTiledExperts = 16, kTiledChunk = 32;
+
+template <bool GLM, bool WBF16, bool XBF16>
+__global__ void __launch_bounds__(kTiledTokens) router_tiled_kernel(const void *wt, const void *x,
+                                                                  int T, int H, int E1,
+                                                                  const float *lbias, int E,
+                                                                  float *logits) {
+  __shared__ float xs[kTiledChunk][kTiledTokens + 1];
+  __shared__ __align__(16) float ws[kTiledChunk][kTiledExperts];
+  const int e0 = blockIdx.x * kTiledExperts, t0 = blockIdx.y * kTiledTokens;
+  const int tid = threadIdx.x;
+  float acc[kTiledExperts];
+#pragma unroll
+  for (int j = 0; j < kTiledExperts; j++) acc[j] = GLM ? -0.0f : 0.0f;
+  for (int h0 = 0; h0 < H; h0 += kTiledChunk) {
+    int hc = min(kTiledChunk, H - h0);
+    __syncthreads();
+    for (int idx = tid; idx < kTiledTokens * kTiledChunk; idx += kTiledTokens) {
+      int tl = idx / kTiledChunk, hh = idx % kTiledChunk;
+      float v = 0.0f;
+      if (t0 + tl < T && hh < hc) v = load_as_f32(x, (size_t)(t0 + tl) * H + h0 + hh, XBF16);
+      xs[hh][tl] = v;
+    }
+    for (int idx = tid; idx < kTiledChunk * kTiledExperts; idx += kTiledTokens) {
+      int hh = idx / kTiledExperts, el = idx % kTiledExperts;
+      float v = 0.0f;
+      if (hh < hc && e0 + el < E1) v = load_as_f32(wt, (size_t)(h0 + hh) * E1 + e0 + el, WBF16);
+      ws[hh][el] = v;
+    }
+    __syncthreads();
+    for (int hh = 0; hh < hc; hh++) {
+      float xv = xs[hh][tid];
+#pragma unroll
+      for (int j = 0; j < kTiledExperts; j += 4) {
+        float4 w4 = *reinterpret_cast<const float4 *>(&ws[hh][j]);
+        acc[j] = chain_step<GLM>(w4.x, xv, acc[j]);
+        acc[j + 1] = chain_step<GLM>(w4.y, xv, acc[j + 1]);
+        acc[j + 2] = chain_step<GLM>(w4.z, xv, acc[j + 2]);
+        acc[j + 3] = chain_step<GLM>(w4.w, xv, acc[j + 3]);
+      }
+    }
+  }
+  if (t0 + tid < T) {
+#pragma unroll
+    for (int j = 0; j < kTiledExperts; j++)
+      if (e0 + j < E1)
+        logits[(size_t)(t0 + tid) * E1 + e0 + j] =
+            (lbias && e0 + j < E) ? __fadd_rn(acc[j], lbias[e0 + j]) : acc[j];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// top-k: one warp per token
+// ---------------------------------------------------------------------------
+
+constexpr int kTopkWarps = 4;
+constexpr int kMaxGlmExperts = 1024;
+
+// softmax family: src/cpu.rs:234-260 (+ softmax_in_place :196-231)
+__global__ void __launch_bounds__(32 * kTopkWarps) topk_softmax_kernel(
+    const float *logits, int T, int E1, int E, int k, uint32_t *sel_idx, float *sel_w,
+    int32_t *status) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kTopkWarps + warp;
+  if (t >= T) return;
+  const float *lg = logits + (size_t)t * E1;
+  bool bad = false;
+  for (int e = lane; e < E; e += 32) bad |= !isfinite(lg[e]);
+  if (__any_sync(0xffffffffu, bad)) {
+    // flag the error and leave an in-range selection so later kernels stay in bounds
+    if (lane == 0) atomicExch(status, kStatusNonFiniteRouter);
+    for (int r = lane; r < k; r += 32) {
+      sel_idx[(size_t)t * k + r] = (uint32_t)r;
+      sel_w[(size_t)t * k + r] = 0.0f;
+    }
+    return;
+  }
+  unsigned long long last = ~0ull;
+  float maximum = 0.0f, sum = 0.0f;
+  float vals[32];
+  uint32_t idxs[32];
+  for (int r = 0; r < k; r++) {
+    unsigned long long best = 0;
+    for (int e = lane; e < E; e += 32) {
+      unsigned long long key = rank_key(lg[e], (uint32_t)e);
+      if (key < last && key > best) best = key;
+    }
+    best = warp_max_u64(best);
+    last = best;
+    uint32_t idx = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+    if (idx >= (uint32_t)E) idx = 0;  // unreachable for k <= eligible experts; keeps reads in range
+    if (r < 32) {
+      idxs[r] = idx;
+      vals[r] = lg[idx];
+    }
+  }
+  if (lane == 0) {
+    maximum = -INFINITY;
+    for (int r = 0; r < k; r++) maximum = fmaxf(maximum, vals[r]);
+    for (int r = 0; r < k; r++) {
+      vals[r] = exp_f32_cr(__fsub_rn(vals[r], maximum));
+      sum = __fadd_rn(sum, vals[r]);
+    }
+    for (int r = 0; r < k; r++) {
+      sel_idx[(size_t)t * k + r] = idxs[r];
+      sel_w[(size_t)t * k + r] = __fdiv_rn(vals[r], sum);
+    }
+  }
+}
+
+// sigmoid + correction bias (+ restated group limit): src/glm52/cpu.rs:731-754
+__global__ void __launch_bounds__(32 * kTopkWarps) topk_sigmoid_kernel(
+    const float *logits, int T, int E1, int E, int k, const float *bias, int n_groups,
+    int topk_groups, int normalize, uint32_t *sel_idx, float *sel_w, int32_t *status) {
+  __shared__ float choice_s[kTopkWarps][kMaxGlmExperts];
+  __shared__ unsigned char keep_s[kTopkWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kTopkWarps + warp;
+  if (t >= T) return;
+  const float *lg = logits + (size_t)t * E1;
+  float *ch = choice_s[warp];
+  bool bad = false;
+  for (int e = lane; e < E; e += 32) {
+    float w = glm_sigmoid(lg[e]);
+    float c = __fadd_rn(w, bias[e]);
+    bad |= !isfinite(w) || !isfinite(c);
+    ch[e] = c;
+  }
+  if (__any_sync(0xffffffffu, bad)) {
+    // flag the error and leave an in-range selection so later kernels stay in bounds
+    if (lane == 0) atomicExch(status, kStatusNonFiniteRouter);
+    for (int r = lane; r < k; r += 32) {
+      sel_idx[(size_t)t * k + r] = (uint32_t)r;
+      sel_w[(size_t)t * k + r] = 0.0f;
+    }
+    return;
+  }
+  __syncwarp();
+  const int per_group = E / n_groups;
+  if (n_groups > 1) {
+    // group score = top1 + top2 of the group's choices; keep the best groups
+    unsigned long long gkey = 0;
+    if (lane < n_groups) {
+      unsigned long long k1 = 0, k2 = 0;
+      for (int i = 0; i < per_group; i++) {
+        int e = lane * per_group + i;
+        unsigned long long key = rank_key(ch[e], (uint32_t)e);
+        if (key > k1) {
+          k2 = k1;
+          k1 = key;
+        } else if (key > k2) {
+          k2 = key;
+        }
+      }
+      float c1 = ch[0xffffffffu - (uint32_t)(k1 & 0xffffffffu)];
+      float c2 = ch[0xffffffffu - (uint32_t)(k2 & 0xffffffffu)];
+      gkey = rank_key(__fadd_rn(c1, c2), (uint32_t)lane);
+    }
+    // rank of this group = number of groups with a larger key
+    int rank = 0;
+    for (int g = 0; g < n_groups; g++) {
+      unsigned long long other = __shfl_sync(0xffffffffu, gkey, g);
+      rank += other > gkey;
+    }
+    if (lane < n_groups) keep_s[warp][lane] = rank < topk_groups;
+    __syncwarp();
+  }
+  unsigned long long last = ~0ull;
+  float weights[32];
+  uint32_t idxs[32];
+  for (int r = 0; r < k; r++) {
+    unsigned long long best = 0;
+    for (int e = lane; e < E; e += 32) {
+      if (n_groups > 1 && !keep_s[warp][e / per_group]) continue;
+      unsigned long long key = rank_key(ch[e], (uint32_t)e);
+      if (key < last && key > best) best = key;
+    }
+    best = warp_max_u64(best);
+    last = best;
+    uint32_t idx = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+    if (idx >= (uint32_t)E) idx = 0;  // unreachable for k <= eligible experts; keeps reads in range
+    if (r < 32) {
+      idxs[r] = idx;
+      weights[r] = glm_sigmoid(lg[idx]);
+    }
+  }
+  if (lane == 0) {
+    float sum = -0.0f;
+    for (int r = 0; r < k; r++) sum = __fadd_rn(sum, weights[r]);
+    sum = __fadd_rn(sum, 1e-20f);
+    for (int r = 0; r < k; r++) {
+      sel_idx[(size_t)t * k + r] = idxs[r];
+      sel_w[(size_t)t * k + r] = normalize ? __fdiv_rn(weights[r], sum) : weights[r];
+    }
+  }
+}
+
+int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float *prob,
+                        int32_t *status, cudaStream_t stream) {
+  topk_softmax_kernel<<<1, 32 * kTopkWarps, 0, stream>>>(logits, 1, n, n, k, idx, prob, status);
+  return 1;
+}
+
+// ---------------------------------------------------------------------------
+// dispatch: one CTA, stable counting sort of the T*k pairs by expert
+// ---------------------------------------------------------------------------
+
+constexpr int kDispatchThreads = 1024, kDispatchWarps = kDispatchThreads / 32;
+
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs a) {
+  extern __shared__ int32_t sm[];
+  const int E = a.E, P = a.T * a.k;
+  int32_t *wc = sm;                              // [warps][E]
+  int32_t *total = sm + kDispatchWarps * E;      // [E + 1]
+  int32_t *flags = total + (E + 1);              // [E + 1] scan scratch
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kDispatchWarps * E; i += blockDim.x) wc[i] = 0;
+  __syncthreads();
+  const int chunk = (P + kDispatchWarps - 1) / kDispatchWarps;
+  const int begin = min(P, warp * chunk), end = min(P, begin + chunk);
+  for (int p = begin + lane; p < end; p += 32) {
+    uint32_t e = a.sel_idx[p];
+    if (e < (uint32_t)E) atomicAdd(&wc[warp * E + e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int running = 0;
+    for (int w = 0; w < kDispatchWarps; w++) {
+      int c = wc[w * E + e];
+      wc[w * E + e] = running;
+      running += c;
+    }
+    total[e] = running;
+  }
+  __syncthreads();
+  // exclusive scan over experts (serial by warp 0 lanes in chunks; E <= 1024)
+  if (threadIdx.x == 0) {
+    int running = 0;
+    for (int e = 0; e < E; e++) {
+      int c = total[e];
+      a.counts[e] = c;
+      a.offsets[e] = running;
+      flags[e] = running;
+      running += c;
+    }
+    a.offsets[E] = running;  // == P
+    a.counts[E] = a.shared ? a.T : 0;
+    a.offsets[E + 1] = running + (a.shared ? a.T : 0);
+    int n = 0;
+    for (int e = 0; e < E; e++)
+      if (total[e] > 0) a.active[n++] = e;
+    if (a.shared && a.T > 0) a.active[n++] = E;
+    *a.n_active = n;
+  }
+  __syncthreads();
+  for (int base = begin; base < end; base += 32) {
+    int p = base + lane;
+    bool valid = p < end;
+    unsigned vmask = __ballot_sync(0xffffffffu, valid);
+    if (valid) {
+      uint32_t e = a.sel_idx[p];
+      if (e >= (uint32_t)E) e = 0;  // rejected upstream; keep indices in range
+      unsigned peers = __match_any_sync(vmask, e);
+      int rank = __popc(peers & ((1u << lane) - 1u));
+      int pos = flags[e] + wc[warp * E + e] + rank;
+      a.sorted[pos] = p;
+      a.inverse[p] = pos;
+      __syncwarp(vmask);
+      if (rank == 0) wc[warp * E + e] += __popc(peers);
+    }
+    __syncwarp();
+  }
+  if (a.shared) {
+    for (int t = threadIdx.x; t < a.T; t += blockDim.x) {
+      a.sorted[P + t] = P + t;
+      a.inverse[P + t] = P + t;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// expert products (CUDA cores): a warp owns a row, lanes split its 32-element
+// units, each unit is dequantised once into registers and applied to a chunk of
+// up to TT tokens staged in shared memory ([TT][units][36] floats, padded so the
+// float4 reads of 32 lanes hit distinct banks).
+// ---------------------------------------------------------------------------
+
+constexpr int kExpertThreads = 256, kExpertWarps = kExpertThreads / 32, kUnitStride = 36;
+
+__device__ __forceinline__ int pair_token(const ForwardArgs &a, int pair) {
+  int P = a.T * a.k;
+  return pair < P ? pair / a.k : pair - P;
+}
+
+__device__ __forceinline__ float expert_input(const ForwardArgs &a, int token, int col) {
+  size_t o = (size_t)token * a.H + col;
+  if (a.family == kGemma) return a.expert_in[o];
+  return load_as_f32(a.x, o, a.input_bf16);
+}
+
+__device__ __forceinline__ float activate(const ForwardArgs &a, int expert, float g, float u) {
+  if (a.family == kGemma) return __fmul_rn(gelu_tanh(g), u);
+  if (a.family == kQwen) return __fmul_rn(qwen_silu(g), u);
+  if (expert == a.E) return __fmul_rn(glm_silu(g), u);  // GLM shared `mlp`
+  return __fmul_rn(glm_cached_silu(g), u);               // GLM routed experts
+}
+
+template <int TT>
+__device__ __forceinline__ void unit_dot(const float *w, const float *xs, int units, int u,
+                                         int nt, float *acc) {
+#pragma unroll
+  for (int t = 0; t < TT; t++) {
+    if (t < nt) {
+      const float4 *xv = reinterpret_cast<const float4 *>(xs + ((size_t)t * units + u) * kUnitStride);
+      float s = acc[t];
+#pragma unroll
+      for (int v = 0; v < 8; v++) {
+        float4 q = xv[v];
+        s = fmaf(w[4 * v], q.x, s);
+        s = fmaf(w[4 * v + 1], q.y, s);
+        s = fmaf(w[4 * v + 2], q.z, s);
+        s = fmaf(w[4 * v + 3], q.w, s);
+      }
+      acc[t] = s;
+    }
+  }
+}
+
+template <class U, int TT>
+__global__ void __launch_bounds__(kExpertThreads) expert_up_kernel(ForwardArgs a,
+                                                                  int rows_per_cta) {
+  extern __shared__ __align__(16) float xs[];
+  const int slot = blockIdx.y;
+  if (slot >= *a.n_active) return;
+  const int e = a.active[slot];
+  const int n = a.counts[e], base = a.offsets[e];
+  const int I = a.I, H = a.H, units = H / 32;
+  const int row0 = blockIdx.x * rows_per_cta;
+  if (row0 >= I) return;
+  const uint64_t rb = row_bytes(a.gate_type, H);
+  const uint8_t *G = e < a.E ? a.gate + (size_t)e * a.gate_stride : a.sh_gate;
+  const uint8_t *Up = e < a.E ? a.up + (size_t)e * a.up_stride : a.sh_up;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c0 = 0; c0 < n; c0 += TT) {
+    const int nt = min(TT, n - c0);
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
+      int tt = idx / H, col = idx - tt * H;
+      int tok = pair_token(a, a.sorted[base + c0 + tt]);
+      xs[((size_t)tt * units + (col >> 5)) * kUnitStride + (col & 31)] = expert_input(a, tok, col);
+    }
+    __syncthreads();
+    for (int r = warp; r < rows_per_cta; r += kExpertWarps) {
+      const int i = row0 + r;
+      if (i >= I) break;
+      float ag[TT], au[TT];
+#pragma unroll
+      for (int t = 0; t < TT; t++) ag[t] = au[t] = 0.0f;
+      const uint8_t *grow = G + (size_t)i * rb, *urow = Up + (size_t)i * rb;
+      for (int u = lane; u < units; u += 32) {
+        float w[32];
+        U::decode(grow, u, w);
+        unit_dot<TT>(w, xs, units, u, nt, ag);
+        U::decode(urow, u, w);
+        unit_dot<TT>(w, xs, units, u, nt, au);
+      }
+#pragma unroll
+      for (int t = 0; t < TT; t++) {
+        ag[t] = warp_sum(ag[t]);
+        au[t] = warp_sum(au[t]);
+      }
+      if (lane == 0) {
+        for (int t = 0; t < nt; t++)
+          a.h[(size_t)(base + c0 + t) * I + i] = activate(a, e, ag[t], au[t]);
+      }
+    }
+  }
+}
+
+template <class U, int TT>
+__global__ void __launch_bounds__(kExpertThreads) expert_down_kernel(ForwardArgs a,
+                                                                    int rows_per_cta) {
+  extern __shared__ __align__(16) float xs[];
+  const int slot = blockIdx.y;
+  if (slot >= *a.n_active) return;
+  const int e = a.active[slot];
+  const int n = a.counts[e], base = a.offsets[e];
+  const int I = a.I, H = a.H, units = I / 32;
+  const int row0 = blockIdx.x * rows_per_cta;
+  if (row0 >= H) return;
+  const uint64_t rb = row_bytes(a.down_type, I);
+  const uint8_t *D = e < a.E ? a.down + (size_t)e * a.down_stride : a.sh_down;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c0 = 0; c0 < n; c0 += TT) {
+    const int nt = min(TT, n - c0);
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nt * I; idx += blockDim.x) {
+      int tt = idx / I, col = idx - tt * I;
+      xs[((size_t)tt * units + (col >> 5)) * kUnitStride + (col & 31)] =
+          a.h[(size_t)(base + c0 + tt) * I + col];
+    }
+    __syncthreads();
+    for (int r = warp; r < rows_per_cta; r += kExpertWarps) {
+      const int row = row0 + r;
+      if (row >= H) break;
+      float acc[TT];
+#pragma unroll
+      for (int t = 0; t < TT; t++) acc[t] = 0.0f;
+      const uint8_t *drow = D + (size_t)row * rb;
+      for (int u = lane; u < units; u += 32) {
+        float w[32];
+        U::decode(drow, u, w);
+        unit_dot<TT>(w, xs, units, u, nt, acc);
+      }
+#pragma unroll
+      for (int t = 0; t < TT; t++) acc[t] = warp_sum(acc[t]);
+      if (lane == 0) {
+        for (int t = 0; t < nt; t++) a.ysorted[(size_t)(base + c0 + t) * H + row] = acc[t];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// weighted combine: selection order, deterministic, no atomics
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) combine_kernel(ForwardArgs a) {
+  const int t = blockIdx.x;
+  const int H = a.H, k = a.k, P = a.T * a.k;
+  float gate = 0.0f;
+  if (a.shared && a.family == kQwen) gate = qwen_sigmoid(a.logits[(size_t)t * a.E1 + a.E]);
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < k; j++) {
+      int p = t * k + j;
+      float v = a.ysorted[(size_t)a.inverse[p] * H + i];
+      float w = a.sel_w[p];
+      if (a.family == kGemma) {
+        acc = __fmaf_rn(v, __fmul_rn(w, a.expert_scale[a.sel_idx[p]]), acc);
+      } else if (a.family == kQwen) {
+        acc = __fmaf_rn(v, w, acc);
+      } else {
+        acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(v, w), a.routed_scale));
+      }
+    }
+    if (a.shared) {
+      float v = a.ysorted[(size_t)(P + t) * H + i];
+      acc = a.family == kQwen ? __fmaf_rn(v, gate, acc) : __fadd_rn(acc, v);
+    }
+    a.y[(size_t)t * H + i] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// forward orchestration
+// ---------------------------------------------------------------------------
+
+template <template <class, int> class K, int TT>
+static void *pick_kernel(int kind) {
+  switch (kind) {
+    case DM_Q4_K: return (void *)K<Q4KUnit, TT>::fn();
+    case DM_Q6_K: return (void *)K<Q6KUnit, TT>::fn();
+    case DM_Q5_0: return (void *)K<Q50Unit, TT>::fn();
+    case DM_Q8_0: return (void *)K<Q80Unit, TT>::fn();
+    case DM_BF16: return (void *)K<BF16Unit, TT>::fn();
+    case DM_F16: return (void *)K<F16Unit, TT>::fn();
+    case DM_F32: return (void *)K<F32Unit, TT>::fn();
+    default: return nullptr;
+  }
+}
+
+template <class U, int TT>
+struct UpK {
+  static decltype(&expert_up_kernel<U, TT>) fn() { return &expert_up_kernel<U, TT>; }
+};
+template <class U, int TT>
+struct DownK {
+  static decltype(&expert_down_kernel<U, TT>) fn() { return &expert_down_kernel<U, TT>; }
+};
+
+typedef void (*ExpertFn)(ForwardArgs, int);
+
+static int choose_tt(int columns) {
+  size_t per_token = (size_t)(columns / 32) * kUnitStride * sizeof(float);
+  return per_token * 8 <= 112 * 1024 ? 8 : 4;
+}
+
+static ExpertFn expert_fn(bool up, int kind, int tt) {
+  if (up) return (ExpertFn)(tt == 8 ? pick_kernel<UpK, 8>(kind) : pick_kernel<UpK, 4>(kind));
+  return (ExpertFn)(tt == 8 ? pick_kernel<DownK, 8>(kind) : pick_kernel<DownK, 4>(kind));
+}
+
+int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev) {
+  int launches = 0;
+  const bool glm = a.family == kGlm;
+  auto mark = [&](int stage) {
+    if (ev) cudaEventRecord(ev[stage], stream);
+  };
+  // 1. Gemma router / expert inputs
+  mark(kStagePrep);
+  const void *router_x = a.x;
+  bool router_x_bf16 = a.input_bf16;
+  if (a.family == kGemma) {
+    size_t smem = (size_t)kPrepTokens * (a.H + 1) * sizeof(float);
+    set_smem(gemma_prep_kernel, smem);
+    gemma_prep_kernel<<<(a.T + kPrepTokens - 1) / kPrepTokens, 256, smem, stream>>>(a);
+    launches++;
+    router_x = a.router_in;
+    router_x_bf16 = false;
+  }
+  // 2. router logits
+  mark(kStageRouter);
+  if (a.T <= 16) {
+    int RT = 4;
+    size_t wbytes = (size_t)a.H * kSmallExperts * (a.router_bf16 ? 2 : 4);
+    while (RT > 1 && wbytes + (size_t)RT * (a.H + 1) * 4 > 200 * 1024) RT >>= 1;
+    size_t smem = wbytes + (size_t)RT * (a.H + 1) * 4;
+    dim3 grid((a.E1 + kSmallExperts - 1) / kSmallExperts, (a.T + RT - 1) / RT);
+#define DM_ROUTER_SMALL(G, W, X)                                                            \
+  {                                                                                         \
+    auto fn = router_small_kernel<G, W, X>;                                                 \
+    set_smem(fn, smem);                                                                     \
+    fn<<<grid, 256, smem, stream>>>(a.router_t, router_x, a.T, a.H, a.E1, RT, a.logit_bias, a.E, a.logits);    \
+  }
+    if (glm && a.router_bf16 && router_x_bf16) DM_ROUTER_SMALL(true, true, true)
+    else if (glm && a.router_bf16) DM_ROUTER_SMALL(true, true, false)
+    else if (glm && router_x_bf16) DM_ROUTER_SMALL(true, false, true)
+    else if (glm) DM_ROUTER_SMALL(true, false, false)
+    else DM_ROUTER_SMALL(false, false, false)
+#undef DM_ROUTER_SMALL
+  } else {
+    dim3 grid((a.E1 + kTiledExperts - 1) / kTiledExperts, (a.T + kTiledTokens - 1) / kTiledTokens);
+#define DM_ROUTER_TILED(G, W, X) \
+  router_tiled_kernel<G, W, X><<<grid, kTiledTokens, 0, stream>>>(a.router_t, router_x, a.T, a.H, a.E1, a.logit_bias, a.E, a.logits);
+    if (glm && a.router_bf16 && router_x_bf16) DM_ROUTER_TILED(true, true, true)
+    else if (glm && a.router_bf16) DM_ROUTER_TILED(true, true, false)
+    else if (glm && router_x_bf16) DM_ROUTER_TILED(true, false, true)
+    else if (glm) DM_ROUTER_TILED(true, false, false)
+    else DM_ROUTER_TILED(false, false, false)
+#undef DM_ROUTER_TILED
+  }
+  launches++;
+  // 3. top-k
+  mark(kStageTopk);
+  int topk_blocks = (a.T + kTopkWarps - 1) / kTopkWarps;
+  if (glm)
+    topk_sigmoid_kernel<<<topk_blocks, 32 * kTopkWarps, 0, stream>>>(
+        a.logits, a.T, a.E1, a.E, a.k, a.bias, a.n_groups, a.topk_groups, a.normalize,
+        a.sel_idx, a.sel_w, a.status);
+  else
+    topk_softmax_kernel<<<topk_blocks, 32 * kTopkWarps, 0, stream>>>(
+        a.logits, a.T, a.E1, a.E, a.k, a.sel_idx, a.sel_w, a.status);
+  launches++;
+  // 4. dispatch
+  mark(kStageDispatch);
+  size_t dsmem = ((size_t)kDispatchWarps * a.E + 2 * (a.E + 1)) * sizeof(int32_t);
+  set_smem(dispatch_kernel, dsmem);
+  dispatch_kernel<<<1, kDispatchThreads, dsmem, stream>>>(a);
+  launches++;
+  // 5. gate/up (+activation) and 6. down, over the active experts
+  const int max_active = std::min(a.E + (a.shared ? 1 : 0), a.T * a.k + (a.shared ? 1 : 0));
+  mark(kStageUp);
+  {
+    int tt = choose_tt(a.H);
+    ExpertFn fn = expert_fn(true, a.gate_type, tt);
+    size_t smem = (size_t)tt * (a.H / 32) * kUnitStride * sizeof(float);
+    set_smem(fn, smem);
+    int rows_per_cta = kExpertWarps * 4;
+    dim3 grid((a.I + rows_per_cta - 1) / rows_per_cta, max_active);
+    fn<<<grid, kExpertThreads, smem, stream>>>(a, rows_per_cta);
+    launches++;
+  }
+  mark(kStageDown);
+  {
+    int tt = choose_tt(a.I);
+    ExpertFn fn = expert_fn(false, a.down_type, tt);
+    size_t smem = (size_t)tt * (a.I / 32) * kUnitStride * sizeof(float);
+    set_smem(fn, smem);
+    int rows_per_cta = kExpertWarps * 8;
+    dim3 grid((a.H + rows_per_cta - 1) / rows_per_cta, max_active);
+    fn<<<grid, kExpertThreads, smem, stream>>>(a, rows_per_cta);
+    launches++;
+  }
+  // 7. combine
+  mark(kStageCombine);
+  combine_kernel<<<a.T, 256, 0, stream>>>(a);
+  launches++;
+  mark(kStageCount);
+  return launches;
+}
+
+// ---------------------------------------------------------------------------
+// Metal-style operators
+// ---------------------------------------------------------------------------
+
+template <class U>
+__global__ void __launch_bounds__(256) gemv_unit_kernel(const uint8_t *w, int rows, int cols,
+                                                       uint64_t rb, const float *x, float *y) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const uint8_t *row = w + (size_t)warp * rb;
+  float acc = 0.0f;
+  for (int u = lane; u < cols / 32; u += 32) {
+    float wv[32];
+    U::decode(row, u, wv);
+#pragma unroll
+    for (int j = 0; j < 32; j++) acc = fmaf(wv[j], x[u * 32 + j], acc);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) y[warp] = acc;
+}
+
+// dense rows of any width (F32 / F16 / BF16), element by element
+__global__ void __launch_bounds__(256) gemv_dense_kernel(const uint8_t *w, int kind, int rows,
+                                                        int cols, const float *x, float *y) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  float acc = 0.0f;
+  for (int c = lane; c < cols; c += 32) {
+    size_t i = (size_t)warp * cols + c;
+    float v;
+    if (kind == DM_F32) v = reinterpret_cast<const float *>(w)[i];
+    else if (kind == DM_F16) v = f16_bits_to_f32(reinterpret_cast<const uint16_t *>(w)[i]);
+    else v = bf16_bits_to_f32(reinterpret_cast<const uint16_t *>(w)[i]);
+    acc = fmaf(v, x[c], acc);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) y[warp] = acc;
+}
+
+int launch_gemv(int kind, const uint8_t *w, int rows, int cols, const float *x, float *y,
+                cudaStream_t stream) {
+  int blocks = (rows + 7) / 8;
+  uint64_t rb = row_bytes(kind, cols);
+  bool aligned16 = ((uintptr_t)w % 16) == 0 && rb % 16 == 0;
+  switch (kind) {
+    case DM_Q4_K:
+      if (!aligned16) return -1;
+      gemv_unit_kernel<Q4KUnit><<<blocks, 256, 0, stream>>>(w, rows, cols, rb, x, y);
+      break;
+    case DM_Q6_K: gemv_unit_kernel<Q6KUnit><<<blocks, 256, 0, stream>>>(w, rows, cols, rb, x, y); break;
+    case DM_Q5_0: gemv_unit_kernel<Q50Unit><<<blocks, 256, 0, stream>>>(w, rows, cols, rb, x, y); break;
+    case DM_Q8_0: gemv_unit_kernel<Q80Unit><<<blocks, 256, 0, stream>>>(w, rows, cols, rb, x, y); break;
+    case DM_F32:
+    case DM_F16:
+    case DM_BF16: gemv_dense_kernel<<<blocks, 256, 0, stream>>>(w, kind, rows, cols, x, y); break;
+    default: return -1;
+  }
+  return 1;
+}
+
+__global__ void elementwise_kernel(int op, const float *a, const float *b, float *out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    float g = a[i];
+    // Metal gelu_mul / silu_mul (metal/kernels.metal:96-122) against the CPU forms
+    out[i] = op == kOpGeluMul ? __fmul_rn(gelu_tanh(g), b[i]) : __fmul_rn(glm_cached_silu(g), b[i]);
+  }
+}
+
+// rms_norm as src/cpu.rs:99-143: one sequential fma chain for the sum of squares
+__global__ void rms_norm_kernel(const float *x, const float *w, float *out, int n, float eps,
+                                int32_t *status) {
+  __shared__ float inv_s;
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s = __fmaf_rn(x[i], x[i], s);
+    float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)n), eps)));
+    if (!isfinite(inv)) *status = kStatusNonFiniteNorm;
+    inv_s = inv;
+  }
+  __syncthreads();
+  float inv = inv_s;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    out[i] = w ? __fmul_rn(__fmul_rn(x[i], w[i]), inv) : __fmul_rn(x[i], inv);
+}
+
+int launch_elementwise(int op, const float *a, const float *b, float *out, int n, float,
+                       cudaStream_t stream) {
+  int blocks = std::min((n + 255) / 256, 1024);
+  elementwise_kernel<<<blocks, 256, 0, stream>>>(op, a, b, out, n);
+  return 1;
+}
+
+int launch_rms_norm(const float *x, const float *w, float *out, int n, float eps,
+                    int32_t *status, cudaStream_t stream) {
+  rms_norm_kernel<<<1, 256, 0, stream>>>(x, w, out, n, eps, status);
+  return 1;
+}
+
+}  // namespace dm

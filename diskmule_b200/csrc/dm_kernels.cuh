@@ -1,0 +1,84 @@
+// dm_kernels.cuh -- kernel argument blocks and launch helpers of the MoE path.
+#pragma once
+
+#include "dm_common.cuh"
+
+namespace dm {
+
+enum Family { kGemma = DM_FAMILY_GEMMA4, kQwen = DM_FAMILY_QWEN35_MOE, kGlm = DM_FAMILY_GLM52 };
+
+// Everything a forward needs on the device, by value.
+struct ForwardArgs {
+  int family;
+  int T, H, I, E, k;       // tokens, hidden, intermediate, routed experts, top-k
+  int E1;                  // router columns: E (+1 for the Qwen shared gate vector)
+  int shared;              // 1 if a shared expert runs for every token
+  int n_groups, topk_groups, normalize;
+  float routed_scale, epsilon, inv_sqrt_hidden;
+  int input_bf16;          // x is bf16 (GLM) instead of f32
+  const void *x;           // [T, H]
+  float *y;                // [T, H]
+  // router
+  int router_bf16;
+  const void *router_t;    // transposed router [H][E1]
+  const float *bias;       // GLM correction bias [E]
+  const float *router_scale, *routed_pre_norm, *expert_scale;
+  const float *logit_bias; // optional [E], softmax families
+  // experts
+  int gate_type, up_type, down_type;
+  const uint8_t *gate, *up, *down;
+  uint64_t gate_stride, up_stride, down_stride;   // bytes per expert
+  const uint8_t *sh_gate, *sh_up, *sh_down;
+  // scratch
+  float *router_in;        // Gemma [T, H]
+  float *expert_in;        // Gemma [T, H] (routed_pre_norm applied)
+  float *logits;           // [T, E1]
+  uint32_t *sel_idx;       // [T, k]
+  float *sel_w;            // [T, k]
+  int32_t *counts;         // [E + 1]
+  int32_t *offsets;        // [E + 2]
+  int32_t *sorted;         // [T*k + T]
+  int32_t *inverse;        // [T*k + T]
+  int32_t *active;         // [E + 1] experts with tokens, ascending
+  int32_t *n_active;       // [1]
+  int32_t *status;         // [1] device error word (0 = ok)
+  float *h;                // [(T*k + T), I]
+  float *ysorted;          // [(T*k + T), H]
+};
+
+enum DeviceStatus : int32_t {
+  kStatusOk = 0,
+  kStatusNonFiniteRouter = 1,
+  kStatusNonFiniteNorm = 2,
+};
+
+// Forward stages, timed by optional events recorded at each stage's start.
+enum Stage {
+  kStagePrep = 0,
+  kStageRouter,
+  kStageTopk,
+  kStageDispatch,
+  kStageUp,
+  kStageDown,
+  kStageCombine,
+  kStageCount
+};
+
+// launchers (dm_kernels.cu); each returns the number of kernels launched or -1.
+// `ev`, when not null, holds kStageCount + 1 events recorded on `stream`.
+int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev);
+int launch_gemv(int kind, const uint8_t *w, int rows, int cols, const float *x, float *y,
+                cudaStream_t stream);
+int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float *prob,
+                        int32_t *status, cudaStream_t stream);
+int launch_elementwise(int op, const float *a, const float *b, float *out, int n,
+                       float eps, cudaStream_t stream);
+int launch_transpose_router(const void *src, int src_bf16, int E, int H, const float *extra_col,
+                            void *dst, cudaStream_t stream);
+
+int launch_rms_norm(const float *x, const float *w, float *out, int n, float eps,
+                    int32_t *status, cudaStream_t stream);
+
+enum ElementwiseOp { kOpGeluMul = 0, kOpSiluMul = 1 };
+
+}  // namespace dm

@@ -1,0 +1,229 @@
+"""Host-side mirror of the reference's Metal backend surface, over the C ABI.
+
+`CudaContext` mirrors `MetalContext` (src/metal.rs:179-1604): the same method
+names, argument meaning and error behaviour (a `DmError` whose `status` names the
+`MetalError` variant). `MoeLayer` is the batched routed-expert block that replaces
+the per-token, per-expert loop of src/gemma4/cpu.rs:559-611 / src/glm52/cpu.rs:
+711-778. Every call goes to libdiskmule_cuda.so; there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _native as N
+from ._native import DmError, check
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return C.c_void_p(a)
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class Buffer:
+    """A device buffer (MetalMappedBuffer / MetalOwnedBuffer, src/metal.rs:207-243)."""
+
+    def __init__(self, handle, ctx):
+        self._h = handle
+        self._ctx = ctx
+
+    @property
+    def handle(self):
+        return self._h
+
+    def __len__(self):
+        return N.lib().dm_buffer_length(self._h)
+
+    @property
+    def device_pointer(self) -> int:
+        return N.lib().dm_buffer_device_pointer(self._h) or 0
+
+    def write(self, data, offset: int = 0):
+        a = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        check(N.lib().dm_buffer_write(self._h, offset, _ptr(a), a.size))
+
+    def read(self, length: int | None = None, offset: int = 0) -> np.ndarray:
+        n = len(self) - offset if length is None else length
+        out = np.empty(n, dtype=np.uint8)
+        check(N.lib().dm_buffer_read(self._h, offset, _ptr(out), n))
+        return out
+
+    def free(self):
+        if self._h:
+            N.lib().dm_buffer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class CudaContext:
+    """MetalContext's method surface on one B200 (src/metal.rs:291-1434)."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        check(N.lib().dm_cuda_create(device, C.byref(h)))
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def device_name(self) -> str:
+        buf = C.create_string_buffer(256)
+        check(N.lib().dm_cuda_device_name(self._h, buf, 256))
+        return buf.value.decode()
+
+    def synchronize(self):
+        check(N.lib().dm_cuda_synchronize(self._h))
+
+    def map_read_only(self, data) -> Buffer:
+        a = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        h = C.c_void_p()
+        check(N.lib().dm_cuda_map_read_only(self._h, _ptr(a), a.size, C.byref(h)))
+        return Buffer(h, self)
+
+    def new_owned_buffer(self, length: int) -> Buffer:
+        h = C.c_void_p()
+        check(N.lib().dm_cuda_new_owned_buffer(self._h, length, C.byref(h)))
+        return Buffer(h, self)
+
+    def matvec(self, kind, rows, columns, encoded, input, output_len=None):
+        enc = np.ascontiguousarray(np.frombuffer(encoded, np.uint8) if isinstance(encoded, (bytes, bytearray)) else encoded).view(np.uint8).reshape(-1)
+        x = np.ascontiguousarray(input, dtype=np.float32)
+        out = np.zeros(rows if output_len is None else output_len, dtype=np.float32)
+        check(N.lib().dm_cuda_matvec(self._h, kind, rows, columns, _ptr(enc), enc.size,
+                                      _ptr(x), x.size, _ptr(out), out.size))
+        return out
+
+    def matvec_mapped(self, kind, rows, columns, mapped: Buffer, offset, length, input,
+                      output_len=None):
+        x = np.ascontiguousarray(input, dtype=np.float32)
+        out = np.zeros(rows if output_len is None else output_len, dtype=np.float32)
+        check(N.lib().dm_cuda_matvec_mapped(self._h, kind, rows, columns, mapped.handle, offset,
+                                             length, _ptr(x), x.size, _ptr(out), out.size))
+        return out
+
+    matvec_owned = matvec_mapped
+
+    def top_k_softmax(self, logits, k):
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        idx = np.zeros(max(k, 1), dtype=np.uint32)
+        prob = np.zeros(max(k, 1), dtype=np.float32)
+        check(N.lib().dm_cuda_top_k_softmax(self._h, _ptr(lg), lg.size, k, _ptr(idx), _ptr(prob)))
+        return [(int(i), float(p)) for i, p in zip(idx[:k], prob[:k])]
+
+    def _binary(self, fn, gate, up):
+        g = np.ascontiguousarray(gate, dtype=np.float32)
+        u = np.ascontiguousarray(up, dtype=np.float32)
+        if g.size != u.size:
+            raise DmError(N.ERR_VECTOR_LENGTH, "up length differs from gate")
+        out = np.zeros_like(g)
+        check(fn(self._h, _ptr(g), _ptr(u), _ptr(out), g.size))
+        return out
+
+    def gelu_mul(self, gate, up):
+        return self._binary(N.lib().dm_cuda_gelu_mul, gate, up)
+
+    def silu_mul(self, gate, up):
+        return self._binary(N.lib().dm_cuda_silu_mul, gate, up)
+
+    def rms_norm(self, input, weight, epsilon):
+        x = np.ascontiguousarray(input, dtype=np.float32)
+        w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+        if w is not None and w.size != x.size:
+            raise DmError(N.ERR_VECTOR_LENGTH, "RMSNorm weight length differs from input")
+        out = np.zeros_like(x)
+        check(N.lib().dm_cuda_rms_norm(self._h, _ptr(x), _ptr(w), x.size, epsilon, _ptr(out)))
+        return out
+
+    def close(self):
+        if self._h:
+            N.lib().dm_cuda_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class MoeLayer:
+    """The batched routed-expert block behind dm_moe_layer_create / dm_moe_forward.
+
+    `desc` is a `_native.MoeDesc` whose weight fields hold device addresses.
+    """
+
+    def __init__(self, ctx: CudaContext, desc: N.MoeDesc, keep_alive=()):
+        self.ctx = ctx
+        self.desc = desc
+        self._keep = list(keep_alive)
+        h = C.c_void_p()
+        check(N.lib().dm_moe_layer_create(ctx.handle, C.byref(desc), C.byref(h)))
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def forward(self, x_ptr: int, y_ptr: int, tokens: int, sel_idx_ptr=None, sel_w_ptr=None,
+                stream: int = 0):
+        """Stream-ordered forward on device pointers (dm_moe_forward)."""
+        check(N.lib().dm_moe_forward(self._h, C.c_void_p(x_ptr), C.c_void_p(y_ptr), tokens,
+                                      C.c_void_p(sel_idx_ptr) if sel_idx_ptr else None,
+                                      C.c_void_p(sel_w_ptr) if sel_w_ptr else None,
+                                      C.c_void_p(stream) if stream else None))
+
+    def forward_host(self, x: np.ndarray):
+        """Synchronous forward on host arrays (dm_moe_forward_host): (y, indices, weights)."""
+        x = np.ascontiguousarray(x)
+        T = x.shape[0]
+        H, k = self.desc.hidden, self.desc.top_k
+        y = np.zeros((T, H), dtype=np.float32)
+        idx = np.zeros((T, k), dtype=np.uint32)
+        w = np.zeros((T, k), dtype=np.float32)
+        check(N.lib().dm_moe_forward_host(self._h, _ptr(x), _ptr(y), T, _ptr(idx), _ptr(w)))
+        return y, idx, w
+
+    def last_dispatch(self, tokens: int):
+        E, k = self.desc.experts, self.desc.top_k
+        counts = np.zeros(E, np.int32)
+        offsets = np.zeros(E + 1, np.int32)
+        sorted_pairs = np.zeros(tokens * k, np.int32)
+        inverse = np.zeros(tokens * k, np.int32)
+        check(N.lib().dm_moe_last_dispatch(self._h, _ptr(counts), _ptr(offsets),
+                                            _ptr(sorted_pairs), _ptr(inverse)))
+        return counts, offsets, sorted_pairs, inverse
+
+    def last_launch_count(self) -> int:
+        return N.lib().dm_moe_last_launch_count(self._h)
+
+    def set_profiling(self, enable: bool):
+        check(N.lib().dm_moe_set_profiling(self._h, int(enable)))
+
+    def stage_times(self) -> dict[str, float]:
+        """Durations (ms) of the last forward's stages (needs set_profiling(True))."""
+        buf = (C.c_float * 16)()
+        n = N.lib().dm_moe_stage_times(self._h, buf, 16)
+        if n < 0:
+            check(n)
+        return {N.lib().dm_moe_stage_name(i).decode(): float(buf[i]) for i in range(n)}
+
+    def close(self):
+        if self._h:
+            N.lib().dm_moe_layer_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

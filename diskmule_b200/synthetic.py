@@ -1,0 +1,274 @@
+"""Seeded synthetic MoE layers with the shapes of the benchmark configurations.
+
+No checkpoints are available, so every weight is generated: block b of a tensor is
+a pure function of (seed, b) (include/diskmule_synth.h), written straight into HBM
+by a kernel or into host memory by the same code on the CPU, bit for bit equal.
+Shapes and value distributions follow the benchmark configurations:
+
+  gemma4  hidden 2816, 128 experts, top-8, intermediate 704, fused Q4_K gate_up,
+          Q5_0 down (Q4_K cannot encode K = 704), router f32 N(0, 0.02)
+  qwen35  hidden 2048, 512 experts, top-10, intermediate 512, Q4_K gate/up, Q6_K down,
+          shared expert + sigmoid gate vector f32 N(0, 0.02)
+  glm52   hidden 6144, 256 experts, top-8, intermediate 2048, bf16 N(0, 0.02), shared
+          expert, correction bias f32 N(0, 0.01), 8 groups / 4 kept, routed scale 2.5
+Block formats: f16 d (and dmin) uniform in [1e-3, 1e-2], all other bytes uniform.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _native as N
+from .moe import CudaContext, MoeLayer
+
+FAMILIES = {"gemma4": N.FAMILY_GEMMA4, "qwen35": N.FAMILY_QWEN35_MOE, "glm52": N.FAMILY_GLM52}
+
+CONFIGS = {
+    "gemma4": dict(family="gemma4", hidden=2816, intermediate=704, experts=128, top_k=8,
+                   gate_type=N.Q4_K, down_type=N.Q5_0, epsilon=1e-6),
+    "qwen35": dict(family="qwen35", hidden=2048, intermediate=512, experts=512, top_k=10,
+                   gate_type=N.Q4_K, down_type=N.Q6_K, shared=True),
+    "glm52": dict(family="glm52", hidden=6144, intermediate=2048, experts=256, top_k=8,
+                  gate_type=N.BF16, down_type=N.BF16, shared=True, n_groups=8, topk_groups=4,
+                  routed_scale=2.5, normalize=True),
+    # reduced shapes of the same families for fast parity sweeps
+    "gemma4-small": dict(family="gemma4", hidden=512, intermediate=128, experts=16, top_k=4,
+                         gate_type=N.Q4_K, down_type=N.Q5_0, epsilon=1e-6),
+    "gemma4-small-q8": dict(family="gemma4", hidden=512, intermediate=128, experts=16, top_k=4,
+                            gate_type=N.Q4_K, down_type=N.Q8_0, epsilon=1e-6),
+    "qwen35-small": dict(family="qwen35", hidden=512, intermediate=256, experts=32, top_k=4,
+                         gate_type=N.Q4_K, down_type=N.Q6_K, shared=True),
+    "glm52-small": dict(family="glm52", hidden=256, intermediate=128, experts=32, top_k=4,
+                        gate_type=N.BF16, down_type=N.BF16, shared=True, n_groups=4,
+                        topk_groups=2, routed_scale=2.5, normalize=True),
+    "glm52-small-flat": dict(family="glm52", hidden=256, intermediate=128, experts=16, top_k=2,
+                             gate_type=N.BF16, down_type=N.BF16, shared=True, n_groups=1,
+                             topk_groups=1, routed_scale=2.5, normalize=True),
+}
+
+SCALE_LO, SCALE_HI = 1e-3, 1e-2
+_BLOCK = {N.F32: (1, 4), N.F16: (1, 2), N.BF16: (1, 2), N.Q5_0: (32, 22), N.Q8_0: (32, 34),
+          N.Q4_K: (256, 144), N.Q6_K: (256, 210)}
+
+
+@dataclass
+class TensorSpec:
+    name: str
+    kind: int
+    rows: int
+    cols: int
+    experts: int = 1
+    seed: int = 0
+    sigma: float = 0.02
+
+    @property
+    def blocks_per_row(self) -> int:
+        e, _ = _BLOCK[self.kind]
+        assert self.cols % e == 0, (self.name, self.cols)
+        return self.cols // e
+
+    @property
+    def row_bytes(self) -> int:
+        return self.blocks_per_row * _BLOCK[self.kind][1]
+
+    @property
+    def expert_bytes(self) -> int:
+        return self.rows * self.row_bytes
+
+    @property
+    def nbytes(self) -> int:
+        return self.experts * self.expert_bytes
+
+    def _range(self, expert: int | None):
+        per = self.rows * self.blocks_per_row
+        return (0, per * self.experts) if expert is None else (expert * per, per)
+
+    def host(self, expert: int | None = None) -> np.ndarray:
+        """Bytes of the whole tensor, or of one expert's slice, generated on the CPU."""
+        first, n = self._range(expert)
+        out = np.empty(n * _BLOCK[self.kind][1], dtype=np.uint8)
+        N.check(N.lib().dm_synth_fill_host(self.kind, self.seed, first, n, self.sigma,
+                                           SCALE_LO, SCALE_HI, out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    def device_fill(self, ptr: int, expert: int | None = None, stream: int = 0):
+        first, n = self._range(expert)
+        N.check(N.lib().dm_synth_fill_device(self.kind, self.seed, first, n, self.sigma,
+                                             SCALE_LO, SCALE_HI, C.c_void_p(ptr),
+                                             C.c_void_p(stream) if stream else None))
+
+
+def layer_specs(cfg: dict, seed: int) -> dict[str, TensorSpec]:
+    H, I, E = cfg["hidden"], cfg["intermediate"], cfg["experts"]
+    fam = cfg["family"]
+    s = lambda i: seed * 1009 + i  # noqa: E731
+    specs = {}
+    if fam == "gemma4":
+        specs["router"] = TensorSpec("router", N.F32, E, H, 1, s(1), 0.02)
+        specs["gate"] = TensorSpec("gate_up", cfg["gate_type"], 2 * I, H, E, s(2))
+        specs["down"] = TensorSpec("down", cfg["down_type"], H, I, E, s(3))
+    elif fam == "qwen35":
+        specs["router"] = TensorSpec("router", N.F32, E, H, 1, s(1), 0.02)
+        specs["gate"] = TensorSpec("gate", cfg["gate_type"], I, H, E, s(2))
+        specs["up"] = TensorSpec("up", cfg["gate_type"], I, H, E, s(3))
+        specs["down"] = TensorSpec("down", cfg["down_type"], H, I, E, s(4))
+        if cfg.get("shared"):
+            specs["shared_gate"] = TensorSpec("shared_gate", cfg["gate_type"], I, H, 1, s(5))
+            specs["shared_up"] = TensorSpec("shared_up", cfg["gate_type"], I, H, 1, s(6))
+            specs["shared_down"] = TensorSpec("shared_down", cfg["down_type"], H, I, 1, s(7))
+            specs["shared_gate_vector"] = TensorSpec("shared_gate_vector", N.F32, 1, H, 1, s(8), 0.02)
+    else:
+        specs["router"] = TensorSpec("router", N.BF16, E, H, 1, s(1), 0.02)
+        specs["bias"] = TensorSpec("correction_bias", N.F32, 1, E, 1, s(9), 0.01)
+        specs["gate"] = TensorSpec("gate", N.BF16, I, H, E, s(2), 0.02)
+        specs["up"] = TensorSpec("up", N.BF16, I, H, E, s(3), 0.02)
+        specs["down"] = TensorSpec("down", N.BF16, H, I, E, s(4), 0.02)
+        if cfg.get("shared"):
+            specs["shared_gate"] = TensorSpec("shared_gate", N.BF16, I, H, 1, s(5), 0.02)
+            specs["shared_up"] = TensorSpec("shared_up", N.BF16, I, H, 1, s(6), 0.02)
+            specs["shared_down"] = TensorSpec("shared_down", N.BF16, H, I, 1, s(7), 0.02)
+    return specs
+
+
+def vectors(cfg: dict, seed: int) -> dict[str, np.ndarray]:
+    """Small per-feature vectors (Gemma norm scales, expert scales): U[0.5, 1.5)."""
+    rng = np.random.default_rng(seed * 7919 + 17)
+    out = {}
+    if cfg["family"] == "gemma4":
+        out["router_scale"] = rng.uniform(0.5, 1.5, cfg["hidden"]).astype(np.float32)
+        out["routed_pre_norm"] = rng.uniform(0.5, 1.5, cfg["hidden"]).astype(np.float32)
+        out["expert_scale"] = rng.uniform(0.5, 1.5, cfg["experts"]).astype(np.float32)
+    return out
+
+
+def zipf_bias(experts: int, s: float, seed: int) -> np.ndarray:
+    """log of Zipf(s) weights over a seeded permutation of the experts (skewed routing)."""
+    rng = np.random.default_rng(seed * 31 + 7)
+    ranks = rng.permutation(experts) + 1
+    z = 1.0 / ranks.astype(np.float64) ** s
+    z /= z.sum()
+    return np.log(z).astype(np.float32)
+
+
+def input_spec(cfg: dict, tokens: int, seed: int) -> TensorSpec:
+    kind = N.BF16 if cfg["family"] == "glm52" else N.F32
+    return TensorSpec("x", kind, tokens, cfg["hidden"], 1, seed * 1009 + 99, 1.0)
+
+
+@dataclass
+class SyntheticLayer:
+    """A device-resident synthetic layer plus the means to rebuild its bytes on the host."""
+
+    name: str
+    cfg: dict
+    seed: int
+    ctx: CudaContext
+    specs: dict
+    vecs: dict
+    buffers: dict = field(default_factory=dict)
+    layer: MoeLayer | None = None
+    logit_bias: np.ndarray | None = None
+
+    def ptr(self, key: str) -> int:
+        return self.buffers[key].device_pointer if key in self.buffers else 0
+
+    def host_weights(self, experts=None) -> dict:
+        """Oracle inputs: full tensors (or the listed experts, others zero)."""
+        cfg = self.cfg
+        w = dict(hidden=cfg["hidden"], intermediate=cfg["intermediate"], experts=cfg["experts"],
+                 top_k=cfg["top_k"], epsilon=cfg.get("epsilon", 1e-6))
+        for key, spec in self.specs.items():
+            if experts is None or spec.experts == 1:
+                w[key] = spec.host()
+            else:
+                full = np.zeros(spec.nbytes, dtype=np.uint8)
+                for e in experts:
+                    full[e * spec.expert_bytes:(e + 1) * spec.expert_bytes] = spec.host(e)
+                w[key] = full
+        for key in ("router", "shared_gate_vector"):
+            if key in w and self.specs[key].kind == N.F32:
+                w[key] = w[key].view(np.float32)
+        if "bias" in w:
+            w["correction_bias"] = w.pop("bias").view(np.float32)
+        w.update(self.vecs)
+        if self.logit_bias is not None:
+            w["router_logit_bias"] = self.logit_bias
+        fam = cfg["family"]
+        if fam == "gemma4":
+            w["gate_up_type"], w["gate_up"] = cfg["gate_type"], w.pop("gate")
+            w["down_type"] = cfg["down_type"]
+        elif fam == "qwen35":
+            w["gate_type"] = w["up_type"] = cfg["gate_type"]
+            w["down_type"] = cfg["down_type"]
+            if cfg.get("shared"):
+                w["shared_intermediate"] = cfg["intermediate"]
+        else:
+            w["weight_type"] = N.BF16
+            w["n_groups"], w["topk_groups"] = cfg["n_groups"], cfg["topk_groups"]
+            w["routed_scale"], w["normalize"] = cfg["routed_scale"], cfg["normalize"]
+            if cfg.get("shared"):
+                w["shared_intermediate"] = cfg["intermediate"]
+        return w
+
+    def inputs(self, tokens: int, seed: int) -> tuple[TensorSpec, np.ndarray]:
+        spec = input_spec(self.cfg, tokens, seed)
+        return spec, spec.host()
+
+    def close(self):
+        if self.layer is not None:
+            self.layer.close()
+            self.layer = None
+        for b in self.buffers.values():
+            b.free()
+        self.buffers.clear()
+
+
+def build_layer(ctx: CudaContext, name: str, seed: int = 1, logit_bias=None) -> SyntheticLayer:
+    cfg = dict(CONFIGS[name])
+    specs = layer_specs(cfg, seed)
+    vecs = vectors(cfg, seed)
+    sl = SyntheticLayer(name, cfg, seed, ctx, specs, vecs)
+    for key, spec in specs.items():
+        buf = ctx.new_owned_buffer(spec.nbytes)
+        spec.device_fill(buf.device_pointer)
+        sl.buffers[key] = buf
+    for key, v in vecs.items():
+        sl.buffers[key] = ctx.map_read_only(v)
+    if logit_bias is not None:
+        sl.logit_bias = np.ascontiguousarray(logit_bias, dtype=np.float32)
+        sl.buffers["router_logit_bias"] = ctx.map_read_only(sl.logit_bias)
+    ctx.synchronize()
+    d = N.MoeDesc()
+    d.family = FAMILIES[cfg["family"]]
+    d.hidden, d.intermediate, d.experts, d.top_k = (cfg["hidden"], cfg["intermediate"],
+                                                    cfg["experts"], cfg["top_k"])
+    d.n_groups = cfg.get("n_groups", 1)
+    d.topk_groups = cfg.get("topk_groups", 1)
+    d.normalize_topk = int(cfg.get("normalize", False))
+    d.routed_scale = cfg.get("routed_scale", 1.0)
+    d.epsilon = cfg.get("epsilon", 1e-6)
+    glm = cfg["family"] == "glm52"
+    d.input_type = N.BF16 if glm else N.F32
+    d.router_type = N.BF16 if glm else N.F32
+    d.router = sl.ptr("router")
+    d.correction_bias = sl.ptr("bias") or None
+    d.router_scale = sl.ptr("router_scale") or None
+    d.routed_pre_norm = sl.ptr("routed_pre_norm") or None
+    d.expert_scale = sl.ptr("expert_scale") or None
+    d.gate_type = cfg["gate_type"]
+    d.up_type = cfg["gate_type"]
+    d.down_type = cfg["down_type"]
+    d.gate = sl.ptr("gate")
+    d.up = sl.ptr("up") or None
+    d.down = sl.ptr("down")
+    if cfg.get("shared"):
+        d.shared_intermediate = cfg["intermediate"]
+        d.shared_gate = sl.ptr("shared_gate")
+        d.shared_up = sl.ptr("shared_up")
+        d.shared_down = sl.ptr("shared_down")
+        d.shared_gate_vector = sl.ptr("shared_gate_vector") or None
+    d.router_logit_bias = sl.ptr("router_logit_bias") or None
+    sl.layer = MoeLayer(ctx, d)
+    return sl

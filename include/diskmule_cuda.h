@@ -1,0 +1,217 @@
+/*
+ * diskmule_cuda.h -- C ABI of the B200 (sm_100a) backend for DiskMule's
+ * routed-expert (MoE) path.
+ *
+ * The Rust host binds these symbols from a `src/cuda.rs` that sits beside
+ * `src/metal.rs`; every entry point names the reference interface it replaces.
+ * Conventions follow the Metal backend (src/metal.rs):
+ *   - row-major [rows, columns] matrices, where GGUF dims are [columns, rows]
+ *     (src/gemma4/metal.rs:866-875);
+ *   - validation happens before any launch, with the error order of
+ *     `prepare_matvec` (src/metal.rs:1513-1560);
+ *   - `*_host` / operator calls take borrowed host slices and return after the
+ *     GPU finished (src/metal.rs:1562-1604);
+ *   - every call returns an int32_t status: 0 = ok, negative = dm_status.
+ * A context is used from one thread at a time (src/runtime.rs:741-760).
+ */
+#ifndef DISKMULE_CUDA_H
+#define DISKMULE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifndef DM_API
+#if defined(__GNUC__)
+#define DM_API __attribute__((visibility("default")))
+#else
+#define DM_API
+#endif
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes: MetalError (src/metal.rs:3-126), CpuError (src/cpu.rs:10-97)
+ *      and ExpertCacheError (src/expert.rs:13-42) variants reachable on this path ---- */
+typedef enum {
+  DM_OK = 0,
+  DM_ERR_NO_DEVICE = -1,              /* MetalError::NoDevice */
+  DM_ERR_ALLOCATION = -2,             /* MetalError::BufferAllocation */
+  DM_ERR_INVALID_ARGUMENT = -3,       /* null handle / pointer, bad descriptor */
+  DM_ERR_UNSUPPORTED_TENSOR_TYPE = -4,/* MetalError::UnsupportedTensorType */
+  DM_ERR_ELEMENT_COUNT = -5,          /* MetalError::InvalidElementCount */
+  DM_ERR_BYTE_LENGTH = -6,            /* MetalError::InvalidByteLength */
+  DM_ERR_INPUT_LENGTH = -7,           /* MetalError::InvalidInputLength */
+  DM_ERR_OUTPUT_LENGTH = -8,          /* MetalError::InvalidOutputLength */
+  DM_ERR_EMPTY_INPUT = -9,            /* MetalError::EmptyInput */
+  DM_ERR_NON_FINITE = -10,            /* MetalError::NonFinite, Glm52CpuError::InvalidRouterScore */
+  DM_ERR_TOP_K = -11,                 /* MetalError::InvalidTopK */
+  DM_ERR_MAPPED_RANGE = -12,          /* MetalError::MappedRange */
+  DM_ERR_OVERFLOW = -13,              /* MetalError::Overflow */
+  DM_ERR_COMMAND = -14,               /* MetalError::Command (a CUDA launch/runtime error) */
+  DM_ERR_INVALID_EXPERT = -15,        /* ExpertCacheError::InvalidExpert */
+  DM_ERR_INVALID_LAYER = -16,         /* ExpertCacheError::InvalidLayer */
+  DM_ERR_ALL_SLOTS_PINNED = -17,      /* ExpertCacheError::AllSlotsPinned */
+  DM_ERR_CANCELLED = -18,             /* ExpertCacheError::Cancelled */
+  DM_ERR_NO_SLOTS = -19,              /* ExpertCacheError::NoSlots */
+  DM_ERR_VECTOR_LENGTH = -20,         /* MetalError::InvalidVectorLength */
+  DM_ERR_POSITIVE_PARAMETER = -21,    /* MetalError::InvalidPositiveParameter */
+  DM_ERR_TIMEOUT = -22,               /* a bounded device or host wait ran out */
+  DM_ERR_NOT_BUILT = -23,             /* the call needs a component this build lacks */
+  DM_ERR_COMMUNICATOR = -24,          /* NCCL / expert-parallel exchange failed */
+} dm_status;
+
+/* GGML tensor type ids (src/gguf.rs:295-318) on the path. */
+typedef enum {
+  DM_F32 = 0,
+  DM_F16 = 1,
+  DM_Q5_0 = 6,
+  DM_Q8_0 = 8,
+  DM_Q4_K = 12,
+  DM_Q6_K = 14,
+  DM_BF16 = 30,
+} dm_tensor_type;
+
+typedef struct dm_cuda_context dm_cuda_context;
+typedef struct dm_buffer dm_buffer;
+typedef struct dm_moe_layer dm_moe_layer;
+
+/* Human-readable name of a status code, and the detail message of the last
+ * failing call on this thread (the Display text of the Rust error). */
+DM_API const char *dm_status_string(int32_t status);
+DM_API const char *dm_last_error_message(void);
+
+/* ---- context: MetalContext::new (src/metal.rs:291-346), device_name (:348-352) ---- */
+DM_API int32_t dm_cuda_create(int32_t device_ordinal, dm_cuda_context **out);
+DM_API void dm_cuda_destroy(dm_cuda_context *ctx);
+DM_API int32_t dm_cuda_device_name(const dm_cuda_context *ctx, char *name, size_t capacity);
+/* Wait for all work on the context's device (the completion wait every Metal call
+ * ends with, src/metal.rs:1562-1604, offered separately for stream-ordered use). */
+DM_API int32_t dm_cuda_synchronize(dm_cuda_context *ctx);
+
+/* ---- buffers ----
+ * dm_cuda_map_read_only replaces MetalContext::map_read_only (src/metal.rs:354-392):
+ * the bytes of a read-only host mapping (e.g. a GGUF/safetensors file) become an
+ * immutable HBM buffer. dm_cuda_new_owned_buffer replaces new_owned_buffer
+ * (:394-402), with dm_buffer_write / dm_buffer_read as the as_mut_bytes / as_bytes
+ * accessors of MetalOwnedBuffer (:213-243). */
+DM_API int32_t dm_cuda_map_read_only(dm_cuda_context *ctx, const void *host, size_t length,
+                              dm_buffer **out);
+DM_API int32_t dm_cuda_new_owned_buffer(dm_cuda_context *ctx, size_t length, dm_buffer **out);
+DM_API int32_t dm_buffer_write(dm_buffer *buffer, size_t offset, const void *source, size_t length);
+DM_API int32_t dm_buffer_read(const dm_buffer *buffer, size_t offset, void *destination,
+                       size_t length);
+DM_API size_t dm_buffer_length(const dm_buffer *buffer);
+DM_API void *dm_buffer_device_pointer(const dm_buffer *buffer);
+DM_API void dm_buffer_free(dm_buffer *buffer);
+
+/* ---- operators (synchronous, host slices) ----
+ * dm_cuda_matvec: MetalContext::matvec (src/metal.rs:648-683).
+ * dm_cuda_matvec_mapped: matvec_mapped (:687-734) and matvec_owned (:1148-1194).
+ * The encoded matrix is row-major GGUF blocks of `kind`; F32/F16/BF16/Q5_0/Q8_0/
+ * Q4_K/Q6_K are supported. The result is an f32 dot product per row (within the
+ * reference tolerance of src/metal.rs:2041-2050, not a bit-exact fma chain). */
+DM_API int32_t dm_cuda_matvec(dm_cuda_context *ctx, int32_t kind, size_t rows, size_t columns,
+                       const uint8_t *encoded, size_t encoded_length, const float *input,
+                       size_t input_length, float *output, size_t output_length);
+DM_API int32_t dm_cuda_matvec_mapped(dm_cuda_context *ctx, int32_t kind, size_t rows,
+                              size_t columns, const dm_buffer *mapped, size_t offset,
+                              size_t encoded_length, const float *input, size_t input_length,
+                              float *output, size_t output_length);
+/* MetalContext::top_k_softmax (src/metal.rs:1392-1434); indices are bit-exact with
+ * cpu::top_k_softmax (src/cpu.rs:234-260). */
+DM_API int32_t dm_cuda_top_k_softmax(dm_cuda_context *ctx, const float *logits, size_t length,
+                              size_t k, uint32_t *indices, float *probabilities);
+/* MetalContext::gelu_mul (:530-552), silu_mul (:554-576), rms_norm (:435-476). */
+DM_API int32_t dm_cuda_gelu_mul(dm_cuda_context *ctx, const float *gate, const float *up,
+                         float *output, size_t length);
+DM_API int32_t dm_cuda_silu_mul(dm_cuda_context *ctx, const float *gate, const float *up,
+                         float *output, size_t length);
+DM_API int32_t dm_cuda_rms_norm(dm_cuda_context *ctx, const float *input, const float *weight,
+                         size_t length, float epsilon, float *output);
+
+/* ---- the batched MoE layer (new: the reference applies one expert at a time) ----
+ * A family fixes the routing, activation, shared expert and combine rules:
+ *   DM_FAMILY_GEMMA4: src/gemma4/cpu.rs:559-611 -- router input rms_norm(x) *
+ *     (router_scale / sqrt(H)), expert input rms_norm(x, routed_pre_norm), f32
+ *     fma-chain router, softmax top-k, fused Q4_K gate_up [E][2I][H], GeGLU-tanh,
+ *     down [E][H][I], combine routed = fma(out, p * expert_scale[e], routed).
+ *     y is `routed` at src/gemma4/cpu.rs:612.
+ *   DM_FAMILY_QWEN35_MOE: Qwen3.5-shaped block, restated (the reference's Qwen3.5
+ *     is dense): f32 router, softmax top-k, SiLU-GLU experts (src/qwen35/cpu.rs:
+ *     415-428, 982-993), y = fma(shared(x), sigmoid(x . shared_gate_vector),
+ *     sum_j fma(expert_j(x), p_j, .)).
+ *   DM_FAMILY_GLM52: src/glm52/cpu.rs:711-778 -- bf16 router with a sequential
+ *     non-fused sum, sigmoid + correction bias, optional group limit (restated),
+ *     norm_topk, routed SiLU g/(1+e^-g), y += out*w*routed_scale, + shared MLP.
+ * Weight pointers are DEVICE addresses of the reference's own byte layouts (GGUF
+ * blocks or safetensors rows, experts contiguous): e.g. dm_buffer_device_pointer of
+ * a dm_cuda_map_read_only buffer plus the tensor's offset. They must stay valid
+ * until dm_moe_layer_destroy. */
+typedef enum {
+  DM_FAMILY_GEMMA4 = 1,
+  DM_FAMILY_QWEN35_MOE = 2,
+  DM_FAMILY_GLM52 = 3,
+} dm_moe_family;
+
+typedef struct {
+  int32_t family;
+  int32_t hidden, intermediate, experts, top_k;
+  int32_t n_groups, topk_groups, normalize_topk; /* GLM; 1/1 = reference routing */
+  float routed_scale;                             /* GLM routed_scaling_factor */
+  float epsilon;                                  /* Gemma rms_norm epsilon */
+  int32_t input_type;                             /* DM_F32, or DM_BF16 for GLM */
+  int32_t router_type;                            /* DM_F32 (Gemma/Qwen), DM_BF16 or DM_F32 (GLM) */
+  const void *router;                             /* [experts, hidden] */
+  const float *correction_bias;                   /* GLM [experts] */
+  const float *router_scale;                      /* Gemma [hidden] */
+  const float *routed_pre_norm;                   /* Gemma [hidden] */
+  const float *expert_scale;                      /* Gemma [experts] */
+  int32_t gate_type, up_type, down_type;
+  const void *gate; /* [experts][intermediate][hidden]; Gemma: fused [experts][2I][hidden] */
+  const void *up;   /* [experts][intermediate][hidden]; NULL for Gemma */
+  const void *down; /* [experts][hidden][intermediate] */
+  int32_t shared_intermediate;                    /* 0 = no shared expert */
+  const void *shared_gate, *shared_up, *shared_down;
+  const float *shared_gate_vector;                /* Qwen [hidden] */
+  /* Optional per-expert logit offset for the softmax families, added once after the
+   * router chain (benchmark knob for skewed routing; NULL = the reference router). */
+  const float *router_logit_bias;                 /* [experts] or NULL */
+} dm_moe_desc;
+
+DM_API int32_t dm_moe_layer_create(dm_cuda_context *ctx, const dm_moe_desc *desc,
+                            dm_moe_layer **out);
+DM_API void dm_moe_layer_destroy(dm_moe_layer *layer);
+
+/* Stream-ordered forward on device pointers: x [tokens, hidden] (input_type),
+ * y [tokens, hidden] f32, optional sel_idx / sel_weight [tokens, top_k] (selection
+ * order, bit-exact indices). `stream` is a cudaStream_t (NULL = the legacy stream).
+ * No host synchronisation happens inside. Replaces the per-layer routed block of
+ * src/gemma4/metal.rs:694-777, src/gemma4/cpu.rs:559-611, src/glm52/cpu.rs:711-778. */
+DM_API int32_t dm_moe_forward(dm_moe_layer *layer, const void *x, float *y, int32_t tokens,
+                       uint32_t *sel_idx, float *sel_weight, void *stream);
+/* The same on host slices, synchronous (the Metal call convention). */
+DM_API int32_t dm_moe_forward_host(dm_moe_layer *layer, const void *x, float *y, int32_t tokens,
+                            uint32_t *sel_idx, float *sel_weight);
+/* Token -> expert dispatch of the last forward, copied to the host: counts[experts],
+ * offsets[experts + 1], sorted_pairs[tokens * top_k] (pair p = t*top_k + j, ordered by
+ * expert, then p) and inverse[tokens * top_k]. Synchronous. */
+DM_API int32_t dm_moe_last_dispatch(dm_moe_layer *layer, int32_t *counts, int32_t *offsets,
+                             int32_t *sorted_pairs, int32_t *inverse);
+/* Per-stage device timers of a forward: the CUDA analog of the phase timers in
+ * GenerationProfile (src/generation.rs:119-141). With profiling on, events are
+ * recorded on the forward's stream at every stage boundary; dm_moe_stage_times
+ * waits for the last forward and writes up to `capacity` stage durations (ms),
+ * returning the number written. Stage names: prep, router, topk, dispatch,
+ * expert_up, expert_down, combine. */
+DM_API int32_t dm_moe_set_profiling(dm_moe_layer *layer, int32_t enable);
+DM_API int32_t dm_moe_stage_times(dm_moe_layer *layer, float *milliseconds, int32_t capacity);
+DM_API const char *dm_moe_stage_name(int32_t stage);
+/* Kernel launches issued by the last forward (a count for benchmarks). */
+DM_API int32_t dm_moe_last_launch_count(const dm_moe_layer *layer);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
