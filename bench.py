@@ -298,9 +298,21 @@ def run_ours(args):
     c1, _, _, _ = sl.layer.last_dispatch(1)
     b1 = stage_bytes(sl, 1, c1)
     dec_bytes = b1["expert_up"] + b1["expert_down"] + b1["router"]
+    sl.layer.set_profiling(True)
+    dtot = {}
+    for _ in range(20):
+        step(1, x1.data_ptr(), y1.data_ptr())
+        for name, t in sl.layer.stage_times().items():
+            dtot[name] = dtot.get(name, 0.0) + t
+    sl.layer.set_profiling(False)
+    dstage = {n: round(1e3 * v / 20, 2) for n, v in dtot.items()}
+    up_bw = b1["expert_up"] / (dstage["expert_up"] * 1e-6) / 1e9 if dstage.get("expert_up") else 0
+    dn_bw = b1["expert_down"] / (dstage["expert_down"] * 1e-6) / 1e9 if dstage.get("expert_down") else 0
     decode = {"tokens_per_s": decode_tps, "us_per_token": 1e3 * dms / args.decode_steps,
               "algorithmic_bytes_per_token": dec_bytes,
-              "hbm_frac": dec_bytes / (dms / args.decode_steps / 1e3) / 1e9 / peak}
+              "hbm_frac": dec_bytes / (dms / args.decode_steps / 1e3) / 1e9 / peak,
+              "stage_us": dstage,
+              "expert_up_hbm_frac": up_bw / peak, "expert_down_hbm_frac": dn_bw / peak}
 
     # ---- end to end through the public host API (pinned host buffers) ----
     xh = torch.empty((T, H), dtype=xdt, pin_memory=True)

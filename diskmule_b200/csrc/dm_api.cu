@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -446,6 +447,29 @@ struct dm_moe_layer {
   // per-stage device timers (GenerationProfile analog)
   bool profiling = false;
   cudaEvent_t events[dm::kStageCount + 1] = {};
+  // repacked copies of the 2-byte-aligned block formats, and their memory
+  dm::GemvPlan plan{};
+  std::vector<void *> owned;
+  // CUDA graphs of repeated calls (keyed by buffers and token count)
+  struct GraphEntry {
+    const void *x;
+    float *y;
+    int tokens;
+    uint32_t *sel_idx;
+    float *sel_weight;
+    int seen;
+    cudaGraphExec_t exec;
+    int launches;
+    int failed = 0;
+  };
+  std::vector<GraphEntry> graphs;
+  bool graphs_enabled = true;
+  cudaStream_t capture = nullptr;
+  void drop_graphs() {
+    for (auto &e : graphs)
+      if (e.exec) cudaGraphExecDestroy(e.exec);
+    graphs.clear();
+  }
 };
 
 namespace {
@@ -461,7 +485,7 @@ int32_t validate_desc(const dm_moe_desc *d) {
     return fail(DM_ERR_ELEMENT_COUNT, "hidden and intermediate must be multiples of 32");
   if (d->top_k <= 0 || d->top_k > d->experts || d->top_k > 32)
     return fail(DM_ERR_TOP_K, "top-k count %d is outside 1..=%d", d->top_k, std::min(d->experts, 32));
-  if (d->experts > 1024) return fail(DM_ERR_INVALID_ARGUMENT, "at most 1024 experts");
+  if (d->experts > 1023) return fail(DM_ERR_INVALID_ARGUMENT, "at most 1023 experts");
   if (!d->router || !d->gate || !d->down) return fail(DM_ERR_INVALID_ARGUMENT, "null weight pointer");
   int types[3] = {d->gate_type, d->up_type, d->down_type};
   for (int i = 0; i < 3; i++) {
@@ -520,6 +544,53 @@ int32_t validate_desc(const dm_moe_desc *d) {
   return DM_OK;
 }
 
+// Repack `blocks` blocks of a Q6_K / Q5_0 / Q8_0 tensor into the split layout.
+int32_t make_split(dm_moe_layer *L, int kind, const void *src, uint64_t blocks,
+                   dm::SplitTensor *out) {
+  dm::SplitLayout s = dm::split_layout(kind);
+  if (s.quant_bytes == 0 || !src) return DM_OK;
+  auto al = [](uint64_t b) { return (b + 255) & ~uint64_t(255); };
+  uint64_t bytes = al(blocks * s.quant_bytes) + al(blocks * s.qh_bytes) + al(blocks * 2);
+  void *mem = nullptr;
+  if (cudaMalloc(&mem, bytes) != cudaSuccess)
+    return fail(DM_ERR_ALLOCATION, "could not allocate %llu bytes for a repacked tensor",
+                (unsigned long long)bytes);
+  L->owned.push_back(mem);
+  uint8_t *p = (uint8_t *)mem;
+  out->quant = p;
+  out->qh = s.qh_bytes ? p + al(blocks * s.quant_bytes) : nullptr;
+  out->d = (uint16_t *)(p + al(blocks * s.quant_bytes) + al(blocks * s.qh_bytes));
+  dm::launch_repack(kind, (const uint8_t *)src, blocks, *out, L->ctx->stream);
+  return DM_OK;
+}
+
+int32_t build_plan(dm_moe_layer *L) {
+  const dm_moe_desc &d = L->desc;
+  const uint64_t E = d.experts, H = d.hidden, I = d.intermediate;
+  int e = 0, b = 0;
+  auto nblocks = [&](int kind, uint64_t rows, uint64_t cols) {
+    dm::block_layout(kind, &e, &b);
+    return rows * (cols / (uint64_t)e);
+  };
+  const bool fused = d.family == DM_FAMILY_GEMMA4;
+  int32_t rc = DM_OK;
+  const uint64_t up_rows = fused ? 2 * I : I;
+  rc = make_split(L, d.gate_type, d.gate, E * nblocks(d.gate_type, up_rows, H), &L->plan.gate);
+  if (rc == DM_OK && fused) L->plan.up = L->plan.gate;
+  if (rc == DM_OK && !fused)
+    rc = make_split(L, d.up_type, d.up, E * nblocks(d.up_type, I, H), &L->plan.up);
+  if (rc == DM_OK)
+    rc = make_split(L, d.down_type, d.down, E * nblocks(d.down_type, H, I), &L->plan.down);
+  if (rc == DM_OK && L->shared) {
+    rc = make_split(L, d.gate_type, d.shared_gate, nblocks(d.gate_type, I, H), &L->plan.sh_gate);
+    if (rc == DM_OK)
+      rc = make_split(L, d.up_type, d.shared_up, nblocks(d.up_type, I, H), &L->plan.sh_up);
+    if (rc == DM_OK)
+      rc = make_split(L, d.down_type, d.shared_down, nblocks(d.down_type, H, I), &L->plan.sh_down);
+  }
+  return rc;
+}
+
 int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   if (tokens <= L->capacity) return DM_OK;
   const dm_moe_desc &d = L->desc;
@@ -531,8 +602,13 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   if (d.family == DM_FAMILY_GEMMA4) bytes += 2 * al(T * H * 4);
   bytes += al(T * L->E1 * 4) + 2 * al(T * k * 4);
   bytes += al((E + 1) * 4) + al((E + 2) * 4) + 2 * al(pairs * 4) + al((E + 1) * 4) + 2 * al(4);
+  bytes += al((pairs + E + 1) * 8) + al(4);
   bytes += al(pairs * I * 4) + al(pairs * H * 4);
-  if (L->scratch) cudaFree(L->scratch);
+  L->drop_graphs();
+  if (L->scratch) {
+    cudaDeviceSynchronize();
+    cudaFree(L->scratch);
+  }
   L->scratch = nullptr;
   L->capacity = 0;
   if (cudaMalloc(&L->scratch, bytes) != cudaSuccess)
@@ -552,6 +628,8 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   a.active = arena.take<int32_t>(E + 1);
   a.n_active = arena.take<int32_t>(1);
   a.status = arena.take<int32_t>(1);
+  a.items = arena.take<int2>(pairs + E + 1);
+  a.n_items = arena.take<int32_t>(1);
   a.h = arena.take<float>(pairs * I);
   a.ysorted = arena.take<float>(pairs * H);
   L->capacity = tokens;
@@ -586,19 +664,24 @@ int32_t dm_moe_layer_create(dm_cuda_context *ctx, const dm_moe_desc *desc, dm_mo
                      : (const uint8_t *)d.up;
   L->down_stride = H * dm::row_bytes(d.down_type, I);
   const int wbytes = d.router_type == DM_BF16 ? 2 : 4;
-  if (cudaMalloc(&L->router_t, (size_t)H * L->E1 * wbytes) != cudaSuccess) {
+  if (cudaMalloc(&L->router_t, (size_t)H * dm::router_ld(L->E1) * wbytes) != cudaSuccess) {
     delete L;
     return fail(DM_ERR_ALLOCATION, "could not allocate the transposed router");
   }
   dm::launch_transpose_router(d.router, d.router_type == DM_BF16, d.experts, d.hidden,
                               qwen_gate ? d.shared_gate_vector : nullptr, L->router_t,
                               ctx->stream);
+  rc = build_plan(L);
+  if (cudaStreamCreateWithFlags(&L->capture, cudaStreamNonBlocking) != cudaSuccess) L->capture = nullptr;
+  {
+    const char *env = getenv("DISKMULE_CUDA_GRAPHS");
+    L->graphs_enabled = L->capture && !(env && (!strcmp(env, "0") || !strcmp(env, "false")));
+  }
   cudaError_t err = cudaStreamSynchronize(ctx->stream);
   if (err == cudaSuccess) err = cudaGetLastError();
-  if (err != cudaSuccess) {
-    cudaFree(L->router_t);
-    delete L;
-    return cuda_fail(err, "router transpose");
+  if (rc != DM_OK || err != cudaSuccess) {
+    dm_moe_layer_destroy(L);
+    return rc != DM_OK ? rc : cuda_fail(err, "layer set-up");
   }
   *out = L;
   return DM_OK;
@@ -613,6 +696,9 @@ void dm_moe_layer_destroy(dm_moe_layer *L) {
   if (L->io) cudaFree(L->io);
   for (auto &e : L->events)
     if (e) cudaEventDestroy(e);
+  for (void *p : L->owned) cudaFree(p);
+  L->drop_graphs();
+  if (L->capture) cudaStreamDestroy(L->capture);
   delete L;
 }
 
@@ -650,6 +736,8 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
   if (tokens == 0) return DM_OK;
   if ((int64_t)tokens * L->desc.top_k > INT32_MAX / 2 || tokens > (1 << 22))
     return fail(DM_ERR_OVERFLOW, "too many tokens in one call (limit 4194304)");
+  if (((uintptr_t)y & 15) || ((uintptr_t)x & 15))
+    return fail(DM_ERR_INVALID_ARGUMENT, "x and y must be 16-byte aligned device pointers");
   cudaSetDevice(L->ctx->device);
   int32_t rc = ensure_layer_scratch(L, tokens);
   if (rc != DM_OK) return rc;
@@ -694,13 +782,72 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
   if (sel_idx) a.sel_idx = sel_idx;
   if (sel_weight) a.sel_w = sel_weight;
   cudaStream_t s = (cudaStream_t)stream;
-  DM_CUDA(cudaMemsetAsync(a.status, 0, 4, s), "status reset");
-  int launches = dm::launch_forward(a, s, L->profiling ? L->events : nullptr);
-  DM_CUDA(cudaGetLastError(), "MoE forward launch");
+  dm::GemvPlan plan = L->plan;
+  plan.nt = tokens == 1 ? 1 : (tokens == 2 ? 2 : 4);
+  plan.max_active = std::min(a.E + (a.shared ? 1 : 0), a.T * a.k + (a.shared ? 1 : 0));
+  {
+    const int pairs = a.T * a.k + (a.shared ? a.T : 0);
+    plan.max_items = std::min(pairs, (pairs + plan.nt - 1) / plan.nt + plan.max_active);
+  }
+  a.chunk = plan.nt;
+  // the GEMV kernels cover whole tasks: 256 elements (Q4_K/Q6_K), 32 (Q5_0/Q8_0),
+  // 128 (BF16) or 64 (F16/F32) per row chunk
+  auto task_elems = [](int kind) {
+    switch (kind) {
+      case DM_Q4_K: case DM_Q6_K: return 256;
+      case DM_Q5_0: case DM_Q8_0: return 32;
+      case DM_BF16: return 128;
+      default: return 64;
+    }
+  };
+  const bool gemv_ok = d.hidden % task_elems(a.gate_type) == 0 &&
+                       d.intermediate % task_elems(a.down_type) == 0;
+  const dm::GemvPlan *gp = gemv_ok ? &plan : nullptr;
+
+  // A call that repeats with the same buffers (a decode loop) is captured once as a
+  // CUDA graph on an internal stream and replayed on the caller's stream.
+  dm_moe_layer::GraphEntry *g = nullptr;
+  if (!L->profiling && L->graphs_enabled) {
+    for (auto &e : L->graphs)
+      if (e.x == x && e.y == y && e.tokens == tokens && e.sel_idx == sel_idx &&
+          e.sel_weight == sel_weight)
+        g = &e;
+    if (!g && L->graphs.size() < 16) {
+      L->graphs.push_back({x, y, tokens, sel_idx, sel_weight, 0, nullptr, 0});
+      g = &L->graphs.back();
+    }
+  }
+  int launches = 0;
+  if (g && !g->exec && g->seen >= 1 && !g->failed) {
+    cudaGraph_t graph = nullptr;
+    cudaError_t err = cudaStreamBeginCapture(L->capture, cudaStreamCaptureModeThreadLocal);
+    if (err == cudaSuccess) {
+      cudaMemsetAsync(a.status, 0, 4, L->capture);
+      launches = dm::launch_forward(a, L->capture, nullptr, gp);
+      err = cudaStreamEndCapture(L->capture, &graph);
+    }
+    if (err == cudaSuccess && launches > 0) err = cudaGraphInstantiate(&g->exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    if (err != cudaSuccess || launches <= 0) {
+      cudaGetLastError();
+      g->failed = 1;
+      g->exec = nullptr;
+    } else {
+      g->launches = launches;
+    }
+  }
+  if (g && g->exec) {
+    DM_CUDA(cudaGraphLaunch(g->exec, s), "MoE graph launch");
+    launches = g->launches;
+  } else {
+    if (g) g->seen++;
+    DM_CUDA(cudaMemsetAsync(a.status, 0, 4, s), "status reset");
+    launches = dm::launch_forward(a, s, L->profiling ? L->events : nullptr, gp);
+    if (launches < 0) return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "no expert kernel for this format");
+    DM_CUDA(cudaGetLastError(), "MoE forward launch");
+  }
   L->last_tokens = tokens;
   L->last_launches = launches;
-  // keep where the dispatch of this call lives for dm_moe_last_dispatch
-  L->args.sel_idx = L->args.sel_idx;
   return DM_OK;
 }
 

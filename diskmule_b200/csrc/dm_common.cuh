@@ -254,6 +254,11 @@ struct F32Unit {
   }
 };
 
+// Allow a kernel the full 227 KB of dynamic shared memory, once per (kernel,
+// device): the attribute persists, and raising the limit alone does not change a
+// launch's occupancy (that follows the shared memory it actually requests).
+cudaError_t ensure_smem_limit(const void *kernel);
+
 // Scratch carved from one device allocation, 256-byte aligned pieces.
 struct Arena {
   uint8_t *base = nullptr;

@@ -14,6 +14,10 @@
 #include "dm_kernels.cuh"
 
 #include <algorithm>
+#include <mutex>
+#include <cstdio>
+#include <set>
+#include <utility>
 
 namespace dm {
 
@@ -41,27 +45,52 @@ __device__ __forceinline__ float load_as_f32(const void *p, size_t i, bool bf16)
   return reinterpret_cast<const float *>(p)[i];
 }
 
+cudaError_t ensure_smem_limit(const void *kernel) {
+  static std::mutex lock;
+  static std::set<std::pair<const void *, int>> done;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return err;
+  std::lock_guard<std::mutex> guard(lock);
+  if (done.count({kernel, device})) return cudaSuccess;
+  int optin = 0;
+  cudaFuncAttributes attr;
+  err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if (err == cudaSuccess) err = cudaFuncGetAttributes(&attr, kernel);
+  if (err == cudaSuccess)
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               optin - (int)attr.sharedSizeBytes);
+  if (err == cudaSuccess) done.insert({kernel, device});
+  return err;
+}
+
+// Raise the kernel's limit when `bytes` needs it; a failure stays recorded as the
+// last CUDA error, so the caller's launch check reports it.
 template <typename F>
 static void set_smem(F *kernel, size_t bytes) {
-  if (bytes > 48 * 1024)
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (bytes > 48 * 1024) {
+    cudaError_t err = ensure_smem_limit((const void *)kernel);
+    if (err != cudaSuccess) fprintf(stderr, "diskmule_cuda: shared memory limit: %s\n", cudaGetErrorString(err));
+  }
 }
 
 // ---------------------------------------------------------------------------
 // router transpose (layer set-up): [E][H] -> [H][E1], optional extra column E
 // ---------------------------------------------------------------------------
 
+// columns >= E1 of the [H][ld] result are zero
 __global__ void transpose_router_kernel(const void *src, int bf16, int E, int H,
-                                        const float *extra, void *dst, int E1) {
-  size_t n = (size_t)H * E1;
+                                        const float *extra, void *dst, int E1, int ld) {
+  size_t n = (size_t)H * ld;
   for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n;
        idx += (size_t)gridDim.x * blockDim.x) {
-    int h = (int)(idx / E1), e = (int)(idx % E1);
+    int h = (int)(idx / ld), e = (int)(idx % ld);
     if (bf16) {
       uint16_t v = e < E ? reinterpret_cast<const uint16_t *>(src)[(size_t)e * H + h] : 0;
       reinterpret_cast<uint16_t *>(dst)[idx] = v;
     } else {
-      float v = e < E ? reinterpret_cast<const float *>(src)[(size_t)e * H + h] : extra[h];
+      float v = e < E ? reinterpret_cast<const float *>(src)[(size_t)e * H + h]
+                      : (e < E1 ? extra[h] : 0.0f);
       reinterpret_cast<float *>(dst)[idx] = v;
     }
   }
@@ -70,9 +99,10 @@ __global__ void transpose_router_kernel(const void *src, int bf16, int E, int H,
 int launch_transpose_router(const void *src, int src_bf16, int E, int H, const float *extra_col,
                             void *dst, cudaStream_t stream) {
   int E1 = E + (extra_col ? 1 : 0);
-  size_t n = (size_t)H * E1;
+  int ld = router_ld(E1);
+  size_t n = (size_t)H * ld;
   int blocks = (int)std::min<size_t>((n + 255) / 256, 4096);
-  transpose_router_kernel<<<blocks, 256, 0, stream>>>(src, src_bf16, E, H, extra_col, dst, E1);
+  transpose_router_kernel<<<blocks, 256, 0, stream>>>(src, src_bf16, E, H, extra_col, dst, E1, ld);
   return 1;
 }
 
@@ -83,15 +113,17 @@ int launch_transpose_router(const void *src, int src_bf16, int E, int H, const f
 constexpr int kPrepTokens = 8;
 
 __global__ void __launch_bounds__(256) gemma_prep_kernel(ForwardArgs a) {
-  extern __shared__ float xs[];  // [kPrepTokens][H + 1]
+  extern __shared__ __align__(16) float xs[];  // [kPrepTokens][H + 4]
   __shared__ float inv_s[kPrepTokens];
-  const int H = a.H, HP = H + 1;
+  const int H = a.H, HP = H + 4;
   const int t0 = blockIdx.x * kPrepTokens;
   const int nt = min(kPrepTokens, a.T - t0);
   const float *x = reinterpret_cast<const float *>(a.x);
-  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
-    int tt = idx / H, i = idx - tt * H;
-    xs[tt * HP + i] = x[(size_t)(t0 + tt) * H + i];
+#pragma unroll 4
+  for (int idx = threadIdx.x; idx < nt * (H / 4); idx += blockDim.x) {
+    int tt = idx / (H / 4), c = idx - tt * (H / 4);
+    *reinterpret_cast<float4 *>(xs + tt * HP + 4 * c) =
+        *reinterpret_cast<const float4 *>(x + (size_t)(t0 + tt) * H + 4 * c);
   }
   __syncthreads();
   if (threadIdx.x < nt) {
@@ -122,38 +154,55 @@ __device__ __forceinline__ float chain_step(float w, float x, float s) {
   return __fmaf_rn(w, x, s);
 }
 
-// Few tokens: a CTA stages the [H][8] column tile of the transposed router and
-// up to RT token rows in shared memory, then 8*RT threads run the chains.
+// Few tokens: a CTA stages the [H][8] column tile of the transposed router ([H][ld],
+// ld a multiple of 8 so each tile row is one 16- or 32-byte vector) and up to RT
+// token rows in shared memory with vector loads, then 8*RT threads run the chains.
 constexpr int kSmallExperts = 8;
 
 template <bool GLM, bool WBF16, bool XBF16>
-__global__ void __launch_bounds__(256) router_small_kernel(const void *wt, const void *x, int T,
-                                                          int H, int E1, int RT,
+__global__ void __launch_bounds__(256) router_small_kernel(const void *wt, int ld, const void *x,
+                                                          int T, int H, int E1, int RT,
                                                           const float *lbias, int E,
                                                           float *logits) {
-  extern __shared__ float smem[];
-  float *xs = smem;                                         // [RT][H + 1]
-  uint16_t *ws16 = reinterpret_cast<uint16_t *>(xs + RT * (H + 1));
-  float *ws32 = reinterpret_cast<float *>(ws16);            // [H][8]
+  extern __shared__ __align__(16) float smem[];
+  const int HP = H + 4;                                     // 16-byte aligned rows
+  float *xs = smem;                                         // [RT][H + 4]
+  float *ws32 = xs + RT * HP;                               // [H][8] f32
+  uint16_t *ws16 = reinterpret_cast<uint16_t *>(ws32);      // [H][8] bf16
   const int e0 = blockIdx.x * kSmallExperts, t0 = blockIdx.y * RT;
-  const int nt = min(RT, T - t0), HP = H + 1;
-  for (int idx = threadIdx.x; idx < H * kSmallExperts; idx += blockDim.x) {
-    int h = idx / kSmallExperts, e = e0 + idx % kSmallExperts;
-    if (WBF16)
-      ws16[idx] = e < E1 ? reinterpret_cast<const uint16_t *>(wt)[(size_t)h * E1 + e] : 0;
-    else
-      ws32[idx] = e < E1 ? reinterpret_cast<const float *>(wt)[(size_t)h * E1 + e] : 0.0f;
+  const int nt = min(RT, T - t0);
+  if (WBF16) {
+    const uint16_t *w = reinterpret_cast<const uint16_t *>(wt) + e0;
+#pragma unroll 4
+    for (int h = threadIdx.x; h < H; h += blockDim.x)
+      reinterpret_cast<uint4 *>(ws16)[h] = *reinterpret_cast<const uint4 *>(w + (size_t)h * ld);
+  } else {
+    const float *w = reinterpret_cast<const float *>(wt) + e0;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < 2 * H; i += blockDim.x)
+      reinterpret_cast<float4 *>(ws32)[i] =
+          *reinterpret_cast<const float4 *>(w + (size_t)(i >> 1) * ld + 4 * (i & 1));
   }
-  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
-    int tt = idx / H, i = idx - tt * H;
-    xs[tt * HP + i] = load_as_f32(x, (size_t)(t0 + tt) * H + i, XBF16);
+  for (int i = threadIdx.x; i < nt * (H / 4); i += blockDim.x) {
+    const int tt = i / (H / 4), c = i - tt * (H / 4);
+    float4 v;
+    if (XBF16) {
+      const uint2 u = *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(x) +
+                                                       (size_t)(t0 + tt) * H + 4 * c);
+      v = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                      __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+    } else {
+      v = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) +
+                                            (size_t)(t0 + tt) * H + 4 * c);
+    }
+    *reinterpret_cast<float4 *>(xs + tt * HP + 4 * c) = v;
   }
   __syncthreads();
-  int el = threadIdx.x % kSmallExperts, tl = threadIdx.x / kSmallExperts;
+  const int el = threadIdx.x % kSmallExperts, tl = threadIdx.x / kSmallExperts;
   if (tl < nt && e0 + el < E1) {
     const float *xr = xs + tl * HP;
     float s = GLM ? -0.0f : 0.0f;
-#pragma unroll 8
+#pragma unroll 16
     for (int h = 0; h < H; h++) {
       float w = WBF16 ? bf16_bits_to_f32(ws16[h * kSmallExperts + el]) : ws32[h * kSmallExperts + el];
       s = chain_step<GLM>(w, xr[h], s);
@@ -168,8 +217,9 @@ __global__ void __launch_bounds__(256) router_small_kernel(const void *wt, const
 constexpr int kTiledTokens = 64, kTiledExperts = 16, kTiledChunk = 32;
 
 template <bool GLM, bool WBF16, bool XBF16>
-__global__ void __launch_bounds__(kTiledTokens) router_tiled_kernel(const void *wt, const void *x,
-                                                                  int T, int H, int E1,
+__global__ void __launch_bounds__(kTiledTokens) router_tiled_kernel(const void *wt, int ld,
+                                                                  const void *x, int T, int H,
+                                                                  int E1,
                                                                   const float *lbias, int E,
                                                                   float *logits) {
   __shared__ float xs[kTiledChunk][kTiledTokens + 1];
@@ -191,7 +241,7 @@ __global__ void __launch_bounds__(kTiledTokens) router_tiled_kernel(const void *
     for (int idx = tid; idx < kTiledChunk * kTiledExperts; idx += kTiledTokens) {
       int hh = idx / kTiledExperts, el = idx % kTiledExperts;
       float v = 0.0f;
-      if (hh < hc && e0 + el < E1) v = load_as_f32(wt, (size_t)(h0 + hh) * E1 + e0 + el, WBF16);
+      if (hh < hc && e0 + el < E1) v = load_as_f32(wt, (size_t)(h0 + hh) * ld + e0 + el, WBF16);
       ws[hh][el] = v;
     }
     __syncthreads();
@@ -223,7 +273,9 @@ __global__ void __launch_bounds__(kTiledTokens) router_tiled_kernel(const void *
 constexpr int kTopkWarps = 4;
 constexpr int kMaxGlmExperts = 1024;
 
-// softmax family: src/cpu.rs:234-260 (+ softmax_in_place :196-231)
+// softmax family: src/cpu.rs:234-260 (+ softmax_in_place :196-231). With REG the
+// token's logits (E <= 1024) stay in registers across the k selection rounds.
+template <bool REG>
 __global__ void __launch_bounds__(32 * kTopkWarps) topk_softmax_kernel(
     const float *logits, int T, int E1, int E, int k, uint32_t *sel_idx, float *sel_w,
     int32_t *status) {
@@ -231,8 +283,19 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_softmax_kernel(
   const int t = blockIdx.x * kTopkWarps + warp;
   if (t >= T) return;
   const float *lg = logits + (size_t)t * E1;
+  constexpr int kPer = REG ? 32 : 1;
+  float v[kPer];
   bool bad = false;
-  for (int e = lane; e < E; e += 32) bad |= !isfinite(lg[e]);
+  if (REG) {
+#pragma unroll
+    for (int j = 0; j < kPer; j++) {
+      int e = lane + 32 * j;
+      v[j] = e < E ? lg[e] : 0.0f;
+      bad |= e < E && !isfinite(v[j]);
+    }
+  } else {
+    for (int e = lane; e < E; e += 32) bad |= !isfinite(lg[e]);
+  }
   if (__any_sync(0xffffffffu, bad)) {
     // flag the error and leave an in-range selection so later kernels stay in bounds
     if (lane == 0) atomicExch(status, kStatusNonFiniteRouter);
@@ -243,26 +306,39 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_softmax_kernel(
     return;
   }
   unsigned long long last = ~0ull;
-  float maximum = 0.0f, sum = 0.0f;
   float vals[32];
   uint32_t idxs[32];
   for (int r = 0; r < k; r++) {
     unsigned long long best = 0;
-    for (int e = lane; e < E; e += 32) {
-      unsigned long long key = rank_key(lg[e], (uint32_t)e);
-      if (key < last && key > best) best = key;
+    if (REG) {
+#pragma unroll
+      for (int j = 0; j < kPer; j++) {
+        int e = lane + 32 * j;
+        unsigned long long key = e < E ? rank_key(v[j], (uint32_t)e) : 0ull;
+        if (key < last && key > best) best = key;
+      }
+    } else {
+      for (int e = lane; e < E; e += 32) {
+        unsigned long long key = rank_key(lg[e], (uint32_t)e);
+        if (key < last && key > best) best = key;
+      }
     }
     best = warp_max_u64(best);
     last = best;
     uint32_t idx = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
-    if (idx >= (uint32_t)E) idx = 0;  // unreachable for k <= eligible experts; keeps reads in range
+    if (idx >= (uint32_t)E) idx = 0;  // unreachable for k <= E; keeps reads in range
     if (r < 32) {
       idxs[r] = idx;
-      vals[r] = lg[idx];
+      vals[r] = __uint_as_float((uint32_t)(best >> 32) ^ 0x80000000u);
     }
   }
   if (lane == 0) {
-    maximum = -INFINITY;
+    // undo rank_key's order-preserving map to recover the selected logits exactly
+    for (int r = 0; r < k; r++) {
+      int32_t key = __float_as_int(vals[r]);
+      vals[r] = __int_as_float(key ^ (int32_t)(((uint32_t)(key >> 31)) >> 1));
+    }
+    float maximum = -INFINITY, sum = 0.0f;
     for (int r = 0; r < k; r++) maximum = fmaxf(maximum, vals[r]);
     for (int r = 0; r < k; r++) {
       vals[r] = exp_f32_cr(__fsub_rn(vals[r], maximum));
@@ -364,7 +440,10 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_sigmoid_kernel(
 
 int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float *prob,
                         int32_t *status, cudaStream_t stream) {
-  topk_softmax_kernel<<<1, 32 * kTopkWarps, 0, stream>>>(logits, 1, n, n, k, idx, prob, status);
+  if (n <= 1024)
+    topk_softmax_kernel<true><<<1, 32 * kTopkWarps, 0, stream>>>(logits, 1, n, n, k, idx, prob, status);
+  else
+    topk_softmax_kernel<false><<<1, 32 * kTopkWarps, 0, stream>>>(logits, 1, n, n, k, idx, prob, status);
   return 1;
 }
 
@@ -374,6 +453,52 @@ int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float 
 
 constexpr int kDispatchThreads = 1024, kDispatchWarps = kDispatchThreads / 32;
 
+__device__ __forceinline__ int warp_inclusive_scan(int v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  return v;
+}
+
+// Exclusive scans of three values over all threads of a kDispatchThreads block;
+// also returns the three totals to every thread.
+__device__ __forceinline__ void block_exclusive_scan3(int &a, int &b, int &c, int &ta, int &tb,
+                                                      int &tc) {
+  __shared__ int ws[3][kDispatchWarps];
+  __shared__ int tot[3];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ia = warp_inclusive_scan(a), ib = warp_inclusive_scan(b), ic = warp_inclusive_scan(c);
+  if (lane == 31) {
+    ws[0][warp] = ia;
+    ws[1][warp] = ib;
+    ws[2][warp] = ic;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int x = ws[0][lane], y = ws[1][lane], z = ws[2][lane];
+    const int sx = warp_inclusive_scan(x), sy = warp_inclusive_scan(y), sz = warp_inclusive_scan(z);
+    ws[0][lane] = sx - x;
+    ws[1][lane] = sy - y;
+    ws[2][lane] = sz - z;
+    if (lane == 31) {
+      tot[0] = sx;
+      tot[1] = sy;
+      tot[2] = sz;
+    }
+  }
+  __syncthreads();
+  a = ws[0][warp] + ia - a;
+  b = ws[1][warp] + ib - b;
+  c = ws[2][warp] + ic - c;
+  ta = tot[0];
+  tb = tot[1];
+  tc = tot[2];
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs a) {
   extern __shared__ int32_t sm[];
   const int E = a.E, P = a.T * a.k;
@@ -381,9 +506,11 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs 
   int32_t *total = sm + kDispatchWarps * E;      // [E + 1]
   int32_t *flags = total + (E + 1);              // [E + 1] scan scratch
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < kDispatchWarps * E; i += blockDim.x) wc[i] = 0;
+  // contiguous chunks of whole warps' worth of pairs: few pairs use few warps
+  const int chunk = max(32, (((P + kDispatchWarps - 1) / kDispatchWarps) + 31) & ~31);
+  const int nw = (P + chunk - 1) / chunk;
+  for (int i = threadIdx.x; i < nw * E; i += blockDim.x) wc[i] = 0;
   __syncthreads();
-  const int chunk = (P + kDispatchWarps - 1) / kDispatchWarps;
   const int begin = min(P, warp * chunk), end = min(P, begin + chunk);
   for (int p = begin + lane; p < end; p += 32) {
     uint32_t e = a.sel_idx[p];
@@ -392,7 +519,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs 
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int running = 0;
-    for (int w = 0; w < kDispatchWarps; w++) {
+    for (int w = 0; w < nw; w++) {
       int c = wc[w * E + e];
       wc[w * E + e] = running;
       running += c;
@@ -400,24 +527,28 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs 
     total[e] = running;
   }
   __syncthreads();
-  // exclusive scan over experts (serial by warp 0 lanes in chunks; E <= 1024)
-  if (threadIdx.x == 0) {
-    int running = 0;
-    for (int e = 0; e < E; e++) {
-      int c = total[e];
-      a.counts[e] = c;
-      a.offsets[e] = running;
-      flags[e] = running;
-      running += c;
+  // Block-wide exclusive scans over the experts (one thread per expert, the shared
+  // expert as index E): token offsets, the compacted active list and the work list
+  // of (expert, first token) chunks of `a.chunk` tokens.
+  {
+    const int e = threadIdx.x;  // E + 1 <= kDispatchThreads
+    const int count = e < E ? total[e] : (e == E && a.shared ? a.T : 0);
+    const int items = (count + a.chunk - 1) / a.chunk;
+    int s_count = count, s_active = count > 0, s_items = items;
+    int tot_count, tot_active, tot_items;
+    block_exclusive_scan3(s_count, s_active, s_items, tot_count, tot_active, tot_items);
+    if (e <= E) {
+      a.counts[e] = count;
+      a.offsets[e] = s_count;
+      if (e < E) flags[e] = s_count;
+      if (count > 0) a.active[s_active] = e;
+      for (int j = 0; j < items; j++) a.items[s_items + j] = make_int2(e, j * a.chunk);
     }
-    a.offsets[E] = running;  // == P
-    a.counts[E] = a.shared ? a.T : 0;
-    a.offsets[E + 1] = running + (a.shared ? a.T : 0);
-    int n = 0;
-    for (int e = 0; e < E; e++)
-      if (total[e] > 0) a.active[n++] = e;
-    if (a.shared && a.T > 0) a.active[n++] = E;
-    *a.n_active = n;
+    if (e == 0) {
+      a.offsets[E + 1] = tot_count;
+      *a.n_active = tot_active;
+      *a.n_items = tot_items;
+    }
   }
   __syncthreads();
   for (int base = begin; base < end; base += 32) {
@@ -592,30 +723,47 @@ __global__ void __launch_bounds__(kExpertThreads) expert_down_kernel(ForwardArgs
 // weighted combine: selection order, deterministic, no atomics
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(256) combine_kernel(ForwardArgs a) {
+__global__ void __launch_bounds__(128) combine_kernel(ForwardArgs a) {
+  __shared__ int pos_s[32];
+  __shared__ float w_s[32];
+  __shared__ float gate_s;
   const int t = blockIdx.x;
   const int H = a.H, k = a.k, P = a.T * a.k;
-  float gate = 0.0f;
-  if (a.shared && a.family == kQwen) gate = qwen_sigmoid(a.logits[(size_t)t * a.E1 + a.E]);
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float acc = 0.0f;
+  if (threadIdx.x < k) {
+    const int p = t * k + threadIdx.x;
+    pos_s[threadIdx.x] = a.inverse[p];
+    float w = a.sel_w[p];
+    if (a.family == kGemma) w = __fmul_rn(w, a.expert_scale[a.sel_idx[p]]);  // p * scale[e]
+    w_s[threadIdx.x] = w;
+  }
+  if (threadIdx.x == 32)
+    gate_s = a.shared && a.family == kQwen ? qwen_sigmoid(a.logits[(size_t)t * a.E1 + a.E]) : 0.0f;
+  __syncthreads();
+  const float gate = gate_s;
+  const int i4 = blockIdx.y * blockDim.x + threadIdx.x;
+  if (i4 < H / 4) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 4
     for (int j = 0; j < k; j++) {
-      int p = t * k + j;
-      float v = a.ysorted[(size_t)a.inverse[p] * H + i];
-      float w = a.sel_w[p];
-      if (a.family == kGemma) {
-        acc = __fmaf_rn(v, __fmul_rn(w, a.expert_scale[a.sel_idx[p]]), acc);
-      } else if (a.family == kQwen) {
-        acc = __fmaf_rn(v, w, acc);
-      } else {
-        acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(v, w), a.routed_scale));
+      const float4 v = *reinterpret_cast<const float4 *>(a.ysorted + (size_t)pos_s[j] * H + 4 * i4);
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+      const float w = w_s[j];
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        if (a.family == kGlm)
+          acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn(vv[c], w), a.routed_scale));
+        else
+          acc[c] = __fmaf_rn(vv[c], w, acc[c]);
       }
     }
     if (a.shared) {
-      float v = a.ysorted[(size_t)(P + t) * H + i];
-      acc = a.family == kQwen ? __fmaf_rn(v, gate, acc) : __fadd_rn(acc, v);
+      const float4 v = *reinterpret_cast<const float4 *>(a.ysorted + (size_t)(P + t) * H + 4 * i4);
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int c = 0; c < 4; c++)
+        acc[c] = a.family == kQwen ? __fmaf_rn(vv[c], gate, acc[c]) : __fadd_rn(acc[c], vv[c]);
     }
-    a.y[(size_t)t * H + i] = acc;
+    *reinterpret_cast<float4 *>(a.y + (size_t)t * H + 4 * i4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
   }
 }
 
@@ -658,7 +806,8 @@ static ExpertFn expert_fn(bool up, int kind, int tt) {
   return (ExpertFn)(tt == 8 ? pick_kernel<DownK, 8>(kind) : pick_kernel<DownK, 4>(kind));
 }
 
-int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev) {
+int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
+                   const GemvPlan *gemv) {
   int launches = 0;
   const bool glm = a.family == kGlm;
   auto mark = [&](int stage) {
@@ -669,7 +818,7 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev) {
   const void *router_x = a.x;
   bool router_x_bf16 = a.input_bf16;
   if (a.family == kGemma) {
-    size_t smem = (size_t)kPrepTokens * (a.H + 1) * sizeof(float);
+    size_t smem = (size_t)kPrepTokens * (a.H + 4) * sizeof(float);
     set_smem(gemma_prep_kernel, smem);
     gemma_prep_kernel<<<(a.T + kPrepTokens - 1) / kPrepTokens, 256, smem, stream>>>(a);
     launches++;
@@ -681,14 +830,14 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev) {
   if (a.T <= 16) {
     int RT = 4;
     size_t wbytes = (size_t)a.H * kSmallExperts * (a.router_bf16 ? 2 : 4);
-    while (RT > 1 && wbytes + (size_t)RT * (a.H + 1) * 4 > 200 * 1024) RT >>= 1;
-    size_t smem = wbytes + (size_t)RT * (a.H + 1) * 4;
+    while (RT > 1 && wbytes + (size_t)RT * (a.H + 4) * 4 > 200 * 1024) RT >>= 1;
+    size_t smem = wbytes + (size_t)RT * (a.H + 4) * 4;
     dim3 grid((a.E1 + kSmallExperts - 1) / kSmallExperts, (a.T + RT - 1) / RT);
 #define DM_ROUTER_SMALL(G, W, X)                                                            \
   {                                                                                         \
     auto fn = router_small_kernel<G, W, X>;                                                 \
     set_smem(fn, smem);                                                                     \
-    fn<<<grid, 256, smem, stream>>>(a.router_t, router_x, a.T, a.H, a.E1, RT, a.logit_bias, a.E, a.logits);    \
+    fn<<<grid, 256, smem, stream>>>(a.router_t, router_ld(a.E1), router_x, a.T, a.H, a.E1, RT, a.logit_bias, a.E, a.logits);    \
   }
     if (glm && a.router_bf16 && router_x_bf16) DM_ROUTER_SMALL(true, true, true)
     else if (glm && a.router_bf16) DM_ROUTER_SMALL(true, true, false)
@@ -699,7 +848,7 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev) {
   } else {
     dim3 grid((a.E1 + kTiledExperts - 1) / kTiledExperts, (a.T + kTiledTokens - 1) / kTiledTokens);
 #define DM_ROUTER_TILED(G, W, X) \
-  router_tiled_kernel<G, W, X><<<grid, kTiledTokens, 0, stream>>>(a.router_t, router_x, a.T, a.H, a.E1, a.logit_bias, a.E, a.logits);
+  router_tiled_kernel<G, W, X><<<grid, kTiledTokens, 0, stream>>>(a.router_t, router_ld(a.E1), router_x, a.T, a.H, a.E1, a.logit_bias, a.E, a.logits);
     if (glm && a.router_bf16 && router_x_bf16) DM_ROUTER_TILED(true, true, true)
     else if (glm && a.router_bf16) DM_ROUTER_TILED(true, true, false)
     else if (glm && router_x_bf16) DM_ROUTER_TILED(true, false, true)
@@ -716,7 +865,7 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev) {
         a.logits, a.T, a.E1, a.E, a.k, a.bias, a.n_groups, a.topk_groups, a.normalize,
         a.sel_idx, a.sel_w, a.status);
   else
-    topk_softmax_kernel<<<topk_blocks, 32 * kTopkWarps, 0, stream>>>(
+    topk_softmax_kernel<true><<<topk_blocks, 32 * kTopkWarps, 0, stream>>>(
         a.logits, a.T, a.E1, a.E, a.k, a.sel_idx, a.sel_w, a.status);
   launches++;
   // 4. dispatch
@@ -728,6 +877,11 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev) {
   // 5. gate/up (+activation) and 6. down, over the active experts
   const int max_active = std::min(a.E + (a.shared ? 1 : 0), a.T * a.k + (a.shared ? 1 : 0));
   mark(kStageUp);
+  if (gemv) {
+    int n = launch_gemv_experts(a, *gemv, stream, ev ? ev[kStageDown] : nullptr);
+    if (n < 0) return -1;
+    launches += n;
+  } else {
   {
     int tt = choose_tt(a.H);
     ExpertFn fn = expert_fn(true, a.gate_type, tt);
@@ -749,9 +903,10 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev) {
     fn<<<grid, kExpertThreads, smem, stream>>>(a, rows_per_cta);
     launches++;
   }
+  }
   // 7. combine
   mark(kStageCombine);
-  combine_kernel<<<a.T, 256, 0, stream>>>(a);
+  combine_kernel<<<dim3(a.T, (a.H / 4 + 127) / 128), 128, 0, stream>>>(a);
   launches++;
   mark(kStageCount);
   return launches;

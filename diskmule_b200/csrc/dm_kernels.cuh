@@ -2,6 +2,7 @@
 #pragma once
 
 #include "dm_common.cuh"
+#include "dm_gemv.cuh"
 
 namespace dm {
 
@@ -41,10 +42,17 @@ struct ForwardArgs {
   int32_t *inverse;        // [T*k + T]
   int32_t *active;         // [E + 1] experts with tokens, ascending
   int32_t *n_active;       // [1]
+  int chunk;               // tokens per work item
+  int2 *items;             // [T*k + T + E + 1] (expert, first token) work items
+  int32_t *n_items;        // [1]
   int32_t *status;         // [1] device error word (0 = ok)
   float *h;                // [(T*k + T), I]
   float *ysorted;          // [(T*k + T), H]
 };
+
+// Row stride (elements) of the transposed router [H][ld]: E1 rounded up to 8 so
+// every 8-expert tile row is one aligned vector.
+__host__ __device__ inline int router_ld(int E1) { return (E1 + 7) & ~7; }
 
 enum DeviceStatus : int32_t {
   kStatusOk = 0,
@@ -66,7 +74,9 @@ enum Stage {
 
 // launchers (dm_kernels.cu); each returns the number of kernels launched or -1.
 // `ev`, when not null, holds kStageCount + 1 events recorded on `stream`.
-int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev);
+// `gemv`, when not null, runs the expert products as the GEMV kernels of dm_gemv.cu.
+int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
+                   const GemvPlan *gemv);
 int launch_gemv(int kind, const uint8_t *w, int rows, int cols, const float *x, float *y,
                 cudaStream_t stream);
 int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float *prob,
