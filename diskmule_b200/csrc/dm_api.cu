@@ -910,3 +910,154 @@ int32_t dm_moe_last_dispatch(dm_moe_layer *L, int32_t *counts, int32_t *offsets,
 int32_t dm_moe_last_launch_count(const dm_moe_layer *L) { return L ? L->last_launches : 0; }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Forward without allocation.
+//
+// Some callers cannot call cudaMalloc when they run a layer: a host runtime that
+// has already carved all of HBM into its own pools (expert slot pools sized to
+// fill the device), or code on a latency-critical stream where cudaMalloc's
+// implicit device-wide synchronisation would stall other streams. For them,
+// dm_moe_forward_noalloc runs the same kernels as dm_moe_forward, but every piece
+// of per-call scratch (router logits, selection, dispatch lists, expert
+// intermediates) is carved from one fixed device array compiled into this
+// library, so the call allocates nothing.
+// ---------------------------------------------------------------------------
+
+// 8 MiB per device, held by every GPU that loads the library until the process
+// exits. In host code this name is only a stand-in for the symbol; kernels get
+// the array's device address, fetched by cudaGetSymbolAddress below.
+static constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+std::mutex g_noalloc_lock;
+void *g_noalloc_address[64] = {};  // per device ordinal, filled on first use
+
+// Device address of the array on `device` (which must be current). The first
+// call on a device looks it up; later calls reuse it.
+int32_t noalloc_scratch(int device, uint8_t **out) {
+  if (device < 0 || device >= 64) return fail(DM_ERR_INVALID_ARGUMENT, "device ordinal out of range");
+  std::lock_guard<std::mutex> guard(g_noalloc_lock);
+  if (!g_noalloc_address[device]) {
+    void *ptr = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress of the static scratch");
+    g_noalloc_address[device] = ptr;
+  }
+  *out = (uint8_t *)g_noalloc_address[device];
+  return DM_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t dm_moe_forward_noalloc(dm_moe_layer *L, const void *x, float *y,
+                                          int32_t tokens, uint32_t *sel_idx, float *sel_weight,
+                                          void *stream) {
+  if (!L || !x || !y) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  if (tokens < 0) return fail(DM_ERR_INVALID_ARGUMENT, "negative token count");
+  if (tokens == 0) return DM_OK;
+  if (((uintptr_t)y & 15) || ((uintptr_t)x & 15))
+    return fail(DM_ERR_INVALID_ARGUMENT, "x and y must be 16-byte aligned device pointers");
+  const dm_moe_desc &d = L->desc;
+  // the same scratch layout as the allocating forward, carved from the static array
+  const size_t T = (size_t)tokens, H = d.hidden, I = d.intermediate, E = d.experts,
+               k = d.top_k;
+  const size_t pairs = T * k + (L->shared ? T : 0);
+  auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+  size_t need = 0;
+  if (d.family == DM_FAMILY_GEMMA4) need += 2 * al(T * H * 4);
+  need += al(T * L->E1 * 4) + 2 * al(T * k * 4);
+  need += al((E + 1) * 4) + al((E + 2) * 4) + 2 * al(pairs * 4) + al((E + 1) * 4) + 2 * al(4);
+  need += al((pairs + E + 1) * 8) + al(4);
+  need += al(pairs * I * 4) + al(pairs * H * 4);
+  if (need > kNoAllocScratchBytes)
+    return fail(DM_ERR_OVERFLOW,
+                "%d tokens need %zu bytes of scratch; the no-allocation forward has %zu "
+                "(use dm_moe_forward or fewer tokens per call)",
+                tokens, need, kNoAllocScratchBytes);
+  DM_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  uint8_t *base = nullptr;
+  int32_t rc = noalloc_scratch(L->ctx->device, &base);
+  if (rc != DM_OK) return rc;
+  dm::Arena arena{base, 0, kNoAllocScratchBytes};
+  dm::ForwardArgs a{};
+  a.router_in = d.family == DM_FAMILY_GEMMA4 ? arena.take<float>(T * H) : nullptr;
+  a.expert_in = d.family == DM_FAMILY_GEMMA4 ? arena.take<float>(T * H) : nullptr;
+  a.logits = arena.take<float>(T * L->E1);
+  a.sel_idx = arena.take<uint32_t>(T * k);
+  a.sel_w = arena.take<float>(T * k);
+  a.counts = arena.take<int32_t>(E + 1);
+  a.offsets = arena.take<int32_t>(E + 2);
+  a.sorted = arena.take<int32_t>(pairs);
+  a.inverse = arena.take<int32_t>(pairs);
+  a.active = arena.take<int32_t>(E + 1);
+  a.n_active = arena.take<int32_t>(1);
+  a.status = arena.take<int32_t>(1);
+  a.items = arena.take<int2>(pairs + E + 1);
+  a.n_items = arena.take<int32_t>(1);
+  a.h = arena.take<float>(pairs * I);
+  a.ysorted = arena.take<float>(pairs * H);
+  a.family = d.family;
+  a.T = tokens;
+  a.H = d.hidden;
+  a.I = d.intermediate;
+  a.E = d.experts;
+  a.k = d.top_k;
+  a.E1 = L->E1;
+  a.shared = L->shared;
+  a.n_groups = d.n_groups;
+  a.topk_groups = d.topk_groups;
+  a.normalize = d.normalize_topk;
+  a.routed_scale = d.routed_scale;
+  a.epsilon = d.epsilon;
+  a.inv_sqrt_hidden = 1.0f / std::sqrt((float)d.hidden);
+  a.input_bf16 = d.input_type == DM_BF16;
+  a.x = x;
+  a.y = y;
+  a.router_bf16 = d.router_type == DM_BF16;
+  a.router_t = L->router_t;
+  a.bias = d.correction_bias;
+  a.router_scale = d.router_scale;
+  a.routed_pre_norm = d.routed_pre_norm;
+  a.expert_scale = d.expert_scale;
+  a.logit_bias = d.family == DM_FAMILY_GLM52 ? nullptr : d.router_logit_bias;
+  a.gate_type = d.gate_type;
+  a.up_type = d.family == DM_FAMILY_GEMMA4 ? d.gate_type : d.up_type;
+  a.down_type = d.down_type;
+  a.gate = (const uint8_t *)d.gate;
+  a.up = L->up_base;
+  a.down = (const uint8_t *)d.down;
+  a.gate_stride = L->gate_stride;
+  a.up_stride = L->up_stride;
+  a.down_stride = L->down_stride;
+  a.sh_gate = (const uint8_t *)d.shared_gate;
+  a.sh_up = (const uint8_t *)d.shared_up;
+  a.sh_down = (const uint8_t *)d.shared_down;
+  if (sel_idx) a.sel_idx = sel_idx;
+  if (sel_weight) a.sel_w = sel_weight;
+  dm::GemvPlan plan = L->plan;
+  plan.nt = tokens == 1 ? 1 : (tokens == 2 ? 2 : 4);
+  plan.max_active = std::min(a.E + (a.shared ? 1 : 0), a.T * a.k + (a.shared ? 1 : 0));
+  plan.max_items = std::min((int)pairs, ((int)pairs + plan.nt - 1) / plan.nt + plan.max_active);
+  a.chunk = plan.nt;
+  auto task_elems = [](int kind) {
+    switch (kind) {
+      case DM_Q4_K: case DM_Q6_K: return 256;
+      case DM_Q5_0: case DM_Q8_0: return 32;
+      case DM_BF16: return 128;
+      default: return 64;
+    }
+  };
+  const bool gemv_ok = d.hidden % task_elems(a.gate_type) == 0 &&
+                       d.intermediate % task_elems(a.down_type) == 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  // Every buffer above is written before it is read within a call, except the
+  // status word, which must start at zero: the array keeps the last call's bytes.
+  DM_CUDA(cudaMemsetAsync(a.status, 0, 4, s), "status reset");
+  const int launches = dm::launch_forward(a, s, nullptr, gemv_ok ? &plan : nullptr);
+  if (launches < 0) return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "no expert kernel for this format");
+  DM_CUDA(cudaGetLastError(), "MoE forward (no allocation) launch");
+  return DM_OK;
+}

@@ -211,6 +211,22 @@ DM_API const char *dm_moe_stage_name(int32_t stage);
 /* Kernel launches issued by the last forward (a count for benchmarks). */
 DM_API int32_t dm_moe_last_launch_count(const dm_moe_layer *layer);
 
+/* dm_moe_forward without any allocation. No counterpart in the reference.
+ * For callers that cannot call cudaMalloc while running a layer: a runtime that
+ * has carved all device memory into its own pools (expert slot pools sized to fill
+ * HBM), or a latency-critical stream where cudaMalloc's implicit device-wide
+ * synchronisation is not acceptable. The call runs the same kernels as
+ * dm_moe_forward with the same arguments, but all per-call scratch comes from one
+ * fixed 8 MiB array compiled into the library (held by every GPU that loads it
+ * until the process exits); a token count whose scratch exceeds 8 MiB is rejected
+ * with DM_ERR_OVERFLOW. The first call on a device looks up the array's device
+ * address, so make that first call before any stream capture. All calls share the
+ * array: calls whose GPU work overlaps in time (other streams, other threads) race
+ * on it and must be serialised by the caller. */
+DM_API int32_t dm_moe_forward_noalloc(dm_moe_layer *layer, const void *x, float *y,
+                                      int32_t tokens, uint32_t *sel_idx, float *sel_weight,
+                                      void *stream);
+
 #ifdef __cplusplus
 }
 #endif
