@@ -16,6 +16,7 @@
 
 #include "../../include/diskmule_cuda.h"
 #include "dm_kernels.cuh"
+#include "dm_tc.cuh"
 
 namespace {
 
@@ -450,6 +451,9 @@ struct dm_moe_layer {
   // repacked copies of the 2-byte-aligned block formats, and their memory
   dm::GemvPlan plan{};
   std::vector<void *> owned;
+  // tensor-core path: packed activations and TMA maps for 16/32/64-token tiles
+  bool tc_ok = false;
+  dm::TcPlan tc[3];
   // CUDA graphs of repeated calls (keyed by buffers and token count)
   struct GraphEntry {
     const void *x;
@@ -604,6 +608,7 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   bytes += al((E + 1) * 4) + al((E + 2) * 4) + 2 * al(pairs * 4) + al((E + 1) * 4) + 2 * al(4);
   bytes += al((pairs + E + 1) * 8) + al(4);
   bytes += al(pairs * I * 4) + al(pairs * H * 4);
+  if (L->tc_ok) bytes += al(2 * pairs * H * 2) + al(2 * pairs * I * 2) + 2 * al(pairs * 4);
   L->drop_graphs();
   if (L->scratch) {
     cudaDeviceSynchronize();
@@ -632,6 +637,23 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   a.n_items = arena.take<int32_t>(1);
   a.h = arena.take<float>(pairs * I);
   a.ysorted = arena.take<float>(pairs * H);
+  if (L->tc_ok) {
+    __half *x16 = arena.take<__half>(2 * pairs * H);  // hi rows, then lo rows
+    __half *h16 = arena.take<__half>(2 * pairs * I);
+    float *x_inv = arena.take<float>(pairs);
+    float *h_inv = arena.take<float>(pairs);
+    const int nts[3] = {16, 32, 64};
+    for (int i = 0; i < 3; i++) {
+      dm::TcPlan &p = L->tc[i];
+      p.nt = nts[i];
+      p.rows = (int)pairs;
+      p.x16 = x16;
+      p.h16 = h16;
+      p.x_inv = x_inv;
+      p.h_inv = h_inv;
+      if (dm::make_tc_maps(p, (int)H, (int)I, p.nt) != 0) L->tc_ok = false;
+    }
+  }
   L->capacity = tokens;
   return DM_OK;
 }
@@ -676,6 +698,10 @@ int32_t dm_moe_layer_create(dm_cuda_context *ctx, const dm_moe_desc *desc, dm_mo
   {
     const char *env = getenv("DISKMULE_CUDA_GRAPHS");
     L->graphs_enabled = L->capture && !(env && (!strcmp(env, "0") || !strcmp(env, "false")));
+    const char *tc_env = getenv("DISKMULE_CUDA_TC");
+    L->tc_ok = d.family != DM_FAMILY_GLM52 &&
+               dm::tc_supported(d.gate_type, d.down_type, d.hidden, d.intermediate) &&
+               !(tc_env && (!strcmp(tc_env, "0") || !strcmp(tc_env, "false")));
   }
   cudaError_t err = cudaStreamSynchronize(ctx->stream);
   if (err == cudaSuccess) err = cudaGetLastError();
@@ -803,6 +829,19 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
   const bool gemv_ok = d.hidden % task_elems(a.gate_type) == 0 &&
                        d.intermediate % task_elems(a.down_type) == 0;
   const dm::GemvPlan *gp = gemv_ok ? &plan : nullptr;
+  // Enough tokens per expert -> the tcgen05 grouped GEMM (16/32/64-token tiles).
+  dm::TcPlan tcp;
+  const dm::TcPlan *tp = nullptr;
+  if (gp && L->tc_ok) {
+    const double avg = (double)tokens * d.top_k / d.experts;
+    if (avg >= 4.0) {
+      tcp = L->tc[avg <= 12.0 ? 0 : (avg <= 24.0 ? 1 : 2)];
+      const int pairs = a.T * a.k + (a.shared ? a.T : 0);
+      tcp.max_items = std::min(pairs, (pairs + tcp.nt - 1) / tcp.nt + plan.max_active);
+      a.chunk = tcp.nt;
+      tp = &tcp;
+    }
+  }
 
   // A call that repeats with the same buffers (a decode loop) is captured once as a
   // CUDA graph on an internal stream and replayed on the caller's stream.
@@ -823,7 +862,7 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
     cudaError_t err = cudaStreamBeginCapture(L->capture, cudaStreamCaptureModeThreadLocal);
     if (err == cudaSuccess) {
       cudaMemsetAsync(a.status, 0, 4, L->capture);
-      launches = dm::launch_forward(a, L->capture, nullptr, gp);
+      launches = dm::launch_forward(a, L->capture, nullptr, gp, tp);
       err = cudaStreamEndCapture(L->capture, &graph);
     }
     if (err == cudaSuccess && launches > 0) err = cudaGraphInstantiate(&g->exec, graph, 0);
@@ -842,7 +881,7 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
   } else {
     if (g) g->seen++;
     DM_CUDA(cudaMemsetAsync(a.status, 0, 4, s), "status reset");
-    launches = dm::launch_forward(a, s, L->profiling ? L->events : nullptr, gp);
+    launches = dm::launch_forward(a, s, L->profiling ? L->events : nullptr, gp, tp);
     if (launches < 0) return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "no expert kernel for this format");
     DM_CUDA(cudaGetLastError(), "MoE forward launch");
   }
@@ -887,6 +926,8 @@ int32_t dm_moe_forward_host(dm_moe_layer *L, const void *x, float *y, int32_t to
   DM_CUDA(cudaStreamSynchronize(s), "MoE forward");
   if (status == dm::kStatusNonFiniteRouter)
     return fail(DM_ERR_NON_FINITE, "router produced a non-finite score");
+  if (status == dm::kStatusTimeout)
+    return fail(DM_ERR_TIMEOUT, "a bounded wait in the tensor-core GEMM ran out");
   if (status == dm::kStatusNonFiniteNorm)
     return fail(DM_ERR_NON_FINITE, "RMSNorm received a non-finite value");
   return DM_OK;

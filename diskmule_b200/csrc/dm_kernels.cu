@@ -12,6 +12,7 @@
 // Expert products accumulate in f32 in a different order than the reference and
 // are held to the relative-L2 tolerance instead.
 #include "dm_kernels.cuh"
+#include "dm_tc.cuh"
 
 #include <algorithm>
 #include <mutex>
@@ -807,7 +808,7 @@ static ExpertFn expert_fn(bool up, int kind, int tt) {
 }
 
 int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
-                   const GemvPlan *gemv) {
+                   const GemvPlan *gemv, const TcPlan *tc) {
   int launches = 0;
   const bool glm = a.family == kGlm;
   auto mark = [&](int stage) {
@@ -877,7 +878,11 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   // 5. gate/up (+activation) and 6. down, over the active experts
   const int max_active = std::min(a.E + (a.shared ? 1 : 0), a.T * a.k + (a.shared ? 1 : 0));
   mark(kStageUp);
-  if (gemv) {
+  if (gemv && tc) {
+    int n = launch_tc_experts(a, *tc, *gemv, stream, ev ? ev[kStageDown] : nullptr);
+    if (n < 0) return -1;
+    launches += n;
+  } else if (gemv) {
     int n = launch_gemv_experts(a, *gemv, stream, ev ? ev[kStageDown] : nullptr);
     if (n < 0) return -1;
     launches += n;

@@ -58,6 +58,7 @@ enum DeviceStatus : int32_t {
   kStatusOk = 0,
   kStatusNonFiniteRouter = 1,
   kStatusNonFiniteNorm = 2,
+  kStatusTimeout = 3,  // a bounded device wait ran out
 };
 
 // Forward stages, timed by optional events recorded at each stage's start.
@@ -74,9 +75,11 @@ enum Stage {
 
 // launchers (dm_kernels.cu); each returns the number of kernels launched or -1.
 // `ev`, when not null, holds kStageCount + 1 events recorded on `stream`.
-// `gemv`, when not null, runs the expert products as the GEMV kernels of dm_gemv.cu.
+// `gemv`, when not null, runs the expert products as the GEMV kernels of dm_gemv.cu;
+// `tc`, when also given, runs them as the tcgen05 grouped GEMM of dm_tc.cu instead.
+struct TcPlan;
 int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
-                   const GemvPlan *gemv);
+                   const GemvPlan *gemv, const TcPlan *tc = nullptr);
 int launch_gemv(int kind, const uint8_t *w, int rows, int cols, const float *x, float *y,
                 cudaStream_t stream);
 int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float *prob,
