@@ -454,6 +454,7 @@ struct dm_moe_layer {
   // tensor-core path: packed activations and TMA maps for 16/32/64-token tiles
   bool tc_ok = false;
   dm::TcPlan tc[3];
+  dm::TcWeights tcw;  // tensor-core weight views (valid while tc_ok)
   // CUDA graphs of repeated calls (keyed by buffers and token count)
   struct GraphEntry {
     const void *x;
@@ -568,6 +569,35 @@ int32_t make_split(dm_moe_layer *L, int kind, const void *src, uint64_t blocks,
   return DM_OK;
 }
 
+// Tensor-core weight views: TMA maps over the gate/up and down weights and the per-step
+// transposed down side arrays. A refused map leaves the layer on the GEMV path.
+int32_t build_tc_weights(dm_moe_layer *L) {
+  const dm_moe_desc &d = L->desc;
+  uint64_t qh_bytes = 0, d_bytes = 0, sh_qh_bytes = 0, sh_d_bytes = 0;
+  dm::tc_side_bytes(d.down_type, d.experts, d.hidden, d.intermediate, &qh_bytes, &d_bytes);
+  if (L->shared)
+    dm::tc_side_bytes(d.down_type, 1, d.hidden, d.intermediate, &sh_qh_bytes, &sh_d_bytes);
+  uint8_t *bufs[4] = {nullptr, nullptr, nullptr, nullptr};
+  const uint64_t sizes[4] = {qh_bytes, d_bytes, sh_qh_bytes, sh_d_bytes};
+  for (int i = 0; i < 4; i++) {
+    if (!sizes[i]) continue;
+    void *mem = nullptr;
+    if (cudaMalloc(&mem, sizes[i]) != cudaSuccess)
+      return fail(DM_ERR_ALLOCATION, "could not allocate %llu bytes for tensor-core side arrays",
+                  (unsigned long long)sizes[i]);
+    L->owned.push_back(mem);
+    bufs[i] = (uint8_t *)mem;
+  }
+  if (dm::make_tc_weights(L->tcw, (const uint8_t *)d.gate, L->up_base, L->gate_stride,
+                          (const uint8_t *)d.shared_gate, (const uint8_t *)d.shared_up,
+                          L->plan.down, L->plan.sh_down, d.down_type, d.experts, d.hidden,
+                          d.intermediate, bufs[0], bufs[1], bufs[2], bufs[3], L->ctx->stream) != 0) {
+    fprintf(stderr, "diskmule_cuda: tensor-core path off for this layer (weight maps refused)\n");
+    L->tc_ok = false;
+  }
+  return DM_OK;
+}
+
 int32_t build_plan(dm_moe_layer *L) {
   const dm_moe_desc &d = L->desc;
   const uint64_t E = d.experts, H = d.hidden, I = d.intermediate;
@@ -608,7 +638,8 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   bytes += al((E + 1) * 4) + al((E + 2) * 4) + 2 * al(pairs * 4) + al((E + 1) * 4) + 2 * al(4);
   bytes += al((pairs + E + 1) * 8) + al(4);
   bytes += al(pairs * I * 4) + al(pairs * H * 4);
-  if (L->tc_ok) bytes += al(2 * pairs * H * 2) + al(2 * pairs * I * 2) + 2 * al(pairs * 4);
+  if (L->tc_ok)
+    bytes += al(2 * pairs * H * 2) + al(2 * pairs * I * 2) + 2 * al(pairs * 4) + al(2 * pairs * I * 4);
   L->drop_graphs();
   if (L->scratch) {
     cudaDeviceSynchronize();
@@ -633,7 +664,7 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   a.active = arena.take<int32_t>(E + 1);
   a.n_active = arena.take<int32_t>(1);
   a.status = arena.take<int32_t>(1);
-  a.items = arena.take<int2>(pairs + E + 1);
+  a.items = arena.take<int4>(pairs + E + 1);
   a.n_items = arena.take<int32_t>(1);
   a.h = arena.take<float>(pairs * I);
   a.ysorted = arena.take<float>(pairs * H);
@@ -642,16 +673,24 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
     __half *h16 = arena.take<__half>(2 * pairs * I);
     float *x_inv = arena.take<float>(pairs);
     float *h_inv = arena.take<float>(pairs);
+    float *gu = arena.take<float>(2 * pairs * I);
     const int nts[3] = {16, 32, 64};
+    int n_sm = 148;
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, L->ctx->device);
+    const char *split_env = getenv("DISKMULE_CUDA_TC_SPLIT");
+    const bool split = !(split_env && (!strcmp(split_env, "0") || !strcmp(split_env, "false")));
     for (int i = 0; i < 3; i++) {
       dm::TcPlan &p = L->tc[i];
       p.nt = nts[i];
+      p.n_sm = n_sm;
+      p.split = split;
       p.rows = (int)pairs;
       p.x16 = x16;
       p.h16 = h16;
       p.x_inv = x_inv;
       p.h_inv = h_inv;
-      if (dm::make_tc_maps(p, (int)H, (int)I, p.nt) != 0) L->tc_ok = false;
+      p.gu = gu;
+      if (dm::make_tc_maps(p, (int)H, (int)I, d.down_type, p.nt) != 0) L->tc_ok = false;
     }
   }
   L->capacity = tokens;
@@ -699,9 +738,13 @@ int32_t dm_moe_layer_create(dm_cuda_context *ctx, const dm_moe_desc *desc, dm_mo
     const char *env = getenv("DISKMULE_CUDA_GRAPHS");
     L->graphs_enabled = L->capture && !(env && (!strcmp(env, "0") || !strcmp(env, "false")));
     const char *tc_env = getenv("DISKMULE_CUDA_TC");
-    L->tc_ok = d.family != DM_FAMILY_GLM52 &&
+    // the tensor-core kernels copy weight blocks in 16-byte pieces
+    const uintptr_t align = (uintptr_t)d.gate | (uintptr_t)L->up_base |
+                            (uintptr_t)d.shared_gate | (uintptr_t)d.shared_up;
+    L->tc_ok = rc == DM_OK && d.family != DM_FAMILY_GLM52 && align % 16 == 0 &&
                dm::tc_supported(d.gate_type, d.down_type, d.hidden, d.intermediate) &&
                !(tc_env && (!strcmp(tc_env, "0") || !strcmp(tc_env, "false")));
+    if (L->tc_ok) rc = build_tc_weights(L);
   }
   cudaError_t err = cudaStreamSynchronize(ctx->stream);
   if (err == cudaSuccess) err = cudaGetLastError();
@@ -836,6 +879,7 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
     const double avg = (double)tokens * d.top_k / d.experts;
     if (avg >= 4.0) {
       tcp = L->tc[avg <= 12.0 ? 0 : (avg <= 24.0 ? 1 : 2)];
+      tcp.weights = &L->tcw;
       const int pairs = a.T * a.k + (a.shared ? a.T : 0);
       tcp.max_items = std::min(pairs, (pairs + tcp.nt - 1) / tcp.nt + plan.max_active);
       a.chunk = tcp.nt;
@@ -1036,7 +1080,7 @@ extern "C" int32_t dm_moe_forward_noalloc(dm_moe_layer *L, const void *x, float 
   a.active = arena.take<int32_t>(E + 1);
   a.n_active = arena.take<int32_t>(1);
   a.status = arena.take<int32_t>(1);
-  a.items = arena.take<int2>(pairs + E + 1);
+  a.items = arena.take<int4>(pairs + E + 1);
   a.n_items = arena.take<int32_t>(1);
   a.h = arena.take<float>(pairs * I);
   a.ysorted = arena.take<float>(pairs * H);

@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_up_kernel(ForwardArgs a, Ma
                                                               int rows_per_cta) {
   extern __shared__ __align__(16) float smem[];
   if ((int)blockIdx.y >= *a.n_items) return;
-  const int2 item = a.items[blockIdx.y];  // (expert, first token of the chunk)
+  const int4 item = a.items[blockIdx.y];  // (expert, first token of the chunk, ...)
   const int e = item.x, c0 = item.y;
   const int base = a.offsets[e];
   const int nt = min(NT, a.counts[e] - c0);
@@ -433,7 +433,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_down_kernel(ForwardArgs a, 
                                                                 int rows_per_cta) {
   extern __shared__ __align__(16) float smem[];
   if ((int)blockIdx.y >= *a.n_items) return;
-  const int2 item = a.items[blockIdx.y];
+  const int4 item = a.items[blockIdx.y];
   const int e = item.x, c0 = item.y;
   const int base = a.offsets[e];
   const int nt = min(NT, a.counts[e] - c0);

@@ -530,7 +530,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs 
   __syncthreads();
   // Block-wide exclusive scans over the experts (one thread per expert, the shared
   // expert as index E): token offsets, the compacted active list and the work list
-  // of (expert, first token) chunks of `a.chunk` tokens.
+  // of (expert, first token, position, tokens) chunks of `a.chunk` tokens.
   {
     const int e = threadIdx.x;  // E + 1 <= kDispatchThreads
     const int count = e < E ? total[e] : (e == E && a.shared ? a.T : 0);
@@ -543,7 +543,9 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs 
       a.offsets[e] = s_count;
       if (e < E) flags[e] = s_count;
       if (count > 0) a.active[s_active] = e;
-      for (int j = 0; j < items; j++) a.items[s_items + j] = make_int2(e, j * a.chunk);
+      for (int j = 0; j < items; j++)
+        a.items[s_items + j] = make_int4(e, j * a.chunk, s_count + j * a.chunk,
+                                         min(a.chunk, count - j * a.chunk));
     }
     if (e == 0) {
       a.offsets[E + 1] = tot_count;
@@ -879,7 +881,7 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   const int max_active = std::min(a.E + (a.shared ? 1 : 0), a.T * a.k + (a.shared ? 1 : 0));
   mark(kStageUp);
   if (gemv && tc) {
-    int n = launch_tc_experts(a, *tc, *gemv, stream, ev ? ev[kStageDown] : nullptr);
+    int n = launch_tc_experts(a, *tc, *tc->weights, stream, ev ? ev[kStageDown] : nullptr);
     if (n < 0) return -1;
     launches += n;
   } else if (gemv) {

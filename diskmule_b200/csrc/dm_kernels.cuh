@@ -43,7 +43,8 @@ struct ForwardArgs {
   int32_t *active;         // [E + 1] experts with tokens, ascending
   int32_t *n_active;       // [1]
   int chunk;               // tokens per work item
-  int2 *items;             // [T*k + T + E + 1] (expert, first token) work items
+  int4 *items;             // [T*k + T + E + 1] work items: (expert, first token within the
+                           // expert, first sorted position, tokens)
   int32_t *n_items;        // [1]
   int32_t *status;         // [1] device error word (0 = ok)
   float *h;                // [(T*k + T), I]

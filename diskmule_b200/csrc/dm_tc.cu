@@ -37,18 +37,24 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
                : "memory");
 }
 
-// Wait for the phase with parity `parity` to complete; false after ~2 s.
+// One try_wait on the phase with parity `parity`; the warp may sleep in it (up to
+// about a millisecond) until the phase completes instead of spinning.
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity), "r"(1000000u)
+      : "memory");
+  return done != 0;
+}
+
+// Wait for the phase with parity `parity` to complete; false after ~0.1 s.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   const long long start = clock64();
   while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (done) return true;
+    if (mbar_try(bar, parity)) return true;
     if (clock64() - start > kWaitCycles) return false;
   }
 }
@@ -59,6 +65,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
       "%3}], [%4];" ::"r"(dst),
       "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3, %4}], [%5];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
       : "memory");
 }
 
@@ -82,16 +97,6 @@ __device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t cols) {
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
                : "memory");
-}
-
-// D[tmem] (+)= A[smem] * B[smem]^T, fp16 inputs, f32 accumulate
-__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
@@ -124,23 +129,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
 // Instruction descriptor: fp16 A and B (K-major), f32 D, M = 128, N = n.
 __host__ __device__ constexpr uint32_t idesc_f16(int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-
-__device__ __forceinline__ uint4 ldg16(const void *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-// Store 8 fp16 values (one 16-byte chunk `c` of the 128-byte row `r` of an atom)
-// with the 128-byte swizzle: chunk c lands at c ^ (r & 7).
-__device__ __forceinline__ void st_chunk(uint32_t atom, int r, int c, uint4 v) {
-  const uint32_t addr = atom + (uint32_t)r * 128u + ((uint32_t)(c ^ (r & 7)) << 4);
-  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
-               "r"(v.z), "r"(v.w)
-               : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -183,82 +171,135 @@ __device__ __forceinline__ uint64_t magic2(uint32_t w, int c) {
 }
 
 // ---------------------------------------------------------------------------
-// producers: one A row's part of a K step, dequantised in f32 and rounded once to
-// fp16, stored in the swizzled layout. A quant byte q becomes f = 0.5 + q/256
-// (exact), so a value alpha*q + beta is fma(f, 256*alpha, beta - 128*alpha): one
-// packed f32x2 fma per two weights, f32-accurate before the fp16 rounding.
+// dequantisation of one 256-wide K step of one weight row into tensor memory.
+// A quant byte q (< 128) becomes f = 0.5 + q/256 exactly (PRMT into the mantissa of
+// 0.5), so a value alpha*q + beta is fma(f, 256*alpha, beta - 128*alpha): one packed
+// f32x2 fma per two weights, f32-accurate, then a single rounding to fp16. Two
+// consecutive K values share one 32-bit TMEM column (lower K in the low half); the
+// row is this thread's TMEM lane.
 // ---------------------------------------------------------------------------
 
-// One group pair gp of a Q4_K super-block (src/cpu.rs:585-616) -> one atom: chunks
-// 0..3 = low nibbles (sub-block 2gp), chunks 4..7 = high nibbles (sub-block 2gp+1),
-// in element order. value = (d*sc)*q - dmin*m. A high nibble is read shifted right by
-// one bit (byte 8*q, below 128 as the magic needs): f = 0.5 + q/32.
-__device__ __forceinline__ void produce_q4k(uint4 hd, uint4 qa, uint4 qb, int gp, uint32_t atom,
-                                            int r) {
+__device__ __forceinline__ uint4 lds16(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds4(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint2 lds8(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint16_t lds2(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+
+// 16 columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// four bytes (each below 128) -> two fp16-pair columns
+__device__ __forceinline__ void deq4(uint32_t w, uint64_t M, uint64_t C, uint32_t *out) {
+  out[0] = to_h2(fma2(magic2(w, 0), M, C));
+  out[1] = to_h2(fma2(magic2(w, 2), M, C));
+}
+
+// Each K step of a row is split between two producer threads: half hf dequantises K
+// values [128 hf, 128 hf + 128) of the step into 64 columns from tcol, reading the row's
+// raw blocks from the step's shared-memory stage.
+
+// Q4_K super-block (src/cpu.rs:585-616) at s: 16-byte header (d, dmin, 12 scale bytes),
+// qs[128]. Half hf = group pairs 2hf, 2hf+1. Group pair gp: low nibbles of
+// qs[32gp .. 32gp+32) are elements 64gp + i (sub-block 2gp), high nibbles elements
+// 64gp + 32 + i (sub-block 2gp+1). value = (d*sc)*q - dmin*m. A high nibble is taken
+// shifted right by one (byte 8q), so f = 0.5 + q/32.
+__device__ __forceinline__ void deq_q4k(uint32_t s, int hf, uint32_t tcol) {
+  const uint4 hd = lds16(s);
   const float d = f16_bits_to_f32((uint16_t)(hd.x & 0xffff));
   const float dmin = f16_bits_to_f32((uint16_t)(hd.x >> 16));
-  const uint32_t sca = hd.y & 0x3F3F3F3Fu, ma = hd.z & 0x3F3F3F3Fu;
-  const uint32_t scb = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
-  const uint32_t mb = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
-  const int jl = 2 * gp, jh = jl + 1;
-  const uint32_t scl = jl < 4 ? (sca >> (8 * jl)) & 0xff : (scb >> (8 * (jl - 4))) & 0xff;
-  const uint32_t ml = jl < 4 ? (ma >> (8 * jl)) & 0xff : (mb >> (8 * (jl - 4))) & 0xff;
-  const uint32_t sch = jh < 4 ? (sca >> (8 * jh)) & 0xff : (scb >> (8 * (jh - 4))) & 0xff;
-  const uint32_t mh = jh < 4 ? (ma >> (8 * jh)) & 0xff : (mb >> (8 * (jh - 4))) & 0xff;
-  const float al = __fmul_rn(d, (float)scl), bl = __fmul_rn(dmin, (float)ml);
-  const float ah = __fmul_rn(d, (float)sch), bh = __fmul_rn(dmin, (float)mh);
-  // low nibble: v = al*q - bl = fma(f, 256 al, -(128 al + bl))
-  const uint64_t Ml = pair(256.0f * al, 256.0f * al);
-  const float cl = -(128.0f * al + bl);
-  const uint64_t Cl = pair(cl, cl);
-  // high nibble (byte = 8 q): v = ah*q - bh = fma(f, 32 ah, -(16 ah + bh))
-  const uint64_t Mh = pair(32.0f * ah, 32.0f * ah);
-  const float ch = -(16.0f * ah + bh);
-  const uint64_t Ch = pair(ch, ch);
-  const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  // scale/min bytes of sub-blocks 4hf .. 4hf+3 (get_scale_min_k4)
+  const uint32_t sc = hf ? ((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u)) : (hd.y & 0x3F3F3F3Fu);
+  const uint32_t mn = hf ? (((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u))
+                         : (hd.z & 0x3F3F3F3Fu);
 #pragma unroll
-  for (int c = 0; c < 4; c++) {
-    uint32_t lo[4], hi[4];
+  for (int g = 0; g < 2; g++) {
+    const float al = __fmul_rn(d, (float)((sc >> (16 * g)) & 0xff));
+    const float bl = __fmul_rn(dmin, (float)((mn >> (16 * g)) & 0xff));
+    const float ah = __fmul_rn(d, (float)((sc >> (16 * g + 8)) & 0xff));
+    const float bh = __fmul_rn(dmin, (float)((mn >> (16 * g + 8)) & 0xff));
+    const uint64_t Ml = pair(256.0f * al, 256.0f * al);
+    const float cl = -(128.0f * al + bl);
+    const uint64_t Cl = pair(cl, cl);
+    const uint64_t Mh = pair(32.0f * ah, 32.0f * ah);
+    const float ch = -(16.0f * ah + bh);
+    const uint64_t Ch = pair(ch, ch);
+    const uint4 qa = lds16(s + 16 + 64 * hf + 32 * g), qb = lds16(s + 32 + 64 * hf + 32 * g);
+    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    uint32_t lo[16], hi[16];
 #pragma unroll
-    for (int k = 0; k < 2; k++) {
-      const uint32_t wl = w[2 * c + k] & 0x0F0F0F0Fu, wh = (w[2 * c + k] >> 1) & 0x78787878u;
-      lo[2 * k] = to_h2(fma2(magic2(wl, 0), Ml, Cl));
-      lo[2 * k + 1] = to_h2(fma2(magic2(wl, 2), Ml, Cl));
-      hi[2 * k] = to_h2(fma2(magic2(wh, 0), Mh, Ch));
-      hi[2 * k + 1] = to_h2(fma2(magic2(wh, 2), Mh, Ch));
+    for (int k = 0; k < 8; k++) {
+      deq4(w[k] & 0x0F0F0F0Fu, Ml, Cl, lo + 2 * k);
+      deq4((w[k] >> 1) & 0x78787878u, Mh, Ch, hi + 2 * k);
     }
-    st_chunk(atom, r, c, make_uint4(lo[0], lo[1], lo[2], lo[3]));
-    st_chunk(atom, r, c + 4, make_uint4(hi[0], hi[1], hi[2], hi[3]));
+    tmem_st16(tcol + 32 * g, lo);
+    tmem_st16(tcol + 32 * g + 16, hi);
   }
 }
 
-// Atom g of half h of a Q6_K super-block (src/cpu.rs:618-645), split layout:
-// elements 128h + 64g + j, i.e. quarters 2g and 2g+1. ql = the half's 64 low-bit bytes
-// (16 words), qh = its 32 high-bit bytes (8 words), sw = the word holding the atom's
-// four scales (scale index 8h + 4g + (j / 16)). value = (d*sc)*(q-32) =
-// fma(f, 256 s, -160 s). Quarter 2g+u takes nibble 4g of ql[8u + i] and high bits
-// 2(2g+u) of qh[i].
-__device__ __forceinline__ void produce_q6k(const uint32_t *ql, const uint32_t *qh, uint32_t sw,
-                                            float d, int g, uint32_t atom, int r) {
-  const int nsh = 4 * g;
+// Q6_K super-block (src/cpu.rs:618-645), split layout at s: ql[128] qh[64] sc[16]; d
+// given. Half h = hf (elements 128h + ...): quarter qq, index l < 32: element
+// 128h + 32qq + l = low nibble (qq < 2) or high nibble of ql[64h + 32(qq&1) + l] | bits 2qq
+// of qh[32h + l] << 4, scale sc[8h + l/16 + 2qq]. value = (d*sc)*(q-32) =
+// fma(f, 256 s, -160 s).
+__device__ __forceinline__ void deq_q6k(uint32_t s, int h, float d, uint32_t tcol) {
+  const uint2 scw = lds8(s + 192 + 8 * h);
+  const uint32_t sc[2] = {scw.x, scw.y};
+  uint32_t ql[16], qh[8];
 #pragma unroll
-  for (int c = 0; c < 8; c++) {
-    const int u = c >> 2;          // quarter 2g + u
-    const int idx0 = 8 * (c & 3);  // first idx of the chunk within the quarter
-    const int sb = (idx0 >> 4) + 2 * u;
-    const float s = __fmul_rn(d, (float)(int8_t)((sw >> (8 * sb)) & 0xff));
-    const uint64_t M = pair(256.0f * s, 256.0f * s), C = pair(-160.0f * s, -160.0f * s);
-    uint32_t out[4];
+  for (int i = 0; i < 4; i++) {
+    const uint4 v = lds16(s + 64 * h + 16 * i);
+    ql[4 * i] = v.x, ql[4 * i + 1] = v.y, ql[4 * i + 2] = v.z, ql[4 * i + 3] = v.w;
+  }
 #pragma unroll
-    for (int wi = 0; wi < 2; wi++) {
-      const int i = idx0 / 4 + wi;
-      const uint32_t src = u ? ql[8 + i] : ql[i];
-      const uint32_t hg = g ? qh[i] : (qh[i] << 4);
-      const uint32_t q = ((src >> nsh) & 0x0F0F0F0Fu) | ((hg >> (2 * u)) & 0x30303030u);
-      out[2 * wi] = to_h2(fma2(magic2(q, 0), M, C));
-      out[2 * wi + 1] = to_h2(fma2(magic2(q, 2), M, C));
+  for (int i = 0; i < 2; i++) {
+    const uint4 v = lds16(s + 128 + 32 * h + 16 * i);
+    qh[4 * i] = v.x, qh[4 * i + 1] = v.y, qh[4 * i + 2] = v.z, qh[4 * i + 3] = v.w;
+  }
+#pragma unroll
+  for (int qq = 0; qq < 4; qq++) {
+    uint32_t out[16];
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+      const int si = half + 2 * qq;
+      const float sv = __fmul_rn(d, (float)(int8_t)((sc[si >> 2] >> (8 * (si & 3))) & 0xff));
+      const uint64_t M = pair(256.0f * sv, 256.0f * sv), C = pair(-160.0f * sv, -160.0f * sv);
+#pragma unroll
+      for (int ii = 0; ii < 4; ii++) {
+        const int i = 4 * half + ii;
+        const uint32_t src = ql[8 * (qq & 1) + i];
+        const uint32_t lo4 = (qq < 2 ? src : src >> 4) & 0x0F0F0F0Fu;
+        const uint32_t hb = qq == 0 ? (qh[i] << 4) : qq == 1 ? (qh[i] << 2) : qq == 2 ? qh[i] : (qh[i] >> 2);
+        deq4(lo4 | (hb & 0x30303030u), M, C, out + 2 * i);
+      }
     }
-    st_chunk(atom, r, c, make_uint4(out[0], out[1], out[2], out[3]));
+    tmem_st16(tcol + 16 * qq, out);
   }
 }
 
@@ -266,33 +307,30 @@ __device__ __forceinline__ uint32_t spread4(uint32_t v) {
   return ((v & 0xfu) * 0x02040810u) & 0x10101010u;
 }
 
-// Q5_0 block b (0 or 1) of a 64-value atom (src/cpu.rs:560-574), split layout ->
-// chunks 4b..4b+3. value = d*(q-16) = fma(f, 256 d, -144 d).
-__device__ __forceinline__ void produce_q50(uint4 qs, uint32_t hb, float d, int b, uint32_t atom,
-                                            int r) {
-  const uint64_t M = pair(256.0f * d, 256.0f * d), C = pair(-144.0f * d, -144.0f * d);
-  const uint32_t w[4] = {qs.x, qs.y, qs.z, qs.w};
-  uint32_t lo[4], hi[4];
+// nb (<= 4) Q5_0 blocks (src/cpu.rs:560-574): qs[16 nb] at sq, qh words at sh, f16 d at
+// sd. Block b: elements 32b + j (j < 16) = low nibble of qs[j] | qh bit j << 4, elements
+// 32b + 16 + j = high nibble | qh bit 16 + j << 4. value = d*(q-16) = fma(f, 256 d, -144 d).
+// Columns 16b.
+__device__ __forceinline__ void deq_q50(uint32_t sq, uint32_t sh, uint32_t sd, int nb,
+                                        uint32_t tcol) {
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    lo[i] = (w[i] & 0x0F0F0F0Fu) | spread4(hb >> (4 * i));
-    hi[i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | spread4(hb >> (16 + 4 * i));
-  }
-  uint32_t o[8];
+  for (int b = 0; b < 4; b++) {
+    if (b < nb) {
+      const uint4 qs = lds16(sq + 16 * b);
+      const uint32_t hb = lds4(sh + 4 * b);
+      const uint32_t dw = lds4(sd + 4 * (b >> 1));
+      const float d = f16_bits_to_f32((uint16_t)((b & 1) ? dw >> 16 : dw & 0xffff));
+      const uint64_t M = pair(256.0f * d, 256.0f * d), C = pair(-144.0f * d, -144.0f * d);
+      const uint32_t w[4] = {qs.x, qs.y, qs.z, qs.w};
+      uint32_t out[16];
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    o[2 * i] = to_h2(fma2(magic2(lo[i], 0), M, C));
-    o[2 * i + 1] = to_h2(fma2(magic2(lo[i], 2), M, C));
+      for (int i = 0; i < 4; i++) {
+        deq4((w[i] & 0x0F0F0F0Fu) | spread4(hb >> (4 * i)), M, C, out + 2 * i);
+        deq4(((w[i] >> 4) & 0x0F0F0F0Fu) | spread4(hb >> (16 + 4 * i)), M, C, out + 8 + 2 * i);
+      }
+      tmem_st16(tcol + 16 * b, out);
+    }
   }
-  st_chunk(atom, r, 4 * b + 0, make_uint4(o[0], o[1], o[2], o[3]));
-  st_chunk(atom, r, 4 * b + 1, make_uint4(o[4], o[5], o[6], o[7]));
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    o[2 * i] = to_h2(fma2(magic2(hi[i], 0), M, C));
-    o[2 * i + 1] = to_h2(fma2(magic2(hi[i], 2), M, C));
-  }
-  st_chunk(atom, r, 4 * b + 2, make_uint4(o[0], o[1], o[2], o[3]));
-  st_chunk(atom, r, 4 * b + 3, make_uint4(o[4], o[5], o[6], o[7]));
 }
 
 // ---------------------------------------------------------------------------
@@ -315,22 +353,43 @@ __device__ __forceinline__ float pow2_scale(float m) {
   return exp2f((float)(13 - ilogbf(m)));
 }
 
-// Row `pos` of the packed matrix: hi = fp16(x*s) in row pos, lo = fp16(x*s - hi) in
-// row pos + lo_offset; x*s = hi + lo to about 2^-22 relative.
+__device__ __forceinline__ float activate(const ForwardArgs &a, int expert, float g, float u) {
+  if (a.family == kGemma) return __fmul_rn(gelu_tanh(g), u);
+  if (a.family == kQwen) return __fmul_rn(qwen_silu(g), u);
+  if (expert == a.E) return __fmul_rn(glm_silu(g), u);
+  return __fmul_rn(glm_cached_silu(g), u);
+}
+
+constexpr int kMaxPackI = 2048;  // intermediate rows staged in shared memory by pack_kernel
+
+// Sorted row `pos` -> hi = fp16(x*s) and lo = fp16(x*s - hi), x*s = hi + lo to about
+// 2^-22 relative. With `split` the two halves are rows 2 pos and 2 pos + 1 (one tile of
+// 2 NT rows then feeds both halves to a single MMA); without it row pos holds hi alone.
+// INPUT: x is the expert input row. Otherwise x = act(gate, up) of the row's gate/up
+// outputs gu[pos][2i] (gate) and gu[pos][2i + 1] (up), i < K.
 template <bool INPUT>
-__global__ void __launch_bounds__(256) pack_kernel(ForwardArgs a, __half *out, float *inv, int K,
-                                                  int lo_offset) {
+__global__ void __launch_bounds__(256) pack_kernel(ForwardArgs a, const float *gu, __half *out,
+                                                  float *inv, int K, int split) {
   __shared__ float red[8];
+  __shared__ __align__(16) float hrow[INPUT ? 4 : kMaxPackI];
   const int pos = blockIdx.x;
   if (pos >= a.offsets[a.E + 1]) return;
   const float *src;
+  const int P = a.T * a.k, pr = a.sorted[pos];
   if (INPUT) {
-    const int P = a.T * a.k, pr = a.sorted[pos];
     const int tok = pr < P ? pr / a.k : pr - P;
     src = (a.family == kGemma ? a.expert_in : reinterpret_cast<const float *>(a.x)) +
           (size_t)tok * K;
   } else {
-    src = a.h + (size_t)pos * K;
+    const int e = pr < P ? (int)a.sel_idx[pr] : a.E;
+    const float *row = gu + (size_t)pos * 2 * K;
+    for (int i = threadIdx.x * 2; i < K; i += blockDim.x * 2) {
+      const float4 v = *reinterpret_cast<const float4 *>(row + 2 * i);
+      hrow[i] = activate(a, e, v.x, v.y);
+      hrow[i + 1] = activate(a, e, v.z, v.w);
+    }
+    __syncthreads();
+    src = hrow;
   }
   float m = 0.0f;
   for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
@@ -347,370 +406,479 @@ __global__ void __launch_bounds__(256) pack_kernel(ForwardArgs a, __half *out, f
       hi[j] = __float2half_rn(xs[j]);
       lo[j] = __float2half_rn(xs[j] - __half2float(hi[j]));
     }
-    *reinterpret_cast<uint2 *>(out + (size_t)pos * K + i) =
+    const size_t row = split ? 2 * (size_t)pos : (size_t)pos;
+    *reinterpret_cast<uint2 *>(out + row * K + i) =
         make_uint2(h2u(__halves2half2(hi[0], hi[1])), h2u(__halves2half2(hi[2], hi[3])));
-    *reinterpret_cast<uint2 *>(out + (size_t)(pos + lo_offset) * K + i) =
-        make_uint2(h2u(__halves2half2(lo[0], lo[1])), h2u(__halves2half2(lo[2], lo[3])));
+    if (split)
+      *reinterpret_cast<uint2 *>(out + (row + 1) * K + i) =
+          make_uint2(h2u(__halves2half2(lo[0], lo[1])), h2u(__halves2half2(lo[2], lo[3])));
   }
   if (threadIdx.x == 0) inv[pos] = 1.0f / s;
 }
 
 // ---------------------------------------------------------------------------
-// GEMM kernels (warp-specialised)
+// persistent grouped expert GEMM
 // ---------------------------------------------------------------------------
-
-__device__ __forceinline__ float activate(const ForwardArgs &a, int expert, float g, float u) {
-  if (a.family == kGemma) return __fmul_rn(gelu_tanh(g), u);
-  if (a.family == kQwen) return __fmul_rn(qwen_silu(g), u);
-  if (expert == a.E) return __fmul_rn(glm_silu(g), u);
-  return __fmul_rn(glm_cached_silu(g), u);
-}
-
-// 8 producer warps (two threads per A row: row t & 127, part t >> 7) and one
-// control warp (TMA + MMA issue); warps 0..3 also own the TMEM lanes for the epilogue.
-constexpr int kProducerThreads = 256;
-constexpr int kProducerWarps = kProducerThreads / 32;
-constexpr int kTcThreads = kProducerThreads + 32;
-constexpr int kStages = 2;
-
-// Stage s: A tile at base + s*stage, B tile (hi | lo) after it; barriers after the
-// stages: tma[s] (B tile landed, transaction bytes), full[s] (A tile written, one
-// arrival per producer warp), empty[s] (stage consumed, tcgen05.commit).
-struct Smem {
-  uint32_t base, stage, a_bytes, bars;
-  uint8_t *generic;  // generic pointer of the aligned base
-  __device__ __forceinline__ uint32_t a(int s) const { return base + (uint32_t)s * stage; }
-  __device__ __forceinline__ uint32_t b(int s) const { return a(s) + a_bytes; }
-  __device__ __forceinline__ uint32_t tma(int s) const { return bars + 8u * s; }
-  __device__ __forceinline__ uint32_t full(int s) const { return bars + 8u * (kStages + s); }
-  __device__ __forceinline__ uint32_t empty(int s) const { return bars + 8u * (2 * kStages + s); }
-  __device__ __forceinline__ uint32_t slot() const { return bars + 8u * 3 * kStages; }
-};
-
-template <int ATOMS, int NT>
-struct Layout {
-  static constexpr uint32_t kA = ATOMS * 16384u;         // 128 rows x 128 B per atom
-  static constexpr uint32_t kBHalf = ATOMS * NT * 128u;  // one of hi / lo
-  static constexpr uint32_t kStage = kA + 2 * kBHalf;
-  static constexpr size_t kSmem = 1024 + kStages * (size_t)kStage + 128;
-};
-
-template <int ATOMS, int NT>
-__device__ __forceinline__ Smem carve(uint8_t *dsm) {
-  using L = Layout<ATOMS, NT>;
-  Smem s;
-  const uint32_t raw = smem_u32(dsm);
-  s.base = (raw + 1023u) & ~1023u;
-  s.generic = dsm + (s.base - raw);
-  s.stage = L::kStage;
-  s.a_bytes = L::kA;
-  s.bars = s.base + kStages * L::kStage;
-  return s;
-}
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ bool aborted(const int *abort_flag, const int32_t *status) {
-  return *reinterpret_cast<const volatile int *>(abort_flag) ||
-         *reinterpret_cast<const volatile int32_t *>(status) == kStatusTimeout;
+__device__ __forceinline__ bool aborted(const int *abort_flag) {
+  return *reinterpret_cast<const volatile int *>(abort_flag) != 0;
 }
 
 // Bounded wait that also gives up as soon as another thread of the CTA has aborted.
-__device__ __forceinline__ bool mbar_wait_or_abort(uint32_t bar, uint32_t parity, const int *abort_flag) {
+__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, const int *abort_flag) {
   const long long start = clock64();
   while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (done) return true;
+    if (mbar_try(bar, parity)) return true;
     if (*reinterpret_cast<const volatile int *>(abort_flag)) return false;
     if (clock64() - start > kWaitCycles) return false;
   }
 }
 
-// Producer side: `P` supplies `Raw load(int ks)` and `void store(const Raw &, int ks,
-// uint32_t a_base)`; step ks+1 is loaded while step ks is dequantised. The decision to
-// stop is taken per warp (vote), so every lane leaves the loop at the same step.
-template <int ATOMS, int NT, class P>
-__device__ __forceinline__ void producer_loop(const Smem &sm, int nsteps, P &prod, int *abort_flag,
-                                              const int32_t *status) {
-  const int lane = threadIdx.x & 31;
-  auto cur = prod.load(0);
-  for (int ks = 0; ks < nsteps; ks++) {
-    const int s = ks % kStages, use = ks / kStages;
-    bool stop = ks >= kStages && !mbar_wait_or_abort(sm.empty(s), (uint32_t)((use - 1) & 1), abort_flag);
-    stop = stop || aborted(abort_flag, status);
-    if (__any_sync(0xffffffffu, stop)) {
-      if (lane == 0) atomicExch(abort_flag, 1);
-      break;
-    }
-    auto nxt = prod.load(ks + 1 < nsteps ? ks + 1 : ks);
-    prod.store(cur, ks, sm.a(s));
-    cur = nxt;
-    fence_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(sm.full(s));
-  }
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Control side (one thread): TMA of the B tiles and the MMA chain.
-template <int ATOMS, int NT>
-__device__ __forceinline__ void control_loop(const Smem &sm, uint32_t tmem, const CUtensorMap *bmap,
-                                             int pos0, int lo_offset, int nsteps, int *abort_flag,
-                                             const int32_t *status, int *issued) {
-  using L = Layout<ATOMS, NT>;
-  constexpr uint32_t idesc = idesc_f16(NT);
-  for (int ks = 0; ks < nsteps; ks++) {
-    const int s = ks % kStages, use = ks / kStages;
-    if ((ks >= kStages && !mbar_wait_or_abort(sm.empty(s), (uint32_t)((use - 1) & 1), abort_flag)) ||
-        aborted(abort_flag, status)) {
-      atomicExch(abort_flag, 1);
-      break;
-    }
-    mbar_expect_tx(sm.tma(s), 2 * L::kBHalf);
-#pragma unroll
-    for (int at = 0; at < ATOMS; at++) {
-      const int k0 = (ks * ATOMS + at) * 64;
-      tma_load_2d(sm.b(s) + at * (NT * 128u), bmap, k0, pos0, sm.tma(s));
-      tma_load_2d(sm.b(s) + L::kBHalf + at * (NT * 128u), bmap, k0, pos0 + lo_offset, sm.tma(s));
-    }
-    if (!mbar_wait(sm.tma(s), (uint32_t)(use & 1)) ||
-        !mbar_wait_or_abort(sm.full(s), (uint32_t)(use & 1), abort_flag)) {
-      atomicExch(abort_flag, 1);
-      break;
-    }
-    fence_after();
-#pragma unroll
-    for (int kk = 0; kk < 4 * ATOMS; kk++) {
-      const uint64_t ad = sw128_desc(sm.a(s) + (kk >> 2) * 16384u + (kk & 3) * 32u);
-      const uint32_t boff = (kk >> 2) * (NT * 128u) + (kk & 3) * 32u;
-      mma_f16(tmem, ad, sw128_desc(sm.b(s) + boff), idesc, (ks == 0 && kk == 0) ? 0u : 1u);
-      mma_f16(tmem, ad, sw128_desc(sm.b(s) + L::kBHalf + boff), idesc, 1u);
-    }
-    mma_commit(sm.empty(s));
-    *issued = ks;
-  }
+// D[tmem] (+)= A[tmem] * B[smem]^T, fp16 inputs, f32 accumulate; A row m is TMEM lane m.
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
-// Barriers and tensor memory (warp 0 allocates). A CTA that starts after another
-// has timed out begins aborted (decided by one thread, seen by all after the barrier).
-template <int NT>
-__device__ __forceinline__ uint32_t setup(const Smem &sm, int *abort_flag, int *issued,
-                                          const int32_t *status) {
-  const int tid = threadIdx.x;
-  if (tid == 0) {
-    *abort_flag = *reinterpret_cast<const volatile int32_t *>(status) == kStatusTimeout;
-    *issued = -1;
-    for (int s = 0; s < kStages; s++) {
-      mbar_init(sm.tma(s), 1);
-      mbar_init(sm.full(s), kProducerWarps);
-      mbar_init(sm.empty(s), 1);
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if ((tid >> 5) == 0) tmem_alloc(sm.slot(), (uint32_t)(NT < 32 ? 32 : NT));
-  fence_before();
-  __syncthreads();
-  fence_after();
-  return *reinterpret_cast<volatile uint32_t *>(sm.generic + (sm.slot() - smem_u32(sm.generic)));
-}
+// Warp roles: 0..3 epilogue (TMEM lane quarter = warp); 4..19 producers, two groups of
+// eight (group g dequantises the steps t = g mod 2; in a group, warp 4 + 8g + 4hf + q
+// covers lanes 32q.. and half hf of the K step); 20 TMA of the activation tiles; 21 TMA
+// of the raw weight tiles; 22 and 23 MMA issue (one tcgen05.mma issuer is latency-bound
+// at ~45 cycles per instruction; two issuers with separate accumulators double the rate,
+// deterministically).
+constexpr int kEpilogueWarps = 4;
+constexpr int kProducerWarps = 16;
+constexpr int kTmaWarp = kEpilogueWarps + kProducerWarps;  // 20
+constexpr int kRawWarp = kTmaWarp + 1;                     // 21
+constexpr int kMmaWarp = kRawWarp + 1;                     // 22, 23
+constexpr int kTcThreads = (kMmaWarp + 2) * 32;            // 768
+constexpr int kStepK = 256;
+constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
+constexpr int kBarBytes = 512;
+constexpr int kMaxRaw = 8;          // raw stages
 
-// After both loops: wait for the last issued MMAs, decide (uniformly) whether the
-// accumulator is complete.
-template <int NT>
-__device__ __forceinline__ bool finish(const Smem &sm, int nsteps, int *abort_flag, int *issued,
-                                       int32_t *status) {
-  __syncthreads();
-  const int last = *issued;
-  bool ok = !*abort_flag && last == nsteps - 1;
-  if (last >= 0 && !mbar_wait(sm.empty(last % kStages), (uint32_t)((last / kStages) & 1)))
-    ok = false;
-  ok = __syncthreads_and(ok ? 1 : 0) != 0;
-  if (!ok && threadIdx.x == 0) atomicExch(status, kStatusTimeout);
-  fence_after();
-  return ok;
-}
+enum TcKind { kUpQ4K = 0, kDownQ6K = 1, kDownQ50 = 2 };
 
-template <int NT>
-__device__ __forceinline__ void read_columns(uint32_t tmem, float *v) {
-  const uint32_t lane_base = ((uint32_t)((threadIdx.x >> 5) & 3) * 32u) << 16;
-#pragma unroll
-  for (int c = 0; c < NT; c += 16) tmem_ld16(tmem + lane_base + c, reinterpret_cast<uint32_t *>(v + c));
-  tmem_wait_ld();
-}
-
-template <int NT>
-__device__ __forceinline__ void teardown(uint32_t tmem) {
-  fence_before();
-  __syncthreads();
-  if ((threadIdx.x >> 5) == 0) {
-    fence_after();
-    tmem_dealloc(tmem, (uint32_t)(NT < 32 ? 32 : NT));
-  }
-}
-
-// gate/up producer: A row r = gate row i0+r/2 (even r) or up row i0+r/2 (odd r);
-// a K step is half a Q4_K super-block (2 atoms = group pairs 2h, 2h+1); thread part p
-// produces group pair 2h+p into atom p.
-struct Q4KProducer {
-  const uint4 *row;  // this row's super-blocks (9 uint4 each)
-  int r, part;
-  struct Raw {
-    uint4 hd, qa, qb;
-  };
-  __device__ __forceinline__ Raw load(int ks) const {
-    const uint4 *blk = row + (ks >> 1) * 9;
-    const int gp = 2 * (ks & 1) + part;
-    return {ldg16(blk), ldg16(blk + 1 + 2 * gp), ldg16(blk + 2 + 2 * gp)};
-  }
-  __device__ __forceinline__ void store(const Raw &w, int ks, uint32_t a_base) const {
-    const int gp = 2 * (ks & 1) + part;
-    produce_q4k(w.hd, w.qa, w.qb, gp, a_base + (uint32_t)part * 16384u, r);
-  }
+// Raw stage of one K step, 128 weight rows, filled by TMA:
+//   Q4_K: row r (gate/up interleaved) at 144 r: one super-block;
+//   Q6_K: row r at 208 r: ql qh sc of one super-block; then the 128 f16 d;
+//   Q5_0: row r at 144 r: qs of 8 blocks (+16 bytes unused); then qh[128][8 words],
+//         then d[128][8 f16].
+// Row strides are odd multiples of 16 bytes, so a warp's 16-byte loads of 32 rows are
+// free of bank conflicts.
+template <int KIND>
+struct RawTile {
+  static constexpr int kRowBytes = KIND == kDownQ6K ? 208 : 144;
+  static constexpr int kQuant = 128 * kRowBytes;
+  static constexpr int kSide = KIND == kDownQ6K ? 256 : KIND == kDownQ50 ? 128 * 32 + 128 * 16 : 0;
+  static constexpr int kBytes = kQuant + kSide;
+  static constexpr int kStage = (kBytes + 1023) / 1024 * 1024;
 };
 
-template <int NT>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_up_q4k_kernel(
-    const __grid_constant__ CUtensorMap xmap, ForwardArgs a, const float *x_inv, int lo_offset) {
-  extern __shared__ uint8_t dsm[];
-  __shared__ int abort_flag, issued;
-  if ((int)blockIdx.y >= *a.n_items) return;
-  const int2 item = a.items[blockIdx.y];
-  const int e = item.x, c0 = item.y;
-  const int pos0 = a.offsets[e] + c0;
-  const int ntok = min(NT, a.counts[e] - c0);
-  const int i0 = blockIdx.x * 64;
-  const Smem sm = carve<2, NT>(dsm);
-  const int tid = threadIdx.x, r = tid & 127;
-  const uint32_t tmem = setup<NT>(sm, &abort_flag, &issued, a.status);
-  const int nsteps = a.H / 128;
-  const int orow = i0 + (r >> 1);
-  if (tid < kProducerThreads) {
-    const bool shared = e == a.E;
-    const uint8_t *mat = (r & 1) ? (shared ? a.sh_up : a.up + (size_t)e * a.up_stride)
-                                 : (shared ? a.sh_gate : a.gate + (size_t)e * a.gate_stride);
-    Q4KProducer prod{reinterpret_cast<const uint4 *>(mat + (size_t)orow * row_bytes(DM_Q4_K, a.H)),
-                     r, tid >> 7};
-    producer_loop<2, NT>(sm, nsteps, prod, &abort_flag, a.status);
-  } else if (tid == kProducerThreads) {
-    control_loop<2, NT>(sm, tmem, &xmap, pos0, lo_offset, nsteps, &abort_flag, a.status, &issued);
-  }
-  const bool ok = finish<NT>(sm, nsteps, &abort_flag, &issued, a.status);
-  if (ok && tid < 128) {
-    float v[NT];
-    read_columns<NT>(tmem, v);
-    const int lane = tid & 31;
+// Tile of NT tokens: B rows NB = NT, or 2 NT with the hi + lo split (interleaved), so
+// one MMA of N = NB covers both halves (an M=128, K=16 MMA costs the same for N <= 64).
+// TMEM (512 columns): NA A buffers of 128 columns, then 2 (double buffer) x NI (issuers)
+// accumulators of NB columns.
+template <int KIND, int NT, bool SPLIT>
+struct Cfg {
+  static constexpr int NB = SPLIT ? 2 * NT : NT;
+  static constexpr int NA = 3 * 128 + 4 * NB <= 512 ? 3 : 2;
+  static constexpr int NI = NA * 128 + 4 * NB <= 512 ? 2 : 1;
+  static constexpr int kAccCol = NA * 128;
+  static constexpr int kBStage = (kStepK / 64) * NB * 128;  // 4 swizzle atoms of NB rows
+  static constexpr int kFixed = 1024 + NA * kBStage + kBarBytes;
+  static constexpr int kRSfit = (kSmemLimit - kFixed) / RawTile<KIND>::kStage;
+  static constexpr int kRS = kRSfit < kMaxRaw ? kRSfit : kMaxRaw;  // raw stages
+  static constexpr int kSmem = kFixed + kRS * RawTile<KIND>::kStage;
+  static constexpr bool kFits = kRS >= 3;
+};
+
+// Stage i: afull (A written: one arrival per producer warp of the group), bfull (B tile
+// landed: TMA bytes), empty (the stage's MMAs are done: one commit per issuer); raw
+// stage j: rawfull (TMA bytes), rawempty (one arrival per producer warp that read it).
+struct Bars {
+  uint32_t base;
+  __device__ __forceinline__ uint32_t afull(int i) const { return base + 8u * i; }
+  __device__ __forceinline__ uint32_t bfull(int i) const { return base + 8u * (3 + i); }
+  __device__ __forceinline__ uint32_t empty(int i) const { return base + 8u * (6 + i); }
+  __device__ __forceinline__ uint32_t accfull(int i) const { return base + 8u * (9 + i); }
+  __device__ __forceinline__ uint32_t accempty(int i) const { return base + 8u * (11 + i); }
+  __device__ __forceinline__ uint32_t drain() const { return base + 8u * 13; }
+  __device__ __forceinline__ uint32_t rawfull(int i) const { return base + 8u * (14 + i); }
+  __device__ __forceinline__ uint32_t rawempty(int i) const { return base + 8u * (14 + kMaxRaw + i); }
+  __device__ __forceinline__ uint32_t slot() const { return base + 8u * (14 + 2 * kMaxRaw); }
+};
+
+// One issuer's MMAs of one K step: slices s = I, I + NI, ... (all 16 on the fast path).
+// desc(addr + off) = desc(addr) + off / 16 while addresses stay below 256 KB.
+template <int NB, int NI, int I>
+__device__ __forceinline__ void issue_step(uint32_t dcol, uint32_t acol, uint32_t bst, int slices,
+                                           bool first) {
+  constexpr uint32_t idesc = idesc_f16(NB);
+  const uint64_t b0 = sw128_desc(bst);
+  if (slices == kStepK / 16) {
 #pragma unroll
-    for (int n = 0; n < NT; n++) {
-      const float u = __shfl_down_sync(0xffffffffu, v[n], 1);
-      if (!(lane & 1) && n < ntok) {
-        const float inv = x_inv[pos0 + n];
-        a.h[(size_t)(pos0 + n) * a.I + orow] = activate(a, e, v[n] * inv, u * inv);
+    for (int s = I; s < kStepK / 16; s += NI) {
+      const uint32_t boff = (uint32_t)(s >> 2) * (NB * 128u) + (uint32_t)(s & 3) * 32u;
+      mma_ts(dcol, acol + 8u * s, b0 + (boff >> 4), idesc, (first && s == I) ? 0u : 1u);
+    }
+  } else {
+#pragma unroll
+    for (int s = I; s < kStepK / 16; s += NI) {
+      if (s < slices) {
+        const uint32_t boff = (uint32_t)(s >> 2) * (NB * 128u) + (uint32_t)(s & 3) * 32u;
+        mma_ts(dcol, acol + 8u * s, b0 + (boff >> 4), idesc, (first && s == I) ? 0u : 1u);
       }
     }
   }
-  teardown<NT>(tmem);
 }
 
-// down producers: row r of the down tile; a K step is half a Q6_K super-block
-// (2 atoms, part p -> atom p) or two Q5_0 blocks (1 atom, part p -> block p).
-struct Q6KProducer {
-  const uint8_t *quant;  // split quant region of this row's first super-block
-  const uint16_t *d;     // f16 d of this row's first super-block
-  int r, part;
-  struct Raw {
-    uint4 ql[4], qh[2];
-    uint32_t sw;
-    uint16_t d;
-  };
-  __device__ __forceinline__ Raw load(int ks) const {
-    const uint4 *q = reinterpret_cast<const uint4 *>(quant + (size_t)(ks >> 1) * 208);
-    const int h = ks & 1;
-    Raw w;
-#pragma unroll
-    for (int i = 0; i < 4; i++) w.ql[i] = ldg16(q + 4 * h + i);
-#pragma unroll
-    for (int i = 0; i < 2; i++) w.qh[i] = ldg16(q + 8 + 2 * h + i);
-    const uint4 sc = ldg16(q + 12);
-    const uint32_t lo = h ? sc.z : sc.x, hi = h ? sc.w : sc.y;
-    w.sw = part ? hi : lo;
-    w.d = d[ks >> 1];
-    return w;
-  }
-  __device__ __forceinline__ void store(const Raw &w, int, uint32_t a_base) const {
-    produce_q6k(reinterpret_cast<const uint32_t *>(w.ql), reinterpret_cast<const uint32_t *>(w.qh),
-                w.sw, f16_bits_to_f32(w.d), part, a_base + (uint32_t)part * 16384u, r);
-  }
+struct Unit {
+  int e, pos0, ntok, tile;
 };
 
-struct Q50Producer {
-  const uint8_t *quant, *qh;  // split regions at this row's first block
-  const uint16_t *d;
-  int r, part;
-  struct Raw {
-    uint4 qs;
-    uint32_t hb;
-    uint16_t d;
-  };
-  __device__ __forceinline__ Raw load(int ks) const {
-    const int blk = 2 * ks + part;
-    return {ldg16(quant + (size_t)blk * 16), *reinterpret_cast<const uint32_t *>(qh + (size_t)blk * 4),
-            d[blk]};
-  }
-  __device__ __forceinline__ void store(const Raw &w, int, uint32_t a_base) const {
-    produce_q50(w.qs, w.hb, f16_bits_to_f32(w.d), part, a_base, r);
-  }
-};
+__device__ __forceinline__ Unit make_unit(int4 rec, int u, int n_tiles) {
+  Unit r;
+  r.e = rec.x;
+  r.pos0 = rec.z;
+  r.ntok = rec.w;
+  r.tile = u % n_tiles;
+  return r;
+}
 
-template <int KIND, int NT>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_down_kernel(
-    const __grid_constant__ CUtensorMap hmap, ForwardArgs a, SplitTensor down,
-    SplitTensor sh_down, const float *h_inv, int lo_offset) {
-  constexpr int ATOMS = KIND == DM_Q6_K ? 2 : 1;
-  extern __shared__ uint8_t dsm[];
-  __shared__ int abort_flag, issued;
-  if ((int)blockIdx.y >= *a.n_items) return;
-  const int2 item = a.items[blockIdx.y];
-  const int e = item.x, c0 = item.y;
-  const int pos0 = a.offsets[e] + c0;
-  const int ntok = min(NT, a.counts[e] - c0);
-  const int m0 = blockIdx.x * 128;
-  const Smem sm = carve<ATOMS, NT>(dsm);
-  const int tid = threadIdx.x, r = tid & 127;
-  const uint32_t tmem = setup<NT>(sm, &abort_flag, &issued, a.status);
-  const int row = m0 + r;
-  const int nsteps = a.I / (64 * ATOMS);
-  if (tid < kProducerThreads) {
-    const bool shared = e == a.E;
-    const SplitTensor &D = shared ? sh_down : down;
-    const int ex = shared ? 0 : e;
-    if (KIND == DM_Q6_K) {
-      const uint64_t g0 = ((uint64_t)ex * a.H + row) * (a.I / 256);
-      Q6KProducer prod{D.quant + g0 * 208, D.d + g0, r, tid >> 7};
-      producer_loop<ATOMS, NT>(sm, nsteps, prod, &abort_flag, a.status);
-    } else {
-      const uint64_t g0 = ((uint64_t)ex * a.H + row) * (a.I / 32);
-      Q50Producer prod{D.quant + g0 * 16, D.qh + g0 * 4, D.d + g0, r, tid >> 7};
-      producer_loop<ATOMS, NT>(sm, nsteps, prod, &abort_flag, a.status);
+// Unit records of one CTA's units in order: the record of unit lu + 1 is loaded when
+// unit lu is first asked for, so its latency hides behind a unit of work.
+struct UnitWalk {
+  const int4 *items;
+  int first, stride, n_tiles, count;
+  int lu = -1;
+  Unit cur;
+  int4 next;
+  __device__ __forceinline__ int4 load(int l) const {
+    return l < count ? items[(first + l * stride) / n_tiles] : make_int4(0, 0, 0, 0);
+  }
+  __device__ __forceinline__ const Unit &at(int l) {
+    if (l != lu) {
+      const int4 rec = (lu >= 0 && l == lu + 1) ? next : load(l);
+      cur = make_unit(rec, first + l * stride, n_tiles);
+      lu = l;
+      next = load(l + 1);
     }
-  } else if (tid == kProducerThreads) {
-    control_loop<ATOMS, NT>(sm, tmem, &hmap, pos0, lo_offset, nsteps, &abort_flag, a.status, &issued);
+    return cur;
   }
-  const bool ok = finish<NT>(sm, nsteps, &abort_flag, &issued, a.status);
-  if (ok && tid < 128) {
-    float v[NT];
-    read_columns<NT>(tmem, v);
+};
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, int c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3, %4, %5}], [%6];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+template <int KIND, int NT, bool SPLIT>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
+    const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap wmap,
+    const __grid_constant__ CUtensorMap sh_wmap, ForwardArgs a, TcSide side, const float *b_inv,
+    float *gu) {
+  using C = Cfg<KIND, NT, SPLIT>;
+  using RT = RawTile<KIND>;
+  constexpr int NB = C::NB, NA = C::NA, NI = C::NI, RS = C::kRS;
+  extern __shared__ uint8_t dsm[];
+  __shared__ int abort_flag;
+  const int K = KIND == kUpQ4K ? a.H : a.I;
+  const int n_tiles = KIND == kUpQ4K ? a.I / 64 : a.H / 128;
+  const int n_units = *a.n_items * n_tiles;
+  if ((int)blockIdx.x >= n_units) return;
+  const int my_units = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int nsteps = (K + kStepK - 1) / kStepK;
+  const int total = my_units * nsteps;
+
+  const uint32_t raw = smem_u32(dsm);
+  const uint32_t b_base = (raw + 1023u) & ~1023u;
+  const uint32_t w_base = b_base + NA * C::kBStage;
+  const Bars bars{w_base + RS * RT::kStage};
+  uint8_t *generic = dsm + (bars.slot() - raw);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    abort_flag = *reinterpret_cast<const volatile int32_t *>(a.status) == kStatusTimeout;
+    for (int i = 0; i < 3; i++) {
+      mbar_init(bars.afull(i), kProducerWarps / 2);
+      mbar_init(bars.bfull(i), 1);
+      mbar_init(bars.empty(i), NI);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(bars.accfull(i), NI);
+      mbar_init(bars.accempty(i), kEpilogueWarps);
+    }
+    mbar_init(bars.drain(), NI);
+    for (int i = 0; i < kMaxRaw; i++) {
+      mbar_init(bars.rawfull(i), 1);
+      mbar_init(bars.rawempty(i), kProducerWarps / 2);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc(bars.slot(), 512);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(generic);
+  const uint32_t unit_stride = gridDim.x;
+
+  if (warp >= kEpilogueWarps && warp < kTmaWarp) {
+    // ---- producers ----
+    const int pw = warp - kEpilogueWarps;  // 0..15
+    const int g = pw >> 3, hf = (pw >> 2) & 1, q = warp & 3, r = 32 * q + lane;
+    for (int t = g; t < total; t += 2) {
+      const int rs = t % RS, ab = t % NA;
+      bool ok = wait_or_abort(bars.rawfull(rs), (uint32_t)((t / RS) & 1), &abort_flag);
+      ok = ok && (t < NA || wait_or_abort(bars.empty(ab), (uint32_t)((t / NA - 1) & 1), &abort_flag));
+      ok = ok && !aborted(&abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) atomicExch(&abort_flag, 1);
+        break;
+      }
+      fence_after();
+      const uint32_t st = w_base + (uint32_t)rs * RT::kStage;
+      const uint32_t tcol = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)ab * 128u + 64u * hf;
+      const int ks = t % nsteps;
+      if (KIND == kUpQ4K) {
+        deq_q4k(st + r * 144u, hf, tcol);
+      } else if (KIND == kDownQ6K) {
+        const float d = f16_bits_to_f32(lds2(st + RT::kQuant + 2u * r));
+        deq_q6k(st + r * 208u, hf, d, tcol);
+      } else {
+        const uint32_t sq = st + r * 144u + 64u * hf;
+        const uint32_t sh = st + RT::kQuant + r * 32u + 16u * hf;
+        const uint32_t sd = st + RT::kQuant + 128 * 32 + r * 16u + 8u * hf;
+        deq_q50(sq, sh, sd, min(4, (K - kStepK * ks) / 32 - 4 * hf), tcol);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars.rawempty(rs));  // this warp's reads of the stage are done
+      tmem_wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars.afull(ab));
+    }
+  } else if (warp == kTmaWarp || warp == kRawWarp) {
+    // ---- TMA: activation tiles (warp 20) and raw weight tiles (warp 21) ----
+    if (lane == 0) {
+      const bool is_b = warp == kTmaWarp;
+      const int depth = is_b ? NA : RS;
+      int t = 0;
+      bool stop = false;
+      UnitWalk walk{a.items, (int)blockIdx.x, (int)unit_stride, n_tiles, my_units};
+      for (int lu = 0; lu < my_units && !stop; lu++) {
+        const Unit un = walk.at(lu);
+        // another CTA's timeout stops this one too (checked once per unit)
+        if (*reinterpret_cast<const volatile int32_t *>(a.status) == kStatusTimeout)
+          atomicExch(&abort_flag, 1);
+        const bool shared = un.e == a.E;
+        for (int ks = 0; ks < nsteps; ks++, t++) {
+          const int i = t % depth;
+          const uint32_t free_bar = is_b ? bars.empty(i) : bars.rawempty(i);
+          if ((t >= depth && !wait_or_abort(free_bar, (uint32_t)((t / depth - 1) & 1), &abort_flag)) ||
+              aborted(&abort_flag)) {
+            atomicExch(&abort_flag, 1);
+            stop = true;
+            break;
+          }
+          if (is_b) {
+            // one box of 4 atoms x NB rows (atoms past K read as zeros, unused)
+            mbar_expect_tx(bars.bfull(i), (uint32_t)C::kBStage);
+            tma_load_3d(b_base + (uint32_t)i * C::kBStage, &bmap, 0, SPLIT ? 2 * un.pos0 : un.pos0,
+                        (kStepK / 64) * ks, bars.bfull(i));
+          } else {
+            const uint32_t dst = w_base + (uint32_t)i * RT::kStage, bar = bars.rawfull(i);
+            const CUtensorMap *map = shared ? &sh_wmap : &wmap;
+            const int ex = shared ? 0 : un.e;
+            mbar_expect_tx(bar, (uint32_t)RT::kBytes);
+            if (KIND == kUpQ4K) {
+              tma_load_4d(dst, map, 144 * ks, 0, un.tile * 64, ex, bar);
+            } else {
+              const int row0 = ex * a.H + un.tile * 128;
+              tma_load_2d(dst, map, (KIND == kDownQ6K ? 208 : 128) * ks, row0, bar);
+              const size_t side_row = ((size_t)ex * nsteps + ks) * a.H + un.tile * 128;
+              if (KIND == kDownQ6K) {
+                bulk_load(dst + RT::kQuant, (shared ? side.sh_d_t : side.d_t) + side_row * 2, 256, bar);
+              } else {
+                bulk_load(dst + RT::kQuant, (shared ? side.sh_qh_t : side.qh_t) + side_row * 32,
+                          128 * 32, bar);
+                bulk_load(dst + RT::kQuant + 128 * 32, (shared ? side.sh_d_t : side.d_t) + side_row * 16,
+                          128 * 16, bar);
+              }
+            }
+          }
+        }
+      }
+      // every armed stage has landed before the CTA may exit
+      for (int i = max(0, t - depth); i < t; i++)
+        mbar_wait(is_b ? bars.bfull(i % depth) : bars.rawfull(i % depth), (uint32_t)((i / depth) & 1));
+    }
+  } else if (warp >= kMmaWarp) {
+    // ---- MMA issue: issuer i takes the K slices s = i mod NI into its own accumulator ----
+    const int issuer = warp - kMmaWarp;
+    if (lane == 0 && issuer < NI) {
+      int t = 0;
+      bool stop = false;
+      for (int lu = 0; lu < my_units && !stop; lu++) {
+        const int acc = lu & 1;
+        if (lu >= 2 && !wait_or_abort(bars.accempty(acc), (uint32_t)(((lu >> 1) - 1) & 1), &abort_flag)) {
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        fence_after();
+        const uint32_t dcol = tmem + C::kAccCol + (uint32_t)((acc * NI + issuer) * NB);
+        for (int ks = 0; ks < nsteps; ks++, t++) {
+          const int ab = t % NA;
+          if (!wait_or_abort(bars.afull(ab), (uint32_t)((t / NA) & 1), &abort_flag) ||
+              !wait_or_abort(bars.bfull(ab), (uint32_t)((t / NA) & 1), &abort_flag)) {
+            atomicExch(&abort_flag, 1);
+            stop = true;
+            break;
+          }
+          fence_after();
+          const int slices = min(kStepK, K - kStepK * ks) / 16;
+          const uint32_t acol = tmem + (uint32_t)ab * 128u;
+          const uint32_t bst = b_base + (uint32_t)ab * C::kBStage;
+          if (issuer == 0)
+            issue_step<NB, NI, 0>(dcol, acol, bst, slices, ks == 0);
+          else
+            issue_step<NB, NI, NI - 1>(dcol, acol, bst, slices, ks == 0);
+          mma_commit(bars.empty(ab));
+        }
+        if (!stop) mma_commit(bars.accfull(acc));
+      }
+      mma_commit(bars.drain());
+      if (!mbar_wait(bars.drain(), 0)) atomicExch(&abort_flag, 1);
+    }
+  } else {
+    // ---- epilogue: warp q owns TMEM lanes 32q..32q+31 ----
+    const int q = warp, r = 32 * q + lane;
+    UnitWalk walk{a.items, (int)blockIdx.x, (int)unit_stride, n_tiles, my_units};
+    for (int lu = 0; lu < my_units; lu++) {
+      const int acc = lu & 1;
+      const Unit un = walk.at(lu);
+      // the unit's row scales, one token per lane (loaded before the wait)
+      const float inv_a = lane < un.ntok ? b_inv[un.pos0 + lane] : 0.0f;
+      const float inv_b = NT > 32 && lane + 32 < un.ntok ? b_inv[un.pos0 + 32 + lane] : 0.0f;
+      const bool ok = wait_or_abort(bars.accfull(acc), (uint32_t)((lu >> 1) & 1), &abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) atomicExch(&abort_flag, 1);
+        break;
+      }
+      fence_after();
+      // column n of each issuer's accumulator: token n (or, with the split, hi of token
+      // n/2 at even n and lo at odd n); the issuers' partial sums are added in order
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + C::kAccCol + (uint32_t)(acc * NI * NB);
+      constexpr int CW = NB < 32 / NI ? NB : 32 / NI;  // columns per chunk and issuer
+      constexpr int TPC = SPLIT ? CW / 2 : CW;         // tokens per chunk
+      // gate/up rows: A rows 2i and 2i+1 hold index 0 and 1 of the gate|up axis
+      const bool swapped = un.e == a.E ? side.sh_up_swapped : side.up_swapped;
+#pragma unroll 1
+      for (int c0 = 0; c0 < NB; c0 += CW) {
+        float w[NI][CW];
 #pragma unroll
-    for (int n = 0; n < NT; n++)
-      if (n < ntok) a.ysorted[(size_t)(pos0 + n) * a.H + row] = v[n] * h_inv[pos0 + n];
+        for (int i = 0; i < NI; i++)
+#pragma unroll
+          for (int c = 0; c < CW; c += 16)
+            tmem_ld16(taddr + i * NB + c0 + c, reinterpret_cast<uint32_t *>(&w[i][c]));
+        tmem_wait_ld();
+        if (c0 + CW >= NB) {  // the accumulators are free for the unit after next
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bars.accempty(acc));
+        }
+        float v[CW];
+#pragma unroll
+        for (int c = 0; c < CW; c++) {
+          v[c] = w[0][c];
+#pragma unroll
+          for (int i = 1; i < NI; i++) v[c] += w[i][c];
+        }
+        const int nbase = SPLIT ? c0 / 2 : c0;
+        // up: gate of i at gu column 2i, up at 2i + 1 (a warp writes 128 contiguous bytes)
+        float *out = KIND == kUpQ4K ? gu : a.ysorted;
+        const int ld = KIND == kUpQ4K ? 2 * a.I : a.H;
+        const int col = KIND == kUpQ4K ? un.tile * 128 + (r ^ (swapped ? 1 : 0)) : un.tile * 128 + r;
+#pragma unroll
+        for (int j = 0; j < TPC; j++) {
+          const float val = SPLIT ? v[2 * j] + v[2 * j + 1] : v[j];
+          const int n = nbase + j;
+          const float inv = __shfl_sync(0xffffffffu, n < 32 ? inv_a : inv_b, n & 31);
+          if (n < un.ntok) out[(size_t)(un.pos0 + n) * ld + col] = val * inv;
+        }
+      }
+    }
   }
-  teardown<NT>(tmem);
+
+  __syncthreads();
+  if (tid == 0 && abort_flag) atomicExch(a.status, kStatusTimeout);
+  if (warp == 0) {
+    fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Per-step transposes of the down side arrays: Q6_K d -> [expert][step][row] f16;
+// Q5_0 qh -> [expert][step][row][8 words], d -> [expert][step][row][8 f16] (zero past
+// the last block of a ragged step).
+__global__ void side_transpose_kernel(int kind, SplitTensor src, int experts, int H, int I,
+                                      uint8_t *qh_t, uint8_t *d_t) {
+  const int nsteps = (I + kStepK - 1) / kStepK;
+  const size_t n = (size_t)experts * nsteps * H;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const int row = (int)(idx % H);
+    const int ks = (int)((idx / H) % nsteps);
+    const size_t e = idx / ((size_t)H * nsteps);
+    const size_t grow = e * H + row;
+    if (kind == DM_Q6_K) {
+      reinterpret_cast<uint16_t *>(d_t)[idx] = src.d[grow * (I / 256) + ks];
+    } else {
+      const int nbr = I / 32;
+      for (int b = 0; b < 8; b++) {
+        const int blk = 8 * ks + b;
+        const bool in = blk < nbr;
+        reinterpret_cast<uint32_t *>(qh_t)[idx * 8 + b] =
+            in ? *reinterpret_cast<const uint32_t *>(src.qh + (grow * nbr + blk) * 4) : 0u;
+        reinterpret_cast<uint16_t *>(d_t)[idx * 8 + b] = in ? src.d[grow * nbr + blk] : (uint16_t)0;
+      }
+    }
+  }
 }
 
 }  // namespace tc
@@ -722,7 +890,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_down_kernel(
 bool tc_supported(int gate_type, int down_type, int H, int I) {
   if (gate_type != DM_Q4_K) return false;
   if (down_type != DM_Q6_K && down_type != DM_Q5_0) return false;
-  if (H % 256 || H % 128 || I % 64) return false;
+  if (H % 256 || I % 64) return false;  // Q4_K rows of whole super-blocks; 128-row down tiles
+  if (I > tc::kMaxPackI) return false;
   if (down_type == DM_Q6_K && I % 256) return false;
   return true;
 }
@@ -739,60 +908,159 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-static bool encode(CUtensorMap *map, void *base, int cols, int rows, int nt) {
+// View of a packed [rows][K] fp16 matrix as (64 elements, row, K/64 atoms): one box of
+// {64, nb, 4} lands as 4 swizzled atoms of nb rows each, the B tile of one K step.
+static bool encode(CUtensorMap *map, void *base, int K, int rows, int nb) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)nt};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(K / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)K * 2, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)nb, 4};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// x16 / h16 hold 2*rows rows: the hi halves in [0, rows), the lo halves in [rows, 2*rows).
-int make_tc_maps(TcPlan &p, int H, int I, int nt) {
-  if (!encode(&p.x_map, p.x16, H, 2 * p.rows, nt)) return -1;
-  if (!encode(&p.h_map, p.h16, I, 2 * p.rows, nt)) return -1;
+template <int KIND>
+static bool fits_split(int nt) {
+  switch (nt) {
+    case 16: return tc::Cfg<KIND, 16, true>::kFits;
+    case 32: return tc::Cfg<KIND, 32, true>::kFits;
+    default: return tc::Cfg<KIND, 64, true>::kFits;
+  }
+}
+
+// x16 / h16 hold 2*rows rows (hi and lo interleaved with the split, hi alone without).
+// The split of a matrix is dropped where its kernel's tiles would not fit shared memory.
+int make_tc_maps(TcPlan &p, int H, int I, int down_type, int nt) {
+  p.split_x = p.split && fits_split<tc::kUpQ4K>(nt);
+  p.split_h = p.split && (down_type == DM_Q6_K ? fits_split<tc::kDownQ6K>(nt)
+                                               : fits_split<tc::kDownQ50>(nt));
+  if (!encode(&p.x_map, p.x16, H, p.split_x ? 2 * p.rows : p.rows, p.split_x ? 2 * nt : nt))
+    return -1;
+  if (!encode(&p.h_map, p.h16, I, p.split_h ? 2 * p.rows : p.rows, p.split_h ? 2 * nt : nt))
+    return -1;
   return 0;
 }
 
+template <int KIND, int NT>
+static bool launch_kind(const CUtensorMap &map, const ForwardArgs &a, const TcWeights &w,
+                        const float *inv, const TcPlan &p, bool split, cudaStream_t s) {
+  const int n_tiles = KIND == tc::kUpQ4K ? a.I / 64 : a.H / 128;
+  const int grid = std::max(1, std::min(p.n_sm, p.max_items * n_tiles));
+  const CUtensorMap &wm = KIND == tc::kUpQ4K ? w.up : w.down;
+  const CUtensorMap &sm = KIND == tc::kUpQ4K ? w.sh_up : w.sh_down;
+  if (split) {
+    if constexpr (tc::Cfg<KIND, NT, true>::kFits) {
+      auto fn = tc::tc_expert_kernel<KIND, NT, true>;
+      ensure_smem_limit((const void *)fn);
+      fn<<<grid, tc::kTcThreads, tc::Cfg<KIND, NT, true>::kSmem, s>>>(map, wm, sm, a, w.side, inv,
+                                                                       p.gu);
+    }
+  } else {
+    static_assert(tc::Cfg<KIND, NT, false>::kFits, "tile configuration exceeds shared memory");
+    auto fn = tc::tc_expert_kernel<KIND, NT, false>;
+    ensure_smem_limit((const void *)fn);
+    fn<<<grid, tc::kTcThreads, tc::Cfg<KIND, NT, false>::kSmem, s>>>(map, wm, sm, a, w.side, inv,
+                                                                      p.gu);
+  }
+  return true;
+}
+
 template <int NT>
-static int launch_nt(const ForwardArgs &a, const TcPlan &p, const GemvPlan &g, cudaStream_t s,
+static int launch_nt(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, cudaStream_t s,
                      cudaEvent_t down_mark) {
   const int rows_bound = a.T * a.k + (a.shared ? a.T : 0);
-  tc::pack_kernel<true><<<rows_bound, 256, 0, s>>>(a, p.x16, p.x_inv, a.H, p.rows);
-  {
-    auto fn = tc::tc_up_q4k_kernel<NT>;
-    ensure_smem_limit((const void *)fn);
-    fn<<<dim3(a.I / 64, p.max_items), tc::kTcThreads, tc::Layout<2, NT>::kSmem, s>>>(
-        p.x_map, a, p.x_inv, p.rows);
-  }
+  tc::pack_kernel<true><<<rows_bound, 256, 0, s>>>(a, nullptr, p.x16, p.x_inv, a.H, p.split_x ? 1 : 0);
+  launch_kind<tc::kUpQ4K, NT>(p.x_map, a, w, p.x_inv, p, p.split_x, s);
   if (down_mark) cudaEventRecord(down_mark, s);
-  tc::pack_kernel<false><<<rows_bound, 256, 0, s>>>(a, p.h16, p.h_inv, a.I, p.rows);
-  if (a.down_type == DM_Q6_K) {
-    auto fn = tc::tc_down_kernel<DM_Q6_K, NT>;
-    ensure_smem_limit((const void *)fn);
-    fn<<<dim3(a.H / 128, p.max_items), tc::kTcThreads, tc::Layout<2, NT>::kSmem, s>>>(
-        p.h_map, a, g.down, g.sh_down, p.h_inv, p.rows);
-  } else {
-    auto fn = tc::tc_down_kernel<DM_Q5_0, NT>;
-    ensure_smem_limit((const void *)fn);
-    fn<<<dim3(a.H / 128, p.max_items), tc::kTcThreads, tc::Layout<1, NT>::kSmem, s>>>(
-        p.h_map, a, g.down, g.sh_down, p.h_inv, p.rows);
-  }
+  tc::pack_kernel<false><<<rows_bound, 256, 0, s>>>(a, p.gu, p.h16, p.h_inv, a.I, p.split_h ? 1 : 0);
+  if (a.down_type == DM_Q6_K)
+    launch_kind<tc::kDownQ6K, NT>(p.h_map, a, w, p.h_inv, p, p.split_h, s);
+  else
+    launch_kind<tc::kDownQ50, NT>(p.h_map, a, w, p.h_inv, p, p.split_h, s);
   return 4;
 }
 
-int launch_tc_experts(const ForwardArgs &a, const TcPlan &p, const GemvPlan &g, cudaStream_t s,
+int launch_tc_experts(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, cudaStream_t s,
                       cudaEvent_t down_mark) {
   switch (p.nt) {
-    case 16: return launch_nt<16>(a, p, g, s, down_mark);
-    case 32: return launch_nt<32>(a, p, g, s, down_mark);
-    case 64: return launch_nt<64>(a, p, g, s, down_mark);
+    case 16: return launch_nt<16>(a, p, w, s, down_mark);
+    case 32: return launch_nt<32>(a, p, w, s, down_mark);
+    case 64: return launch_nt<64>(a, p, w, s, down_mark);
     default: return -1;
   }
+}
+
+void tc_side_bytes(int down_type, uint64_t experts, int H, int I, uint64_t *qh_bytes,
+                   uint64_t *d_bytes) {
+  const uint64_t rows = experts * (uint64_t)((I + tc::kStepK - 1) / tc::kStepK) * H;
+  *qh_bytes = down_type == DM_Q5_0 ? rows * 32 : 0;
+  *d_bytes = down_type == DM_Q5_0 ? rows * 16 : rows * 2;
+}
+
+// gate/up rows as {row bytes, gate|up, row, expert}: the lower of the two base addresses
+// is the origin and the other sits one "gate|up" stride away.
+static bool encode_up(CUtensorMap *map, const uint8_t *gate, const uint8_t *up, uint64_t row_bytes,
+                      int I, int experts, uint64_t expert_stride, int *swapped) {
+  auto fn = encode_fn();
+  if (!fn || !gate || !up) return false;
+  const uint8_t *origin = gate < up ? gate : up;
+  *swapped = gate < up ? 0 : 1;
+  cuuint64_t dims[4] = {row_bytes, 2, (cuuint64_t)I, (cuuint64_t)experts};
+  cuuint64_t strides[3] = {(cuuint64_t)(gate < up ? up - gate : gate - up), row_bytes,
+                           expert_stride};
+  cuuint32_t box[4] = {144, 2, 64, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void *)origin, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// down quant bytes as {row bytes, row}, box {box_x, 128}
+static bool encode_rows(CUtensorMap *map, const uint8_t *base, uint64_t row_bytes, uint64_t rows,
+                        uint32_t box_x) {
+  auto fn = encode_fn();
+  if (!fn || !base) return false;
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_x, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)base, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int make_tc_weights(TcWeights &w, const uint8_t *gate, const uint8_t *up, uint64_t expert_stride,
+                    const uint8_t *sh_gate, const uint8_t *sh_up, const SplitTensor &down,
+                    const SplitTensor &sh_down, int down_type, int experts, int H, int I,
+                    uint8_t *qh_t, uint8_t *d_t, uint8_t *sh_qh_t, uint8_t *sh_d_t,
+                    cudaStream_t stream) {
+  const uint64_t up_row = (uint64_t)(H / 256) * 144;
+  if (!encode_up(&w.up, gate, up, up_row, I, experts, expert_stride, &w.side.up_swapped)) return -1;
+  const bool shared = sh_gate != nullptr;
+  if (shared && !encode_up(&w.sh_up, sh_gate, sh_up, up_row, I, 1, up_row * I, &w.side.sh_up_swapped))
+    return -1;
+  const bool q6 = down_type == DM_Q6_K;
+  const uint64_t down_row = q6 ? (uint64_t)(I / 256) * 208 : (uint64_t)(I / 32) * 16;
+  const uint32_t box_x = q6 ? 208 : 144;
+  if (!encode_rows(&w.down, down.quant, down_row, (uint64_t)experts * H, box_x)) return -1;
+  if (shared && !encode_rows(&w.sh_down, sh_down.quant, down_row, (uint64_t)H, box_x)) return -1;
+  if (!shared) {  // the kernels take both maps; the shared ones are never used
+    w.sh_up = w.up;
+    w.sh_down = w.down;
+  }
+  const int threads = 256;
+  tc::side_transpose_kernel<<<1024, threads, 0, stream>>>(down_type, down, experts, H, I, qh_t, d_t);
+  if (shared)
+    tc::side_transpose_kernel<<<256, threads, 0, stream>>>(down_type, sh_down, 1, H, I, sh_qh_t,
+                                                          sh_d_t);
+  w.side.qh_t = qh_t;
+  w.side.d_t = d_t;
+  w.side.sh_qh_t = sh_qh_t;
+  w.side.sh_d_t = sh_d_t;
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace dm
