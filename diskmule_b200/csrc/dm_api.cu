@@ -433,6 +433,7 @@ struct dm_moe_layer {
   int E1 = 0;
   bool shared = false;
   void *router_t = nullptr;  // transposed router [H][E1]
+  float *router_dup = nullptr;  // [H][router_dup_ld(E1)] f32 router for many tokens
   uint64_t gate_stride = 0, up_stride = 0, down_stride = 0;
   const uint8_t *up_base = nullptr;
   // scratch
@@ -638,6 +639,8 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   bytes += al((E + 1) * 4) + al((E + 2) * 4) + 2 * al(pairs * 4) + al((E + 1) * 4) + 2 * al(4);
   bytes += al((pairs + E + 1) * 8) + al(4);
   bytes += al(pairs * I * 4) + al(pairs * H * 4);
+  const uint64_t xld = (T + 31) / 32 * 32;  // transposed router input for many tokens
+  bytes += al(H * xld * 8);
   if (L->tc_ok)
     bytes += al(2 * pairs * H * 2) + al(2 * pairs * I * 2) + 2 * al(pairs * 4) + al(2 * pairs * I * 4);
   L->drop_graphs();
@@ -655,6 +658,7 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   a.router_in = d.family == DM_FAMILY_GEMMA4 ? arena.take<float>(T * H) : nullptr;
   a.expert_in = d.family == DM_FAMILY_GEMMA4 ? arena.take<float>(T * H) : nullptr;
   a.logits = arena.take<float>(T * L->E1);
+  a.xT = arena.take<float>(H * xld * 2);
   a.sel_idx = arena.take<uint32_t>(T * k);
   a.sel_w = arena.take<float>(T * k);
   a.counts = arena.take<int32_t>(E + 1);
@@ -732,6 +736,12 @@ int32_t dm_moe_layer_create(dm_cuda_context *ctx, const dm_moe_desc *desc, dm_mo
   dm::launch_transpose_router(d.router, d.router_type == DM_BF16, d.experts, d.hidden,
                               qwen_gate ? d.shared_gate_vector : nullptr, L->router_t,
                               ctx->stream);
+  if (cudaMalloc(&L->router_dup, (size_t)H * dm::router_dup_ld(L->E1) * sizeof(float)) ==
+      cudaSuccess)
+    dm::launch_dup_router(L->router_t, d.router_type == DM_BF16, (int)H, L->E1, L->router_dup,
+                          ctx->stream);
+  else
+    L->router_dup = nullptr;  // the many-token router then runs the chain-per-thread kernel
   rc = build_plan(L);
   if (cudaStreamCreateWithFlags(&L->capture, cudaStreamNonBlocking) != cudaSuccess) L->capture = nullptr;
   {
@@ -761,6 +771,7 @@ void dm_moe_layer_destroy(dm_moe_layer *L) {
   cudaSetDevice(L->ctx->device);
   cudaStreamSynchronize(L->ctx->stream);
   if (L->router_t) cudaFree(L->router_t);
+  if (L->router_dup) cudaFree(L->router_dup);
   if (L->scratch) cudaFree(L->scratch);
   if (L->io) cudaFree(L->io);
   for (auto &e : L->events)
@@ -831,6 +842,7 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
   a.y = y;
   a.router_bf16 = d.router_type == DM_BF16;
   a.router_t = L->router_t;
+  a.router_dup = L->router_dup;
   a.bias = d.correction_bias;
   a.router_scale = d.router_scale;
   a.routed_pre_norm = d.routed_pre_norm;

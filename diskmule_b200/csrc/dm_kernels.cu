@@ -130,6 +130,7 @@ __global__ void __launch_bounds__(256) gemma_prep_kernel(ForwardArgs a) {
   if (threadIdx.x < nt) {
     const float *row = xs + threadIdx.x * HP;
     float s = 0.0f;
+#pragma unroll 16
     for (int i = 0; i < H; i++) s = __fmaf_rn(row[i], row[i], s);
     float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)H), a.epsilon)));
     if (!isfinite(inv)) atomicExch(a.status, kStatusNonFiniteNorm);
@@ -213,58 +214,144 @@ __global__ void __launch_bounds__(256) router_small_kernel(const void *wt, int l
   }
 }
 
-// Many tokens: thread = token, 16 experts per thread (16 independent chains),
-// column chunks of 32 staged through shared memory.
-constexpr int kTiledTokens = 64, kTiledExperts = 16, kTiledChunk = 32;
+// Many tokens: register-tiled SIMT matmul. A CTA computes a 32-token x 64-expert tile;
+// thread (tx, ty) holds tokens 4ty.. x experts 4tx.. = 16 chains, each still one
+// sequential chain over h in the reference's order (so logits stay bit-exact), computed
+// two experts at a time with packed f32x2 instructions (one rounding per element, as
+// scalar code). Operands come from x transposed and duplicated per forward, [h][t][2]
+// (a 16-byte load yields two (x, x) pairs; a warp reads only two distinct x chunks), and
+// the router padded to f32 [h][64k] at set-up, through a 4-stage cp.async pipeline of
+// 32-wide h chunks.
+constexpr int kRgTokens = 32, kRgExperts = 64, kRgChunk = 32, kRgThreads = 128, kRgStages = 4;
+constexpr int kRgXBytes = kRgChunk * kRgTokens * 8;
+constexpr int kRgStageBytes = kRgXBytes + kRgChunk * kRgExperts * 4;
 
-template <bool GLM, bool WBF16, bool XBF16>
-__global__ void __launch_bounds__(kTiledTokens) router_tiled_kernel(const void *wt, int ld,
-                                                                  const void *x, int T, int H,
-                                                                  int E1,
-                                                                  const float *lbias, int E,
-                                                                  float *logits) {
-  __shared__ float xs[kTiledChunk][kTiledTokens + 1];
-  __shared__ __align__(16) float ws[kTiledChunk][kTiledExperts];
-  const int e0 = blockIdx.x * kTiledExperts, t0 = blockIdx.y * kTiledTokens;
-  const int tid = threadIdx.x;
-  float acc[kTiledExperts];
+template <bool GLM>
+__device__ __forceinline__ uint64_t rg_step(uint64_t w, uint64_t x, uint64_t s) {
+  uint64_t r;
+  if (GLM) {
+    uint64_t p;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(w), "l"(x));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(s), "l"(p));
+  } else {
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(w), "l"(x), "l"(s));
+  }
+  return r;
+}
+
+__device__ __forceinline__ void rg_cp16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ ulonglong2 rg_lds(uint32_t addr) {
+  ulonglong2 v;
+  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "r"(addr));
+  return v;
+}
+
+template <bool GLM>
+__global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w32, int wld,
+                                                                 const float *xT2, int xld, int T,
+                                                                 int H, int E1, const float *lbias,
+                                                                 int E, float *logits) {
+  extern __shared__ __align__(16) uint8_t rg_smem[];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int e0 = blockIdx.x * kRgExperts, t0 = blockIdx.y * kRgTokens;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(rg_smem);
+  const int nchunks = H / kRgChunk;
+  auto issue = [&](int c) {
+    if (c < nchunks) {
+      const uint32_t st = sbase + (uint32_t)(c % kRgStages) * kRgStageBytes;
+      const int h0 = c * kRgChunk;
 #pragma unroll
-  for (int j = 0; j < kTiledExperts; j++) acc[j] = GLM ? -0.0f : 0.0f;
-  for (int h0 = 0; h0 < H; h0 += kTiledChunk) {
-    int hc = min(kTiledChunk, H - h0);
-    __syncthreads();
-    for (int idx = tid; idx < kTiledTokens * kTiledChunk; idx += kTiledTokens) {
-      int tl = idx / kTiledChunk, hh = idx % kTiledChunk;
-      float v = 0.0f;
-      if (t0 + tl < T && hh < hc) v = load_as_f32(x, (size_t)(t0 + tl) * H + h0 + hh, XBF16);
-      xs[hh][tl] = v;
-    }
-    for (int idx = tid; idx < kTiledChunk * kTiledExperts; idx += kTiledTokens) {
-      int hh = idx / kTiledExperts, el = idx % kTiledExperts;
-      float v = 0.0f;
-      if (hh < hc && e0 + el < E1) v = load_as_f32(wt, (size_t)(h0 + hh) * ld + e0 + el, WBF16);
-      ws[hh][el] = v;
-    }
-    __syncthreads();
-    for (int hh = 0; hh < hc; hh++) {
-      float xv = xs[hh][tid];
+      for (int i = 0; i < 4; i++) {  // x: 32 rows x 16 pieces (32 tokens x 8 bytes)
+        const int f = tid + kRgThreads * i, row = f >> 4, piece = f & 15;
+        rg_cp16(st + row * 256 + piece * 16, xT2 + ((size_t)(h0 + row) * xld + t0) * 2 + 4 * piece);
+      }
 #pragma unroll
-      for (int j = 0; j < kTiledExperts; j += 4) {
-        float4 w4 = *reinterpret_cast<const float4 *>(&ws[hh][j]);
-        acc[j] = chain_step<GLM>(w4.x, xv, acc[j]);
-        acc[j + 1] = chain_step<GLM>(w4.y, xv, acc[j + 1]);
-        acc[j + 2] = chain_step<GLM>(w4.z, xv, acc[j + 2]);
-        acc[j + 3] = chain_step<GLM>(w4.w, xv, acc[j + 3]);
+      for (int i = 0; i < 4; i++) {  // w: 32 rows x 16 pieces (64 experts x 4 bytes)
+        const int f = tid + kRgThreads * i, row = f >> 4, piece = f & 15;
+        rg_cp16(st + kRgXBytes + row * 256 + piece * 16, w32 + (size_t)(h0 + row) * wld + e0 + 4 * piece);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  uint64_t acc[4][2];  // token 4ty + i, experts (4tx + 2jp, 4tx + 2jp + 1)
+  const float z = GLM ? -0.0f : 0.0f;
+  const uint64_t z2 = ((uint64_t)__float_as_uint(z) << 32) | __float_as_uint(z);
+#pragma unroll
+  for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = z2;
+#pragma unroll
+  for (int c = 0; c < kRgStages - 1; c++) issue(c);
+  for (int c = 0; c < nchunks; c++) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kRgStages - 2) : "memory");
+    __syncthreads();  // chunk c is in; every thread is done with chunk c - 1
+    issue(c + kRgStages - 1);
+    const uint32_t st = sbase + (uint32_t)(c % kRgStages) * kRgStageBytes;
+#pragma unroll
+    for (int kk = 0; kk < kRgChunk; kk++) {
+      const ulonglong2 xa = rg_lds(st + kk * 256 + ty * 32);
+      const ulonglong2 xb = rg_lds(st + kk * 256 + ty * 32 + 16);
+      const ulonglong2 w = rg_lds(st + kRgXBytes + kk * 256 + tx * 16);
+      const uint64_t xp[4] = {xa.x, xa.y, xb.x, xb.y};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        acc[i][0] = rg_step<GLM>(w.x, xp[i], acc[i][0]);
+        acc[i][1] = rg_step<GLM>(w.y, xp[i], acc[i][1]);
       }
     }
   }
-  if (t0 + tid < T) {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 #pragma unroll
-    for (int j = 0; j < kTiledExperts; j++)
-      if (e0 + j < E1)
-        logits[(size_t)(t0 + tid) * E1 + e0 + j] =
-            (lbias && e0 + j < E) ? __fadd_rn(acc[j], lbias[e0 + j]) : acc[j];
+  for (int i = 0; i < 4; i++) {
+    const int t = t0 + 4 * ty + i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int e = e0 + 4 * tx + j;
+      const float v = __uint_as_float((uint32_t)(acc[i][j >> 1] >> (32 * (j & 1))));
+      if (e < E1) logits[(size_t)t * E1 + e] = (lbias && e < E) ? __fadd_rn(v, lbias[e]) : v;
+    }
   }
+}
+
+// x [T][H] (f32 or bf16) -> xT2 [H][xld][2] f32, each value twice; tokens T..xld-1 zero.
+__global__ void __launch_bounds__(256) transpose_x_kernel(const void *x, int bf16, int T, int H,
+                                                         int xld, float *xT2) {
+  __shared__ float tile[32][33];
+  const int h0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
+  const int c = threadIdx.x & 31, r0 = threadIdx.x >> 5;
+  for (int r = r0; r < 32; r += 8) {
+    const int t = t0 + r, h = h0 + c;
+    float v = 0.0f;
+    if (t < T && h < H) v = load_as_f32(x, (size_t)t * H + h, bf16 != 0);
+    tile[r][c] = v;
+  }
+  __syncthreads();
+  for (int r = r0; r < 32; r += 8) {
+    const int h = h0 + r, t = t0 + c;
+    const float v = tile[c][r];
+    if (h < H && t < xld) reinterpret_cast<float2 *>(xT2)[(size_t)h * xld + t] = make_float2(v, v);
+  }
+}
+
+// router [H][ld] (f32 or bf16) -> [H][dld] f32 (zero past ld)
+__global__ void pad_router_kernel(const void *src, int bf16, int H, int ld, int dld, float *dst) {
+  const size_t n = (size_t)H * dld;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const int h = (int)(idx / dld), e = (int)(idx % dld);
+    dst[idx] = e < ld ? load_as_f32(src, (size_t)h * ld + e, bf16 != 0) : 0.0f;
+  }
+}
+
+int launch_dup_router(const void *router_t, int bf16, int H, int E1, float *dst,
+                      cudaStream_t stream) {
+  const int dld = router_dup_ld(E1);
+  const size_t n = (size_t)H * dld;
+  pad_router_kernel<<<(int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, stream>>>(
+      router_t, bf16, H, router_ld(E1), dld, dst);
+  return 1;
 }
 
 // ---------------------------------------------------------------------------
@@ -830,7 +917,7 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   }
   // 2. router logits
   mark(kStageRouter);
-  if (a.T <= 16) {
+  if (a.T <= 16 || !a.xT || !a.router_dup || a.H % kRgChunk) {
     int RT = 4;
     size_t wbytes = (size_t)a.H * kSmallExperts * (a.router_bf16 ? 2 : 4);
     while (RT > 1 && wbytes + (size_t)RT * (a.H + 4) * 4 > 200 * 1024) RT >>= 1;
@@ -849,14 +936,21 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
     else DM_ROUTER_SMALL(false, false, false)
 #undef DM_ROUTER_SMALL
   } else {
-    dim3 grid((a.E1 + kTiledExperts - 1) / kTiledExperts, (a.T + kTiledTokens - 1) / kTiledTokens);
-#define DM_ROUTER_TILED(G, W, X) \
-  router_tiled_kernel<G, W, X><<<grid, kTiledTokens, 0, stream>>>(a.router_t, router_ld(a.E1), router_x, a.T, a.H, a.E1, a.logit_bias, a.E, a.logits);
-    if (glm && a.router_bf16 && router_x_bf16) DM_ROUTER_TILED(true, true, true)
-    else if (glm && a.router_bf16) DM_ROUTER_TILED(true, true, false)
-    else if (glm && router_x_bf16) DM_ROUTER_TILED(true, false, true)
-    else if (glm) DM_ROUTER_TILED(true, false, false)
-    else DM_ROUTER_TILED(false, false, false)
+    const int xld = (a.T + kRgTokens - 1) / kRgTokens * kRgTokens;
+    transpose_x_kernel<<<dim3((a.H + 31) / 32, xld / 32), 256, 0, stream>>>(
+        router_x, router_x_bf16 ? 1 : 0, a.T, a.H, xld, a.xT);
+    launches++;
+    dim3 grid((a.E1 + kRgExperts - 1) / kRgExperts, xld / kRgTokens);
+    const size_t smem = (size_t)kRgStages * kRgStageBytes;
+#define DM_ROUTER_TILED(G)                                                                   \
+  {                                                                                          \
+    auto fn = router_gemm_kernel<G>;                                                         \
+    set_smem(fn, smem);                                                                      \
+    fn<<<grid, kRgThreads, smem, stream>>>(a.router_dup, router_dup_ld(a.E1), a.xT, xld, a.T, \
+                                           a.H, a.E1, a.logit_bias, a.E, a.logits);          \
+  }
+    if (glm) DM_ROUTER_TILED(true)
+    else DM_ROUTER_TILED(false)
 #undef DM_ROUTER_TILED
   }
   launches++;

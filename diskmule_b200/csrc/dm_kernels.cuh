@@ -25,6 +25,8 @@ struct ForwardArgs {
   const float *bias;       // GLM correction bias [E]
   const float *router_scale, *routed_pre_norm, *expert_scale;
   const float *logit_bias; // optional [E], softmax families
+  const float *router_dup; // [H][router_dup_ld] f32 router copy (many tokens), or null
+  float *xT;               // [H][T rounded up to 32][2] transposed, duplicated router input
   // experts
   int gate_type, up_type, down_type;
   const uint8_t *gate, *up, *down;
@@ -54,6 +56,9 @@ struct ForwardArgs {
 // Row stride (elements) of the transposed router [H][ld]: E1 rounded up to 8 so
 // every 8-expert tile row is one aligned vector.
 __host__ __device__ inline int router_ld(int E1) { return (E1 + 7) & ~7; }
+// Row stride of the f32 router copy [H][ld] used for many tokens: E1 rounded up to the
+// 64-expert tile.
+__host__ __device__ inline int router_dup_ld(int E1) { return (E1 + 63) & ~63; }
 
 enum DeviceStatus : int32_t {
   kStatusOk = 0,
@@ -87,6 +92,9 @@ int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float 
                         int32_t *status, cudaStream_t stream);
 int launch_elementwise(int op, const float *a, const float *b, float *out, int n,
                        float eps, cudaStream_t stream);
+// [H][ld] router -> [H][router_dup_ld] f32 (layer set-up)
+int launch_dup_router(const void *router_t, int bf16, int H, int E1, float *dst,
+                      cudaStream_t stream);
 int launch_transpose_router(const void *src, int src_bf16, int E, int H, const float *extra_col,
                             void *dst, cudaStream_t stream);
 
