@@ -574,6 +574,16 @@ int32_t make_split(dm_moe_layer *L, int kind, const void *src, uint64_t blocks,
 // transposed down side arrays. A refused map leaves the layer on the GEMV path.
 int32_t build_tc_weights(dm_moe_layer *L) {
   const dm_moe_desc &d = L->desc;
+  if (d.down_type == DM_BF16) {
+    if (dm::make_tc_weights_bf16(L->tcw, (const uint8_t *)d.gate, L->up_base, L->gate_stride,
+                                 (const uint8_t *)d.shared_gate, (const uint8_t *)d.shared_up,
+                                 (const uint8_t *)d.down, (const uint8_t *)d.shared_down, d.experts,
+                                 d.hidden, d.intermediate) != 0) {
+      fprintf(stderr, "diskmule_cuda: tensor-core path off for this layer (weight maps refused)\n");
+      L->tc_ok = false;
+    }
+    return DM_OK;
+  }
   uint64_t qh_bytes = 0, d_bytes = 0, sh_qh_bytes = 0, sh_d_bytes = 0;
   dm::tc_side_bytes(d.down_type, d.experts, d.hidden, d.intermediate, &qh_bytes, &d_bytes);
   if (L->shared)
@@ -637,7 +647,7 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   if (d.family == DM_FAMILY_GEMMA4) bytes += 2 * al(T * H * 4);
   bytes += al(T * L->E1 * 4) + 2 * al(T * k * 4);
   bytes += al((E + 1) * 4) + al((E + 2) * 4) + 2 * al(pairs * 4) + al((E + 1) * 4) + 2 * al(4);
-  bytes += al((pairs + E + 1) * 8) + al(4);
+  bytes += al((pairs + E + 1) * sizeof(int4)) + al(4);
   bytes += al(pairs * I * 4) + al(pairs * H * 4);
   const uint64_t xld = (T + 31) / 32 * 32;  // transposed router input for many tokens
   bytes += al(H * xld * 8);
@@ -678,7 +688,9 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
     float *x_inv = arena.take<float>(pairs);
     float *h_inv = arena.take<float>(pairs);
     float *gu = arena.take<float>(2 * pairs * I);
-    const int nts[3] = {16, 32, 64};
+    // token tiles: 16/32/64 for quantised weights; bf16 (GLM) always 128
+    const bool bf16 = d.down_type == DM_BF16;
+    const int nts[3] = {bf16 ? 128 : 16, bf16 ? 128 : 32, bf16 ? 128 : 64};
     int n_sm = 148;
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, L->ctx->device);
     const char *split_env = getenv("DISKMULE_CUDA_TC_SPLIT");
@@ -697,6 +709,7 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
       if (dm::make_tc_maps(p, (int)H, (int)I, d.down_type, p.nt) != 0) L->tc_ok = false;
     }
   }
+  if (arena.overflow) return fail(DM_ERR_ALLOCATION, "layer scratch carve exceeded its allocation");
   L->capacity = tokens;
   return DM_OK;
 }
@@ -751,7 +764,7 @@ int32_t dm_moe_layer_create(dm_cuda_context *ctx, const dm_moe_desc *desc, dm_mo
     // the tensor-core kernels copy weight blocks in 16-byte pieces
     const uintptr_t align = (uintptr_t)d.gate | (uintptr_t)L->up_base |
                             (uintptr_t)d.shared_gate | (uintptr_t)d.shared_up;
-    L->tc_ok = rc == DM_OK && d.family != DM_FAMILY_GLM52 && align % 16 == 0 &&
+    L->tc_ok = rc == DM_OK && align % 16 == 0 &&
                dm::tc_supported(d.gate_type, d.down_type, d.hidden, d.intermediate) &&
                !(tc_env && (!strcmp(tc_env, "0") || !strcmp(tc_env, "false")));
     if (L->tc_ok) rc = build_tc_weights(L);
@@ -889,7 +902,7 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
   const dm::TcPlan *tp = nullptr;
   if (gp && L->tc_ok) {
     const double avg = (double)tokens * d.top_k / d.experts;
-    if (avg >= 4.0) {
+    if (avg >= (d.down_type == DM_BF16 ? 16.0 : 4.0)) {
       tcp = L->tc[avg <= 12.0 ? 0 : (avg <= 24.0 ? 1 : 2)];
       tcp.weights = &L->tcw;
       const int pairs = a.T * a.k + (a.shared ? a.T : 0);
@@ -1067,7 +1080,7 @@ extern "C" int32_t dm_moe_forward_noalloc(dm_moe_layer *L, const void *x, float 
   if (d.family == DM_FAMILY_GEMMA4) need += 2 * al(T * H * 4);
   need += al(T * L->E1 * 4) + 2 * al(T * k * 4);
   need += al((E + 1) * 4) + al((E + 2) * 4) + 2 * al(pairs * 4) + al((E + 1) * 4) + 2 * al(4);
-  need += al((pairs + E + 1) * 8) + al(4);
+  need += al((pairs + E + 1) * sizeof(int4)) + al(4);
   need += al(pairs * I * 4) + al(pairs * H * 4);
   if (need > kNoAllocScratchBytes)
     return fail(DM_ERR_OVERFLOW,
@@ -1096,6 +1109,7 @@ extern "C" int32_t dm_moe_forward_noalloc(dm_moe_layer *L, const void *x, float 
   a.n_items = arena.take<int32_t>(1);
   a.h = arena.take<float>(pairs * I);
   a.ysorted = arena.take<float>(pairs * H);
+  if (arena.overflow) return fail(DM_ERR_ALLOCATION, "scratch carve exceeded the static array");
   a.family = d.family;
   a.T = tokens;
   a.H = d.hidden;

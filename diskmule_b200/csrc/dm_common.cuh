@@ -260,12 +260,19 @@ struct F32Unit {
 cudaError_t ensure_smem_limit(const void *kernel);
 
 // Scratch carved from one device allocation, 256-byte aligned pieces.
+// Carves 256-byte-aligned pieces from one allocation; a request past the capacity
+// returns null and sets `overflow` (the caller checks it once after carving).
 struct Arena {
   uint8_t *base = nullptr;
   size_t used = 0, capacity = 0;
+  bool overflow = false;
   template <class T>
   T *take(size_t count) {
     size_t bytes = (count * sizeof(T) + 255) & ~size_t(255);
+    if (used + bytes > capacity) {
+      overflow = true;
+      return nullptr;
+    }
     T *p = reinterpret_cast<T *>(base + used);
     used += bytes;
     return p;

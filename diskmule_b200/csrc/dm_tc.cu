@@ -881,6 +881,233 @@ __global__ void side_transpose_kernel(int kind, SplitTensor src, int experts, in
   }
 }
 
+// ---------------------------------------------------------------------------
+// bf16 grouped GEMM (GLM): the weights need no dequantisation, so A (128 weight rows x
+// 64 K, 128-byte swizzle) and B (the tile's tokens) both come by TMA into shared memory
+// and one thread issues tcgen05.mma (kind::f16 with bf16 operands, f32 accumulate).
+// Products of bf16 values are exact in f32, so only the summation order differs from
+// the reference's sequential w*x sum.
+//   warps 0..3 epilogue, warp 4 TMA, warp 5 MMA issue.
+// ---------------------------------------------------------------------------
+
+constexpr int kBfThreads = 6 * 32;
+constexpr int kBfStepK = 64;
+
+template <int NB>
+struct BfCfg {
+  static constexpr int kA = 128 * 128;        // 128 rows x 64 bf16
+  static constexpr int kB = NB * 128;         // NB rows x 64 bf16
+  static constexpr int kStage = kA + kB;
+  static constexpr int kStages = (kSmemLimit - 1024 - 256) / kStage < 6 ? (kSmemLimit - 1024 - 256) / kStage : 6;
+  static constexpr int kSmem = 1024 + kStages * kStage + 256;
+};
+
+__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// UP: gate/up rows (64 gate + 64 up interleaved), K = H, output gu; else down rows, K = I,
+// output ysorted. SPLIT: B rows are hi/lo pairs (2 per token).
+template <bool UP, int NB, bool SPLIT>
+__global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
+    const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap wmap,
+    const __grid_constant__ CUtensorMap sh_wmap, ForwardArgs a, TcSide side, float *gu) {
+  using C = BfCfg<NB>;
+  constexpr int S = C::kStages;
+  constexpr int TPT = SPLIT ? NB / 2 : NB;  // tokens per tile
+  extern __shared__ uint8_t dsm[];
+  __shared__ int abort_flag;
+  const int K = UP ? a.H : a.I;
+  const int n_tiles = UP ? a.I / 64 : a.H / 128;
+  const int n_units = *a.n_items * n_tiles;
+  if ((int)blockIdx.x >= n_units) return;
+  const int my_units = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int nsteps = K / kBfStepK;
+
+  const uint32_t raw = smem_u32(dsm);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t bars = base + S * C::kStage;  // full[S], empty[S], accfull[2], accempty[2], slot
+  auto full = [&](int i) { return bars + 8u * i; };
+  auto empty = [&](int i) { return bars + 8u * (S + i); };
+  auto accfull = [&](int i) { return bars + 8u * (2 * S + i); };
+  auto accempty = [&](int i) { return bars + 8u * (2 * S + 2 + i); };
+  const uint32_t slot = bars + 8u * (2 * S + 4);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    abort_flag = *reinterpret_cast<const volatile int32_t *>(a.status) == kStatusTimeout;
+    for (int i = 0; i < S; i++) {
+      mbar_init(full(i), 1);
+      mbar_init(empty(i), 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(accfull(i), 1);
+      mbar_init(accempty(i), 4);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  constexpr uint32_t kCols = 2 * NB <= 32 ? 32 : 2 * NB;  // power of two: 2 accumulators
+  if (warp == 0) tmem_alloc(slot, kCols);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(dsm + (slot - raw));
+  const uint32_t unit_stride = gridDim.x;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      int t = 0;
+      bool stop = false;
+      UnitWalk walk{a.items, (int)blockIdx.x, (int)unit_stride, n_tiles, my_units};
+      for (int lu = 0; lu < my_units && !stop; lu++) {
+        const Unit un = walk.at(lu);
+        if (*reinterpret_cast<const volatile int32_t *>(a.status) == kStatusTimeout)
+          atomicExch(&abort_flag, 1);
+        const bool shared = un.e == a.E;
+        const int ex = shared ? 0 : un.e;
+        for (int ks = 0; ks < nsteps; ks++, t++) {
+          const int i = t % S;
+          if ((t >= S && !wait_or_abort(empty(i), (uint32_t)((t / S - 1) & 1), &abort_flag)) ||
+              aborted(&abort_flag)) {
+            atomicExch(&abort_flag, 1);
+            stop = true;
+            break;
+          }
+          const uint32_t st = base + (uint32_t)i * C::kStage;
+          mbar_expect_tx(full(i), (uint32_t)C::kStage);
+          if (UP)
+            tma_load_4d(st, shared ? &sh_wmap : &wmap, kBfStepK * ks, 0, un.tile * 64, ex, full(i));
+          else
+            tma_load_2d(st, shared ? &sh_wmap : &wmap, kBfStepK * ks, ex * a.H + un.tile * 128, full(i));
+          tma_load_2d(st + C::kA, &bmap, kBfStepK * ks, SPLIT ? 2 * un.pos0 : un.pos0, full(i));
+        }
+      }
+      for (int i = max(0, t - S); i < t; i++) mbar_wait(full(i % S), (uint32_t)((i / S) & 1));
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      int t = 0;
+      bool stop = false;
+      UnitWalk walk{a.items, (int)blockIdx.x, (int)unit_stride, n_tiles, my_units};
+      for (int lu = 0; lu < my_units && !stop; lu++) {
+        const Unit un = walk.at(lu);
+        const int acc = lu & 1;
+        if (lu >= 2 && !wait_or_abort(accempty(acc), (uint32_t)(((lu >> 1) - 1) & 1), &abort_flag)) {
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        fence_after();
+        // N sized to the unit's tokens (a multiple of 16): ragged tiles cost less
+        const int rows = SPLIT ? 2 * un.ntok : un.ntok;
+        const int n = min(NB, (rows + 15) & ~15);
+        const uint32_t idesc = idesc_bf16(n);
+        const uint32_t dcol = tmem + (uint32_t)(acc * NB);
+        for (int ks = 0; ks < nsteps; ks++, t++) {
+          const int i = t % S;
+          if (!wait_or_abort(full(i), (uint32_t)((t / S) & 1), &abort_flag)) {
+            atomicExch(&abort_flag, 1);
+            stop = true;
+            break;
+          }
+          fence_after();
+          const uint32_t st = base + (uint32_t)i * C::kStage;
+          const uint64_t a0 = sw128_desc(st), b0 = sw128_desc(st + C::kA);
+#pragma unroll
+          for (int s = 0; s < kBfStepK / 16; s++)
+            mma_ss(dcol, a0 + 2u * s, b0 + 2u * s, idesc, (ks | s) ? 1u : 0u);
+          mma_commit(empty(i));
+        }
+        if (!stop) mma_commit(accfull(acc));
+      }
+      // every issued MMA is done before the CTA may exit (the last commit covers them all)
+      if (t > 0) mbar_wait(empty((t - 1) % S), (uint32_t)(((t - 1) / S) & 1));
+    }
+  } else if (warp < 4) {
+    const int q = warp, r = 32 * q + lane;
+    UnitWalk walk{a.items, (int)blockIdx.x, (int)unit_stride, n_tiles, my_units};
+    for (int lu = 0; lu < my_units; lu++) {
+      const int acc = lu & 1;
+      const Unit un = walk.at(lu);
+      const bool ok = wait_or_abort(accfull(acc), (uint32_t)((lu >> 1) & 1), &abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) atomicExch(&abort_flag, 1);
+        break;
+      }
+      fence_after();
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * NB);
+      const bool swapped = un.e == a.E ? side.sh_up_swapped : side.up_swapped;
+      float *out = UP ? gu : a.ysorted;
+      const int ld = UP ? 2 * a.I : a.H;
+      const int col = UP ? un.tile * 128 + (r ^ (swapped ? 1 : 0)) : un.tile * 128 + r;
+      const int rows = SPLIT ? 2 * un.ntok : un.ntok;
+#pragma unroll 1
+      for (int c0 = 0; c0 < NB; c0 += 32) {
+        if (c0 < rows) {
+          float w[32];
+          tmem_ld16(taddr + c0, reinterpret_cast<uint32_t *>(w));
+          tmem_ld16(taddr + c0 + 16, reinterpret_cast<uint32_t *>(w + 16));
+          tmem_wait_ld();
+          const int nbase = SPLIT ? c0 / 2 : c0;
+#pragma unroll
+          for (int j = 0; j < (SPLIT ? 16 : 32); j++) {
+            const int n = nbase + j;
+            const float v = SPLIT ? w[2 * j] + w[2 * j + 1] : w[j];
+            if (n < un.ntok) out[(size_t)(un.pos0 + n) * ld + col] = v;
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(accempty(acc));
+    }
+  }
+  __syncthreads();
+  if (tid == 0 && abort_flag) atomicExch(a.status, kStatusTimeout);
+  if (warp == 0) {
+    fence_after();
+    tmem_dealloc(tmem, kCols);
+  }
+}
+
+// bf16 inputs gathered into sorted order: out[pos] = x[token of pos] (bf16 copy).
+__global__ void __launch_bounds__(256) gather_bf16_kernel(ForwardArgs a, __nv_bfloat16 *out) {
+  const int pos = blockIdx.x;
+  if (pos >= a.offsets[a.E + 1]) return;
+  const int P = a.T * a.k, pr = a.sorted[pos];
+  const int tok = pr < P ? pr / a.k : pr - P;
+  const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(a.x) + (size_t)tok * a.H);
+  uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)pos * a.H);
+  for (int i = threadIdx.x; i < a.H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// h = act(gate, up) from gu, as bf16 hi (row 2 pos) + lo (row 2 pos + 1).
+__global__ void __launch_bounds__(256) pack_h_bf16_kernel(ForwardArgs a, const float *gu,
+                                                         __nv_bfloat16 *out) {
+  const int pos = blockIdx.x;
+  if (pos >= a.offsets[a.E + 1]) return;
+  const int P = a.T * a.k, pr = a.sorted[pos];
+  const int e = pr < P ? (int)a.sel_idx[pr] : a.E;
+  const int I = a.I;
+  const float *row = gu + (size_t)pos * 2 * I;
+  for (int i = threadIdx.x * 2; i < I; i += blockDim.x * 2) {
+    const float4 v = *reinterpret_cast<const float4 *>(row + 2 * i);
+    const float h0 = activate(a, e, v.x, v.y), h1 = activate(a, e, v.z, v.w);
+    const __nv_bfloat16 a0 = __float2bfloat16_rn(h0), a1 = __float2bfloat16_rn(h1);
+    const __nv_bfloat16 b0 = __float2bfloat16_rn(h0 - __bfloat162float(a0));
+    const __nv_bfloat16 b1 = __float2bfloat16_rn(h1 - __bfloat162float(a1));
+    *reinterpret_cast<__nv_bfloat162 *>(out + (size_t)2 * pos * I + i) = __halves2bfloat162(a0, a1);
+    *reinterpret_cast<__nv_bfloat162 *>(out + (size_t)(2 * pos + 1) * I + i) = __halves2bfloat162(b0, b1);
+  }
+}
+
 }  // namespace tc
 
 // ---------------------------------------------------------------------------
@@ -888,6 +1115,7 @@ __global__ void side_transpose_kernel(int kind, SplitTensor src, int experts, in
 // ---------------------------------------------------------------------------
 
 bool tc_supported(int gate_type, int down_type, int H, int I) {
+  if (gate_type == DM_BF16 && down_type == DM_BF16) return H % 128 == 0 && I % 64 == 0;
   if (gate_type != DM_Q4_K) return false;
   if (down_type != DM_Q6_K && down_type != DM_Q5_0) return false;
   if (H % 256 || I % 64) return false;  // Q4_K rows of whole super-blocks; 128-row down tiles
@@ -933,7 +1161,27 @@ static bool fits_split(int nt) {
 
 // x16 / h16 hold 2*rows rows (hi and lo interleaved with the split, hi alone without).
 // The split of a matrix is dropped where its kernel's tiles would not fit shared memory.
+static bool encode_bf16_rows(CUtensorMap *map, const void *base, int K, uint64_t rows, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn || !base) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void *)base, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int make_tc_maps(TcPlan &p, int H, int I, int down_type, int nt) {
+  if (down_type == DM_BF16) {  // gathered bf16 inputs; intermediates as hi/lo row pairs
+    p.bf16 = true;
+    p.split_x = false;
+    p.split_h = true;
+    if (!encode_bf16_rows(&p.x_map, p.x16, H, (uint64_t)p.rows, nt)) return -1;
+    if (!encode_bf16_rows(&p.h_map, p.h16, I, 2 * (uint64_t)p.rows, 2 * nt)) return -1;
+    return 0;
+  }
   p.split_x = p.split && fits_split<tc::kUpQ4K>(nt);
   p.split_h = p.split && (down_type == DM_Q6_K ? fits_split<tc::kDownQ6K>(nt)
                                                : fits_split<tc::kDownQ50>(nt));
@@ -983,8 +1231,33 @@ static int launch_nt(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, 
   return 4;
 }
 
+static int launch_bf16(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, cudaStream_t s,
+                       cudaEvent_t down_mark) {
+  constexpr int NT = 128;
+  if (p.nt != NT) return -1;
+  const int rows_bound = a.T * a.k + (a.shared ? a.T : 0);
+  tc::gather_bf16_kernel<<<rows_bound, 256, 0, s>>>(a, reinterpret_cast<__nv_bfloat16 *>(p.x16));
+  {
+    auto fn = tc::tc_bf16_kernel<true, NT, false>;
+    ensure_smem_limit((const void *)fn);
+    const int grid = std::max(1, std::min(p.n_sm, p.max_items * (a.I / 64)));
+    fn<<<grid, tc::kBfThreads, tc::BfCfg<NT>::kSmem, s>>>(p.x_map, w.up, w.sh_up, a, w.side, p.gu);
+  }
+  if (down_mark) cudaEventRecord(down_mark, s);
+  tc::pack_h_bf16_kernel<<<rows_bound, 256, 0, s>>>(a, p.gu, reinterpret_cast<__nv_bfloat16 *>(p.h16));
+  {
+    auto fn = tc::tc_bf16_kernel<false, 2 * NT, true>;
+    ensure_smem_limit((const void *)fn);
+    const int grid = std::max(1, std::min(p.n_sm, p.max_items * (a.H / 128)));
+    fn<<<grid, tc::kBfThreads, tc::BfCfg<2 * NT>::kSmem, s>>>(p.h_map, w.down, w.sh_down, a, w.side,
+                                                              p.gu);
+  }
+  return 4;
+}
+
 int launch_tc_experts(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, cudaStream_t s,
                       cudaEvent_t down_mark) {
+  if (p.bf16) return launch_bf16(a, p, w, s, down_mark);
   switch (p.nt) {
     case 16: return launch_nt<16>(a, p, w, s, down_mark);
     case 32: return launch_nt<32>(a, p, w, s, down_mark);
@@ -1030,6 +1303,41 @@ static bool encode_rows(CUtensorMap *map, const uint8_t *base, uint64_t row_byte
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)base, dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// bf16 gate/up rows as {K, gate|up, row, expert} (box {64, 2, 64, 1}, 128-byte swizzle):
+// 64 interleaved gate/up row pairs of one 64-wide K step.
+static bool encode_up_bf16(CUtensorMap *map, const uint8_t *gate, const uint8_t *up, int H, int I,
+                           int experts, uint64_t expert_stride, int *swapped) {
+  auto fn = encode_fn();
+  if (!fn || !gate || !up) return false;
+  const uint8_t *origin = gate < up ? gate : up;
+  *swapped = gate < up ? 0 : 1;
+  cuuint64_t dims[4] = {(cuuint64_t)H, 2, (cuuint64_t)I, (cuuint64_t)experts};
+  cuuint64_t strides[3] = {(cuuint64_t)(gate < up ? up - gate : gate - up), (cuuint64_t)H * 2,
+                           expert_stride};
+  cuuint32_t box[4] = {64, 2, 64, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, (void *)origin, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int make_tc_weights_bf16(TcWeights &w, const uint8_t *gate, const uint8_t *up, uint64_t expert_stride,
+                         const uint8_t *sh_gate, const uint8_t *sh_up, const uint8_t *down,
+                         const uint8_t *sh_down, int experts, int H, int I) {
+  if (!encode_up_bf16(&w.up, gate, up, H, I, experts, expert_stride, &w.side.up_swapped)) return -1;
+  if (!encode_bf16_rows(&w.down, down, I, (uint64_t)experts * H, 128)) return -1;
+  const bool shared = sh_gate != nullptr;
+  if (shared) {
+    if (!encode_up_bf16(&w.sh_up, sh_gate, sh_up, H, I, 1, (uint64_t)I * H * 2, &w.side.sh_up_swapped))
+      return -1;
+    if (!encode_bf16_rows(&w.sh_down, sh_down, I, (uint64_t)H, 128)) return -1;
+  } else {
+    w.sh_up = w.up;
+    w.sh_down = w.down;
+  }
+  return 0;
 }
 
 int make_tc_weights(TcWeights &w, const uint8_t *gate, const uint8_t *up, uint64_t expert_stride,

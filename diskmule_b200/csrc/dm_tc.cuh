@@ -31,6 +31,7 @@ struct TcPlan {
   int n_sm = 148;      // persistent grid size
   bool split = true;   // B as hi + lo fp16 halves where shared memory allows:
   bool split_x = true, split_h = true;  // as encoded for the inputs / intermediates
+  bool bf16 = false;   // bf16 weights: gathered bf16 inputs, bf16 hi/lo intermediates
   __half *x16 = nullptr;   // [rows][H] packed expert inputs (sorted order)
   float *x_inv = nullptr;  // [rows] 1 / scale of each packed input row
   __half *h16 = nullptr;   // [rows][I] packed intermediates
@@ -66,6 +67,11 @@ int make_tc_weights(TcWeights &w, const uint8_t *gate, const uint8_t *up, uint64
                     const SplitTensor &sh_down, int down_type, int experts, int H, int I,
                     uint8_t *qh_t, uint8_t *d_t, uint8_t *sh_qh_t, uint8_t *sh_d_t,
                     cudaStream_t stream);
+
+// bf16 weights (no side arrays): gate/up {K, gate|up, row, expert}, down {K, expert*H + row}.
+int make_tc_weights_bf16(TcWeights &w, const uint8_t *gate, const uint8_t *up, uint64_t expert_stride,
+                         const uint8_t *sh_gate, const uint8_t *sh_up, const uint8_t *down,
+                         const uint8_t *sh_down, int experts, int H, int I);
 
 // Whether the tensor-core path covers these formats / shapes.
 bool tc_supported(int gate_type, int down_type, int H, int I);

@@ -116,6 +116,23 @@ def test_full_size_glm_layer_matches_the_oracle(ctx):
         sl.close()
 
 
+def test_full_size_glm_batch_on_tensor_cores(ctx):
+    # 512 tokens x top-8 over 256 experts = 16 per expert: the bf16 tcgen05 path
+    T, sub = 512, [0, 300, 511]
+    sl = build_layer(ctx, "glm52", seed=6)
+    try:
+        spec, raw = sl.inputs(T, seed=19)
+        y, idx, wt = sl.layer.forward_host(device_input(spec, raw, T))
+        experts = sorted(set(idx[sub].ravel().tolist()))
+        x32 = as_f32(spec, raw, T)[sub]
+        y_ref, idx_ref, wt_ref = run_oracle(sl, x32, experts=experts)
+        check(y[sub], idx[sub], wt[sub], y_ref, idx_ref, wt_ref)
+        check_dispatch(sl, T, idx)
+        assert np.all(np.isfinite(y))
+    finally:
+        sl.close()
+
+
 @pytest.mark.parametrize("name,T,sub", [("qwen35", 512, [0, 1, 255, 511]),
                                          ("gemma4", 128, [0, 63, 127])])
 def test_full_batch_matches_the_oracle_on_a_token_subsample(ctx, name, T, sub):
