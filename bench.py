@@ -40,6 +40,9 @@ def parse_args():
     p.add_argument("--tokens", type=int, default=512)
     p.add_argument("--decode-steps", type=int, default=200)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--ep", action="store_true",
+                   help="expert parallelism over the ranks (config 4: --config glm52 --tokens 8192 "
+                        "tokens in total, split over the GPUs)")
     return p.parse_args()
 
 
@@ -361,10 +364,165 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# expert parallelism (config 4)
+# ---------------------------------------------------------------------------
+
+def cpu_glm_sample_tokens_per_second(cfg_name: str, sample: int, threads: int, seed: int = 1):
+    """The oracle GLM block on `sample` tokens, with host weights for the experts those
+    tokens select only (the full pool is tens of GB)."""
+    from diskmule_b200 import _native as N
+    from diskmule_b200.synthetic import CONFIGS, SyntheticLayer, input_spec, layer_specs, vectors
+    from oracle import oracle as O
+    cfg = dict(CONFIGS[cfg_name])
+    specs = layer_specs(cfg, seed)
+    sl = SyntheticLayer(cfg_name, cfg, seed, None, specs, vectors(cfg, seed))
+    raw = input_spec(cfg, sample, 21).host()
+    x = (raw.view(np.uint16).reshape(sample, -1).astype(np.uint32) << 16).view(np.float32)
+    router = specs["router"].host()
+    bias = specs["bias"].host().view(np.float32)
+    chosen = set()
+    for t in range(sample):
+        _, lg = O.glm_matvec(N.BF16, cfg["experts"], cfg["hidden"], router, x[t], threads)
+        _, idx, _ = O.glm_select(lg, bias, cfg["top_k"], cfg["n_groups"], cfg["topk_groups"],
+                                 cfg["normalize"])
+        chosen.update(int(i) for i in idx)
+    w = sl.host_weights(sorted(chosen))
+    t0 = time.perf_counter()
+    rc, _, _, _ = O.glm_moe(w, x, threads=threads)
+    assert rc == O.OK
+    return sample / (time.perf_counter() - t0)
+
+
+def run_ep(args):
+    import datetime
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if "MASTER_ADDR" not in os.environ:  # a single process: a one-rank group
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ.setdefault("MASTER_PORT", "29533")
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    from diskmule_b200.ep import ExpertParallel, cuda_backend_for
+    from diskmule_b200.moe import CudaContext
+    from diskmule_b200.synthetic import CONFIGS, build_layer, input_spec
+
+    cfg = dict(CONFIGS[args.config])
+    E, H, I, k = cfg["experts"], cfg["hidden"], cfg["intermediate"], cfg["top_k"]
+    per = E // world
+    T_total = args.tokens
+    T = T_total // world
+    ctx = CudaContext(local)
+    sl = build_layer(ctx, args.config, seed=1, expert_range=(rank * per, per))
+    xdt = torch.bfloat16 if cfg["family"] == "glm52" else torch.float32
+    x = torch.empty((T, H), dtype=xdt, device="cuda")
+    input_spec(cfg, T, 21 + rank).device_fill(x.data_ptr())
+    ctx.synchronize()
+    backend = cuda_backend_for(sl)
+    ep = ExpertParallel(backend, E, k)
+    stream = torch.cuda.current_stream()
+
+    for _ in range(args.warmup):
+        y = ep.forward(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            y = ep.forward(x)
+        end.record(stream)
+        torch.cuda.synchronize()
+    dist.barrier()
+    ms = max_over_ranks(start.elapsed_time(end))
+    value = T_total * args.steps / (ms / 1e3)
+    # launches of one step (route + received rows + shared rows + combine)
+    launches = 0
+    T_probe = T
+    ep.forward(x)
+    launches = sl.layer.last_launch_count()  # combine; the others are counted below
+    routed = backend.route(x)
+    launches += sl.layer.last_launch_count()
+    ids = torch.zeros((T_probe,), dtype=torch.int32, device="cuda")
+    backend.expert_rows(x if cfg["family"] != "gemma4" else routed.expert_in, ids)
+    launches += 2 * sl.layer.last_launch_count()
+
+    # e2e: host input copied in and output copied back every step
+    xh = torch.empty((T, H), dtype=xdt, pin_memory=True)
+    xh.copy_(x.cpu())
+    yh = torch.empty((T, H), dtype=torch.float32, pin_memory=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        xd = xh.to("cuda", non_blocking=True)
+        yh.copy_(ep.forward(xd), non_blocking=True)
+        torch.cuda.synchronize()
+    el = max_over_ranks(time.perf_counter() - t0)
+
+    # tensor roofline: useful FLOPs per GPU per step / time
+    shared = 1 if cfg.get("shared") else 0
+    flops = T * (k + shared) * 3 * 2 * H * I
+    peaks = {}
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            peaks = json.load(f)
+    peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops") or 1590.0
+    achieved = flops / (ms / args.steps / 1e3) / 1e12
+    if rank == 0:
+        cpu = None
+        if world == 1 and cfg["family"] == "glm52":
+            threads = os.cpu_count() or 1
+            sample = 8
+            cpu = {"value": cpu_glm_sample_tokens_per_second(args.config, sample, threads),
+                   "unit": "tokens/s", "cores": threads, "kind": "port",
+                   "sample": f"{sample} tokens of the {args.config} block (host weights of the "
+                             "experts they select)"}
+        line = {
+            "metric": f"MoE-layer tokens/s ({args.config} prefill T={T_total}, expert parallel)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{args.config} MoE block, prefill T={T_total} split over "
+                                   f"{world} GPU(s), experts sharded {per} per GPU",
+                       "parallelism": f"ep{world}", "tokens_per_gpu": T,
+                       "l2": "weights larger than L2; no flush needed"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                         "kernel": "whole EP step", "algorithmic_flops_per_gpu": flops},
+            "e2e": {"value": T_total * args.steps / el, "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(T * H * (2 if xdt == torch.bfloat16 else 4)),
+                    "d2h_bytes_per_step": int(T * H * 4)},
+            "gpu_launches": launches * args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    sl.close()
+    ctx.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.ep:
+        run_ep(args)
     else:
         run_ours(args)
 

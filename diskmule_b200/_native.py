@@ -98,6 +98,11 @@ SIGNATURES = {
     "dm_moe_set_profiling": ([P, I32], I32),
     "dm_moe_stage_times": ([P, P, I32], I32),
     "dm_moe_stage_name": ([I32], C.c_char_p),
+    "dm_moe_layer_create_ep": ([P, C.POINTER(MoeDesc), I32, I32, C.POINTER(P)], I32),
+    "dm_moe_local_experts": ([P, C.POINTER(I32), C.POINTER(I32)], I32),
+    "dm_moe_route": ([P, P, I32, P, P, P, P, P], I32),
+    "dm_moe_expert_rows": ([P, P, P, I32, P, P], I32),
+    "dm_moe_combine_rows": ([P, I32, P, P, P, P, P, P], I32),
     "dm_synth_fill_host": ([I32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float,
                             C.c_float, P], I32),
     "dm_synth_fill_device": ([I32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float,

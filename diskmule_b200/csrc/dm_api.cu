@@ -431,6 +431,10 @@ struct dm_moe_layer {
   dm_cuda_context *ctx = nullptr;
   dm_moe_desc desc{};
   int E1 = 0;
+  // Experts whose weights this layer holds: [first_expert, first_expert + local_experts)
+  // of the desc.experts routed by the router (all of them unless created for expert
+  // parallelism).
+  int first_expert = 0, local_experts = 0;
   bool shared = false;
   void *router_t = nullptr;  // transposed router [H][E1]
   float *router_dup = nullptr;  // [H][router_dup_ld(E1)] f32 router for many tokens
@@ -577,15 +581,15 @@ int32_t build_tc_weights(dm_moe_layer *L) {
   if (d.down_type == DM_BF16) {
     if (dm::make_tc_weights_bf16(L->tcw, (const uint8_t *)d.gate, L->up_base, L->gate_stride,
                                  (const uint8_t *)d.shared_gate, (const uint8_t *)d.shared_up,
-                                 (const uint8_t *)d.down, (const uint8_t *)d.shared_down, d.experts,
-                                 d.hidden, d.intermediate) != 0) {
+                                 (const uint8_t *)d.down, (const uint8_t *)d.shared_down,
+                                 L->local_experts, d.hidden, d.intermediate) != 0) {
       fprintf(stderr, "diskmule_cuda: tensor-core path off for this layer (weight maps refused)\n");
       L->tc_ok = false;
     }
     return DM_OK;
   }
   uint64_t qh_bytes = 0, d_bytes = 0, sh_qh_bytes = 0, sh_d_bytes = 0;
-  dm::tc_side_bytes(d.down_type, d.experts, d.hidden, d.intermediate, &qh_bytes, &d_bytes);
+  dm::tc_side_bytes(d.down_type, L->local_experts, d.hidden, d.intermediate, &qh_bytes, &d_bytes);
   if (L->shared)
     dm::tc_side_bytes(d.down_type, 1, d.hidden, d.intermediate, &sh_qh_bytes, &sh_d_bytes);
   uint8_t *bufs[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -601,7 +605,7 @@ int32_t build_tc_weights(dm_moe_layer *L) {
   }
   if (dm::make_tc_weights(L->tcw, (const uint8_t *)d.gate, L->up_base, L->gate_stride,
                           (const uint8_t *)d.shared_gate, (const uint8_t *)d.shared_up,
-                          L->plan.down, L->plan.sh_down, d.down_type, d.experts, d.hidden,
+                          L->plan.down, L->plan.sh_down, d.down_type, L->local_experts, d.hidden,
                           d.intermediate, bufs[0], bufs[1], bufs[2], bufs[3], L->ctx->stream) != 0) {
     fprintf(stderr, "diskmule_cuda: tensor-core path off for this layer (weight maps refused)\n");
     L->tc_ok = false;
@@ -611,7 +615,7 @@ int32_t build_tc_weights(dm_moe_layer *L) {
 
 int32_t build_plan(dm_moe_layer *L) {
   const dm_moe_desc &d = L->desc;
-  const uint64_t E = d.experts, H = d.hidden, I = d.intermediate;
+  const uint64_t E = L->local_experts, H = d.hidden, I = d.intermediate;
   int e = 0, b = 0;
   auto nblocks = [&](int kind, uint64_t rows, uint64_t cols) {
     dm::block_layout(kind, &e, &b);
@@ -718,7 +722,25 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
 
 extern "C" {
 
+static int32_t create_layer(dm_cuda_context *ctx, const dm_moe_desc *desc, int32_t first_expert,
+                            int32_t local_experts, dm_moe_layer **out);
+
 int32_t dm_moe_layer_create(dm_cuda_context *ctx, const dm_moe_desc *desc, dm_moe_layer **out) {
+  if (!desc) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  return create_layer(ctx, desc, 0, desc->experts, out);
+}
+
+int32_t dm_moe_layer_create_ep(dm_cuda_context *ctx, const dm_moe_desc *desc, int32_t first_expert,
+                               int32_t local_experts, dm_moe_layer **out) {
+  if (!desc) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  if (first_expert < 0 || local_experts <= 0 || first_expert + local_experts > desc->experts)
+    return fail(DM_ERR_INVALID_ARGUMENT, "expert range [%d, %d) is outside 0..%d", first_expert,
+                first_expert + local_experts, desc->experts);
+  return create_layer(ctx, desc, first_expert, local_experts, out);
+}
+
+static int32_t create_layer(dm_cuda_context *ctx, const dm_moe_desc *desc, int32_t first_expert,
+                            int32_t local_experts, dm_moe_layer **out) {
   if (!ctx || !out) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
   *out = nullptr;
   int32_t rc = validate_desc(desc);
@@ -728,6 +750,8 @@ int32_t dm_moe_layer_create(dm_cuda_context *ctx, const dm_moe_desc *desc, dm_mo
   if (!L) return fail(DM_ERR_ALLOCATION, "host allocation failed");
   L->ctx = ctx;
   L->desc = *desc;
+  L->first_expert = first_expert;
+  L->local_experts = local_experts;
   dm_moe_desc &d = L->desc;
   if (d.n_groups <= 0) d.n_groups = 1;
   if (d.topk_groups <= 0) d.topk_groups = 1;
@@ -822,18 +846,10 @@ const char *dm_moe_stage_name(int32_t stage) {
   return stage >= 0 && stage < dm::kStageCount ? names[stage] : "";
 }
 
-int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
-                       uint32_t *sel_idx, float *sel_weight, void *stream) {
-  if (!L || !x || !y) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
-  if (tokens < 0) return fail(DM_ERR_INVALID_ARGUMENT, "negative token count");
-  if (tokens == 0) return DM_OK;
-  if ((int64_t)tokens * L->desc.top_k > INT32_MAX / 2 || tokens > (1 << 22))
-    return fail(DM_ERR_OVERFLOW, "too many tokens in one call (limit 4194304)");
-  if (((uintptr_t)y & 15) || ((uintptr_t)x & 15))
-    return fail(DM_ERR_INVALID_ARGUMENT, "x and y must be 16-byte aligned device pointers");
-  cudaSetDevice(L->ctx->device);
-  int32_t rc = ensure_layer_scratch(L, tokens);
-  if (rc != DM_OK) return rc;
+namespace {
+
+// Forward arguments for `tokens` rows of `x` (the scratch is already sized).
+dm::ForwardArgs fill_args(dm_moe_layer *L, const void *x, float *y, int32_t tokens) {
   const dm_moe_desc &d = L->desc;
   dm::ForwardArgs a = L->args;
   a.family = d.family;
@@ -844,6 +860,7 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
   a.k = d.top_k;
   a.E1 = L->E1;
   a.shared = L->shared;
+  a.rows_mode = 0;
   a.n_groups = d.n_groups;
   a.topk_groups = d.topk_groups;
   a.normalize = d.normalize_topk;
@@ -873,17 +890,27 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
   a.sh_gate = (const uint8_t *)d.shared_gate;
   a.sh_up = (const uint8_t *)d.shared_up;
   a.sh_down = (const uint8_t *)d.shared_down;
-  if (sel_idx) a.sel_idx = sel_idx;
-  if (sel_weight) a.sel_w = sel_weight;
-  cudaStream_t s = (cudaStream_t)stream;
-  dm::GemvPlan plan = L->plan;
-  plan.nt = tokens == 1 ? 1 : (tokens == 2 ? 2 : 4);
-  plan.max_active = std::min(a.E + (a.shared ? 1 : 0), a.T * a.k + (a.shared ? 1 : 0));
-  {
-    const int pairs = a.T * a.k + (a.shared ? a.T : 0);
-    plan.max_items = std::min(pairs, (pairs + plan.nt - 1) / plan.nt + plan.max_active);
-  }
-  a.chunk = plan.nt;
+  return a;
+}
+
+// Expert-kernel plans for the dispatch described by `a` (tokens, k, experts, shared or
+// rows mode); sets a.chunk. `gp` / `tp` are null when that path does not apply.
+struct Plans {
+  dm::GemvPlan plan;
+  dm::TcPlan tcp;
+  const dm::GemvPlan *gp = nullptr;
+  const dm::TcPlan *tp = nullptr;
+};
+
+void choose_plans(dm_moe_layer *L, dm::ForwardArgs &a, Plans &P) {
+  const dm_moe_desc &d = L->desc;
+  const int pairs = a.T * a.k + (a.shared ? a.T : 0);
+  const int buckets = a.E + ((a.shared || a.rows_mode) ? 1 : 0);
+  P.plan = L->plan;
+  P.plan.nt = a.T == 1 ? 1 : (a.T == 2 ? 2 : 4);
+  P.plan.max_active = std::min(buckets, pairs + (a.shared ? 1 : 0));
+  P.plan.max_items = std::min(pairs, (pairs + P.plan.nt - 1) / P.plan.nt + P.plan.max_active);
+  a.chunk = P.plan.nt;
   // the GEMV kernels cover whole tasks: 256 elements (Q4_K/Q6_K), 32 (Q5_0/Q8_0),
   // 128 (BF16) or 64 (F16/F32) per row chunk
   auto task_elems = [](int kind) {
@@ -896,21 +923,47 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
   };
   const bool gemv_ok = d.hidden % task_elems(a.gate_type) == 0 &&
                        d.intermediate % task_elems(a.down_type) == 0;
-  const dm::GemvPlan *gp = gemv_ok ? &plan : nullptr;
-  // Enough tokens per expert -> the tcgen05 grouped GEMM (16/32/64-token tiles).
-  dm::TcPlan tcp;
-  const dm::TcPlan *tp = nullptr;
-  if (gp && L->tc_ok) {
-    const double avg = (double)tokens * d.top_k / d.experts;
+  P.gp = gemv_ok ? &P.plan : nullptr;
+  P.tp = nullptr;
+  // Enough tokens per expert -> the tcgen05 grouped GEMM.
+  if (P.gp && L->tc_ok) {
+    const double avg = a.rows_mode ? (double)pairs / buckets : (double)a.T * a.k / a.E;
     if (avg >= (d.down_type == DM_BF16 ? 16.0 : 4.0)) {
-      tcp = L->tc[avg <= 12.0 ? 0 : (avg <= 24.0 ? 1 : 2)];
-      tcp.weights = &L->tcw;
-      const int pairs = a.T * a.k + (a.shared ? a.T : 0);
-      tcp.max_items = std::min(pairs, (pairs + tcp.nt - 1) / tcp.nt + plan.max_active);
-      a.chunk = tcp.nt;
-      tp = &tcp;
+      P.tcp = L->tc[avg <= 12.0 ? 0 : (avg <= 24.0 ? 1 : 2)];
+      P.tcp.weights = &L->tcw;
+      P.tcp.max_items = std::min(pairs, (pairs + P.tcp.nt - 1) / P.tcp.nt + P.plan.max_active);
+      a.chunk = P.tcp.nt;
+      P.tp = &P.tcp;
     }
   }
+}
+
+}  // namespace
+
+int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
+                       uint32_t *sel_idx, float *sel_weight, void *stream) {
+  if (!L || !x || !y) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  if (tokens < 0) return fail(DM_ERR_INVALID_ARGUMENT, "negative token count");
+  if (tokens == 0) return DM_OK;
+  if (L->local_experts != L->desc.experts)
+    return fail(DM_ERR_INVALID_ARGUMENT,
+                "this layer holds experts %d..%d only: use dm_moe_route / dm_moe_expert_rows",
+                L->first_expert, L->first_expert + L->local_experts - 1);
+  if ((int64_t)tokens * L->desc.top_k > INT32_MAX / 2 || tokens > (1 << 22))
+    return fail(DM_ERR_OVERFLOW, "too many tokens in one call (limit 4194304)");
+  if (((uintptr_t)y & 15) || ((uintptr_t)x & 15))
+    return fail(DM_ERR_INVALID_ARGUMENT, "x and y must be 16-byte aligned device pointers");
+  cudaSetDevice(L->ctx->device);
+  int32_t rc = ensure_layer_scratch(L, tokens);
+  if (rc != DM_OK) return rc;
+  dm::ForwardArgs a = fill_args(L, x, y, tokens);
+  if (sel_idx) a.sel_idx = sel_idx;
+  if (sel_weight) a.sel_w = sel_weight;
+  cudaStream_t s = (cudaStream_t)stream;
+  Plans plans;
+  choose_plans(L, a, plans);
+  const dm::GemvPlan *gp = plans.gp;
+  const dm::TcPlan *tp = plans.tp;
 
   // A call that repeats with the same buffers (a decode loop) is captured once as a
   // CUDA graph on an internal stream and replayed on the caller's stream.
@@ -999,6 +1052,107 @@ int32_t dm_moe_forward_host(dm_moe_layer *L, const void *x, float *y, int32_t to
     return fail(DM_ERR_TIMEOUT, "a bounded wait in the tensor-core GEMM ran out");
   if (status == dm::kStatusNonFiniteNorm)
     return fail(DM_ERR_NON_FINITE, "RMSNorm received a non-finite value");
+  return DM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// expert parallelism: route, experts on received rows, combine of returned rows
+// ---------------------------------------------------------------------------
+
+namespace {
+
+int32_t finish_launch(dm_moe_layer *L, int launches, int tokens) {
+  if (launches < 0) return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "no expert kernel for this format");
+  DM_CUDA(cudaGetLastError(), "MoE launch");
+  L->last_tokens = tokens;
+  L->last_launches = launches;
+  return DM_OK;
+}
+
+}  // namespace
+
+int32_t dm_moe_route(dm_moe_layer *L, const void *x, int32_t tokens, uint32_t *sel_idx,
+                     float *sel_weight, float *expert_in, float *logits, void *stream) {
+  if (!L || !x || !sel_idx || !sel_weight) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  if (tokens < 0) return fail(DM_ERR_INVALID_ARGUMENT, "negative token count");
+  if (tokens == 0) return DM_OK;
+  if (tokens > (1 << 22)) return fail(DM_ERR_OVERFLOW, "too many tokens in one call (limit 4194304)");
+  if ((uintptr_t)x & 15) return fail(DM_ERR_INVALID_ARGUMENT, "x must be 16-byte aligned");
+  cudaSetDevice(L->ctx->device);
+  int32_t rc = ensure_layer_scratch(L, tokens);
+  if (rc != DM_OK) return rc;
+  dm::ForwardArgs a = fill_args(L, x, nullptr, tokens);
+  a.sel_idx = sel_idx;
+  a.sel_w = sel_weight;
+  cudaStream_t s = (cudaStream_t)stream;
+  DM_CUDA(cudaMemsetAsync(a.status, 0, 4, s), "status reset");
+  const int launches = dm::launch_forward(a, s, nullptr, nullptr, nullptr, dm::kRunRoute);
+  const dm_moe_desc &d = L->desc;
+  if (expert_in && d.family == DM_FAMILY_GEMMA4)
+    DM_CUDA(cudaMemcpyAsync(expert_in, a.expert_in, (size_t)tokens * d.hidden * 4,
+                            cudaMemcpyDeviceToDevice, s), "expert input copy");
+  if (logits)
+    DM_CUDA(cudaMemcpyAsync(logits, a.logits, (size_t)tokens * L->E1 * 4, cudaMemcpyDeviceToDevice,
+                            s), "logit copy");
+  return finish_launch(L, launches, tokens);
+}
+
+int32_t dm_moe_expert_rows(dm_moe_layer *L, const void *rows, const int32_t *expert_ids,
+                           int32_t count, float *out, void *stream) {
+  if (!L || !rows || !expert_ids || !out) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  if (count < 0) return fail(DM_ERR_INVALID_ARGUMENT, "negative row count");
+  if (count == 0) return DM_OK;
+  if (count > (1 << 22)) return fail(DM_ERR_OVERFLOW, "too many rows in one call (limit 4194304)");
+  if (((uintptr_t)rows & 15) || ((uintptr_t)out & 15))
+    return fail(DM_ERR_INVALID_ARGUMENT, "rows and out must be 16-byte aligned device pointers");
+  cudaSetDevice(L->ctx->device);
+  int32_t rc = ensure_layer_scratch(L, count);
+  if (rc != DM_OK) return rc;
+  dm::ForwardArgs a = fill_args(L, rows, out, count);
+  a.k = 1;
+  a.E = L->local_experts;  // ids are local; id E is the shared expert
+  a.shared = 0;
+  a.rows_mode = 1;
+  a.sel_idx = (uint32_t *)expert_ids;
+  if (L->desc.family == DM_FAMILY_GEMMA4) a.expert_in = (float *)rows;  // pre-normalised rows
+  cudaStream_t s = (cudaStream_t)stream;
+  Plans plans;
+  choose_plans(L, a, plans);
+  DM_CUDA(cudaMemsetAsync(a.status, 0, 4, s), "status reset");
+  const int launches = dm::launch_forward(a, s, nullptr, plans.gp, plans.tp,
+                                          dm::kRunExperts | dm::kRunScatter);
+  return finish_launch(L, launches, count);
+}
+
+int32_t dm_moe_combine_rows(dm_moe_layer *L, int32_t tokens, const uint32_t *sel_idx,
+                            const float *sel_weight, const float *logits, const float *pair_out,
+                            float *y, void *stream) {
+  if (!L || !sel_idx || !sel_weight || !pair_out || !y)
+    return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  if (tokens < 0) return fail(DM_ERR_INVALID_ARGUMENT, "negative token count");
+  if (tokens == 0) return DM_OK;
+  if (L->desc.family == DM_FAMILY_QWEN35_MOE && L->shared && !logits)
+    return fail(DM_ERR_INVALID_ARGUMENT, "the Qwen shared-expert gate needs the router logits");
+  if (((uintptr_t)pair_out & 15) || ((uintptr_t)y & 15))
+    return fail(DM_ERR_INVALID_ARGUMENT, "pair_out and y must be 16-byte aligned device pointers");
+  cudaSetDevice(L->ctx->device);
+  int32_t rc = ensure_layer_scratch(L, tokens);
+  if (rc != DM_OK) return rc;
+  dm::ForwardArgs a = fill_args(L, nullptr, y, tokens);
+  a.sel_idx = (uint32_t *)sel_idx;
+  a.sel_w = (float *)sel_weight;
+  if (logits) a.logits = (float *)logits;
+  a.ysorted = (float *)pair_out;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int launches = dm::launch_forward(a, s, nullptr, nullptr, nullptr,
+                                          dm::kRunIdentity | dm::kRunCombine);
+  return finish_launch(L, launches, tokens);
+}
+
+int32_t dm_moe_local_experts(const dm_moe_layer *L, int32_t *first_expert, int32_t *count) {
+  if (!L || !first_expert || !count) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  *first_expert = L->first_expert;
+  *count = L->local_experts;
   return DM_OK;
 }
 

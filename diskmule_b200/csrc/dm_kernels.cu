@@ -587,29 +587,32 @@ __device__ __forceinline__ void block_exclusive_scan3(int &a, int &b, int &c, in
   __syncthreads();
 }
 
+// Rows mode (expert-parallel rows): sel_idx holds explicit expert ids where id E is the
+// shared expert, so E + 1 buckets are counted and no shared pairs are added.
 __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs a) {
   extern __shared__ int32_t sm[];
   const int E = a.E, P = a.T * a.k;
-  int32_t *wc = sm;                              // [warps][E]
-  int32_t *total = sm + kDispatchWarps * E;      // [E + 1]
+  const int EB = E + (a.rows_mode ? 1 : 0);      // buckets counted from sel_idx
+  int32_t *wc = sm;                              // [warps][EB]
+  int32_t *total = sm + kDispatchWarps * (E + 1);  // [E + 1]
   int32_t *flags = total + (E + 1);              // [E + 1] scan scratch
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // contiguous chunks of whole warps' worth of pairs: few pairs use few warps
   const int chunk = max(32, (((P + kDispatchWarps - 1) / kDispatchWarps) + 31) & ~31);
   const int nw = (P + chunk - 1) / chunk;
-  for (int i = threadIdx.x; i < nw * E; i += blockDim.x) wc[i] = 0;
+  for (int i = threadIdx.x; i < nw * EB; i += blockDim.x) wc[i] = 0;
   __syncthreads();
   const int begin = min(P, warp * chunk), end = min(P, begin + chunk);
   for (int p = begin + lane; p < end; p += 32) {
     uint32_t e = a.sel_idx[p];
-    if (e < (uint32_t)E) atomicAdd(&wc[warp * E + e], 1);
+    if (e < (uint32_t)EB) atomicAdd(&wc[warp * EB + e], 1);
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+  for (int e = threadIdx.x; e < EB; e += blockDim.x) {
     int running = 0;
     for (int w = 0; w < nw; w++) {
-      int c = wc[w * E + e];
-      wc[w * E + e] = running;
+      int c = wc[w * EB + e];
+      wc[w * EB + e] = running;
       running += c;
     }
     total[e] = running;
@@ -620,7 +623,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs 
   // of (expert, first token, position, tokens) chunks of `a.chunk` tokens.
   {
     const int e = threadIdx.x;  // E + 1 <= kDispatchThreads
-    const int count = e < E ? total[e] : (e == E && a.shared ? a.T : 0);
+    const int count = e < EB ? total[e] : (e == E && a.shared ? a.T : 0);
     const int items = (count + a.chunk - 1) / a.chunk;
     int s_count = count, s_active = count > 0, s_items = items;
     int tot_count, tot_active, tot_items;
@@ -628,7 +631,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs 
     if (e <= E) {
       a.counts[e] = count;
       a.offsets[e] = s_count;
-      if (e < E) flags[e] = s_count;
+      if (e < EB) flags[e] = s_count;
       if (count > 0) a.active[s_active] = e;
       for (int j = 0; j < items; j++)
         a.items[s_items + j] = make_int4(e, j * a.chunk, s_count + j * a.chunk,
@@ -647,14 +650,14 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs 
     unsigned vmask = __ballot_sync(0xffffffffu, valid);
     if (valid) {
       uint32_t e = a.sel_idx[p];
-      if (e >= (uint32_t)E) e = 0;  // rejected upstream; keep indices in range
+      if (e >= (uint32_t)EB) e = 0;  // rejected upstream; keep indices in range
       unsigned peers = __match_any_sync(vmask, e);
       int rank = __popc(peers & ((1u << lane) - 1u));
-      int pos = flags[e] + wc[warp * E + e] + rank;
+      int pos = flags[e] + wc[warp * EB + e] + rank;
       a.sorted[pos] = p;
       a.inverse[p] = pos;
       __syncwarp(vmask);
-      if (rank == 0) wc[warp * E + e] += __popc(peers);
+      if (rank == 0) wc[warp * EB + e] += __popc(peers);
     }
     __syncwarp();
   }
@@ -896,13 +899,32 @@ static ExpertFn expert_fn(bool up, int kind, int tt) {
   return (ExpertFn)(tt == 8 ? pick_kernel<DownK, 8>(kind) : pick_kernel<DownK, 4>(kind));
 }
 
+// Per-row outputs of the rows mode: out[r] = ysorted[inverse[r]] (k = 1, unweighted).
+__global__ void __launch_bounds__(128) scatter_rows_kernel(ForwardArgs a) {
+  const int r = blockIdx.x, i4 = blockIdx.y * blockDim.x + threadIdx.x;
+  if (i4 >= a.H / 4) return;
+  const float4 v = *reinterpret_cast<const float4 *>(a.ysorted + (size_t)a.inverse[r] * a.H + 4 * i4);
+  *reinterpret_cast<float4 *>(a.y + (size_t)r * a.H + 4 * i4) = v;
+}
+
+// the identity position map used when pair outputs arrive already in pair order
+__global__ void iota_kernel(int32_t *v, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) v[i] = i;
+}
+
 int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
-                   const GemvPlan *gemv, const TcPlan *tc) {
+                   const GemvPlan *gemv, const TcPlan *tc, int mode) {
   int launches = 0;
+  if (mode & kRunIdentity) {  // pair outputs given in pair order (expert-parallel combine)
+    const int n = a.T * a.k + (a.shared ? a.T : 0);
+    iota_kernel<<<(n + 255) / 256, 256, 0, stream>>>(a.inverse, n);
+    launches++;
+  }
   const bool glm = a.family == kGlm;
   auto mark = [&](int stage) {
     if (ev) cudaEventRecord(ev[stage], stream);
   };
+  if (mode & kRunRoute) {
   // 1. Gemma router / expert inputs
   mark(kStagePrep);
   const void *router_x = a.x;
@@ -965,9 +987,11 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
     topk_softmax_kernel<true><<<topk_blocks, 32 * kTopkWarps, 0, stream>>>(
         a.logits, a.T, a.E1, a.E, a.k, a.sel_idx, a.sel_w, a.status);
   launches++;
+  }
+  if (mode & kRunExperts) {
   // 4. dispatch
   mark(kStageDispatch);
-  size_t dsmem = ((size_t)kDispatchWarps * a.E + 2 * (a.E + 1)) * sizeof(int32_t);
+  size_t dsmem = ((size_t)kDispatchWarps * (a.E + 1) + 2 * (a.E + 1)) * sizeof(int32_t);
   set_smem(dispatch_kernel, dsmem);
   dispatch_kernel<<<1, kDispatchThreads, dsmem, stream>>>(a);
   launches++;
@@ -1005,10 +1029,17 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
     launches++;
   }
   }
-  // 7. combine
+  }
+  // 7. combine (or the per-row outputs of the rows mode)
   mark(kStageCombine);
-  combine_kernel<<<dim3(a.T, (a.H / 4 + 127) / 128), 128, 0, stream>>>(a);
-  launches++;
+  if (mode & kRunCombine) {
+    combine_kernel<<<dim3(a.T, (a.H / 4 + 127) / 128), 128, 0, stream>>>(a);
+    launches++;
+  }
+  if (mode & kRunScatter) {
+    scatter_rows_kernel<<<dim3(a.T, (a.H / 4 + 127) / 128), 128, 0, stream>>>(a);
+    launches++;
+  }
   mark(kStageCount);
   return launches;
 }

@@ -44,6 +44,7 @@ struct ForwardArgs {
   int32_t *inverse;        // [T*k + T]
   int32_t *active;         // [E + 1] experts with tokens, ascending
   int32_t *n_active;       // [1]
+  int rows_mode;           // sel_idx are explicit expert ids (id E = shared), k = 1
   int chunk;               // tokens per work item
   int4 *items;             // [T*k + T + E + 1] work items: (expert, first token within the
                            // expert, first sorted position, tokens)
@@ -84,8 +85,18 @@ enum Stage {
 // `gemv`, when not null, runs the expert products as the GEMV kernels of dm_gemv.cu;
 // `tc`, when also given, runs them as the tcgen05 grouped GEMM of dm_tc.cu instead.
 struct TcPlan;
+// Stages run by launch_forward.
+enum RunStages : int {
+  kRunRoute = 1,     // Gemma prep, router logits, top-k
+  kRunExperts = 2,   // dispatch, gate/up, down
+  kRunCombine = 4,   // weighted combine into y
+  kRunScatter = 8,   // rows mode: per-row outputs into y
+  kRunIdentity = 16, // fill inverse with the identity (pair outputs given in pair order)
+  kRunAll = kRunRoute | kRunExperts | kRunCombine,
+};
+
 int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
-                   const GemvPlan *gemv, const TcPlan *tc = nullptr);
+                   const GemvPlan *gemv, const TcPlan *tc = nullptr, int mode = kRunAll);
 int launch_gemv(int kind, const uint8_t *w, int rows, int cols, const float *x, float *y,
                 cudaStream_t stream);
 int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float *prob,

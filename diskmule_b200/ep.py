@@ -1,0 +1,148 @@
+"""Expert parallelism: experts sharded over the ranks of a process group.
+
+Rank g holds experts [g*E/n, (g+1)*E/n) of every layer plus the replicated router and
+shared expert, and routes its own T/n tokens. One forward (the GLM block of
+src/glm52/cpu.rs:711-778 split across GPUs):
+
+  1. route the local tokens (router + top-k, global expert ids);
+  2. order the (token, slot) pairs by owning rank (stable, so pair order is kept per
+     rank) and exchange the per-rank pair counts (all-to-all);
+  3. all-to-all the token rows and the expert ids local to the receiver;
+  4. run the received rows through the local experts (unweighted outputs);
+  5. all-to-all the outputs back and put them in pair order;
+  6. run the shared expert on the local tokens and combine in selection order.
+
+The collectives are torch.distributed all_to_all_single (NCCL over NVLink on GPUs,
+gloo on CPU in the tests); the compute steps are a backend's. `CudaBackend` runs them
+through the C ABI (dm_moe_route / dm_moe_expert_rows / dm_moe_combine_rows).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def exchange_plan(sel_idx: torch.Tensor, experts: int, world: int):
+    """Destination rank of every pair, the pair order grouped by destination and the
+    per-destination counts. Pairs are p = t*k + j in row-major order of sel_idx."""
+    flat = sel_idx.reshape(-1).long()
+    per = experts // world
+    dest = torch.div(flat, per, rounding_mode="floor")
+    order = torch.argsort(dest, stable=True)
+    counts = torch.bincount(dest, minlength=world)
+    local_ids = (flat - dest * per)[order].to(torch.int32)
+    return order, counts, local_ids
+
+
+def all_to_all(send: torch.Tensor, send_counts: list[int], recv_counts: list[int], group=None):
+    """Variable-size all-to-all along dim 0 (2-byte integer rows travel as bf16 bits:
+    NCCL has no 16-bit integer type)."""
+    wire = send.view(torch.bfloat16) if send.dtype in (torch.uint16, torch.int16) else send
+    recv = wire.new_empty((sum(recv_counts),) + tuple(wire.shape[1:]))
+    dist.all_to_all_single(recv, wire.contiguous(), recv_counts, send_counts, group=group)
+    return recv.view(send.dtype) if wire is not send else recv
+
+
+class ExpertParallel:
+    """EP forward over `backend` (route, rows, expert_rows, combine, local_experts)."""
+
+    def __init__(self, backend, experts: int, top_k: int, group=None):
+        self.backend = backend
+        self.experts = experts
+        self.top_k = top_k
+        self.group = group
+        self.world = dist.get_world_size(group)
+        if experts % self.world:
+            raise ValueError(f"{experts} experts do not split over {self.world} ranks")
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        b, k = self.backend, self.top_k
+        T = x.shape[0]
+        routed = b.route(x)
+        order, counts, local_ids = exchange_plan(routed.sel_idx, self.experts, self.world)
+        counts_dev = counts.to(x.device)
+        recv_counts_dev = torch.empty_like(counts_dev)
+        dist.all_to_all_single(recv_counts_dev, counts_dev, group=self.group)
+        send_counts = counts.tolist()
+        recv_counts = recv_counts_dev.cpu().tolist()
+        rows = b.rows(x, routed)                       # [T, H] rows the experts consume
+        send_rows = rows.index_select(0, torch.div(order, k, rounding_mode="floor").to(rows.device))
+        recv_rows = all_to_all(send_rows, send_counts, recv_counts, self.group)
+        recv_ids = all_to_all(local_ids.to(x.device), send_counts, recv_counts, self.group)
+        out = b.expert_rows(recv_rows, recv_ids)       # [R, H] f32
+        back = all_to_all(out, recv_counts, send_counts, self.group)
+        P = T * k
+        shared = b.has_shared
+        pair_out = back.new_empty((P + (T if shared else 0), back.shape[1]))
+        pair_out.index_copy_(0, order.to(back.device), back)
+        if shared:
+            _, local = b.local_experts()
+            ids = torch.full((T,), local, dtype=torch.int32, device=x.device)
+            pair_out[P:] = b.expert_rows(rows, ids)
+        return b.combine(routed, pair_out)
+
+
+class Routed:
+    """The result of a backend's route step."""
+
+    def __init__(self, sel_idx, sel_w, expert_in=None, logits=None):
+        self.sel_idx, self.sel_w, self.expert_in, self.logits = sel_idx, sel_w, expert_in, logits
+
+
+class CudaBackend:
+    """The EP compute steps on a `MoeLayer` built for this rank's expert range."""
+
+    def __init__(self, layer, family: str, hidden: int, top_k: int, router_columns: int,
+                 shared: bool):
+        self.layer = layer
+        self.family = family
+        self.hidden = hidden
+        self.top_k = top_k
+        self.router_columns = router_columns
+        self.has_shared = shared
+
+    def _stream(self) -> int:
+        return torch.cuda.current_stream().cuda_stream
+
+    def local_experts(self):
+        return self.layer.local_experts()
+
+    def route(self, x: torch.Tensor) -> Routed:
+        T = x.shape[0]
+        sel_idx = torch.empty((T, self.top_k), dtype=torch.int32, device=x.device)
+        sel_w = torch.empty((T, self.top_k), dtype=torch.float32, device=x.device)
+        expert_in = (torch.empty((T, self.hidden), dtype=torch.float32, device=x.device)
+                     if self.family == "gemma4" else None)
+        logits = (torch.empty((T, self.router_columns), dtype=torch.float32, device=x.device)
+                  if self.family == "qwen35" and self.has_shared else None)
+        self.layer.route(x.data_ptr(), T, sel_idx.data_ptr(), sel_w.data_ptr(),
+                         expert_in.data_ptr() if expert_in is not None else 0,
+                         logits.data_ptr() if logits is not None else 0, self._stream())
+        return Routed(sel_idx, sel_w, expert_in, logits)
+
+    def rows(self, x: torch.Tensor, routed: Routed) -> torch.Tensor:
+        return routed.expert_in if routed.expert_in is not None else x
+
+    def expert_rows(self, rows: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+        out = torch.empty((rows.shape[0], self.hidden), dtype=torch.float32, device=rows.device)
+        if rows.shape[0]:
+            self.layer.expert_rows(rows.contiguous().data_ptr(), ids.contiguous().data_ptr(),
+                                   rows.shape[0], out.data_ptr(), self._stream())
+        return out
+
+    def combine(self, routed: Routed, pair_out: torch.Tensor) -> torch.Tensor:
+        T = routed.sel_idx.shape[0]
+        y = torch.empty((T, self.hidden), dtype=torch.float32, device=pair_out.device)
+        self.layer.combine_rows(T, routed.sel_idx.data_ptr(), routed.sel_w.data_ptr(),
+                                pair_out.contiguous().data_ptr(), y.data_ptr(),
+                                routed.logits.data_ptr() if routed.logits is not None else 0,
+                                self._stream())
+        return y
+
+
+def cuda_backend_for(sl) -> CudaBackend:
+    """Backend over a `synthetic.SyntheticLayer` built with an expert range."""
+    cfg = sl.cfg
+    shared = bool(cfg.get("shared"))
+    columns = cfg["experts"] + (1 if cfg["family"] == "qwen35" and shared else 0)
+    return CudaBackend(sl.layer, cfg["family"], cfg["hidden"], cfg["top_k"], columns, shared)

@@ -162,12 +162,19 @@ class MoeLayer:
     `desc` is a `_native.MoeDesc` whose weight fields hold device addresses.
     """
 
-    def __init__(self, ctx: CudaContext, desc: N.MoeDesc, keep_alive=()):
+    def __init__(self, ctx: CudaContext, desc: N.MoeDesc, keep_alive=(), expert_range=None):
+        """`expert_range=(first, count)`: a layer holding those experts only (the
+        desc's expert weights are that range), for expert parallelism."""
         self.ctx = ctx
         self.desc = desc
         self._keep = list(keep_alive)
         h = C.c_void_p()
-        check(N.lib().dm_moe_layer_create(ctx.handle, C.byref(desc), C.byref(h)))
+        if expert_range is None:
+            check(N.lib().dm_moe_layer_create(ctx.handle, C.byref(desc), C.byref(h)))
+        else:
+            first, count = expert_range
+            check(N.lib().dm_moe_layer_create_ep(ctx.handle, C.byref(desc), int(first), int(count),
+                                                 C.byref(h)))
         self._h = h
 
     @property
@@ -181,6 +188,35 @@ class MoeLayer:
                                       C.c_void_p(sel_idx_ptr) if sel_idx_ptr else None,
                                       C.c_void_p(sel_w_ptr) if sel_w_ptr else None,
                                       C.c_void_p(stream) if stream else None))
+
+    def local_experts(self) -> tuple[int, int]:
+        first, count = C.c_int32(), C.c_int32()
+        check(N.lib().dm_moe_local_experts(self._h, C.byref(first), C.byref(count)))
+        return first.value, count.value
+
+    def route(self, x_ptr: int, tokens: int, sel_idx_ptr: int, sel_w_ptr: int,
+              expert_in_ptr: int = 0, logits_ptr: int = 0, stream: int = 0):
+        """Router + top-k only (dm_moe_route), device pointers."""
+        check(N.lib().dm_moe_route(self._h, C.c_void_p(x_ptr), tokens, C.c_void_p(sel_idx_ptr),
+                                    C.c_void_p(sel_w_ptr),
+                                    C.c_void_p(expert_in_ptr) if expert_in_ptr else None,
+                                    C.c_void_p(logits_ptr) if logits_ptr else None,
+                                    C.c_void_p(stream) if stream else None))
+
+    def expert_rows(self, rows_ptr: int, ids_ptr: int, count: int, out_ptr: int, stream: int = 0):
+        """Unweighted expert outputs of rows on this layer's experts (dm_moe_expert_rows)."""
+        check(N.lib().dm_moe_expert_rows(self._h, C.c_void_p(rows_ptr), C.c_void_p(ids_ptr),
+                                          count, C.c_void_p(out_ptr),
+                                          C.c_void_p(stream) if stream else None))
+
+    def combine_rows(self, tokens: int, sel_idx_ptr: int, sel_w_ptr: int, pair_out_ptr: int,
+                     y_ptr: int, logits_ptr: int = 0, stream: int = 0):
+        """Weighted combine of per-pair outputs given in pair order (dm_moe_combine_rows)."""
+        check(N.lib().dm_moe_combine_rows(self._h, tokens, C.c_void_p(sel_idx_ptr),
+                                           C.c_void_p(sel_w_ptr),
+                                           C.c_void_p(logits_ptr) if logits_ptr else None,
+                                           C.c_void_p(pair_out_ptr), C.c_void_p(y_ptr),
+                                           C.c_void_p(stream) if stream else None))
 
     def forward_host(self, x: np.ndarray):
         """Synchronous forward on host arrays (dm_moe_forward_host): (y, indices, weights)."""

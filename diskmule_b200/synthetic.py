@@ -81,9 +81,9 @@ class TensorSpec:
     def nbytes(self) -> int:
         return self.experts * self.expert_bytes
 
-    def _range(self, expert: int | None):
+    def _range(self, expert: int | None, count: int = 1):
         per = self.rows * self.blocks_per_row
-        return (0, per * self.experts) if expert is None else (expert * per, per)
+        return (0, per * self.experts) if expert is None else (expert * per, per * count)
 
     def host(self, expert: int | None = None) -> np.ndarray:
         """Bytes of the whole tensor, or of one expert's slice, generated on the CPU."""
@@ -93,8 +93,9 @@ class TensorSpec:
                                            SCALE_LO, SCALE_HI, out.ctypes.data_as(C.c_void_p)))
         return out
 
-    def device_fill(self, ptr: int, expert: int | None = None, stream: int = 0):
-        first, n = self._range(expert)
+    def device_fill(self, ptr: int, expert: int | None = None, stream: int = 0, count: int = 1):
+        """Device bytes of the whole tensor, or of experts expert..expert+count-1."""
+        first, n = self._range(expert, count)
         N.check(N.lib().dm_synth_fill_device(self.kind, self.seed, first, n, self.sigma,
                                              SCALE_LO, SCALE_HI, C.c_void_p(ptr),
                                              C.c_void_p(stream) if stream else None))
@@ -225,14 +226,23 @@ class SyntheticLayer:
         self.buffers.clear()
 
 
-def build_layer(ctx: CudaContext, name: str, seed: int = 1, logit_bias=None) -> SyntheticLayer:
+def build_layer(ctx: CudaContext, name: str, seed: int = 1, logit_bias=None,
+                expert_range=None) -> SyntheticLayer:
+    """A device-resident synthetic layer. `expert_range=(first, count)` builds a shard
+    holding only those experts' weights (the same bytes as in the whole layer) for
+    expert parallelism; the router and shared expert stay whole."""
     cfg = dict(CONFIGS[name])
     specs = layer_specs(cfg, seed)
     vecs = vectors(cfg, seed)
     sl = SyntheticLayer(name, cfg, seed, ctx, specs, vecs)
     for key, spec in specs.items():
-        buf = ctx.new_owned_buffer(spec.nbytes)
-        spec.device_fill(buf.device_pointer)
+        if expert_range is not None and spec.experts > 1:
+            first, count = expert_range
+            buf = ctx.new_owned_buffer(count * spec.expert_bytes)
+            spec.device_fill(buf.device_pointer, expert=first, count=count)
+        else:
+            buf = ctx.new_owned_buffer(spec.nbytes)
+            spec.device_fill(buf.device_pointer)
         sl.buffers[key] = buf
     for key, v in vecs.items():
         sl.buffers[key] = ctx.map_read_only(v)
@@ -270,5 +280,5 @@ def build_layer(ctx: CudaContext, name: str, seed: int = 1, logit_bias=None) -> 
         d.shared_down = sl.ptr("shared_down")
         d.shared_gate_vector = sl.ptr("shared_gate_vector") or None
     d.router_logit_bias = sl.ptr("router_logit_bias") or None
-    sl.layer = MoeLayer(ctx, d)
+    sl.layer = MoeLayer(ctx, d, expert_range=expert_range)
     return sl

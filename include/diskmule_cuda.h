@@ -227,6 +227,47 @@ DM_API int32_t dm_moe_forward_noalloc(dm_moe_layer *layer, const void *x, float 
                                       int32_t tokens, uint32_t *sel_idx, float *sel_weight,
                                       void *stream);
 
+/* ---- expert parallelism --------------------------------------------------------
+ * The reference runs every expert of a layer in one process (src/glm52/cpu.rs:711-778,
+ * src/glm52/expert.rs:183-267); these calls split that block so expert weights can be
+ * sharded over GPUs, with the token rows exchanged by the caller (NCCL all-to-all):
+ *   dm_moe_route        router + top-k on local tokens (global expert ids)
+ *   dm_moe_expert_rows  gate/up/down of received rows on this GPU's experts
+ *   dm_moe_combine_rows weighted combine of the returned rows + shared expert
+ * Composed, they give the same result as dm_moe_forward on one GPU. */
+
+/* A layer holding the weights of experts [first_expert, first_expert + local_experts)
+ * only: desc->gate/up/down point at those experts (local_experts x the per-expert
+ * stride); the router, correction bias and shared expert are whole (desc->experts
+ * columns). dm_moe_forward refuses such a layer unless it holds every expert. */
+DM_API int32_t dm_moe_layer_create_ep(dm_cuda_context *ctx, const dm_moe_desc *desc,
+                                      int32_t first_expert, int32_t local_experts,
+                                      dm_moe_layer **out);
+/* Experts held by the layer. */
+DM_API int32_t dm_moe_local_experts(const dm_moe_layer *layer, int32_t *first_expert,
+                                    int32_t *count);
+/* Router logits and top-k of x [tokens, hidden] (device): sel_idx / sel_weight
+ * [tokens, top_k] as in dm_moe_forward. Optional copies: the Gemma expert inputs
+ * (expert_in [tokens, hidden] f32, the rows to send) and the router logits
+ * (logits [tokens, experts (+1 Qwen shared gate)] f32). */
+DM_API int32_t dm_moe_route(dm_moe_layer *layer, const void *x, int32_t tokens,
+                            uint32_t *sel_idx, float *sel_weight, float *expert_in,
+                            float *logits, void *stream);
+/* Expert products of `count` rows (device, [count, hidden], input_type; Gemma: the
+ * expert inputs from dm_moe_route) on this layer's experts: expert_ids[r] is the
+ * local expert of row r (0..local_experts-1) or local_experts for the shared
+ * expert. out [count, hidden] f32 receives each row's unweighted expert output. */
+DM_API int32_t dm_moe_expert_rows(dm_moe_layer *layer, const void *rows,
+                                  const int32_t *expert_ids, int32_t count, float *out,
+                                  void *stream);
+/* y [tokens, hidden] f32 = the weighted combine of pair_out, which holds the expert
+ * output of pair p = t*top_k + j in row p and the shared expert's output of token t in
+ * row tokens*top_k + t (when the layer has one); sel_idx / sel_weight / logits are
+ * dm_moe_route's (logits needed for the Qwen shared gate only). */
+DM_API int32_t dm_moe_combine_rows(dm_moe_layer *layer, int32_t tokens, const uint32_t *sel_idx,
+                                   const float *sel_weight, const float *logits,
+                                   const float *pair_out, float *y, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
