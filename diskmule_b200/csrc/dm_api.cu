@@ -44,6 +44,10 @@ int32_t cuda_fail(cudaError_t err, const char *what) {
 
 struct dm_cuda_context {
   int device = 0;
+  // Buffers and layers hold a reference: dm_cuda_destroy frees the context once the
+  // last of them is released, so a late free (a garbage collector) stays valid.
+  int refs = 0;
+  bool closed = false;
   cudaStream_t stream = nullptr;
   char name[256] = {0};
   // operator scratch (grown on demand)
@@ -133,14 +137,41 @@ int32_t dm_cuda_create(int32_t device_ordinal, dm_cuda_context **out) {
   return DM_OK;
 }
 
-void dm_cuda_destroy(dm_cuda_context *ctx) {
-  if (!ctx) return;
+static void free_context(dm_cuda_context *ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->status) cudaFree(ctx->status);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  cudaGetLastError();  // teardown leaves no error behind for unrelated calls
   delete ctx;
+}
+
+static std::mutex g_ctx_mutex;
+
+static void retain_context(dm_cuda_context *ctx) {
+  std::lock_guard<std::mutex> lock(g_ctx_mutex);
+  ctx->refs++;
+}
+
+static void release_context(dm_cuda_context *ctx) {
+  bool last = false;
+  {
+    std::lock_guard<std::mutex> lock(g_ctx_mutex);
+    last = --ctx->refs == 0 && ctx->closed;
+  }
+  if (last) free_context(ctx);
+}
+
+void dm_cuda_destroy(dm_cuda_context *ctx) {
+  if (!ctx) return;
+  bool now = false;
+  {
+    std::lock_guard<std::mutex> lock(g_ctx_mutex);
+    ctx->closed = true;
+    now = ctx->refs == 0;
+  }
+  if (now) free_context(ctx);
 }
 
 int32_t dm_cuda_device_name(const dm_cuda_context *ctx, char *name, size_t capacity) {
@@ -172,6 +203,7 @@ static int32_t new_buffer(dm_cuda_context *ctx, size_t length, bool read_only, d
     return fail(DM_ERR_ALLOCATION, "host allocation failed");
   }
   b->ctx = ctx;
+  retain_context(ctx);
   b->device = p;
   b->length = length;
   b->read_only = read_only;
@@ -237,9 +269,12 @@ void *dm_buffer_device_pointer(const dm_buffer *b) { return b ? b->device : null
 
 void dm_buffer_free(dm_buffer *b) {
   if (!b) return;
-  cudaSetDevice(b->ctx->device);
+  dm_cuda_context *ctx = b->ctx;
+  cudaSetDevice(ctx->device);
   cudaFree(b->device);
+  cudaGetLastError();
   delete b;
+  release_context(ctx);
 }
 
 // ---- operators ----
@@ -438,6 +473,7 @@ struct dm_moe_layer {
   bool shared = false;
   void *router_t = nullptr;  // transposed router [H][E1]
   float *router_dup = nullptr;  // [H][router_dup_ld(E1)] f32 router for many tokens
+  float *router_rows = nullptr; // [E1][H] f32 router rows for few tokens
   uint64_t gate_stride = 0, up_stride = 0, down_stride = 0;
   const uint8_t *up_base = nullptr;
   // scratch
@@ -493,6 +529,8 @@ int32_t validate_desc(const dm_moe_desc *d) {
     return fail(DM_ERR_INVALID_ARGUMENT, "hidden, intermediate and experts must be positive");
   if (d->hidden % 32 || d->intermediate % 32)
     return fail(DM_ERR_ELEMENT_COUNT, "hidden and intermediate must be multiples of 32");
+  if (d->hidden > 12288)
+    return fail(DM_ERR_ELEMENT_COUNT, "hidden %d is above the supported 12288", d->hidden);
   if (d->top_k <= 0 || d->top_k > d->experts || d->top_k > 32)
     return fail(DM_ERR_TOP_K, "top-k count %d is outside 1..=%d", d->top_k, std::min(d->experts, 32));
   if (d->experts > 1023) return fail(DM_ERR_INVALID_ARGUMENT, "at most 1023 experts");
@@ -749,6 +787,7 @@ static int32_t create_layer(dm_cuda_context *ctx, const dm_moe_desc *desc, int32
   auto *L = new (std::nothrow) dm_moe_layer();
   if (!L) return fail(DM_ERR_ALLOCATION, "host allocation failed");
   L->ctx = ctx;
+  retain_context(ctx);
   L->desc = *desc;
   L->first_expert = first_expert;
   L->local_experts = local_experts;
@@ -767,12 +806,20 @@ static int32_t create_layer(dm_cuda_context *ctx, const dm_moe_desc *desc, int32
   L->down_stride = H * dm::row_bytes(d.down_type, I);
   const int wbytes = d.router_type == DM_BF16 ? 2 : 4;
   if (cudaMalloc(&L->router_t, (size_t)H * dm::router_ld(L->E1) * wbytes) != cudaSuccess) {
-    delete L;
+    L->router_t = nullptr;
+    dm_moe_layer_destroy(L);
     return fail(DM_ERR_ALLOCATION, "could not allocate the transposed router");
   }
   dm::launch_transpose_router(d.router, d.router_type == DM_BF16, d.experts, d.hidden,
                               qwen_gate ? d.shared_gate_vector : nullptr, L->router_t,
                               ctx->stream);
+  if (cudaMalloc(&L->router_rows, (size_t)L->E1 * H * sizeof(float)) != cudaSuccess) {
+    L->router_rows = nullptr;
+    dm_moe_layer_destroy(L);
+    return fail(DM_ERR_ALLOCATION, "could not allocate the router rows");
+  }
+  dm::launch_router_rows(d.router, d.router_type == DM_BF16, d.experts, d.hidden,
+                         qwen_gate ? d.shared_gate_vector : nullptr, L->router_rows, ctx->stream);
   if (cudaMalloc(&L->router_dup, (size_t)H * dm::router_dup_ld(L->E1) * sizeof(float)) ==
       cudaSuccess)
     dm::launch_dup_router(L->router_t, d.router_type == DM_BF16, (int)H, L->E1, L->router_dup,
@@ -809,6 +856,7 @@ void dm_moe_layer_destroy(dm_moe_layer *L) {
   cudaStreamSynchronize(L->ctx->stream);
   if (L->router_t) cudaFree(L->router_t);
   if (L->router_dup) cudaFree(L->router_dup);
+  if (L->router_rows) cudaFree(L->router_rows);
   if (L->scratch) cudaFree(L->scratch);
   if (L->io) cudaFree(L->io);
   for (auto &e : L->events)
@@ -816,7 +864,10 @@ void dm_moe_layer_destroy(dm_moe_layer *L) {
   for (void *p : L->owned) cudaFree(p);
   L->drop_graphs();
   if (L->capture) cudaStreamDestroy(L->capture);
+  cudaGetLastError();  // teardown leaves no error behind for unrelated calls
+  dm_cuda_context *ctx = L->ctx;
   delete L;
+  release_context(ctx);
 }
 
 int32_t dm_moe_set_profiling(dm_moe_layer *L, int32_t enable) {
@@ -873,6 +924,7 @@ dm::ForwardArgs fill_args(dm_moe_layer *L, const void *x, float *y, int32_t toke
   a.router_bf16 = d.router_type == DM_BF16;
   a.router_t = L->router_t;
   a.router_dup = L->router_dup;
+  a.router_rows = L->router_rows;
   a.bias = d.correction_bias;
   a.router_scale = d.router_scale;
   a.routed_pre_norm = d.routed_pre_norm;
@@ -1283,6 +1335,7 @@ extern "C" int32_t dm_moe_forward_noalloc(dm_moe_layer *L, const void *x, float 
   a.y = y;
   a.router_bf16 = d.router_type == DM_BF16;
   a.router_t = L->router_t;
+  a.router_rows = L->router_rows;
   a.bias = d.correction_bias;
   a.router_scale = d.router_scale;
   a.routed_pre_norm = d.routed_pre_norm;

@@ -363,6 +363,26 @@ __device__ __forceinline__ void stage_rows(float *xs, float *s16, int K, int gro
 
 __device__ __forceinline__ float act_fn(const ForwardArgs &a, int expert, float g, float u);
 
+// Ask L2 for the bytes of this thread's first task before x is staged, so the weight
+// fetch from HBM overlaps the staging and the barriers.
+template <int KIND>
+__device__ __forceinline__ void prefetch_task(const MatrixRef &m, int expert, int row, int task) {
+  const uint8_t *p;
+  int bytes;
+  if (KIND == DM_Q6_K || KIND == DM_Q5_0 || KIND == DM_Q8_0) {
+    const int nb = (int)(m.row_bytes / (KIND == DM_Q6_K ? 210 : (KIND == DM_Q5_0 ? 22 : 34)));
+    const uint64_t g = ((uint64_t)expert * m.rows + row) * nb + task;
+    const int qb = KIND == DM_Q6_K ? 208 : (KIND == DM_Q5_0 ? 16 : 32);
+    p = m.split.quant + g * qb;
+    bytes = qb * (KIND == DM_Q6_K ? 1 : Task<KIND>::kElems / 32);
+  } else {
+    const int tb = KIND == DM_Q4_K ? 144 : Task<KIND>::kElems * (KIND == DM_F32 ? 4 : 2);
+    p = m.base + (uint64_t)expert * m.stride + (uint64_t)row * m.row_bytes + (uint64_t)task * tb;
+    bytes = tb;
+  }
+  for (int o = 0; o < bytes; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + o));
+}
+
 template <int KIND, int NT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_up_kernel(ForwardArgs a, MatrixRef gate,
                                                               MatrixRef up, MatrixRef sh_gate,
@@ -390,6 +410,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_up_kernel(ForwardArgs a, Ma
   const int ex = shared ? 0 : e;
   const int tasks = 2 * nrows * nb;
   const int P = a.T * a.k;
+  if ((int)threadIdx.x < tasks) {
+    const int which = threadIdx.x / (nrows * nb), rem = threadIdx.x - which * nrows * nb;
+    prefetch_task<KIND>(which ? U : G, ex, i0 + rem / nb + (which ? up_row_offset : 0), rem % nb);
+  }
   stage_rows<NT>(xs, s16, H, kTask, nt, [&](int t, int k) {
     int pair = a.sorted[base + c0 + t];
     int tok = pair < P ? pair / a.k : pair - P;
@@ -451,6 +475,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_down_kernel(ForwardArgs a, 
   const MatrixRef &D = shared ? sh_down : down;
   const int ex = shared ? 0 : e;
   const int tasks = nrows * nb;
+  if ((int)threadIdx.x < tasks) prefetch_task<KIND>(D, ex, r0 + threadIdx.x / nb, threadIdx.x % nb);
   stage_rows<NT>(xs, s16, I, kTask, nt,
                  [&](int t, int k) {
                    return *reinterpret_cast<const float4 *>(a.h + (size_t)(base + c0 + t) * I + k);

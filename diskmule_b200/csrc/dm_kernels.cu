@@ -156,35 +156,55 @@ __device__ __forceinline__ float chain_step(float w, float x, float s) {
   return __fmaf_rn(w, x, s);
 }
 
-// Few tokens: a CTA stages the [H][8] column tile of the transposed router ([H][ld],
-// ld a multiple of 8 so each tile row is one 16- or 32-byte vector) and up to RT
-// token rows in shared memory with vector loads, then 8*RT threads run the chains.
+// Few tokens: a CTA owns 8 experts and up to RT tokens; 8*RT threads run the sequential
+// chains. The experts' router rows ([E1][H] f32 copy made at set-up, so one row is
+// contiguous) are requested up front with cp.async in chunks of kRsChunk columns, each
+// chunk completing an mbarrier, and land in rows padded by 16 bytes (the 8 threads of a
+// token read 8 rows at the same column without bank conflicts). A chain thread reads 4
+// weights and 4 inputs per 16-byte load, so the chain runs at the FMA latency.
 constexpr int kSmallExperts = 8;
+constexpr int kRsChunk = 256;
+constexpr int kRsMaxChunks = 48;  // H <= 12288
 
-template <bool GLM, bool WBF16, bool XBF16>
-__global__ void __launch_bounds__(256) router_small_kernel(const void *wt, int ld, const void *x,
-                                                          int T, int H, int E1, int RT,
+__device__ __forceinline__ void rs_cp16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+template <bool GLM, bool XBF16>
+__global__ void __launch_bounds__(256) router_small_kernel(const float *rows, const void *x, int T,
+                                                          int H, int E1, int RT,
                                                           const float *lbias, int E,
-                                                          float *logits) {
+                                                          float *logits, int32_t *status) {
   extern __shared__ __align__(16) float smem[];
-  const int HP = H + 4;                                     // 16-byte aligned rows
+  __shared__ __align__(8) unsigned long long bars[kRsMaxChunks];
+  const int HP = H + 4;                                     // padded rows (16 bytes)
   float *xs = smem;                                         // [RT][H + 4]
-  float *ws32 = xs + RT * HP;                               // [H][8] f32
-  uint16_t *ws16 = reinterpret_cast<uint16_t *>(ws32);      // [H][8] bf16
+  float *ws = xs + RT * HP;                                 // [8][H + 4]
   const int e0 = blockIdx.x * kSmallExperts, t0 = blockIdx.y * RT;
   const int nt = min(RT, T - t0);
-  if (WBF16) {
-    const uint16_t *w = reinterpret_cast<const uint16_t *>(wt) + e0;
-#pragma unroll 4
-    for (int h = threadIdx.x; h < H; h += blockDim.x)
-      reinterpret_cast<uint4 *>(ws16)[h] = *reinterpret_cast<const uint4 *>(w + (size_t)h * ld);
-  } else {
-    const float *w = reinterpret_cast<const float *>(wt) + e0;
-#pragma unroll 4
-    for (int i = threadIdx.x; i < 2 * H; i += blockDim.x)
-      reinterpret_cast<float4 *>(ws32)[i] =
-          *reinterpret_cast<const float4 *>(w + (size_t)(i >> 1) * ld + 4 * (i & 1));
+  const int ne = min(kSmallExperts, E1 - e0);
+  const int nchunks = (H + kRsChunk - 1) / kRsChunk;
+  const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(bars);
+  if (threadIdx.x == 0) {
+    for (int c = 0; c < nchunks; c++)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar0 + 8 * c), "r"(blockDim.x));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  __syncthreads();
+  // router rows: every thread copies its pieces of each chunk, then arms the chunk's barrier
+  const uint32_t wbase = (uint32_t)__cvta_generic_to_shared(ws);
+  constexpr int kPieces = kRsChunk / 4;                     // 16-byte pieces per row chunk
+  for (int c = 0; c < nchunks; c++) {
+    const int h0 = c * kRsChunk, pieces = min(kRsChunk, H - h0) / 4;
+    for (int i = threadIdx.x; i < ne * kPieces; i += blockDim.x) {
+      const int el = i / kPieces, piece = i % kPieces;
+      if (piece < pieces)
+        rs_cp16(wbase + (uint32_t)(el * HP + h0 + 4 * piece) * 4,
+                rows + (size_t)(e0 + el) * H + h0 + 4 * piece);
+    }
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar0 + 8 * c) : "memory");
+  }
+  // token rows (converted to f32) while the router rows stream in
   for (int i = threadIdx.x; i < nt * (H / 4); i += blockDim.x) {
     const int tt = i / (H / 4), c = i - tt * (H / 4);
     float4 v;
@@ -199,19 +219,79 @@ __global__ void __launch_bounds__(256) router_small_kernel(const void *wt, int l
     }
     *reinterpret_cast<float4 *>(xs + tt * HP + 4 * c) = v;
   }
-  __syncthreads();
+  __syncthreads();  // token rows staged
   const int el = threadIdx.x % kSmallExperts, tl = threadIdx.x / kSmallExperts;
-  if (tl < nt && e0 + el < E1) {
+  if (tl < nt && el < ne) {
     const float *xr = xs + tl * HP;
+    const float *wr = ws + el * HP;
     float s = GLM ? -0.0f : 0.0f;
-#pragma unroll 16
-    for (int h = 0; h < H; h++) {
-      float w = WBF16 ? bf16_bits_to_f32(ws16[h * kSmallExperts + el]) : ws32[h * kSmallExperts + el];
-      s = chain_step<GLM>(w, xr[h], s);
+    for (int c = 0; c < nchunks; c++) {
+      // bounded wait for chunk c (its copies complete by themselves)
+      const long long start = clock64();
+      uint32_t done = 0;
+      while (!done) {
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(bar0 + 8 * c)
+            : "memory");
+        if (!done && clock64() - start > 200000000ll) {
+          atomicExch(status, kStatusTimeout);
+          break;
+        }
+      }
+      const int h0 = c * kRsChunk, h1 = min(H, h0 + kRsChunk);
+      // 16 steps per round; the next round's operands are loaded before this round's
+      // FMAs so the shared-memory latency hides behind the chain (H % 32 == 0)
+      float4 w[4], xv[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        w[i] = *reinterpret_cast<const float4 *>(wr + h0 + 4 * i);
+        xv[i] = *reinterpret_cast<const float4 *>(xr + h0 + 4 * i);
+      }
+      for (int h = h0; h < h1; h += 16) {
+        float4 wn[4], xn[4];
+        const int hn = h + 16 < h1 ? h + 16 : h;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          wn[i] = *reinterpret_cast<const float4 *>(wr + hn + 4 * i);
+          xn[i] = *reinterpret_cast<const float4 *>(xr + hn + 4 * i);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          s = chain_step<GLM>(w[i].x, xv[i].x, s);
+          s = chain_step<GLM>(w[i].y, xv[i].y, s);
+          s = chain_step<GLM>(w[i].z, xv[i].z, s);
+          s = chain_step<GLM>(w[i].w, xv[i].w, s);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) w[i] = wn[i], xv[i] = xn[i];
+      }
     }
     if (lbias && e0 + el < E) s = __fadd_rn(s, lbias[e0 + el]);
     logits[(size_t)(t0 + tl) * E1 + e0 + el] = s;
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// router [E][H] (f32 or bf16) + optional extra row (Qwen shared gate) -> [E1][H] f32
+__global__ void router_rows_kernel(const void *src, int bf16, int E, int H, const float *extra,
+                                   float *dst) {
+  const size_t n = (size_t)(E + (extra ? 1 : 0)) * H;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = idx / H, h = idx % H;
+    dst[idx] = e < (size_t)E ? load_as_f32(src, idx, bf16 != 0) : extra[h];
+  }
+}
+
+int launch_router_rows(const void *router, int bf16, int E, int H, const float *extra_col,
+                       float *dst, cudaStream_t stream) {
+  const size_t n = (size_t)(E + (extra_col ? 1 : 0)) * H;
+  router_rows_kernel<<<(int)std::min<size_t>((n + 255) / 256, 4096), 256, 0, stream>>>(
+      router, bf16, E, H, extra_col, dst);
+  return 1;
 }
 
 // Many tokens: register-tiled SIMT matmul. A CTA computes a 32-token x 64-expert tile;
@@ -435,6 +515,69 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_softmax_kernel(
     for (int r = 0; r < k; r++) {
       sel_idx[(size_t)t * k + r] = idxs[r];
       sel_w[(size_t)t * k + r] = __fdiv_rn(vals[r], sum);
+    }
+  }
+}
+
+// softmax family for the forward (E <= 1023): one CTA per token, one thread per logit.
+// Two-level rank selection: each thread ranks its key within its warp (shuffles), each
+// warp's k best become candidates, and every candidate's rank among all candidates is
+// its selection position (keys are unique: value, then lower index). Then the
+// reference's softmax over the k winners (src/cpu.rs:196-231: max, exp, sequential sum
+// in selection order, divide).
+__global__ void __launch_bounds__(1024) topk_rank_softmax_kernel(const float *logits, int T, int E1,
+                                                                int E, int k, uint32_t *sel_idx,
+                                                                float *sel_w, int32_t *status) {
+  __shared__ unsigned long long cand[32 * 32];
+  __shared__ unsigned long long chosen[32];
+  __shared__ int bad_s;
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  if (tid == 0) bad_s = 0;
+  __syncthreads();
+  const float v = tid < E ? logits[(size_t)t * E1 + tid] : 0.0f;
+  if (tid < E && !isfinite(v)) bad_s = 1;
+  const unsigned long long key = tid < E ? rank_key(v, (uint32_t)tid) : 0ull;
+  int wr = 0;
+#pragma unroll
+  for (int j = 0; j < 32; j++) wr += __shfl_sync(0xffffffffu, key, j) > key ? 1 : 0;
+  if (wr < k) cand[warp * k + wr] = key;
+  __syncthreads();
+  if (bad_s) {
+    // flag the error and leave an in-range selection so later kernels stay in bounds
+    if (tid == 0) atomicExch(status, kStatusNonFiniteRouter);
+    if (tid < k) {
+      sel_idx[(size_t)t * k + tid] = (uint32_t)tid;
+      sel_w[(size_t)t * k + tid] = 0.0f;
+    }
+    return;
+  }
+  const int C = nwarps * k;
+  for (int c = tid; c < C; c += blockDim.x) {
+    const unsigned long long mine = cand[c];
+    int r = 0;
+    for (int j = 0; j < C; j++) r += cand[j] > mine ? 1 : 0;
+    if (r < k) chosen[r] = mine;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float val = -INFINITY;
+    uint32_t idx = 0;
+    if (lane < k) {
+      const unsigned long long best = chosen[lane];
+      idx = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+      const int32_t kb = (int32_t)((uint32_t)(best >> 32) ^ 0x80000000u);
+      val = __int_as_float(kb ^ (int32_t)(((uint32_t)(kb >> 31)) >> 1));
+    }
+    float m = val;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float ex = lane < k ? exp_f32_cr(__fsub_rn(val, m)) : 0.0f;
+    float sum = 0.0f;
+    for (int r = 0; r < k; r++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, r));
+    if (lane < k) {
+      sel_idx[(size_t)t * k + lane] = idx;
+      sel_w[(size_t)t * k + lane] = __fdiv_rn(ex, sum);
     }
   }
 }
@@ -816,7 +959,9 @@ __global__ void __launch_bounds__(kExpertThreads) expert_down_kernel(ForwardArgs
 // weighted combine: selection order, deterministic, no atomics
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(128) combine_kernel(ForwardArgs a) {
+constexpr int kCombineThreads = 64;
+
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(ForwardArgs a) {
   __shared__ int pos_s[32];
   __shared__ float w_s[32];
   __shared__ float gate_s;
@@ -836,17 +981,26 @@ __global__ void __launch_bounds__(128) combine_kernel(ForwardArgs a) {
   const int i4 = blockIdx.y * blockDim.x + threadIdx.x;
   if (i4 < H / 4) {
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 4
-    for (int j = 0; j < k; j++) {
-      const float4 v = *reinterpret_cast<const float4 *>(a.ysorted + (size_t)pos_s[j] * H + 4 * i4);
-      const float vv[4] = {v.x, v.y, v.z, v.w};
-      const float w = w_s[j];
+    // selection order; the rows of up to 8 pairs are loaded before they are added
+    for (int j0 = 0; j0 < k; j0 += 8) {
+      float4 v[8];
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        if (a.family == kGlm)
-          acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn(vv[c], w), a.routed_scale));
-        else
-          acc[c] = __fmaf_rn(vv[c], w, acc[c]);
+      for (int j = 0; j < 8; j++)
+        if (j0 + j < k)
+          v[j] = *reinterpret_cast<const float4 *>(a.ysorted + (size_t)pos_s[j0 + j] * H + 4 * i4);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        if (j0 + j < k) {
+          const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+          const float w = w_s[j0 + j];
+#pragma unroll
+          for (int c = 0; c < 4; c++) {
+            if (a.family == kGlm)
+              acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn(vv[c], w), a.routed_scale));
+            else
+              acc[c] = __fmaf_rn(vv[c], w, acc[c]);
+          }
+        }
       }
     }
     if (a.shared) {
@@ -899,6 +1053,84 @@ static ExpertFn expert_fn(bool up, int kind, int tt) {
   return (ExpertFn)(tt == 8 ? pick_kernel<DownK, 8>(kind) : pick_kernel<DownK, 4>(kind));
 }
 
+// The same dispatch for at most kSmallPairs pairs (decode) with one warp: bucket counts
+// in shared memory, one segmented warp scan over the E + 1 buckets for the offsets,
+// the active list and the work items, and each pair's position from the pairs before
+// it with the same expert (stable: expert, then pair index).
+constexpr int kSmallPairs = 64;
+
+__global__ void __launch_bounds__(32) dispatch_small_kernel(ForwardArgs a) {
+  extern __shared__ int32_t cnt[];  // [E + 1]
+  const int E = a.E, P = a.T * a.k, lane = threadIdx.x;
+  const int EB = E + (a.rows_mode ? 1 : 0);
+  for (int e = lane; e <= E; e += 32) cnt[e] = 0;
+  __syncwarp();
+  uint32_t mine[kSmallPairs / 32];
+#pragma unroll
+  for (int j = 0; j < kSmallPairs / 32; j++) {
+    const int p = lane + 32 * j;
+    uint32_t e = p < P ? a.sel_idx[p] : 0xffffffffu;
+    if (p < P && e >= (uint32_t)EB) e = 0;  // rejected upstream; keep indices in range
+    mine[j] = e;
+    if (p < P) atomicAdd(&cnt[e], 1);
+  }
+  __syncwarp();
+  if (a.shared && lane == 0) cnt[E] = a.T;
+  __syncwarp();
+  // rounds of 32 consecutive buckets (bucket e on lane e % 32): a warp scan per round plus
+  // the running totals, so every store of a round is one coalesced access
+  int c_run = 0, a_run = 0, i_run = 0;
+  for (int e0 = 0; e0 <= E; e0 += 32) {
+    const int e = e0 + lane;
+    const int c = e <= E ? cnt[e] : 0;
+    const int items = (c + a.chunk - 1) / a.chunk;
+    int c_inc = c, a_inc = c > 0, i_inc = items;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int cc = __shfl_up_sync(0xffffffffu, c_inc, o);
+      const int ac = __shfl_up_sync(0xffffffffu, a_inc, o);
+      const int ic = __shfl_up_sync(0xffffffffu, i_inc, o);
+      if (lane >= o) c_inc += cc, a_inc += ac, i_inc += ic;
+    }
+    const int c_off = c_run + c_inc - c, a_off = a_run + a_inc - (c > 0), i_off = i_run + i_inc - items;
+    if (e <= E) {
+      a.counts[e] = c;
+      a.offsets[e] = c_off;
+      if (c > 0) a.active[a_off] = e;
+      for (int j = 0; j < items; j++)
+        a.items[i_off + j] = make_int4(e, j * a.chunk, c_off + j * a.chunk, min(a.chunk, c - j * a.chunk));
+      cnt[e] = c_off;  // becomes the bucket's first position
+    }
+    c_run += __shfl_sync(0xffffffffu, c_inc, 31);
+    a_run += __shfl_sync(0xffffffffu, a_inc, 31);
+    i_run += __shfl_sync(0xffffffffu, i_inc, 31);
+  }
+  const int tot_c = c_run, tot_a = a_run, tot_i = i_run;
+  if (lane == 0) {
+    a.offsets[E + 1] = tot_c;
+    *a.n_active = tot_a;
+    *a.n_items = tot_i;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < kSmallPairs / 32; j++) {
+    const int p = lane + 32 * j;
+    if (p < P) {
+      const uint32_t e = mine[j];
+      int before = 0;
+      for (int q = 0; q < p; q++) before += a.sel_idx[q] == e || (a.sel_idx[q] >= (uint32_t)EB && e == 0);
+      const int pos = cnt[e] + before;
+      a.sorted[pos] = p;
+      a.inverse[p] = pos;
+    }
+  }
+  if (a.shared)
+    for (int t = lane; t < a.T; t += 32) {
+      a.sorted[P + t] = P + t;
+      a.inverse[P + t] = P + t;
+    }
+}
+
 // Per-row outputs of the rows mode: out[r] = ysorted[inverse[r]] (k = 1, unweighted).
 __global__ void __launch_bounds__(128) scatter_rows_kernel(ForwardArgs a) {
   const int r = blockIdx.x, i4 = blockIdx.y * blockDim.x + threadIdx.x;
@@ -941,21 +1173,20 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   mark(kStageRouter);
   if (a.T <= 16 || !a.xT || !a.router_dup || a.H % kRgChunk) {
     int RT = 4;
-    size_t wbytes = (size_t)a.H * kSmallExperts * (a.router_bf16 ? 2 : 4);
-    while (RT > 1 && wbytes + (size_t)RT * (a.H + 4) * 4 > 200 * 1024) RT >>= 1;
-    size_t smem = wbytes + (size_t)RT * (a.H + 4) * 4;
+    auto bytes = [&](int rt) { return ((size_t)rt + kSmallExperts) * (a.H + 4) * 4; };
+    while (RT > 1 && bytes(RT) > 200 * 1024) RT >>= 1;
+    const size_t smem = bytes(RT);
     dim3 grid((a.E1 + kSmallExperts - 1) / kSmallExperts, (a.T + RT - 1) / RT);
-#define DM_ROUTER_SMALL(G, W, X)                                                            \
+#define DM_ROUTER_SMALL(G, X)                                                               \
   {                                                                                         \
-    auto fn = router_small_kernel<G, W, X>;                                                 \
+    auto fn = router_small_kernel<G, X>;                                                    \
     set_smem(fn, smem);                                                                     \
-    fn<<<grid, 256, smem, stream>>>(a.router_t, router_ld(a.E1), router_x, a.T, a.H, a.E1, RT, a.logit_bias, a.E, a.logits);    \
+    fn<<<grid, 256, smem, stream>>>(a.router_rows, router_x, a.T, a.H, a.E1, RT, a.logit_bias, \
+                                    a.E, a.logits, a.status);                               \
   }
-    if (glm && a.router_bf16 && router_x_bf16) DM_ROUTER_SMALL(true, true, true)
-    else if (glm && a.router_bf16) DM_ROUTER_SMALL(true, true, false)
-    else if (glm && router_x_bf16) DM_ROUTER_SMALL(true, false, true)
-    else if (glm) DM_ROUTER_SMALL(true, false, false)
-    else DM_ROUTER_SMALL(false, false, false)
+    if (glm && router_x_bf16) DM_ROUTER_SMALL(true, true)
+    else if (glm) DM_ROUTER_SMALL(true, false)
+    else DM_ROUTER_SMALL(false, false)
 #undef DM_ROUTER_SMALL
   } else {
     const int xld = (a.T + kRgTokens - 1) / kRgTokens * kRgTokens;
@@ -984,16 +1215,20 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
         a.logits, a.T, a.E1, a.E, a.k, a.bias, a.n_groups, a.topk_groups, a.normalize,
         a.sel_idx, a.sel_w, a.status);
   else
-    topk_softmax_kernel<true><<<topk_blocks, 32 * kTopkWarps, 0, stream>>>(
+    topk_rank_softmax_kernel<<<a.T, 32 * ((a.E + 31) / 32), 0, stream>>>(
         a.logits, a.T, a.E1, a.E, a.k, a.sel_idx, a.sel_w, a.status);
   launches++;
   }
   if (mode & kRunExperts) {
   // 4. dispatch
   mark(kStageDispatch);
-  size_t dsmem = ((size_t)kDispatchWarps * (a.E + 1) + 2 * (a.E + 1)) * sizeof(int32_t);
-  set_smem(dispatch_kernel, dsmem);
-  dispatch_kernel<<<1, kDispatchThreads, dsmem, stream>>>(a);
+  if (a.T * a.k <= kSmallPairs) {
+    dispatch_small_kernel<<<1, 32, (size_t)(a.E + 1) * sizeof(int32_t), stream>>>(a);
+  } else {
+    size_t dsmem = ((size_t)kDispatchWarps * (a.E + 1) + 2 * (a.E + 1)) * sizeof(int32_t);
+    set_smem(dispatch_kernel, dsmem);
+    dispatch_kernel<<<1, kDispatchThreads, dsmem, stream>>>(a);
+  }
   launches++;
   // 5. gate/up (+activation) and 6. down, over the active experts
   const int max_active = std::min(a.E + (a.shared ? 1 : 0), a.T * a.k + (a.shared ? 1 : 0));
@@ -1033,7 +1268,8 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   // 7. combine (or the per-row outputs of the rows mode)
   mark(kStageCombine);
   if (mode & kRunCombine) {
-    combine_kernel<<<dim3(a.T, (a.H / 4 + 127) / 128), 128, 0, stream>>>(a);
+    combine_kernel<<<dim3(a.T, (a.H / 4 + kCombineThreads - 1) / kCombineThreads), kCombineThreads, 0,
+                     stream>>>(a);
     launches++;
   }
   if (mode & kRunScatter) {

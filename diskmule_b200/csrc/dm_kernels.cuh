@@ -26,6 +26,7 @@ struct ForwardArgs {
   const float *router_scale, *routed_pre_norm, *expert_scale;
   const float *logit_bias; // optional [E], softmax families
   const float *router_dup; // [H][router_dup_ld] f32 router copy (many tokens), or null
+  const float *router_rows;  // [E1][H] f32 router rows (few tokens)
   float *xT;               // [H][T rounded up to 32][2] transposed, duplicated router input
   // experts
   int gate_type, up_type, down_type;
@@ -103,6 +104,9 @@ int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float 
                         int32_t *status, cudaStream_t stream);
 int launch_elementwise(int op, const float *a, const float *b, float *out, int n,
                        float eps, cudaStream_t stream);
+// router [E][H] (+ the Qwen shared-gate row) -> [E1][H] f32 rows (layer set-up)
+int launch_router_rows(const void *router, int bf16, int E, int H, const float *extra_col,
+                       float *dst, cudaStream_t stream);
 // [H][ld] router -> [H][router_dup_ld] f32 (layer set-up)
 int launch_dup_router(const void *router_t, int bf16, int H, int E1, float *dst,
                       cudaStream_t stream);
