@@ -1,4 +1,5 @@
-"""ctypes declarations of the C ABI (include/diskmule_cuda.h, include/diskmule_synth.h).
+"""ctypes declarations of the C ABI (include/diskmule_cuda.h, include/diskmule_stack.h,
+include/diskmule_synth.h).
 
 The product path is the CUDA library `libdiskmule_cuda.so` built next to this file.
 Nothing here falls back to a CPU implementation: if the library is missing the
@@ -38,6 +39,7 @@ ERR_POSITIVE_PARAMETER = -21
 ERR_TIMEOUT = -22
 ERR_NOT_BUILT = -23
 ERR_COMMUNICATOR = -24
+ERR_IO = -25
 
 # dm_tensor_type (GGML ids)
 F32, F16, Q5_0, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 6, 8, 12, 14, 30
@@ -66,6 +68,27 @@ class MoeDesc(C.Structure):
         ("router_logit_bias", P),
     ]
 
+
+class ExpertLayout(C.Structure):
+    """dm_expert_layout: one layer's experts in a host source."""
+    _fields_ = [
+        ("expert_count", I32), ("tensor_count", I32),
+        ("bytes", C.c_uint64 * 4), ("offset", C.c_uint64 * 4),
+        ("host", P), ("expert_host", C.POINTER(P)),
+    ]
+
+
+class ExpertCacheStats(C.Structure):
+    """dm_expert_cache_stats (ExpertCacheStats, src/expert.rs:53-62)."""
+    _fields_ = [
+        ("hits", C.c_uint64), ("misses", C.c_uint64), ("evictions", C.c_uint64),
+        ("reads", C.c_uint64), ("bytes_read", C.c_uint64), ("io_wait_ns", C.c_uint64),
+        ("resident_bytes", C.c_uint64), ("h2d_bytes", C.c_uint64), ("fills", C.c_uint64),
+    ]
+
+
+# int64_t read(void *user, int32_t layer, int32_t expert, int32_t tensor, void *dst, uint64_t n)
+READ_FN = C.CFUNCTYPE(C.c_int64, P, I32, I32, I32, P, C.c_uint64)
 
 # Every symbol the headers declare, with its ctypes signature.
 SIGNATURES = {
@@ -103,6 +126,28 @@ SIGNATURES = {
     "dm_moe_route": ([P, P, I32, P, P, P, P, P], I32),
     "dm_moe_expert_rows": ([P, P, P, I32, P, P], I32),
     "dm_moe_combine_rows": ([P, I32, P, P, P, P, P, P], I32),
+    "dm_cuda_host_alloc": ([P, SZ, C.POINTER(P)], I32),
+    "dm_cuda_host_free": ([P, P], None),
+    "dm_cuda_host_register": ([P, P, SZ], I32),
+    "dm_cuda_host_unregister": ([P, P], I32),
+    "dm_expert_cache_create": ([P, C.POINTER(ExpertLayout), I32, I32, I32, C.POINTER(P)], I32),
+    "dm_expert_cache_set_reader": ([P, READ_FN, P], I32),
+    "dm_expert_cache_destroy": ([P], None),
+    "dm_expert_cache_slots_per_layer": ([P], I32),
+    "dm_expert_cache_slot_memory": ([P, I32, I32, C.POINTER(P), C.POINTER(C.c_uint64)], I32),
+    "dm_expert_cache_acquire": ([P, I32, I32, C.POINTER(I32), C.POINTER(I32), C.POINTER(I32)], I32),
+    "dm_expert_cache_wait_slot": ([P, I32, I32, P], I32),
+    "dm_expert_cache_release_slot": ([P, I32, I32, P], I32),
+    "dm_expert_cache_set_pinned": ([P, I32, I32, I32], I32),
+    "dm_expert_cache_slot_expert": ([P, I32, I32, C.POINTER(I32)], I32),
+    "dm_expert_cache_read_slot": ([P, I32, I32, I32, P, C.c_uint64], I32),
+    "dm_expert_cache_get_stats": ([P, C.POINTER(ExpertCacheStats)], I32),
+    "dm_expert_cache_synchronize": ([P], I32),
+    "dm_moe_layer_create_cached": ([P, C.POINTER(MoeDesc), P, I32, C.POINTER(P)], I32),
+    "dm_moe_forward_cached": ([P, P, P, I32, P, P, C.POINTER(I32), P], I32),
+    "dm_stack_embed": ([P, P, I32, I32, I32, P, P, P, P], I32),
+    "dm_stack_add_rms_norm": ([P, P, P, P, I32, C.c_float, P, P, P], I32),
+    "dm_stack_lm_head_argmax": ([P, P, I32, I32, I32, P, P, P, P, P], I32),
     "dm_synth_fill_host": ([I32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float,
                             C.c_float, P], I32),
     "dm_synth_fill_device": ([I32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float,

@@ -15,10 +15,9 @@
 #include <vector>
 
 #include "../../include/diskmule_cuda.h"
-#include "dm_kernels.cuh"
-#include "dm_tc.cuh"
+#include "dm_internal.cuh"
 
-namespace {
+namespace dmi {
 
 thread_local char g_message[512] = "";
 
@@ -34,47 +33,13 @@ int32_t cuda_fail(cudaError_t err, const char *what) {
   return fail(DM_ERR_COMMAND, "%s: %s", what, cudaGetErrorString(err));
 }
 
-#define DM_CUDA(call, what)                        \
-  do {                                             \
-    cudaError_t err__ = (call);                    \
-    if (err__ != cudaSuccess) return cuda_fail(err__, what); \
-  } while (0)
+}  // namespace dmi
 
-}  // namespace
-
-struct dm_cuda_context {
-  int device = 0;
-  // Buffers and layers hold a reference: dm_cuda_destroy frees the context once the
-  // last of them is released, so a late free (a garbage collector) stays valid.
-  int refs = 0;
-  bool closed = false;
-  cudaStream_t stream = nullptr;
-  char name[256] = {0};
-  // operator scratch (grown on demand)
-  void *scratch = nullptr;
-  size_t scratch_bytes = 0;
-  int32_t *status = nullptr;
-
-  int32_t ensure_scratch(size_t bytes) {
-    if (bytes <= scratch_bytes) return DM_OK;
-    if (scratch) cudaFree(scratch);
-    scratch = nullptr;
-    scratch_bytes = 0;
-    size_t want = std::max(bytes, (size_t)1 << 20);
-    cudaError_t err = cudaMalloc(&scratch, want);
-    if (err != cudaSuccess)
-      return fail(DM_ERR_ALLOCATION, "could not allocate a %zu-byte device buffer", want);
-    scratch_bytes = want;
-    return DM_OK;
-  }
-};
-
-struct dm_buffer {
-  dm_cuda_context *ctx = nullptr;
-  void *device = nullptr;
-  size_t length = 0;
-  bool read_only = false;
-};
+using dmi::cuda_fail;
+using dmi::fail;
+using dmi::g_message;
+using dmi::release_context;
+using dmi::retain_context;
 
 extern "C" {
 
@@ -105,6 +70,7 @@ const char *dm_status_string(int32_t status) {
     case DM_ERR_TIMEOUT: return "a bounded wait ran out";
     case DM_ERR_NOT_BUILT: return "component not built";
     case DM_ERR_COMMUNICATOR: return "expert-parallel exchange failed";
+    case DM_ERR_IO: return "expert source read failed";
     default: return "unknown status";
   }
 }
@@ -137,6 +103,8 @@ int32_t dm_cuda_create(int32_t device_ordinal, dm_cuda_context **out) {
   return DM_OK;
 }
 
+}  // extern "C"
+
 static void free_context(dm_cuda_context *ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
@@ -149,12 +117,12 @@ static void free_context(dm_cuda_context *ctx) {
 
 static std::mutex g_ctx_mutex;
 
-static void retain_context(dm_cuda_context *ctx) {
+void dmi::retain_context(dm_cuda_context *ctx) {
   std::lock_guard<std::mutex> lock(g_ctx_mutex);
   ctx->refs++;
 }
 
-static void release_context(dm_cuda_context *ctx) {
+void dmi::release_context(dm_cuda_context *ctx) {
   bool last = false;
   {
     std::lock_guard<std::mutex> lock(g_ctx_mutex);
@@ -162,6 +130,8 @@ static void release_context(dm_cuda_context *ctx) {
   }
   if (last) free_context(ctx);
 }
+
+extern "C" {
 
 void dm_cuda_destroy(dm_cuda_context *ctx) {
   if (!ctx) return;
@@ -462,61 +432,6 @@ int32_t dm_cuda_rms_norm(dm_cuda_context *ctx, const float *input, const float *
 // MoE layer
 // ---------------------------------------------------------------------------
 
-struct dm_moe_layer {
-  dm_cuda_context *ctx = nullptr;
-  dm_moe_desc desc{};
-  int E1 = 0;
-  // Experts whose weights this layer holds: [first_expert, first_expert + local_experts)
-  // of the desc.experts routed by the router (all of them unless created for expert
-  // parallelism).
-  int first_expert = 0, local_experts = 0;
-  bool shared = false;
-  void *router_t = nullptr;  // transposed router [H][E1]
-  float *router_dup = nullptr;  // [H][router_dup_ld(E1)] f32 router for many tokens
-  float *router_rows = nullptr; // [E1][H] f32 router rows for few tokens
-  uint64_t gate_stride = 0, up_stride = 0, down_stride = 0;
-  const uint8_t *up_base = nullptr;
-  // scratch
-  void *scratch = nullptr;
-  size_t scratch_bytes = 0;
-  int capacity = 0;
-  dm::ForwardArgs args{};
-  int last_tokens = 0;
-  int last_launches = 0;
-  // host-call staging
-  void *io = nullptr;
-  size_t io_bytes = 0;
-  // per-stage device timers (GenerationProfile analog)
-  bool profiling = false;
-  cudaEvent_t events[dm::kStageCount + 1] = {};
-  // repacked copies of the 2-byte-aligned block formats, and their memory
-  dm::GemvPlan plan{};
-  std::vector<void *> owned;
-  // tensor-core path: packed activations and TMA maps for 16/32/64-token tiles
-  bool tc_ok = false;
-  dm::TcPlan tc[3];
-  dm::TcWeights tcw;  // tensor-core weight views (valid while tc_ok)
-  // CUDA graphs of repeated calls (keyed by buffers and token count)
-  struct GraphEntry {
-    const void *x;
-    float *y;
-    int tokens;
-    uint32_t *sel_idx;
-    float *sel_weight;
-    int seen;
-    cudaGraphExec_t exec;
-    int launches;
-    int failed = 0;
-  };
-  std::vector<GraphEntry> graphs;
-  bool graphs_enabled = true;
-  cudaStream_t capture = nullptr;
-  void drop_graphs() {
-    for (auto &e : graphs)
-      if (e.exec) cudaGraphExecDestroy(e.exec);
-    graphs.clear();
-  }
-};
 
 namespace {
 
@@ -761,7 +676,7 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
 extern "C" {
 
 static int32_t create_layer(dm_cuda_context *ctx, const dm_moe_desc *desc, int32_t first_expert,
-                            int32_t local_experts, dm_moe_layer **out);
+                            int32_t local_experts, dm_moe_layer **out, bool cached = false);
 
 int32_t dm_moe_layer_create(dm_cuda_context *ctx, const dm_moe_desc *desc, dm_moe_layer **out) {
   if (!desc) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
@@ -778,7 +693,7 @@ int32_t dm_moe_layer_create_ep(dm_cuda_context *ctx, const dm_moe_desc *desc, in
 }
 
 static int32_t create_layer(dm_cuda_context *ctx, const dm_moe_desc *desc, int32_t first_expert,
-                            int32_t local_experts, dm_moe_layer **out) {
+                            int32_t local_experts, dm_moe_layer **out, bool cached) {
   if (!ctx || !out) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
   *out = nullptr;
   int32_t rc = validate_desc(desc);
@@ -835,7 +750,9 @@ static int32_t create_layer(dm_cuda_context *ctx, const dm_moe_desc *desc, int32
     // the tensor-core kernels copy weight blocks in 16-byte pieces
     const uintptr_t align = (uintptr_t)d.gate | (uintptr_t)L->up_base |
                             (uintptr_t)d.shared_gate | (uintptr_t)d.shared_up;
-    L->tc_ok = rc == DM_OK && align % 16 == 0 &&
+    // Slots of an expert cache change under the layer: only the bf16 kernels, which
+    // read the weights through TMA maps alone, keep no per-expert side arrays.
+    L->tc_ok = rc == DM_OK && align % 16 == 0 && (!cached || d.down_type == DM_BF16) &&
                dm::tc_supported(d.gate_type, d.down_type, d.hidden, d.intermediate) &&
                !(tc_env && (!strcmp(tc_env, "0") || !strcmp(tc_env, "false")));
     if (L->tc_ok) rc = build_tc_weights(L);
@@ -864,10 +781,50 @@ void dm_moe_layer_destroy(dm_moe_layer *L) {
   for (void *p : L->owned) cudaFree(p);
   L->drop_graphs();
   if (L->capture) cudaStreamDestroy(L->capture);
+  dmi::release_cached_scratch(L->cached);
+  if (L->cache) dmi::cache_release(L->cache);
   cudaGetLastError();  // teardown leaves no error behind for unrelated calls
   dm_cuda_context *ctx = L->ctx;
   delete L;
   release_context(ctx);
+}
+
+int32_t dm_moe_layer_create_cached(dm_cuda_context *ctx, const dm_moe_desc *desc,
+                                   dm_expert_cache *cache, int32_t layer, dm_moe_layer **out) {
+  if (!ctx || !desc || !cache || !out) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  if (!dmi::cache_on_device(cache, ctx->device))
+    return fail(DM_ERR_INVALID_ARGUMENT, "the expert cache does not hold its slots on this device");
+  int tensors = 0, slots = 0;
+  uint8_t *const *mem = nullptr;
+  const uint64_t *bytes = nullptr;
+  int32_t rc = dmi::cache_layer_view(cache, layer, &tensors, &slots, &mem, &bytes);
+  if (rc != DM_OK) return rc;
+  const bool fused = desc->family == DM_FAMILY_GEMMA4;
+  if (tensors != (fused ? 2 : 3))
+    return fail(DM_ERR_INVALID_ARGUMENT, "cache layer %d has %d tensors; the family needs %d", layer,
+                tensors, fused ? 2 : 3);
+  const uint64_t H = desc->hidden, I = desc->intermediate;
+  const uint64_t gate_bytes = (fused ? 2 * I : I) * dm::row_bytes(desc->gate_type, H);
+  const uint64_t down_bytes = H * dm::row_bytes(desc->down_type, I);
+  const uint64_t want[3] = {gate_bytes, fused ? down_bytes : gate_bytes, down_bytes};
+  for (int i = 0; i < tensors; i++)
+    if (bytes[i] != want[i])
+      return fail(DM_ERR_BYTE_LENGTH, "cache tensor %d holds %llu bytes per expert; the layer needs %llu",
+                  i, (unsigned long long)bytes[i], (unsigned long long)want[i]);
+  if (slots > 1023) return fail(DM_ERR_INVALID_ARGUMENT, "at most 1023 slots per layer");
+  dm_moe_desc d = *desc;
+  d.gate = mem[0];
+  d.up = fused ? nullptr : mem[1];
+  d.down = mem[fused ? 1 : 2];
+  dm_moe_layer *L = nullptr;
+  rc = create_layer(ctx, &d, 0, slots, &L, true);
+  if (rc != DM_OK) return rc;
+  L->cache = cache;
+  L->cache_layer = layer;
+  dmi::cache_retain(cache);
+  *out = L;
+  return DM_OK;
 }
 
 int32_t dm_moe_set_profiling(dm_moe_layer *L, int32_t enable) {

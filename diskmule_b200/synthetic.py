@@ -224,32 +224,17 @@ class SyntheticLayer:
         for b in self.buffers.values():
             b.free()
         self.buffers.clear()
+        if getattr(self, "cache", None) is not None:
+            self.cache.close()
+            self.cache = None
+        if getattr(self, "pool", None) is not None:
+            self.pool.free()
+            self.pool = None
 
 
-def build_layer(ctx: CudaContext, name: str, seed: int = 1, logit_bias=None,
-                expert_range=None) -> SyntheticLayer:
-    """A device-resident synthetic layer. `expert_range=(first, count)` builds a shard
-    holding only those experts' weights (the same bytes as in the whole layer) for
-    expert parallelism; the router and shared expert stay whole."""
-    cfg = dict(CONFIGS[name])
-    specs = layer_specs(cfg, seed)
-    vecs = vectors(cfg, seed)
-    sl = SyntheticLayer(name, cfg, seed, ctx, specs, vecs)
-    for key, spec in specs.items():
-        if expert_range is not None and spec.experts > 1:
-            first, count = expert_range
-            buf = ctx.new_owned_buffer(count * spec.expert_bytes)
-            spec.device_fill(buf.device_pointer, expert=first, count=count)
-        else:
-            buf = ctx.new_owned_buffer(spec.nbytes)
-            spec.device_fill(buf.device_pointer)
-        sl.buffers[key] = buf
-    for key, v in vecs.items():
-        sl.buffers[key] = ctx.map_read_only(v)
-    if logit_bias is not None:
-        sl.logit_bias = np.ascontiguousarray(logit_bias, dtype=np.float32)
-        sl.buffers["router_logit_bias"] = ctx.map_read_only(sl.logit_bias)
-    ctx.synchronize()
+def _desc(sl: SyntheticLayer) -> N.MoeDesc:
+    """The layer descriptor over `sl`'s device buffers."""
+    cfg = sl.cfg
     d = N.MoeDesc()
     d.family = FAMILIES[cfg["family"]]
     d.hidden, d.intermediate, d.experts, d.top_k = (cfg["hidden"], cfg["intermediate"],
@@ -280,5 +265,84 @@ def build_layer(ctx: CudaContext, name: str, seed: int = 1, logit_bias=None,
         d.shared_down = sl.ptr("shared_down")
         d.shared_gate_vector = sl.ptr("shared_gate_vector") or None
     d.router_logit_bias = sl.ptr("router_logit_bias") or None
+    return d
+
+
+def build_layer(ctx: CudaContext, name: str, seed: int = 1, logit_bias=None,
+                expert_range=None) -> SyntheticLayer:
+    """A device-resident synthetic layer. `expert_range=(first, count)` builds a shard
+    holding only those experts' weights (the same bytes as in the whole layer) for
+    expert parallelism; the router and shared expert stay whole."""
+    cfg = dict(CONFIGS[name])
+    specs = layer_specs(cfg, seed)
+    vecs = vectors(cfg, seed)
+    sl = SyntheticLayer(name, cfg, seed, ctx, specs, vecs)
+    for key, spec in specs.items():
+        if expert_range is not None and spec.experts > 1:
+            first, count = expert_range
+            buf = ctx.new_owned_buffer(count * spec.expert_bytes)
+            spec.device_fill(buf.device_pointer, expert=first, count=count)
+        else:
+            buf = ctx.new_owned_buffer(spec.nbytes)
+            spec.device_fill(buf.device_pointer)
+        sl.buffers[key] = buf
+    for key, v in vecs.items():
+        sl.buffers[key] = ctx.map_read_only(v)
+    if logit_bias is not None:
+        sl.logit_bias = np.ascontiguousarray(logit_bias, dtype=np.float32)
+        sl.buffers["router_logit_bias"] = ctx.map_read_only(sl.logit_bias)
+    ctx.synchronize()
+    d = _desc(sl)
     sl.layer = MoeLayer(ctx, d, expert_range=expert_range)
+    return sl
+
+
+EXPERT_TENSORS = {"gemma4": ("gate", "down"), "qwen35": ("gate", "up", "down"),
+                  "glm52": ("gate", "up", "down")}
+
+
+def build_cached_layer(ctx: CudaContext, name: str, seed: int = 1, slots: int = 8,
+                       global_clock: bool | None = None, logit_bias=None,
+                       input_type: int | None = None) -> SyntheticLayer:
+    """A synthetic layer whose experts are out of core: the expert tensors sit in
+    page-locked host memory in the reference's layout ([experts][rows][blocks] per
+    tensor, tensors one after another), and the layer holds `slots` of them in HBM
+    through an expert cache (GLM rules for the GLM family unless `global_clock` says
+    otherwise). The router, shared expert and vectors are device-resident as in
+    `build_layer`; `sl.cache` is the cache and `sl.pool` the host source."""
+    from .cache import CachedMoeLayer, ExpertCache, PinnedHost, layout
+    cfg = dict(CONFIGS[name])
+    specs = layer_specs(cfg, seed)
+    vecs = vectors(cfg, seed)
+    sl = SyntheticLayer(name, cfg, seed, ctx, specs, vecs)
+    keys = EXPERT_TENSORS[cfg["family"]]
+    E = cfg["experts"]
+    sizes = [specs[k].expert_bytes for k in keys]
+    pool = PinnedHost(ctx, E * sum(sizes))
+    offsets, off = [], 0
+    for k, n in zip(keys, sizes):
+        pool.array(off, E * n)[:] = specs[k].host()
+        offsets.append(off)
+        off += E * n
+    if global_clock is None:
+        global_clock = cfg["family"] == "glm52"
+    sl.cache = ExpertCache(ctx, [layout(E, sizes, host=pool.pointer, offsets=offsets)], slots,
+                           global_clock=global_clock)
+    sl.pool = pool
+    for key, spec in specs.items():
+        if key in keys:
+            continue
+        buf = ctx.new_owned_buffer(spec.nbytes)
+        spec.device_fill(buf.device_pointer)
+        sl.buffers[key] = buf
+    for key, v in vecs.items():
+        sl.buffers[key] = ctx.map_read_only(v)
+    if logit_bias is not None:
+        sl.logit_bias = np.ascontiguousarray(logit_bias, dtype=np.float32)
+        sl.buffers["router_logit_bias"] = ctx.map_read_only(sl.logit_bias)
+    ctx.synchronize()
+    d = _desc(sl)
+    if input_type is not None:
+        d.input_type = input_type
+    sl.layer = CachedMoeLayer(ctx, d, sl.cache, 0)
     return sl

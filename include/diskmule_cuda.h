@@ -60,6 +60,7 @@ typedef enum {
   DM_ERR_TIMEOUT = -22,               /* a bounded device or host wait ran out */
   DM_ERR_NOT_BUILT = -23,             /* the call needs a component this build lacks */
   DM_ERR_COMMUNICATOR = -24,          /* NCCL / expert-parallel exchange failed */
+  DM_ERR_IO = -25,                    /* ExpertCacheError::Io: a source read failed or was short */
 } dm_status;
 
 /* GGML tensor type ids (src/gguf.rs:295-318) on the path. */
@@ -267,6 +268,135 @@ DM_API int32_t dm_moe_expert_rows(dm_moe_layer *layer, const void *rows,
 DM_API int32_t dm_moe_combine_rows(dm_moe_layer *layer, int32_t tokens, const uint32_t *sel_idx,
                                    const float *sel_weight, const float *logits,
                                    const float *pair_out, float *y, void *stream);
+
+/* ---- pinned host memory ----------------------------------------------------------
+ * The out-of-core expert pool lives in page-locked host memory so that a cache miss
+ * is one DMA copy over PCIe (the reference reads the file with pread instead,
+ * src/expert.rs:241-256). dm_cuda_host_alloc returns new pinned memory
+ * (cudaHostAlloc, portable across devices); dm_cuda_host_register pins an existing
+ * range, e.g. a read-only mapping of the model file. */
+DM_API int32_t dm_cuda_host_alloc(dm_cuda_context *ctx, size_t length, void **out);
+DM_API void dm_cuda_host_free(dm_cuda_context *ctx, void *host);
+DM_API int32_t dm_cuda_host_register(dm_cuda_context *ctx, void *host, size_t length);
+DM_API int32_t dm_cuda_host_unregister(dm_cuda_context *ctx, void *host);
+
+/* ---- expert residency ------------------------------------------------------------
+ * dm_expert_cache replaces ExpertCache (src/expert.rs:64-229, per-layer clock, slots
+ * pinned during use, two reads per miss) and Glm52ExpertCache
+ * (src/glm52/expert.rs:66-256, one clock across layers, three reads per miss):
+ * `global_clock` selects the GLM rules. Each layer holds `slots_per_layer` slots in
+ * HBM, one contiguous array per tensor ([slots][bytes[i]]). acquire() keeps the
+ * reference's bookkeeping exactly -- clock += 1; a hit sets last_used; a miss takes
+ * the unpinned slot with the smallest (occupied, last_used, index), counts an
+ * eviction if it was occupied, then reads the expert -- and counts hits, misses,
+ * evictions, reads, bytes_read and resident_bytes as the reference does. The read is
+ * a cudaMemcpyAsync from the pinned source on the cache's own copy stream, ordered
+ * after the work that last read the slot (release_slot) and before the work that
+ * waits for it (wait_slot), so fills overlap compute on other slots.
+ *
+ * A source is either pinned host memory described by the layout, or a read callback
+ * (dm_expert_cache_set_reader) that the cache calls on the host into its own pinned
+ * staging, as the reference's pread. All of an expert's tensors are read before any
+ * slot byte changes, so a failed or short read leaves the slot as it was; the counters
+ * then stand as the reference leaves them (misses and evictions counted, reads and
+ * bytes not). With ctx == NULL the slots are host memory and fills are memcpy: the
+ * same bookkeeping, usable without a GPU. */
+typedef struct dm_expert_cache dm_expert_cache;
+
+/* One layer's experts. Tensor i (i < tensor_count <= 4; Gemma/GGUF: gate_up, down;
+ * GLM/Qwen: gate, up, down) of expert e is bytes[i] bytes at
+ *   expert_host[e] + offset[i]          when expert_host is set (one blob per expert),
+ *   host + offset[i] + e * bytes[i]     otherwise (the GGUF layout: ExpertLayerLayout,
+ *                                        src/expert.rs:44-51).
+ * Neither is read when the cache has a reader callback. */
+typedef struct {
+  int32_t expert_count;
+  int32_t tensor_count;
+  uint64_t bytes[4];
+  uint64_t offset[4];
+  const void *host;
+  const void *const *expert_host;
+} dm_expert_layout;
+
+/* ExpertCacheStats (src/expert.rs:53-62) / Glm52ExpertCacheStats
+ * (src/glm52/expert.rs:55-64), plus what the copy engine did. io_wait_ns is the
+ * device time of the fills (the reference's time spent in reads). */
+typedef struct {
+  uint64_t hits, misses, evictions, reads, bytes_read;
+  uint64_t io_wait_ns;
+  uint64_t resident_bytes;
+  uint64_t h2d_bytes;  /* bytes copied host -> slot */
+  uint64_t fills;      /* fills issued */
+} dm_expert_cache_stats;
+
+/* Reader callback: fill `destination` with `length` bytes of tensor `tensor` of
+ * (layer, expert); return the number of bytes read (less = a short read) or a
+ * negative errno. */
+typedef int64_t (*dm_expert_read_fn)(void *user, int32_t layer, int32_t expert, int32_t tensor,
+                                     void *destination, uint64_t length);
+
+/* ExpertCache::new (src/expert.rs:87-128) / Glm52ExpertCache::new
+ * (src/glm52/expert.rs:103-148): zero slots -> DM_ERR_NO_SLOTS. A layout's host source
+ * must be page-locked (dm_cuda_host_alloc / dm_cuda_host_register) for a device
+ * cache. */
+DM_API int32_t dm_expert_cache_create(dm_cuda_context *ctx, const dm_expert_layout *layouts,
+                                      int32_t layers, int32_t slots_per_layer,
+                                      int32_t global_clock, dm_expert_cache **out);
+DM_API int32_t dm_expert_cache_set_reader(dm_expert_cache *cache, dm_expert_read_fn read,
+                                          void *user);
+/* Layers created on the cache keep it alive until they are destroyed. */
+DM_API void dm_expert_cache_destroy(dm_expert_cache *cache);
+DM_API int32_t dm_expert_cache_slots_per_layer(const dm_expert_cache *cache);
+/* Base address and per-slot stride of tensor `tensor`'s slot array in `layer`. */
+DM_API int32_t dm_expert_cache_slot_memory(const dm_expert_cache *cache, int32_t layer,
+                                           int32_t tensor, void **base, uint64_t *stride);
+/* The acquire step of with_expert (src/expert.rs:138-164, src/glm52/expert.rs:157-181):
+ * `cancelled` (may be NULL) is read before and after, as the reference does, and --
+ * with the GLM rules -- once more before a miss's read, where a cancel leaves the slot
+ * as it was. Returns the slot and whether it was a miss; the fill is queued, not
+ * waited for. */
+DM_API int32_t dm_expert_cache_acquire(dm_expert_cache *cache, int32_t layer, int32_t expert,
+                                       const int32_t *cancelled, int32_t *slot, int32_t *miss);
+/* Make `stream` wait for the slot's last fill / record that `stream`'s work so far
+ * reads the slot (the next fill of the slot waits for it). */
+DM_API int32_t dm_expert_cache_wait_slot(dm_expert_cache *cache, int32_t layer, int32_t slot,
+                                         void *stream);
+DM_API int32_t dm_expert_cache_release_slot(dm_expert_cache *cache, int32_t layer, int32_t slot,
+                                            void *stream);
+/* ExpertSlot::pinned (src/expert.rs:78-84): a pinned slot is never a victim (the GLM
+ * rules have no pinning and ignore it). */
+DM_API int32_t dm_expert_cache_set_pinned(dm_expert_cache *cache, int32_t layer, int32_t slot,
+                                          int32_t pinned);
+/* Expert held by a slot (-1 = empty). */
+DM_API int32_t dm_expert_cache_slot_expert(const dm_expert_cache *cache, int32_t layer,
+                                           int32_t slot, int32_t *expert);
+/* Copy a slot's tensor bytes to the host after its fill (synchronous). */
+DM_API int32_t dm_expert_cache_read_slot(dm_expert_cache *cache, int32_t layer, int32_t slot,
+                                         int32_t tensor, void *destination, uint64_t length);
+/* Counters (waits, bounded, for the fills in flight to time them). */
+DM_API int32_t dm_expert_cache_get_stats(dm_expert_cache *cache, dm_expert_cache_stats *out);
+/* Wait (bounded: DM_ERR_TIMEOUT) for every fill issued so far. */
+DM_API int32_t dm_expert_cache_synchronize(dm_expert_cache *cache);
+
+/* A MoE layer whose experts are cache layer `layer`'s slots: desc is as for
+ * dm_moe_layer_create, except gate/up/down, which are taken from the cache (its
+ * tensor sizes must match the layer's expert strides: gate_up + down for Gemma,
+ * gate + up + down otherwise). The router and shared expert stay resident. */
+DM_API int32_t dm_moe_layer_create_cached(dm_cuda_context *ctx, const dm_moe_desc *desc,
+                                          dm_expert_cache *cache, int32_t layer,
+                                          dm_moe_layer **out);
+/* The routed block with out-of-core experts: router + top-k, then every (token,
+ * expert) pair acquired in the reference's order (tokens in order, experts in
+ * selection order, src/glm52/cpu.rs:755-772, src/gemma4/cpu.rs:559-611), misses
+ * filled on the copy stream, the shared expert and resident experts computed first
+ * and each missed expert as soon as its fill lands, then the combine. When a miss
+ * would evict a slot that an earlier pair of the same call still has to read, the
+ * pending pairs run first, so every pair sees its own expert -- the sequential
+ * reference's semantics. The call waits (bounded) for the routed selection, which
+ * the host bookkeeping needs; everything after it is queued on `stream`. */
+DM_API int32_t dm_moe_forward_cached(dm_moe_layer *layer, const void *x, float *y,
+                                     int32_t tokens, uint32_t *sel_idx, float *sel_weight,
+                                     const int32_t *cancelled, void *stream);
 
 #ifdef __cplusplus
 }

@@ -368,6 +368,20 @@ int dmo_argmax(const float *values, size_t n, size_t *index) {
 /* GLM-5.2 helpers                                                          */
 /* ------------------------------------------------------------------------ */
 
+/* src/glm52/cpu.rs:912-924: the mean square is a sequential f64 sum of the (exact)
+ * squares divided by n in f64; scale = 1 / sqrt(ms as f32 + eps) in f32;
+ * out = value * scale * weight, left to right. */
+int dmo_glm_rms_norm(const float *input, const float *weight, size_t n, float epsilon,
+                     float *output) {
+  if (n == 0) return DMO_ERR_EMPTY;
+  double sum = 0.0;
+  for (size_t i = 0; i < n; i++) sum += (double)input[i] * (double)input[i];
+  const float mean_square = (float)(sum / (double)n);
+  const float scale = 1.0f / sqrtf(mean_square + epsilon);
+  for (size_t i = 0; i < n; i++) output[i] = input[i] * scale * weight[i];
+  return DMO_OK;
+}
+
 /* src/glm52/cpu.rs:980-982 */
 float dmo_glm_sigmoid(float value) { return 1.0f / (1.0f + expf(-value)); }
 /* src/glm52/cpu.rs:984-986 (used by the shared-expert `mlp`, :897-910) */
@@ -694,10 +708,13 @@ static int glm_token(const dmo_glm_layer *L, const float *x, float *y, uint32_t 
   size_t expert_in = I * H * width;
   for (size_t j = 0; rc == DMO_OK && j < k; j++) {
     size_t e = sel_idx[j];
-    dmo_glm_matvec(L->weight_type, I, H, L->gate + e * expert_in, x, gate, threads);
-    dmo_glm_matvec(L->weight_type, I, H, L->up + e * expert_in, x, up, threads);
+    const uint8_t *wg = L->expert_blobs ? L->expert_blobs[e] : L->gate + e * expert_in;
+    const uint8_t *wu = L->expert_blobs ? L->expert_blobs[e] + expert_in : L->up + e * expert_in;
+    const uint8_t *wd = L->expert_blobs ? L->expert_blobs[e] + 2 * expert_in : L->down + e * expert_in;
+    dmo_glm_matvec(L->weight_type, I, H, wg, x, gate, threads);
+    dmo_glm_matvec(L->weight_type, I, H, wu, x, up, threads);
     for (size_t i = 0; i < I; i++) gate[i] = dmo_glm_cached_silu(gate[i]) * up[i];
-    dmo_glm_matvec(L->weight_type, H, I, L->down + e * expert_in, gate, out, threads);
+    dmo_glm_matvec(L->weight_type, H, I, wd, gate, out, threads);
     for (size_t i = 0; i < H; i++) y[i] = y[i] + out[i] * sel_weight[j] * L->routed_scale;
   }
   if (rc == DMO_OK && SI > 0) {

@@ -80,6 +80,8 @@ int dmo_top_k_softmax(const float *logits, size_t n, size_t k, uint32_t *indices
 int dmo_argmax(const float *values, size_t n, size_t *index);
 
 /* ---- GLM-5.2 helpers (src/glm52/cpu.rs, src/glm52/expert.rs) ---- */
+int dmo_glm_rms_norm(const float *input, const float *weight, size_t n, float epsilon,
+                     float *output);
 int dmo_glm_matvec(int kind, size_t rows, size_t columns, const uint8_t *encoded,
                    const float *input, float *output, int threads);
 float dmo_glm_sigmoid(float value);
@@ -143,6 +145,9 @@ typedef struct {
   const uint8_t *down;           /* [experts][hidden][intermediate] */
   int32_t shared_intermediate;   /* 0 = no shared expert */
   const uint8_t *shared_gate, *shared_up, *shared_down;
+  /* optional: expert e's weights as one blob gate | up | down (then gate/up/down
+   * above are not read) -- the layout of an out-of-core expert pool */
+  const uint8_t *const *expert_blobs;
 } dmo_glm_layer;
 
 int dmo_glm_moe(const dmo_glm_layer *layer, const float *x, size_t tokens, float *y,

@@ -72,6 +72,7 @@ def _declare(L):
     L.dmo_softmax_in_place.argtypes = [P, SZ]
     L.dmo_top_k_softmax.argtypes = [P, SZ, SZ, P, P]
     L.dmo_argmax.argtypes = [P, SZ, C.POINTER(C.c_size_t)]
+    L.dmo_glm_rms_norm.argtypes = [P, P, SZ, C.c_float, P]
     L.dmo_glm_matvec.argtypes = [C.c_int, SZ, SZ, P, P, P, C.c_int]
     for name in ("dmo_glm_sigmoid", "dmo_glm_silu", "dmo_glm_cached_silu",
                  "dmo_qwen_sigmoid", "dmo_qwen_silu"):
@@ -141,6 +142,15 @@ def rms_norm(x, weight, eps):
     w = None if weight is None else _f32(weight)
     out = np.zeros_like(x)
     rc = lib().dmo_rms_norm(_ptr(x), _ptr(w), x.size, eps, _ptr(out))
+    return rc, out
+
+
+def glm_rms_norm(x, weight, eps):
+    """src/glm52/cpu.rs:912-924 (f64 mean square)."""
+    x = _f32(x)
+    w = _f32(weight)
+    out = np.zeros_like(x)
+    rc = lib().dmo_glm_rms_norm(_ptr(x), _ptr(w), x.size, eps, _ptr(out))
     return rc, out
 
 
@@ -220,7 +230,7 @@ class GlmLayer(C.Structure):
                 ("routed_scale", C.c_float), ("weight_type", I32), ("router", P),
                 ("correction_bias", P), ("gate", P), ("up", P), ("down", P),
                 ("shared_intermediate", I32), ("shared_gate", P), ("shared_up", P),
-                ("shared_down", P)]
+                ("shared_down", P), ("expert_blobs", C.POINTER(P))]
 
 
 def gemma_moe(w: dict, x, threads: int = 1):
@@ -266,9 +276,13 @@ def glm_moe(w: dict, x, threads: int = 1):
     layer = GlmLayer(H, w["intermediate"], w["experts"], k, w.get("n_groups", 1),
                      w.get("topk_groups", 1), int(w.get("normalize", True)),
                      w.get("routed_scale", 1.0), w.get("weight_type", BF16), _ptr(w["router"]),
-                     _ptr(w["correction_bias"]), _ptr(w["gate"]), _ptr(w["up"]),
-                     _ptr(w["down"]), si, _ptr(w.get("shared_gate")), _ptr(w.get("shared_up")),
+                     _ptr(w["correction_bias"]), _ptr(w.get("gate")), _ptr(w.get("up")),
+                     _ptr(w.get("down")), si, _ptr(w.get("shared_gate")), _ptr(w.get("shared_up")),
                      _ptr(w.get("shared_down")))
+    blobs = w.get("expert_blobs")  # host addresses of per-expert gate|up|down blobs
+    if blobs is not None:
+        keep = (P * len(blobs))(*[int(b) for b in blobs])
+        layer.expert_blobs = C.cast(keep, C.POINTER(P))
     y = np.zeros((T, H), dtype=np.float32)
     idx = np.zeros((T, k), dtype=np.uint32)
     wt = np.zeros((T, k), dtype=np.float32)
