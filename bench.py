@@ -52,7 +52,7 @@ def parse_args():
     p.add_argument("--pool-experts", type=int, default=0,
                    help="distinct expert blobs in host memory (0: every expert, if host memory "
                         "allows)")
-    p.add_argument("--check-steps", type=int, default=4,
+    p.add_argument("--check-steps", type=int, default=16,
                    help="decode steps replayed on the CPU oracle (token parity, CPU baseline)")
     return p.parse_args()
 
@@ -611,6 +611,9 @@ def run_stack(args):
     stream = torch.cuda.current_stream()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(0) as clk:
+        # nvidia-smi's start-up stalls driver calls for a moment; this path calls the
+        # driver every layer, so the timed region starts after it has settled
+        time.sleep(2.0)
         a.record(stream)
         tokens = st.decode(warm[-1] if warm else first, args.steps)
         b.record(stream)
