@@ -507,6 +507,187 @@ __device__ __forceinline__ float act_fn(const ForwardArgs &a, int expert, float 
 }
 
 // ---------------------------------------------------------------------------
+// dense weights (BF16 / F16 / F32): one warp per row, coalesced 512-byte loads
+//
+// A warp streams a row as 512-byte pieces (lane l takes bytes 16·(l + 32i) .. +16), with
+// four pieces in flight per matrix, and dots them with the x rows staged once per CTA in
+// shared memory as f32; each CTA covers many rows, so the staging is a few percent of
+// the weight bytes even at H = 6144. Row sums are a fixed shuffle tree (deterministic).
+// ---------------------------------------------------------------------------
+
+template <int KIND>
+__device__ __forceinline__ void dense_unpack(const uint4 v, float *w) {
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    if (KIND == DM_BF16) {
+      w[2 * j] = __uint_as_float(u[j] << 16);
+      w[2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+    } else if (KIND == DM_F16) {
+      w[2 * j] = f16_bits_to_f32((uint16_t)(u[j] & 0xffff));
+      w[2 * j + 1] = f16_bits_to_f32((uint16_t)(u[j] >> 16));
+    } else {
+      w[j] = __uint_as_float(u[j]);
+    }
+  }
+}
+
+// Elements per 16-byte piece.
+template <int KIND> struct DenseElems { static constexpr int kN = KIND == DM_F32 ? 4 : 8; };
+
+// acc[t] += row . x_t over one row of `chunks` 16-byte pieces (this lane's share).
+template <int KIND, int NT>
+__device__ __forceinline__ void dense_row_dot(const uint8_t *__restrict__ row, int chunks,
+                                              const float *xs, int xld, int nt, float *acc) {
+  constexpr int kE = DenseElems<KIND>::kN;
+  const int lane = threadIdx.x & 31;
+  constexpr int kU = 4;
+  for (int c0 = lane; c0 < chunks; c0 += 32 * kU) {
+    uint4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; u++) {
+      const int c = c0 + 32 * u;
+      v[u] = c < chunks ? ldg16(row + 16 * (size_t)c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; u++) {
+      const int c = c0 + 32 * u;
+      if (c >= chunks) break;
+      float w[kE];
+      dense_unpack<KIND>(v[u], w);
+#pragma unroll
+      for (int t = 0; t < NT; t++) {
+        if (t < nt) {
+          const float *xp = xs + t * xld + c * kE;
+          float s = acc[t];
+#pragma unroll
+          for (int i = 0; i < kE; i += 4) {
+            const float4 xv = *reinterpret_cast<const float4 *>(xp + i);
+            s = fmaf(w[i], xv.x, s);
+            s = fmaf(w[i + 1], xv.y, s);
+            s = fmaf(w[i + 2], xv.z, s);
+            s = fmaf(w[i + 3], xv.w, s);
+          }
+          acc[t] = s;
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+constexpr int kDenseThreads = 256;
+
+template <int KIND, int NT>
+__global__ void __launch_bounds__(kDenseThreads) dense_up_kernel(ForwardArgs a, MatrixRef gate,
+                                                                 MatrixRef up, MatrixRef sh_gate,
+                                                                 MatrixRef sh_up,
+                                                                 int up_row_offset,
+                                                                 int rows_per_cta) {
+  extern __shared__ __align__(16) float smem[];
+  if ((int)blockIdx.y >= *a.n_items) return;
+  const int4 item = a.items[blockIdx.y];
+  const int e = item.x, c0 = item.y;
+  const int base = a.offsets[e];
+  const int nt = min(NT, a.counts[e] - c0);
+  const int H = a.H, I = a.I;
+  const int i0 = blockIdx.x * rows_per_cta;
+  if (i0 >= I) return;
+  const int nrows = min(rows_per_cta, I - i0);
+  const bool shared = e == a.E;
+  const MatrixRef &G = shared ? sh_gate : gate;
+  const MatrixRef &U = shared ? sh_up : up;
+  const int ex = shared ? 0 : e;
+  const int P = a.T * a.k;
+  const int xld = H + 4;
+  float *xs = smem;
+  // stage the x rows of this item's tokens as f32
+  for (int idx = threadIdx.x; idx < nt * (H / 4); idx += blockDim.x) {
+    const int t = idx / (H / 4), k = 4 * (idx - t * (H / 4));
+    const int pair = a.sorted[base + c0 + t];
+    const int tok = pair < P ? pair / a.k : pair - P;
+    const size_t o = (size_t)tok * H + k;
+    float4 v;
+    if (a.family == kGemma) {
+      v = *reinterpret_cast<const float4 *>(a.expert_in + o);
+    } else if (a.input_bf16) {
+      const uint2 q = *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(a.x) + o);
+      v = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xffff0000u),
+                      __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xffff0000u));
+    } else {
+      v = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + o);
+    }
+    *reinterpret_cast<float4 *>(xs + t * xld + k) = v;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int chunks = (int)(G.row_bytes / 16);
+  for (int r = warp; r < nrows; r += kDenseThreads / 32) {
+    const int row = i0 + r;
+    float g[NT], u[NT];
+#pragma unroll
+    for (int t = 0; t < NT; t++) g[t] = u[t] = 0.0f;
+    dense_row_dot<KIND, NT>(G.base + (uint64_t)ex * G.stride + (uint64_t)row * G.row_bytes, chunks,
+                            xs, xld, nt, g);
+    dense_row_dot<KIND, NT>(U.base + (uint64_t)ex * U.stride +
+                                (uint64_t)(row + up_row_offset) * U.row_bytes,
+                            chunks, xs, xld, nt, u);
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+      const float gs = warp_sum(g[t]), us = warp_sum(u[t]);
+      if (lane == 0 && t < nt) a.h[(size_t)(base + c0 + t) * I + row] = act_fn(a, e, gs, us);
+    }
+  }
+}
+
+template <int KIND, int NT>
+__global__ void __launch_bounds__(kDenseThreads) dense_down_kernel(ForwardArgs a, MatrixRef down,
+                                                                   MatrixRef sh_down,
+                                                                   int rows_per_cta) {
+  extern __shared__ __align__(16) float smem[];
+  if ((int)blockIdx.y >= *a.n_items) return;
+  const int4 item = a.items[blockIdx.y];
+  const int e = item.x, c0 = item.y;
+  const int base = a.offsets[e];
+  const int nt = min(NT, a.counts[e] - c0);
+  const int H = a.H, I = a.I;
+  const int r0 = blockIdx.x * rows_per_cta;
+  if (r0 >= H) return;
+  const int nrows = min(rows_per_cta, H - r0);
+  const bool shared = e == a.E;
+  const MatrixRef &D = shared ? sh_down : down;
+  const int ex = shared ? 0 : e;
+  const int xld = I + 4;
+  float *xs = smem;
+  for (int idx = threadIdx.x; idx < nt * (I / 4); idx += blockDim.x) {
+    const int t = idx / (I / 4), k = 4 * (idx - t * (I / 4));
+    *reinterpret_cast<float4 *>(xs + t * xld + k) =
+        *reinterpret_cast<const float4 *>(a.h + (size_t)(base + c0 + t) * I + k);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int chunks = (int)(D.row_bytes / 16);
+  for (int r = warp; r < nrows; r += kDenseThreads / 32) {
+    const int row = r0 + r;
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; t++) acc[t] = 0.0f;
+    dense_row_dot<KIND, NT>(D.base + (uint64_t)ex * D.stride + (uint64_t)row * D.row_bytes, chunks,
+                            xs, xld, nt, acc);
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+      const float s = warp_sum(acc[t]);
+      if (lane == 0 && t < nt) a.ysorted[(size_t)(base + c0 + t) * H + row] = s;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // launcher
 // ---------------------------------------------------------------------------
 
@@ -521,8 +702,46 @@ static MatrixRef matrix(int kind, const uint8_t *base, uint64_t stride, int rows
   return m;
 }
 
+constexpr bool is_dense(int kind) { return kind == DM_BF16 || kind == DM_F16 || kind == DM_F32; }
+
+// Rows per CTA of the dense kernels: 32 rows make the x staging (one row of f32 per
+// token) about 3% of the weight bytes; fewer when the grid would not fill the SMs twice.
+static int dense_rows(int rows_total, int items) {
+  int r = 32;
+  while (r > 8 && (long)((rows_total + r - 1) / r) * items < 2L * 148) r /= 2;
+  return r;
+}
+
+template <int KIND, int NT>
+static void launch_dense_up(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s) {
+  const int up_rows = a.family == kGemma ? 2 * a.I : a.I;
+  MatrixRef g = matrix(KIND, a.gate, a.gate_stride, up_rows, a.H, p.gate);
+  MatrixRef u = matrix(KIND, a.family == kGemma ? a.gate : a.up, a.up_stride, up_rows, a.H, p.up);
+  MatrixRef sg = matrix(KIND, a.sh_gate, 0, a.I, a.H, p.sh_gate);
+  MatrixRef su = matrix(KIND, a.sh_up, 0, a.I, a.H, p.sh_up);
+  const int rows = dense_rows(a.I, p.max_items);
+  const size_t smem = (size_t)NT * (a.H + 4) * 4;
+  auto fn = dense_up_kernel<KIND, NT>;
+  if (smem > 48 * 1024) ensure_smem_limit((const void *)fn);
+  dim3 grid((a.I + rows - 1) / rows, p.max_items);
+  fn<<<grid, kDenseThreads, smem, s>>>(a, g, u, sg, su, a.family == kGemma ? a.I : 0, rows);
+}
+
+template <int KIND, int NT>
+static void launch_dense_down(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s) {
+  MatrixRef d = matrix(KIND, a.down, a.down_stride, a.H, a.I, p.down);
+  MatrixRef sd = matrix(KIND, a.sh_down, 0, a.H, a.I, p.sh_down);
+  const int rows = dense_rows(a.H, p.max_items);
+  const size_t smem = (size_t)NT * (a.I + 4) * 4;
+  auto fn = dense_down_kernel<KIND, NT>;
+  if (smem > 48 * 1024) ensure_smem_limit((const void *)fn);
+  dim3 grid((a.H + rows - 1) / rows, p.max_items);
+  fn<<<grid, kDenseThreads, smem, s>>>(a, d, sd, rows);
+}
+
 template <int KIND, int NT>
 static void launch_up(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s) {
+  if (is_dense(KIND)) return launch_dense_up<KIND, NT>(a, p, s);
   constexpr int kTask = Task<KIND>::kElems;
   const int nb = a.H / kTask;
   const int rows = std::max(1, kGemvThreads / (2 * nb));
@@ -541,6 +760,7 @@ static void launch_up(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s) {
 
 template <int KIND, int NT>
 static void launch_down(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s) {
+  if (is_dense(KIND)) return launch_dense_down<KIND, NT>(a, p, s);
   constexpr int kTask = Task<KIND>::kElems;
   const int nb = a.I / kTask;
   const int rows = std::max(1, kGemvThreads / nb);
