@@ -228,11 +228,31 @@ __device__ __forceinline__ void deq4(uint32_t w, uint64_t M, uint64_t C, uint32_
 // Q4_K super-block (src/cpu.rs:585-616) at s: 16-byte header (d, dmin, 12 scale bytes),
 // qs[128]. Half hf = group pairs 2hf, 2hf+1. Group pair gp: low nibbles of
 // qs[32gp .. 32gp+32) are elements 64gp + i (sub-block 2gp), high nibbles elements
-// 64gp + 32 + i (sub-block 2gp+1). value = (d*sc)*q - dmin*m. A high nibble is taken
-// shifted right by one (byte 8q), so f = 0.5 + q/32.
+// 64gp + 32 + i (sub-block 2gp+1). value = d*(sc*q) - dmin*m, built in fp16 without
+// the ALU pipe's byte shuffles:
+//   one LOP3 turns the nibbles of bytes 0 and 2 (or 1 and 3) of a word into the fp16 pair
+//   1024 + q (low nibble) or 1024 + 16q (high nibble), exact;
+//   fma(1024 + q, sc, -1024 sc) (or fma(1024 + 16q, sc/16, -64 sc)) = sc*q exactly
+//   (the product is exact inside the fma and sc*q <= 945 is an fp16 integer);
+//   fma(sc*q, d, fp16(-dmin*m)) with d the block's own fp16 value: one rounding of the
+//   product, the same as rounding the f32 value once to fp16, plus the rounding of the
+//   small bias term.
+// A column therefore holds K values (4j, 4j+2) or (4j+1, 4j+3) of a group of four; the
+// activation tiles are packed in the same order (pack_kernel<true>).
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t h2dup(float v) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %1;" : "=r"(h) : "f"(v));
+  return h;
+}
+
 __device__ __forceinline__ void deq_q4k(uint32_t s, int hf, uint32_t tcol) {
   const uint4 hd = lds16(s);
-  const float d = f16_bits_to_f32((uint16_t)(hd.x & 0xffff));
+  const uint32_t D = __byte_perm(hd.x, 0, 0x1010);  // (d, d) as fp16x2
   const float dmin = f16_bits_to_f32((uint16_t)(hd.x >> 16));
   // scale/min bytes of sub-blocks 4hf .. 4hf+3 (get_scale_min_k4)
   const uint32_t sc = hf ? ((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u)) : (hd.y & 0x3F3F3F3Fu);
@@ -240,23 +260,21 @@ __device__ __forceinline__ void deq_q4k(uint32_t s, int hf, uint32_t tcol) {
                          : (hd.z & 0x3F3F3F3Fu);
 #pragma unroll
   for (int g = 0; g < 2; g++) {
-    const float al = __fmul_rn(d, (float)((sc >> (16 * g)) & 0xff));
-    const float bl = __fmul_rn(dmin, (float)((mn >> (16 * g)) & 0xff));
-    const float ah = __fmul_rn(d, (float)((sc >> (16 * g + 8)) & 0xff));
-    const float bh = __fmul_rn(dmin, (float)((mn >> (16 * g + 8)) & 0xff));
-    const uint64_t Ml = pair(256.0f * al, 256.0f * al);
-    const float cl = -(128.0f * al + bl);
-    const uint64_t Cl = pair(cl, cl);
-    const uint64_t Mh = pair(32.0f * ah, 32.0f * ah);
-    const float ch = -(16.0f * ah + bh);
-    const uint64_t Ch = pair(ch, ch);
+    const float scl = (float)((sc >> (16 * g)) & 0xff), sch = (float)((sc >> (16 * g + 8)) & 0xff);
+    const float mnl = (float)((mn >> (16 * g)) & 0xff), mnh = (float)((mn >> (16 * g + 8)) & 0xff);
+    const uint32_t SL = h2dup(scl), CL = h2dup(-1024.0f * scl);
+    const uint32_t SH = h2dup(0.0625f * sch), CH = h2dup(-64.0f * sch);
+    const uint32_t BL = h2dup(-(dmin * mnl)), BH = h2dup(-(dmin * mnh));  // dmin*m exact in f32
     const uint4 qa = lds16(s + 16 + 64 * hf + 32 * g), qb = lds16(s + 32 + 64 * hf + 32 * g);
     const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
     uint32_t lo[16], hi[16];
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-      deq4(w[k] & 0x0F0F0F0Fu, Ml, Cl, lo + 2 * k);
-      deq4((w[k] >> 1) & 0x78787878u, Mh, Ch, hi + 2 * k);
+      const uint32_t w8 = w[k] >> 8;
+      lo[2 * k] = hfma2(hfma2((w[k] & 0x000F000Fu) | 0x64006400u, SL, CL), D, BL);
+      lo[2 * k + 1] = hfma2(hfma2((w8 & 0x000F000Fu) | 0x64006400u, SL, CL), D, BL);
+      hi[2 * k] = hfma2(hfma2((w[k] & 0x00F000F0u) | 0x64006400u, SH, CH), D, BH);
+      hi[2 * k + 1] = hfma2(hfma2((w8 & 0x00F000F0u) | 0x64006400u, SH, CH), D, BH);
     }
     tmem_st16(tcol + 32 * g, lo);
     tmem_st16(tcol + 32 * g + 16, hi);
@@ -406,12 +424,15 @@ __global__ void __launch_bounds__(256) pack_kernel(ForwardArgs a, const float *g
       hi[j] = __float2half_rn(xs[j]);
       lo[j] = __float2half_rn(xs[j] - __half2float(hi[j]));
     }
+    // expert inputs feed the Q4_K gate/up tiles, whose columns pair K values (0, 2) and
+    // (1, 3) of each group of four (deq_q4k): the same order here
+    const int a1 = INPUT ? 2 : 1, a2 = INPUT ? 1 : 2;
     const size_t row = split ? 2 * (size_t)pos : (size_t)pos;
     *reinterpret_cast<uint2 *>(out + row * K + i) =
-        make_uint2(h2u(__halves2half2(hi[0], hi[1])), h2u(__halves2half2(hi[2], hi[3])));
+        make_uint2(h2u(__halves2half2(hi[0], hi[a1])), h2u(__halves2half2(hi[a2], hi[3])));
     if (split)
       *reinterpret_cast<uint2 *>(out + (row + 1) * K + i) =
-          make_uint2(h2u(__halves2half2(lo[0], lo[1])), h2u(__halves2half2(lo[2], lo[3])));
+          make_uint2(h2u(__halves2half2(lo[0], lo[a1])), h2u(__halves2half2(lo[a2], lo[3])));
   }
   if (threadIdx.x == 0) inv[pos] = 1.0f / s;
 }
@@ -428,11 +449,20 @@ __device__ __forceinline__ bool aborted(const int *abort_flag) {
   return *reinterpret_cast<const volatile int *>(abort_flag) != 0;
 }
 
-// Bounded wait that also gives up as soon as another thread of the CTA has aborted.
+// Bounded wait that also gives up once another thread of the CTA has aborted. The abort
+// flag and the clock are checked every 8 tries, so a spinning warp issues few
+// instructions besides the try itself (the producers share the issue slots); SLEEP_NS > 0
+// backs off between tries, for waits that have slack (the epilogue's accumulator wait,
+// the TMA warps' free-slot waits).
+template <int SLEEP_NS = 0>
 __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, const int *abort_flag) {
   const long long start = clock64();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+#pragma unroll 1
+    for (int i = 0; i < 8; i++) {
+      if (mbar_try(bar, parity)) return true;
+      if (SLEEP_NS > 0) __nanosleep(SLEEP_NS);
+    }
     if (*reinterpret_cast<const volatile int *>(abort_flag)) return false;
     if (clock64() - start > kWaitCycles) return false;
   }
@@ -465,15 +495,17 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t bdesc, u
 // Warp roles: 0..3 epilogue (TMEM lane quarter = warp); 4..19 producers, two groups of
 // eight (group g dequantises the steps t = g mod 2; in a group, warp 4 + 8g + 4hf + q
 // covers lanes 32q.. and half hf of the K step); 20 TMA of the activation tiles; 21 TMA
-// of the raw weight tiles; 22 and 23 MMA issue (one tcgen05.mma issuer is latency-bound
-// at ~45 cycles per instruction; two issuers with separate accumulators double the rate,
-// deterministically).
+// of the raw weight tiles; 22..25 MMA issue (one tcgen05.mma issuer is latency-bound at
+// ~45 cycles per instruction in isolation and ~120 beside busy producer warps; up to four
+// issuers, one per SM sub-partition, each into its own accumulator, raise the rate; the
+// epilogue adds their partial sums in issuer order, so results stay deterministic).
 constexpr int kEpilogueWarps = 4;
 constexpr int kProducerWarps = 16;
 constexpr int kTmaWarp = kEpilogueWarps + kProducerWarps;  // 20
 constexpr int kRawWarp = kTmaWarp + 1;                     // 21
-constexpr int kMmaWarp = kRawWarp + 1;                     // 22, 23
-constexpr int kTcThreads = (kMmaWarp + 2) * 32;            // 768
+constexpr int kMmaWarp = kRawWarp + 1;                     // 22 .. 25
+constexpr int kMaxIssuers = 4;
+constexpr int kTcThreads = (kMmaWarp + kMaxIssuers) * 32;  // 832
 constexpr int kStepK = 256;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
 constexpr int kBarBytes = 512;
@@ -504,8 +536,14 @@ struct RawTile {
 template <int KIND, int NT, bool SPLIT>
 struct Cfg {
   static constexpr int NB = SPLIT ? 2 * NT : NT;
-  static constexpr int NA = 3 * 128 + 4 * NB <= 512 ? 3 : 2;
-  static constexpr int NI = NA * 128 + 4 * NB <= 512 ? 2 : 1;
+  // Tensor memory (512 columns): NA A stages of 128 columns, then AB accumulator buffers
+  // of NI issuers x NB columns. Four issuers (one per SM sub-partition) when their
+  // accumulators fit beside three A stages, single-buffered if need be (the epilogue
+  // then reads all partial sums before it stores); otherwise two or one, double-buffered.
+  static constexpr int NI4_AB = 3 * 128 + 2 * 4 * NB <= 512 ? 2 : (3 * 128 + 4 * NB <= 512 ? 1 : 0);
+  static constexpr int NA = NI4_AB ? 3 : (3 * 128 + 4 * NB <= 512 ? 3 : 2);
+  static constexpr int NI = NI4_AB ? 4 : (NA * 128 + 4 * NB <= 512 ? 2 : 1);
+  static constexpr int AB = NI4_AB ? NI4_AB : 2;
   static constexpr int kAccCol = NA * 128;
   static constexpr int kBStage = (kStepK / 64) * NB * 128;  // 4 swizzle atoms of NB rows
   static constexpr int kFixed = 1024 + NA * kBStage + kBarBytes;
@@ -710,7 +748,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
         for (int ks = 0; ks < nsteps; ks++, t++) {
           const int i = t % depth;
           const uint32_t free_bar = is_b ? bars.empty(i) : bars.rawempty(i);
-          if ((t >= depth && !wait_or_abort(free_bar, (uint32_t)((t / depth - 1) & 1), &abort_flag)) ||
+          if ((t >= depth && !wait_or_abort<64>(free_bar, (uint32_t)((t / depth - 1) & 1), &abort_flag)) ||
               aborted(&abort_flag)) {
             atomicExch(&abort_flag, 1);
             stop = true;
@@ -755,8 +793,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
       int t = 0;
       bool stop = false;
       for (int lu = 0; lu < my_units && !stop; lu++) {
-        const int acc = lu & 1;
-        if (lu >= 2 && !wait_or_abort(bars.accempty(acc), (uint32_t)(((lu >> 1) - 1) & 1), &abort_flag)) {
+        const int acc = lu % C::AB;
+        if (lu >= C::AB &&
+            !wait_or_abort(bars.accempty(acc), (uint32_t)((lu / C::AB - 1) & 1), &abort_flag)) {
           atomicExch(&abort_flag, 1);
           break;
         }
@@ -774,10 +813,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
           const int slices = min(kStepK, K - kStepK * ks) / 16;
           const uint32_t acol = tmem + (uint32_t)ab * 128u;
           const uint32_t bst = b_base + (uint32_t)ab * C::kBStage;
-          if (issuer == 0)
-            issue_step<NB, NI, 0>(dcol, acol, bst, slices, ks == 0);
-          else
-            issue_step<NB, NI, NI - 1>(dcol, acol, bst, slices, ks == 0);
+          switch (issuer) {
+            case 0: issue_step<NB, NI, 0>(dcol, acol, bst, slices, ks == 0); break;
+            case 1: issue_step<NB, NI, 1 % NI>(dcol, acol, bst, slices, ks == 0); break;
+            case 2: issue_step<NB, NI, 2 % NI>(dcol, acol, bst, slices, ks == 0); break;
+            default: issue_step<NB, NI, 3 % NI>(dcol, acol, bst, slices, ks == 0); break;
+          }
           mma_commit(bars.empty(ab));
         }
         if (!stop) mma_commit(bars.accfull(acc));
@@ -790,12 +831,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
     const int q = warp, r = 32 * q + lane;
     UnitWalk walk{a.items, (int)blockIdx.x, (int)unit_stride, n_tiles, my_units};
     for (int lu = 0; lu < my_units; lu++) {
-      const int acc = lu & 1;
+      const int acc = lu % C::AB;
       const Unit un = walk.at(lu);
       // the unit's row scales, one token per lane (loaded before the wait)
       const float inv_a = lane < un.ntok ? b_inv[un.pos0 + lane] : 0.0f;
       const float inv_b = NT > 32 && lane + 32 < un.ntok ? b_inv[un.pos0 + 32 + lane] : 0.0f;
-      const bool ok = wait_or_abort(bars.accfull(acc), (uint32_t)((lu >> 1) & 1), &abort_flag);
+      const bool ok = wait_or_abort<128>(bars.accfull(acc), (uint32_t)((lu / C::AB) & 1), &abort_flag);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) atomicExch(&abort_flag, 1);
         break;
@@ -808,6 +849,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
       constexpr int TPC = SPLIT ? CW / 2 : CW;         // tokens per chunk
       // gate/up rows: A rows 2i and 2i+1 hold index 0 and 1 of the gate|up axis
       const bool swapped = un.e == a.E ? side.sh_up_swapped : side.up_swapped;
+      float *out = KIND == kUpQ4K ? gu : a.ysorted;
+      const int ld = KIND == kUpQ4K ? 2 * a.I : a.H;
+      const int col = KIND == kUpQ4K ? un.tile * 128 + (r ^ (swapped ? 1 : 0)) : un.tile * 128 + r;
+      if constexpr (C::AB == 1) {
+        // single accumulator buffer: add the issuers' partial sums (in issuer order) into
+        // registers, free the accumulators for the next unit, then store
+        float v[NB];
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+#pragma unroll
+          for (int c0 = 0; c0 < NB; c0 += 16) {
+            float w[16];
+            tmem_ld16(taddr + i * NB + c0, reinterpret_cast<uint32_t *>(w));
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 16; c++) v[c0 + c] = i == 0 ? w[c] : v[c0 + c] + w[c];
+          }
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bars.accempty(acc));
+#pragma unroll
+        for (int j = 0; j < (SPLIT ? NB / 2 : NB); j++) {
+          const float val = SPLIT ? v[2 * j] + v[2 * j + 1] : v[j];
+          const float inv = __shfl_sync(0xffffffffu, j < 32 ? inv_a : inv_b, j & 31);
+          if (j < un.ntok) out[(size_t)(un.pos0 + j) * ld + col] = val * inv;
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < NB; c0 += CW) {
         float w[NI][CW];
@@ -831,9 +901,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
         }
         const int nbase = SPLIT ? c0 / 2 : c0;
         // up: gate of i at gu column 2i, up at 2i + 1 (a warp writes 128 contiguous bytes)
-        float *out = KIND == kUpQ4K ? gu : a.ysorted;
-        const int ld = KIND == kUpQ4K ? 2 * a.I : a.H;
-        const int col = KIND == kUpQ4K ? un.tile * 128 + (r ^ (swapped ? 1 : 0)) : un.tile * 128 + r;
 #pragma unroll
         for (int j = 0; j < TPC; j++) {
           const float val = SPLIT ? v[2 * j] + v[2 * j + 1] : v[j];
@@ -975,7 +1042,7 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
         const int ex = shared ? 0 : un.e;
         for (int ks = 0; ks < nsteps; ks++, t++) {
           const int i = t % S;
-          if ((t >= S && !wait_or_abort(empty(i), (uint32_t)((t / S - 1) & 1), &abort_flag)) ||
+          if ((t >= S && !wait_or_abort<64>(empty(i), (uint32_t)((t / S - 1) & 1), &abort_flag)) ||
               aborted(&abort_flag)) {
             atomicExch(&abort_flag, 1);
             stop = true;
@@ -1036,7 +1103,7 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
     for (int lu = 0; lu < my_units; lu++) {
       const int acc = lu & 1;
       const Unit un = walk.at(lu);
-      const bool ok = wait_or_abort(accfull(acc), (uint32_t)((lu >> 1) & 1), &abort_flag);
+      const bool ok = wait_or_abort<128>(accfull(acc), (uint32_t)((lu >> 1) & 1), &abort_flag);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) atomicExch(&abort_flag, 1);
         break;
