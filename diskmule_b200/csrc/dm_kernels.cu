@@ -111,38 +111,106 @@ int launch_transpose_router(const void *src, int src_bf16, int E, int H, const f
 // Gemma router / expert input (src/gemma4/cpu.rs:559-573, rms_norm src/cpu.rs:99-143)
 // ---------------------------------------------------------------------------
 
-constexpr int kPrepTokens = 8;
+// Gemma router and expert inputs (src/gemma4/cpu.rs:559-573, rms_norm src/cpu.rs:99-143).
+// The sum of squares is the reference's sequential fma fold, so each token's chain is one
+// thread: a CTA takes 16 tokens, streams their rows through a 3-stage ring of 256-column
+// chunks (cp.async, all threads), and warp 0 runs the 16 chains at fma latency; then all
+// threads write both outputs (x re-read from L2).
+constexpr int kPrepTokens = 16;
+constexpr int kPrepChunk = 256;
+constexpr int kPrepStages = 3;
+constexpr int kPrepLd = kPrepChunk + 4;  // padded row: lane t reads row t at one column
+
+__device__ __forceinline__ void prep_cp16(float *dst, const float *src) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
 
 __global__ void __launch_bounds__(256) gemma_prep_kernel(ForwardArgs a) {
-  extern __shared__ __align__(16) float xs[];  // [kPrepTokens][H + 4]
+  extern __shared__ __align__(16) float ring[];  // [kPrepStages][kPrepTokens][kPrepLd]
   __shared__ float inv_s[kPrepTokens];
-  const int H = a.H, HP = H + 4;
+  const int H = a.H;
   const int t0 = blockIdx.x * kPrepTokens;
   const int nt = min(kPrepTokens, a.T - t0);
   const float *x = reinterpret_cast<const float *>(a.x);
-#pragma unroll 4
-  for (int idx = threadIdx.x; idx < nt * (H / 4); idx += blockDim.x) {
-    int tt = idx / (H / 4), c = idx - tt * (H / 4);
-    *reinterpret_cast<float4 *>(xs + tt * HP + 4 * c) =
-        *reinterpret_cast<const float4 *>(x + (size_t)(t0 + tt) * H + 4 * c);
+  // the norm vectors are read by every token of the CTA: ask L2 for them now
+  for (int i = threadIdx.x * 32; i < H; i += blockDim.x * 32) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(a.router_scale + i));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(a.routed_pre_norm + i));
   }
-  __syncthreads();
+  // Few tokens: whole rows fit the buffer ([nt][H + 4]), all requested at once.
+  // Otherwise 256-column chunks through the ring.
+  const int HP = H + 4;
+  const bool flat = nt * HP <= kPrepStages * kPrepTokens * kPrepLd;
+  const int nchunks = flat ? 1 : (H + kPrepChunk - 1) / kPrepChunk;
+  const int cw = flat ? H : kPrepChunk, ld = flat ? HP : kPrepLd;
+  auto issue = [&](int c) {
+    if (c < nchunks) {
+      const int c0 = c * cw, w4 = min(cw, H - c0) / 4;
+      float *st = ring + (flat ? 0 : (c % kPrepStages) * kPrepTokens * kPrepLd);
+      for (int idx = threadIdx.x; idx < nt * w4; idx += blockDim.x) {
+        const int tt = idx / w4, q = idx - tt * w4;
+        prep_cp16(st + tt * ld + 4 * q, x + (size_t)(t0 + tt) * H + c0 + 4 * q);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int c = 0; c < kPrepStages - 1; c++) issue(c);
+  float s = 0.0f;
+  for (int c = 0; c < nchunks; c++) {
+    issue(c + kPrepStages - 1);
+    asm volatile("cp.async.wait_group %0;" ::"n"(kPrepStages - 1) : "memory");
+    __syncthreads();
+    if (threadIdx.x < nt) {
+      const float *row = ring + (flat ? 0 : (c % kPrepStages) * kPrepTokens * kPrepLd) + threadIdx.x * ld;
+      const int w = min(cw, H - c * cw);
+#pragma unroll 4
+      for (int i = 0; i < w; i += 4) {  // 16-byte reads: padded rows spread the banks
+        const float4 v = *reinterpret_cast<const float4 *>(row + i);
+        s = __fmaf_rn(v.x, v.x, s);
+        s = __fmaf_rn(v.y, v.y, s);
+        s = __fmaf_rn(v.z, v.z, s);
+        s = __fmaf_rn(v.w, v.w, s);
+      }
+    }
+    __syncthreads();  // the stage is refilled by the next iteration's issue
+  }
   if (threadIdx.x < nt) {
-    const float *row = xs + threadIdx.x * HP;
-    float s = 0.0f;
-#pragma unroll 16
-    for (int i = 0; i < H; i++) s = __fmaf_rn(row[i], row[i], s);
-    float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)H), a.epsilon)));
+    const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)H), a.epsilon)));
     if (!isfinite(inv)) atomicExch(a.status, kStatusNonFiniteNorm);
     inv_s[threadIdx.x] = inv;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < nt * H; idx += blockDim.x) {
-    int tt = idx / H, i = idx - tt * H;
-    float v = xs[tt * HP + i], inv = inv_s[tt];
-    size_t o = (size_t)(t0 + tt) * H + i;
-    a.router_in[o] = __fmul_rn(__fmul_rn(v, inv), __fmul_rn(a.router_scale[i], a.inv_sqrt_hidden));
-    a.expert_in[o] = __fmul_rn(__fmul_rn(v, a.routed_pre_norm[i]), inv);
+  // outputs: four independent 16-byte pieces per thread and pass, so the L2 reads overlap
+  const int h4 = H / 4, n4 = nt * h4;
+  for (int base = threadIdx.x; base < n4; base += 4 * blockDim.x) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int idx = base + u * blockDim.x;
+      if (idx < n4) {
+        const int tt = idx / h4, q = idx - tt * h4;
+        v[u] = *reinterpret_cast<const float4 *>(x + (size_t)(t0 + tt) * H + 4 * q);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int idx = base + u * blockDim.x;
+      if (idx >= n4) break;
+      const int tt = idx / h4, q = idx - tt * h4;
+      const size_t o = (size_t)(t0 + tt) * H + 4 * q;
+      const float inv = inv_s[tt];
+      const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      float ri[4], ei[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {  // caller vectors: 4-byte alignment only
+        const float rr = a.router_scale[4 * q + j], pp = a.routed_pre_norm[4 * q + j];
+        ri[j] = __fmul_rn(__fmul_rn(vv[j], inv), __fmul_rn(rr, a.inv_sqrt_hidden));
+        ei[j] = __fmul_rn(__fmul_rn(vv[j], pp), inv);
+      }
+      *reinterpret_cast<float4 *>(a.router_in + o) = make_float4(ri[0], ri[1], ri[2], ri[3]);
+      *reinterpret_cast<float4 *>(a.expert_in + o) = make_float4(ei[0], ei[1], ei[2], ei[3]);
+    }
   }
 }
 
@@ -1162,7 +1230,7 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   const void *router_x = a.x;
   bool router_x_bf16 = a.input_bf16;
   if (a.family == kGemma) {
-    size_t smem = (size_t)kPrepTokens * (a.H + 4) * sizeof(float);
+    size_t smem = (size_t)kPrepStages * kPrepTokens * kPrepLd * sizeof(float);
     set_smem(gemma_prep_kernel, smem);
     gemma_prep_kernel<<<(a.T + kPrepTokens - 1) / kPrepTokens, 256, smem, stream>>>(a);
     launches++;
