@@ -5,6 +5,8 @@
 // the per-element value follows the reference (e.g. Q4_K: (d*sc)*q - dmin*m).
 #pragma once
 
+#include <utility>
+
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -258,6 +260,28 @@ struct F32Unit {
 // device): the attribute persists, and raising the limit alone does not change a
 // launch's occupancy (that follows the shared memory it actually requests).
 cudaError_t ensure_smem_limit(const void *kernel);
+
+// Programmatic dependent launch along the forward chain: a kernel launched this way may
+// be scheduled while its predecessor drains, so its first statement is pdl_wait(), which
+// returns once the predecessor has completed and its writes are visible (and at once when
+// the kernel was launched without the attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args &&...args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Scratch carved from one device allocation, 256-byte aligned pieces.
 // Carves 256-byte-aligned pieces from one allocation; a request past the capacity

@@ -388,6 +388,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_up_kernel(ForwardArgs a, Ma
                                                               MatrixRef up, MatrixRef sh_gate,
                                                               MatrixRef sh_up, int up_row_offset,
                                                               int rows_per_cta) {
+  pdl_wait();
   extern __shared__ __align__(16) float smem[];
   if ((int)blockIdx.y >= *a.n_items) return;
   const int4 item = a.items[blockIdx.y];  // (expert, first token of the chunk, ...)
@@ -455,6 +456,7 @@ template <int KIND, int NT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_down_kernel(ForwardArgs a, MatrixRef down,
                                                                 MatrixRef sh_down,
                                                                 int rows_per_cta) {
+  pdl_wait();
   extern __shared__ __align__(16) float smem[];
   if ((int)blockIdx.y >= *a.n_items) return;
   const int4 item = a.items[blockIdx.y];
@@ -589,6 +591,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_up_kernel(ForwardArgs a, 
                                                                  MatrixRef sh_up,
                                                                  int up_row_offset,
                                                                  int rows_per_cta) {
+  pdl_wait();
   extern __shared__ __align__(16) float smem[];
   if ((int)blockIdx.y >= *a.n_items) return;
   const int4 item = a.items[blockIdx.y];
@@ -649,6 +652,7 @@ template <int KIND, int NT>
 __global__ void __launch_bounds__(kDenseThreads) dense_down_kernel(ForwardArgs a, MatrixRef down,
                                                                    MatrixRef sh_down,
                                                                    int rows_per_cta) {
+  pdl_wait();
   extern __shared__ __align__(16) float smem[];
   if ((int)blockIdx.y >= *a.n_items) return;
   const int4 item = a.items[blockIdx.y];
@@ -724,7 +728,7 @@ static void launch_dense_up(const ForwardArgs &a, const GemvPlan &p, cudaStream_
   auto fn = dense_up_kernel<KIND, NT>;
   if (smem > 48 * 1024) ensure_smem_limit((const void *)fn);
   dim3 grid((a.I + rows - 1) / rows, p.max_items);
-  fn<<<grid, kDenseThreads, smem, s>>>(a, g, u, sg, su, a.family == kGemma ? a.I : 0, rows);
+  launch_pdl(fn, grid, dim3(kDenseThreads), smem, s, a, g, u, sg, su, a.family == kGemma ? a.I : 0, rows);
 }
 
 template <int KIND, int NT>
@@ -736,7 +740,7 @@ static void launch_dense_down(const ForwardArgs &a, const GemvPlan &p, cudaStrea
   auto fn = dense_down_kernel<KIND, NT>;
   if (smem > 48 * 1024) ensure_smem_limit((const void *)fn);
   dim3 grid((a.H + rows - 1) / rows, p.max_items);
-  fn<<<grid, kDenseThreads, smem, s>>>(a, d, sd, rows);
+  launch_pdl(fn, grid, dim3(kDenseThreads), smem, s, a, d, sd, rows);
 }
 
 template <int KIND, int NT>
@@ -755,7 +759,7 @@ static void launch_up(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s) {
   MatrixRef u = matrix(KIND, a.family == kGemma ? a.gate : a.up, a.up_stride, up_rows, a.H, p.up);
   MatrixRef sg = matrix(KIND, a.sh_gate, 0, a.I, a.H, p.sh_gate);
   MatrixRef su = matrix(KIND, a.sh_up, 0, a.I, a.H, p.sh_up);
-  fn<<<grid, kGemvThreads, smem, s>>>(a, g, u, sg, su, a.family == kGemma ? a.I : 0, rows);
+  launch_pdl(fn, grid, dim3(kGemvThreads), smem, s, a, g, u, sg, su, a.family == kGemma ? a.I : 0, rows);
 }
 
 template <int KIND, int NT>
@@ -771,7 +775,7 @@ static void launch_down(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s)
   dim3 grid((a.H + rows - 1) / rows, p.max_items);
   MatrixRef d = matrix(KIND, a.down, a.down_stride, a.H, a.I, p.down);
   MatrixRef sd = matrix(KIND, a.sh_down, 0, a.H, a.I, p.sh_down);
-  fn<<<grid, kGemvThreads, smem, s>>>(a, d, sd, rows);
+  launch_pdl(fn, grid, dim3(kGemvThreads), smem, s, a, d, sd, rows);
 }
 
 template <int NT>

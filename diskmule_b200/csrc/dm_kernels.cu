@@ -127,6 +127,7 @@ __device__ __forceinline__ void prep_cp16(float *dst, const float *src) {
 }
 
 __global__ void __launch_bounds__(256) gemma_prep_kernel(ForwardArgs a) {
+  pdl_wait();
   extern __shared__ __align__(16) float ring[];  // [kPrepStages][kPrepTokens][kPrepLd]
   __shared__ float inv_s[kPrepTokens];
   const int H = a.H;
@@ -243,6 +244,7 @@ __global__ void __launch_bounds__(256) router_small_kernel(const float *rows, co
                                                           int H, int E1, int RT,
                                                           const float *lbias, int E,
                                                           float *logits, int32_t *status) {
+  pdl_wait();
   extern __shared__ __align__(16) float smem[];
   __shared__ __align__(8) unsigned long long bars[kRsMaxChunks];
   const int HP = H + 4;                                     // padded rows (16 bytes)
@@ -402,6 +404,7 @@ __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w3
                                                                  const float *xT2, int xld, int T,
                                                                  int H, int E1, const float *lbias,
                                                                  int E, float *logits) {
+  pdl_wait();
   extern __shared__ __align__(16) uint8_t rg_smem[];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int e0 = blockIdx.x * kRgExperts, t0 = blockIdx.y * kRgTokens;
@@ -466,6 +469,7 @@ __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w3
 // x [T][H] (f32 or bf16) -> xT2 [H][xld][2] f32, each value twice; tokens T..xld-1 zero.
 __global__ void __launch_bounds__(256) transpose_x_kernel(const void *x, int bf16, int T, int H,
                                                          int xld, float *xT2) {
+  pdl_wait();
   __shared__ float tile[32][33];
   const int h0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
   const int c = threadIdx.x & 31, r0 = threadIdx.x >> 5;
@@ -596,6 +600,7 @@ __global__ void __launch_bounds__(32 * kTopkWarps) topk_softmax_kernel(
 __global__ void __launch_bounds__(1024) topk_rank_softmax_kernel(const float *logits, int T, int E1,
                                                                 int E, int k, uint32_t *sel_idx,
                                                                 float *sel_w, int32_t *status) {
+  pdl_wait();
   __shared__ unsigned long long cand[32 * 32];
   __shared__ unsigned long long chosen[32];
   __shared__ int bad_s;
@@ -654,6 +659,7 @@ __global__ void __launch_bounds__(1024) topk_rank_softmax_kernel(const float *lo
 __global__ void __launch_bounds__(32 * kTopkWarps) topk_sigmoid_kernel(
     const float *logits, int T, int E1, int E, int k, const float *bias, int n_groups,
     int topk_groups, int normalize, uint32_t *sel_idx, float *sel_w, int32_t *status) {
+  pdl_wait();
   __shared__ float choice_s[kTopkWarps][kMaxGlmExperts];
   __shared__ unsigned char keep_s[kTopkWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -801,6 +807,7 @@ __device__ __forceinline__ void block_exclusive_scan3(int &a, int &b, int &c, in
 // Rows mode (expert-parallel rows): sel_idx holds explicit expert ids where id E is the
 // shared expert, so E + 1 buckets are counted and no shared pairs are added.
 __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs a) {
+  pdl_wait();
   extern __shared__ int32_t sm[];
   const int E = a.E, P = a.T * a.k;
   const int EB = E + (a.rows_mode ? 1 : 0);      // buckets counted from sel_idx
@@ -931,6 +938,7 @@ __device__ __forceinline__ void unit_dot(const float *w, const float *xs, int un
 template <class U, int TT>
 __global__ void __launch_bounds__(kExpertThreads) expert_up_kernel(ForwardArgs a,
                                                                   int rows_per_cta) {
+  pdl_wait();
   extern __shared__ __align__(16) float xs[];
   const int slot = blockIdx.y;
   if (slot >= *a.n_active) return;
@@ -982,6 +990,7 @@ __global__ void __launch_bounds__(kExpertThreads) expert_up_kernel(ForwardArgs a
 template <class U, int TT>
 __global__ void __launch_bounds__(kExpertThreads) expert_down_kernel(ForwardArgs a,
                                                                     int rows_per_cta) {
+  pdl_wait();
   extern __shared__ __align__(16) float xs[];
   const int slot = blockIdx.y;
   if (slot >= *a.n_active) return;
@@ -1030,6 +1039,7 @@ __global__ void __launch_bounds__(kExpertThreads) expert_down_kernel(ForwardArgs
 constexpr int kCombineThreads = 64;
 
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(ForwardArgs a) {
+  pdl_wait();
   __shared__ int pos_s[32];
   __shared__ float w_s[32];
   __shared__ float gate_s;
@@ -1128,6 +1138,7 @@ static ExpertFn expert_fn(bool up, int kind, int tt) {
 constexpr int kSmallPairs = 64;
 
 __global__ void __launch_bounds__(32) dispatch_small_kernel(ForwardArgs a) {
+  pdl_wait();
   extern __shared__ int32_t cnt[];  // [E + 1]
   const int E = a.E, P = a.T * a.k, lane = threadIdx.x;
   const int EB = E + (a.rows_mode ? 1 : 0);
@@ -1201,6 +1212,7 @@ __global__ void __launch_bounds__(32) dispatch_small_kernel(ForwardArgs a) {
 
 // Per-row outputs of the rows mode: out[r] = ysorted[inverse[r]] (k = 1, unweighted).
 __global__ void __launch_bounds__(128) scatter_rows_kernel(ForwardArgs a) {
+  pdl_wait();
   const int r = blockIdx.x, i4 = blockIdx.y * blockDim.x + threadIdx.x;
   if (i4 >= a.H / 4) return;
   const float4 v = *reinterpret_cast<const float4 *>(a.ysorted + (size_t)a.inverse[r] * a.H + 4 * i4);
@@ -1209,6 +1221,7 @@ __global__ void __launch_bounds__(128) scatter_rows_kernel(ForwardArgs a) {
 
 // the identity position map used when pair outputs arrive already in pair order
 __global__ void iota_kernel(int32_t *v, int n) {
+  pdl_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) v[i] = i;
 }
 
@@ -1217,7 +1230,7 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   int launches = 0;
   if (mode & kRunIdentity) {  // pair outputs given in pair order (expert-parallel combine)
     const int n = a.T * a.k + (a.shared ? a.T : 0);
-    iota_kernel<<<(n + 255) / 256, 256, 0, stream>>>(a.inverse, n);
+    launch_pdl(iota_kernel, dim3((n + 255) / 256), dim3(256), 0, stream, a.inverse, n);
     launches++;
   }
   const bool glm = a.family == kGlm;
@@ -1232,7 +1245,7 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   if (a.family == kGemma) {
     size_t smem = (size_t)kPrepStages * kPrepTokens * kPrepLd * sizeof(float);
     set_smem(gemma_prep_kernel, smem);
-    gemma_prep_kernel<<<(a.T + kPrepTokens - 1) / kPrepTokens, 256, smem, stream>>>(a);
+    launch_pdl(gemma_prep_kernel, dim3((a.T + kPrepTokens - 1) / kPrepTokens), dim3(256), smem, stream, a);
     launches++;
     router_x = a.router_in;
     router_x_bf16 = false;
@@ -1249,8 +1262,8 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   {                                                                                         \
     auto fn = router_small_kernel<G, X>;                                                    \
     set_smem(fn, smem);                                                                     \
-    fn<<<grid, 256, smem, stream>>>(a.router_rows, router_x, a.T, a.H, a.E1, RT, a.logit_bias, \
-                                    a.E, a.logits, a.status);                               \
+    launch_pdl(fn, grid, dim3(256), smem, stream, (const float *)a.router_rows, router_x, a.T,  \
+               a.H, a.E1, RT, a.logit_bias, a.E, a.logits, a.status);                       \
   }
     if (glm && router_x_bf16) DM_ROUTER_SMALL(true, true)
     else if (glm) DM_ROUTER_SMALL(true, false)
@@ -1258,8 +1271,8 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
 #undef DM_ROUTER_SMALL
   } else {
     const int xld = (a.T + kRgTokens - 1) / kRgTokens * kRgTokens;
-    transpose_x_kernel<<<dim3((a.H + 31) / 32, xld / 32), 256, 0, stream>>>(
-        router_x, router_x_bf16 ? 1 : 0, a.T, a.H, xld, a.xT);
+    launch_pdl(transpose_x_kernel, dim3((a.H + 31) / 32, xld / 32), dim3(256), 0, stream, router_x,
+               router_x_bf16 ? 1 : 0, a.T, a.H, xld, a.xT);
     launches++;
     dim3 grid((a.E1 + kRgExperts - 1) / kRgExperts, xld / kRgTokens);
     const size_t smem = (size_t)kRgStages * kRgStageBytes;
@@ -1267,8 +1280,9 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   {                                                                                          \
     auto fn = router_gemm_kernel<G>;                                                         \
     set_smem(fn, smem);                                                                      \
-    fn<<<grid, kRgThreads, smem, stream>>>(a.router_dup, router_dup_ld(a.E1), a.xT, xld, a.T, \
-                                           a.H, a.E1, a.logit_bias, a.E, a.logits);          \
+    launch_pdl(fn, grid, dim3(kRgThreads), smem, stream, (const float *)a.router_dup,          \
+               router_dup_ld(a.E1), (const float *)a.xT, xld, a.T, a.H, a.E1, a.logit_bias, a.E,  \
+               a.logits);                                                                    \
   }
     if (glm) DM_ROUTER_TILED(true)
     else DM_ROUTER_TILED(false)
@@ -1279,23 +1293,23 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   mark(kStageTopk);
   int topk_blocks = (a.T + kTopkWarps - 1) / kTopkWarps;
   if (glm)
-    topk_sigmoid_kernel<<<topk_blocks, 32 * kTopkWarps, 0, stream>>>(
-        a.logits, a.T, a.E1, a.E, a.k, a.bias, a.n_groups, a.topk_groups, a.normalize,
-        a.sel_idx, a.sel_w, a.status);
+    launch_pdl(topk_sigmoid_kernel, dim3(topk_blocks), dim3(32 * kTopkWarps), 0, stream,
+               (const float *)a.logits, a.T, a.E1, a.E, a.k, a.bias, a.n_groups, a.topk_groups,
+               a.normalize, a.sel_idx, a.sel_w, a.status);
   else
-    topk_rank_softmax_kernel<<<a.T, 32 * ((a.E + 31) / 32), 0, stream>>>(
-        a.logits, a.T, a.E1, a.E, a.k, a.sel_idx, a.sel_w, a.status);
+    launch_pdl(topk_rank_softmax_kernel, dim3(a.T), dim3(32 * ((a.E + 31) / 32)), 0, stream,
+               (const float *)a.logits, a.T, a.E1, a.E, a.k, a.sel_idx, a.sel_w, a.status);
   launches++;
   }
   if (mode & kRunExperts) {
   // 4. dispatch
   mark(kStageDispatch);
   if (a.T * a.k <= kSmallPairs) {
-    dispatch_small_kernel<<<1, 32, (size_t)(a.E + 1) * sizeof(int32_t), stream>>>(a);
+    launch_pdl(dispatch_small_kernel, dim3(1), dim3(32), (size_t)(a.E + 1) * sizeof(int32_t), stream, a);
   } else {
     size_t dsmem = ((size_t)kDispatchWarps * (a.E + 1) + 2 * (a.E + 1)) * sizeof(int32_t);
     set_smem(dispatch_kernel, dsmem);
-    dispatch_kernel<<<1, kDispatchThreads, dsmem, stream>>>(a);
+    launch_pdl(dispatch_kernel, dim3(1), dim3(kDispatchThreads), dsmem, stream, a);
   }
   launches++;
   // 5. gate/up (+activation) and 6. down, over the active experts
@@ -1336,12 +1350,12 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   // 7. combine (or the per-row outputs of the rows mode)
   mark(kStageCombine);
   if (mode & kRunCombine) {
-    combine_kernel<<<dim3(a.T, (a.H / 4 + kCombineThreads - 1) / kCombineThreads), kCombineThreads, 0,
-                     stream>>>(a);
+    launch_pdl(combine_kernel, dim3(a.T, (a.H / 4 + kCombineThreads - 1) / kCombineThreads),
+               dim3(kCombineThreads), 0, stream, a);
     launches++;
   }
   if (mode & kRunScatter) {
-    scatter_rows_kernel<<<dim3(a.T, (a.H / 4 + 127) / 128), 128, 0, stream>>>(a);
+    launch_pdl(scatter_rows_kernel, dim3(a.T, (a.H / 4 + 127) / 128), dim3(128), 0, stream, a);
     launches++;
   }
   mark(kStageCount);
