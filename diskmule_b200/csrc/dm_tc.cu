@@ -385,15 +385,22 @@ constexpr int kMaxPackI = 2048;  // intermediate rows staged in shared memory by
 // 2 NT rows then feeds both halves to a single MMA); without it row pos holds hi alone.
 // INPUT: x is the expert input row. Otherwise x = act(gate, up) of the row's gate/up
 // outputs gu[pos][2i] (gate) and gu[pos][2i + 1] (up), i < K.
+// One warp per row (8 rows per CTA): lane l takes the 16-byte pieces l, l + 32, ...;
+// the row maximum is a shuffle reduction; an input row is read twice (L2), an
+// intermediate row is activated once into the warp's shared-memory row.
+constexpr int kPackRows = 8;
+
 template <bool INPUT>
-__global__ void __launch_bounds__(256) pack_kernel(ForwardArgs a, const float *gu, __half *out,
-                                                  float *inv, int K, int split) {
-  __shared__ float red[8];
-  __shared__ __align__(16) float hrow[INPUT ? 4 : kMaxPackI];
-  const int pos = blockIdx.x;
+__global__ void __launch_bounds__(32 * kPackRows) pack_kernel(ForwardArgs a, const float *gu,
+                                                             __half *out, float *inv, int K,
+                                                             int split) {
+  extern __shared__ __align__(16) float hrows[];  // [kPackRows][K] (intermediates only)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = blockIdx.x * kPackRows + warp;
   if (pos >= a.offsets[a.E + 1]) return;
   const float *src;
   const int P = a.T * a.k, pr = a.sorted[pos];
+  const int k4 = K / 4;
   if (INPUT) {
     const int tok = pr < P ? pr / a.k : pr - P;
     src = (a.family == kGemma ? a.expert_in : reinterpret_cast<const float *>(a.x)) +
@@ -401,22 +408,31 @@ __global__ void __launch_bounds__(256) pack_kernel(ForwardArgs a, const float *g
   } else {
     const int e = pr < P ? (int)a.sel_idx[pr] : a.E;
     const float *row = gu + (size_t)pos * 2 * K;
-    for (int i = threadIdx.x * 2; i < K; i += blockDim.x * 2) {
-      const float4 v = *reinterpret_cast<const float4 *>(row + 2 * i);
-      hrow[i] = activate(a, e, v.x, v.y);
-      hrow[i + 1] = activate(a, e, v.z, v.w);
+    float *h = hrows + (size_t)warp * K;
+    for (int q = lane; q < k4; q += 32) {
+      const float4 g0 = *reinterpret_cast<const float4 *>(row + 8 * q);
+      const float4 g1 = *reinterpret_cast<const float4 *>(row + 8 * q + 4);
+      *reinterpret_cast<float4 *>(h + 4 * q) =
+          make_float4(activate(a, e, g0.x, g0.y), activate(a, e, g0.z, g0.w),
+                      activate(a, e, g1.x, g1.y), activate(a, e, g1.z, g1.w));
     }
-    __syncthreads();
-    src = hrow;
+    __syncwarp();
+    src = h;
   }
   float m = 0.0f;
-  for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
-    const float4 v = *reinterpret_cast<const float4 *>(src + i);
+  for (int q = lane; q < k4; q += 32) {
+    const float4 v = *reinterpret_cast<const float4 *>(src + 4 * q);
     m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
-  const float s = pow2_scale(block_max(m, red));
-  for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
-    const float4 v = *reinterpret_cast<const float4 *>(src + i);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float s = pow2_scale(m);
+  // expert inputs feed the Q4_K gate/up tiles, whose columns pair K values (0, 2) and
+  // (1, 3) of each group of four (deq_q4k): the same order here
+  const int a1 = INPUT ? 2 : 1, a2 = INPUT ? 1 : 2;
+  const size_t orow = split ? 2 * (size_t)pos : (size_t)pos;
+  for (int q = lane; q < k4; q += 32) {
+    const float4 v = *reinterpret_cast<const float4 *>(src + 4 * q);
     const float xs[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
     __half hi[4], lo[4];
 #pragma unroll
@@ -424,17 +440,13 @@ __global__ void __launch_bounds__(256) pack_kernel(ForwardArgs a, const float *g
       hi[j] = __float2half_rn(xs[j]);
       lo[j] = __float2half_rn(xs[j] - __half2float(hi[j]));
     }
-    // expert inputs feed the Q4_K gate/up tiles, whose columns pair K values (0, 2) and
-    // (1, 3) of each group of four (deq_q4k): the same order here
-    const int a1 = INPUT ? 2 : 1, a2 = INPUT ? 1 : 2;
-    const size_t row = split ? 2 * (size_t)pos : (size_t)pos;
-    *reinterpret_cast<uint2 *>(out + row * K + i) =
+    *reinterpret_cast<uint2 *>(out + orow * K + 4 * q) =
         make_uint2(h2u(__halves2half2(hi[0], hi[a1])), h2u(__halves2half2(hi[a2], hi[3])));
     if (split)
-      *reinterpret_cast<uint2 *>(out + (row + 1) * K + i) =
+      *reinterpret_cast<uint2 *>(out + (orow + 1) * K + 4 * q) =
           make_uint2(h2u(__halves2half2(lo[0], lo[a1])), h2u(__halves2half2(lo[a2], lo[3])));
   }
-  if (threadIdx.x == 0) inv[pos] = 1.0f / s;
+  if (lane == 0) inv[pos] = 1.0f / s;
 }
 
 // ---------------------------------------------------------------------------
@@ -1287,10 +1299,16 @@ template <int NT>
 static int launch_nt(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, cudaStream_t s,
                      cudaEvent_t down_mark) {
   const int rows_bound = a.T * a.k + (a.shared ? a.T : 0);
-  tc::pack_kernel<true><<<rows_bound, 256, 0, s>>>(a, nullptr, p.x16, p.x_inv, a.H, p.split_x ? 1 : 0);
+  tc::pack_kernel<true><<<(rows_bound + tc::kPackRows - 1) / tc::kPackRows, 32 * tc::kPackRows, 0, s>>>(
+      a, nullptr, p.x16, p.x_inv, a.H, p.split_x ? 1 : 0);
   launch_kind<tc::kUpQ4K, NT>(p.x_map, a, w, p.x_inv, p, p.split_x, s);
   if (down_mark) cudaEventRecord(down_mark, s);
-  tc::pack_kernel<false><<<rows_bound, 256, 0, s>>>(a, p.gu, p.h16, p.h_inv, a.I, p.split_h ? 1 : 0);
+  {
+    const size_t hsmem = (size_t)tc::kPackRows * a.I * sizeof(float);
+    if (hsmem > 48 * 1024) ensure_smem_limit((const void *)tc::pack_kernel<false>);
+    tc::pack_kernel<false><<<(rows_bound + tc::kPackRows - 1) / tc::kPackRows, 32 * tc::kPackRows,
+                             hsmem, s>>>(a, p.gu, p.h16, p.h_inv, a.I, p.split_h ? 1 : 0);
+  }
   if (a.down_type == DM_Q6_K)
     launch_kind<tc::kDownQ6K, NT>(p.h_map, a, w, p.h_inv, p, p.split_h, s);
   else
