@@ -647,7 +647,7 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
     float *gu = arena.take<float>(2 * pairs * I);
     // token tiles: 16/32/64 for quantised weights; bf16 (GLM) always 128
     const bool bf16 = d.down_type == DM_BF16;
-    const int nts[3] = {bf16 ? 128 : 16, bf16 ? 128 : 32, bf16 ? 128 : 64};
+    const int nts[3] = {bf16 ? 256 : 16, bf16 ? 256 : 32, bf16 ? 256 : 64};
     int n_sm = 148;
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, L->ctx->device);
     const char *split_env = getenv("DISKMULE_CUDA_TC_SPLIT");

@@ -995,8 +995,11 @@ __device__ __forceinline__ void mma_ss(uint32_t d, uint64_t adesc, uint64_t bdes
 }
 
 // UP: gate/up rows (64 gate + 64 up interleaved), K = H, output gu; else down rows, K = I,
-// output ysorted. SPLIT: B rows are hi/lo pairs (2 per token).
-template <bool UP, int NB, bool SPLIT>
+// output ysorted. SPLIT: B rows are hi/lo pairs (2 per token). HALVES = 2: a work item
+// holds up to 2 x TPT tokens and each (item, row tile) is two units of TPT tokens; a unit
+// without tokens is skipped by every warp role alike, and the accumulator buffers and
+// barrier phases follow the count of units actually run.
+template <bool UP, int NB, bool SPLIT, int HALVES>
 __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
     const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap wmap,
     const __grid_constant__ CUtensorMap sh_wmap, ForwardArgs a, TcSide side, float *gu) {
@@ -1007,10 +1010,30 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
   __shared__ int abort_flag;
   const int K = UP ? a.H : a.I;
   const int n_tiles = UP ? a.I / 64 : a.H / 128;
-  const int n_units = *a.n_items * n_tiles;
+  const int n_units = *a.n_items * n_tiles * HALVES;
   if ((int)blockIdx.x >= n_units) return;
   const int my_units = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   const int nsteps = K / kBfStepK;
+  // the record of the unit after this one is requested while this one runs
+  int4 rec_next = make_int4(0, 0, 0, 0);
+  int item_next = -1;
+  auto unit_at = [&](int lu) {
+    const int u = (int)blockIdx.x + lu * (int)gridDim.x;
+    const int item = u / (n_tiles * HALVES), rem = u - item * (n_tiles * HALVES);
+    const int half = rem / n_tiles;  // every tile of the first half, then of the second
+    const int4 rec = item == item_next ? rec_next : a.items[item];
+    const int un_next = u + (int)gridDim.x;
+    if (un_next < n_units) {
+      item_next = un_next / (n_tiles * HALVES);
+      rec_next = a.items[item_next];
+    }
+    Unit un;
+    un.e = rec.x;
+    un.tile = rem - half * n_tiles;
+    un.pos0 = rec.z + half * TPT;
+    un.ntok = min(TPT, rec.w - half * TPT);
+    return un;
+  };
 
   const uint32_t raw = smem_u32(dsm);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -1039,15 +1062,14 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
   __syncthreads();
   fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(dsm + (slot - raw));
-  const uint32_t unit_stride = gridDim.x;
 
   if (warp == 4) {
     if (lane == 0) {
       int t = 0;
       bool stop = false;
-      UnitWalk walk{a.items, (int)blockIdx.x, (int)unit_stride, n_tiles, my_units};
       for (int lu = 0; lu < my_units && !stop; lu++) {
-        const Unit un = walk.at(lu);
+        const Unit un = unit_at(lu);
+        if (un.ntok <= 0) continue;
         if (*reinterpret_cast<const volatile int32_t *>(a.status) == kStatusTimeout)
           atomicExch(&abort_flag, 1);
         const bool shared = un.e == a.E;
@@ -1073,16 +1095,17 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
     }
   } else if (warp == 5) {
     if (lane == 0) {
-      int t = 0;
+      int t = 0, pu = 0;
       bool stop = false;
-      UnitWalk walk{a.items, (int)blockIdx.x, (int)unit_stride, n_tiles, my_units};
       for (int lu = 0; lu < my_units && !stop; lu++) {
-        const Unit un = walk.at(lu);
-        const int acc = lu & 1;
-        if (lu >= 2 && !wait_or_abort(accempty(acc), (uint32_t)(((lu >> 1) - 1) & 1), &abort_flag)) {
+        const Unit un = unit_at(lu);
+        if (un.ntok <= 0) continue;
+        const int acc = pu & 1;
+        if (pu >= 2 && !wait_or_abort(accempty(acc), (uint32_t)(((pu >> 1) - 1) & 1), &abort_flag)) {
           atomicExch(&abort_flag, 1);
           break;
         }
+        pu++;
         fence_after();
         // N sized to the unit's tokens (a multiple of 16): ragged tiles cost less
         const int rows = SPLIT ? 2 * un.ntok : un.ntok;
@@ -1111,11 +1134,13 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
     }
   } else if (warp < 4) {
     const int q = warp, r = 32 * q + lane;
-    UnitWalk walk{a.items, (int)blockIdx.x, (int)unit_stride, n_tiles, my_units};
+    int pu = 0;
     for (int lu = 0; lu < my_units; lu++) {
-      const int acc = lu & 1;
-      const Unit un = walk.at(lu);
-      const bool ok = wait_or_abort<128>(accfull(acc), (uint32_t)((lu >> 1) & 1), &abort_flag);
+      const Unit un = unit_at(lu);
+      if (un.ntok <= 0) continue;
+      const int acc = pu & 1;
+      const bool ok = wait_or_abort<128>(accfull(acc), (uint32_t)((pu >> 1) & 1), &abort_flag);
+      pu++;
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) atomicExch(&abort_flag, 1);
         break;
@@ -1257,8 +1282,9 @@ int make_tc_maps(TcPlan &p, int H, int I, int down_type, int nt) {
     p.bf16 = true;
     p.split_x = false;
     p.split_h = true;
+    // x tiles: nt tokens; h tiles: nt rows = nt / 2 tokens as hi/lo pairs
     if (!encode_bf16_rows(&p.x_map, p.x16, H, (uint64_t)p.rows, nt)) return -1;
-    if (!encode_bf16_rows(&p.h_map, p.h16, I, 2 * (uint64_t)p.rows, 2 * nt)) return -1;
+    if (!encode_bf16_rows(&p.h_map, p.h16, I, 2 * (uint64_t)p.rows, nt)) return -1;
     return 0;
   }
   p.split_x = p.split && fits_split<tc::kUpQ4K>(nt);
@@ -1316,14 +1342,17 @@ static int launch_nt(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, 
   return 4;
 }
 
+// Work items of up to 256 tokens: gate/up takes a whole item per unit (N = 256, every
+// weight tile read once per item); down, whose hi/lo rows double N, takes each item as
+// two units of 128 tokens.
 static int launch_bf16(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, cudaStream_t s,
                        cudaEvent_t down_mark) {
-  constexpr int NT = 128;
+  constexpr int NT = 256;
   if (p.nt != NT) return -1;
   const int rows_bound = a.T * a.k + (a.shared ? a.T : 0);
   tc::gather_bf16_kernel<<<rows_bound, 256, 0, s>>>(a, reinterpret_cast<__nv_bfloat16 *>(p.x16));
   {
-    auto fn = tc::tc_bf16_kernel<true, NT, false>;
+    auto fn = tc::tc_bf16_kernel<true, NT, false, 1>;
     ensure_smem_limit((const void *)fn);
     const int grid = std::max(1, std::min(p.n_sm, p.max_items * (a.I / 64)));
     fn<<<grid, tc::kBfThreads, tc::BfCfg<NT>::kSmem, s>>>(p.x_map, w.up, w.sh_up, a, w.side, p.gu);
@@ -1331,10 +1360,10 @@ static int launch_bf16(const ForwardArgs &a, const TcPlan &p, const TcWeights &w
   if (down_mark) cudaEventRecord(down_mark, s);
   tc::pack_h_bf16_kernel<<<rows_bound, 256, 0, s>>>(a, p.gu, reinterpret_cast<__nv_bfloat16 *>(p.h16));
   {
-    auto fn = tc::tc_bf16_kernel<false, 2 * NT, true>;
+    auto fn = tc::tc_bf16_kernel<false, NT, true, 2>;
     ensure_smem_limit((const void *)fn);
-    const int grid = std::max(1, std::min(p.n_sm, p.max_items * (a.H / 128)));
-    fn<<<grid, tc::kBfThreads, tc::BfCfg<2 * NT>::kSmem, s>>>(p.h_map, w.down, w.sh_down, a, w.side,
+    const int grid = std::max(1, std::min(p.n_sm, 2 * p.max_items * (a.H / 128)));
+    fn<<<grid, tc::kBfThreads, tc::BfCfg<NT>::kSmem, s>>>(p.h_map, w.down, w.sh_down, a, w.side,
                                                               p.gu);
   }
   return 4;
