@@ -64,13 +64,20 @@ REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_powe
 
 
 class ClockSampler:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    """nvidia-smi sampled every 200 ms while the timed region runs. Only one process
+    samples (`active`): several nvidia-smi pollers slow the driver calls of paths that
+    synchronise with the host every step. Entering waits `settle` seconds, so the timed
+    region starts after nvidia-smi's own start-up."""
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, active: bool = True, settle: float = 1.5):
         self.index = index
         self.proc = None
+        self.active = active
+        self.settle = settle
 
     def __enter__(self):
+        if not self.active:
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={CLOCK_QUERY}", "--format=csv,noheader,nounits",
@@ -78,6 +85,8 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+        if self.proc is not None and self.settle > 0:
+            time.sleep(self.settle)
         return self
 
     def __exit__(self, *exc):
@@ -260,7 +269,9 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, active=rank == 0) as clk:
+        barrier()  # rank 0 entered after the sampler settled
+        torch.cuda.synchronize()
         start.record(stream)
         for _ in range(args.steps):
             step(T, x.data_ptr(), y.data_ptr())
@@ -467,7 +478,9 @@ def run_ep(args):
     torch.cuda.synchronize()
     dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, active=rank == 0) as clk:
+        dist.barrier()  # rank 0 entered after the sampler settled
+        torch.cuda.synchronize()
         start.record(stream)
         for _ in range(args.steps):
             y = ep.forward(x)
@@ -627,10 +640,7 @@ def run_stack(args):
     s0 = st.cache.stats()
     stream = torch.cuda.current_stream()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(0) as clk:
-        # nvidia-smi's start-up stalls driver calls for a moment; this path calls the
-        # driver every layer, so the timed region starts after it has settled
-        time.sleep(2.0)
+    with ClockSampler(0, settle=2.0) as clk:
         a.record(stream)
         tokens = st.decode(warm[-1] if warm else first, args.steps)
         b.record(stream)
