@@ -1131,80 +1131,86 @@ static ExpertFn expert_fn(bool up, int kind, int tt) {
   return (ExpertFn)(tt == 8 ? pick_kernel<DownK, 8>(kind) : pick_kernel<DownK, 4>(kind));
 }
 
-// The same dispatch for at most kSmallPairs pairs (decode) with one warp: bucket counts
-// in shared memory, one segmented warp scan over the E + 1 buckets for the offsets,
-// the active list and the work items, and each pair's position from the pairs before
-// it with the same expert (stable: expert, then pair index).
+// The same dispatch for at most kSmallPairs pairs (decode) in one CTA with a thread per
+// bucket: counts in shared memory, one block-wide exclusive scan over the E + 1 buckets
+// for the offsets, the active list and the work items, and each pair's position from
+// the pairs before it with the same expert (stable: expert, then pair index).
 constexpr int kSmallPairs = 64;
 
-__global__ void __launch_bounds__(32) dispatch_small_kernel(ForwardArgs a) {
+__global__ void __launch_bounds__(1024) dispatch_small_kernel(ForwardArgs a) {
   pdl_wait();
-  extern __shared__ int32_t cnt[];  // [E + 1]
-  const int E = a.E, P = a.T * a.k, lane = threadIdx.x;
+  __shared__ int32_t cnt[1024];       // bucket counts, then first positions
+  __shared__ uint32_t sel[kSmallPairs];
+  __shared__ int32_t wsum[3][32];     // per-warp totals of counts, active buckets, items
+  const int E = a.E, P = a.T * a.k, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int EB = E + (a.rows_mode ? 1 : 0);
-  for (int e = lane; e <= E; e += 32) cnt[e] = 0;
-  __syncwarp();
-  uint32_t mine[kSmallPairs / 32];
-#pragma unroll
-  for (int j = 0; j < kSmallPairs / 32; j++) {
-    const int p = lane + 32 * j;
-    uint32_t e = p < P ? a.sel_idx[p] : 0xffffffffu;
-    if (p < P && e >= (uint32_t)EB) e = 0;  // rejected upstream; keep indices in range
-    mine[j] = e;
-    if (p < P) atomicAdd(&cnt[e], 1);
+  if (tid <= E) cnt[tid] = 0;
+  if (tid < P) {
+    uint32_t e = a.sel_idx[tid];
+    if (e >= (uint32_t)EB) e = 0;  // rejected upstream; keep indices in range
+    sel[tid] = e;
   }
-  __syncwarp();
-  if (a.shared && lane == 0) cnt[E] = a.T;
-  __syncwarp();
-  // rounds of 32 consecutive buckets (bucket e on lane e % 32): a warp scan per round plus
-  // the running totals, so every store of a round is one coalesced access
-  int c_run = 0, a_run = 0, i_run = 0;
-  for (int e0 = 0; e0 <= E; e0 += 32) {
-    const int e = e0 + lane;
-    const int c = e <= E ? cnt[e] : 0;
-    const int items = (c + a.chunk - 1) / a.chunk;
-    int c_inc = c, a_inc = c > 0, i_inc = items;
+  __syncthreads();
+  if (tid < P) atomicAdd(&cnt[sel[tid]], 1);
+  __syncthreads();
+  if (a.shared && tid == 0) cnt[E] = a.T;
+  __syncthreads();
+  // one thread per bucket: a block-wide exclusive scan of counts, active flags and items
+  const int e = tid;
+  const int c = e <= E ? cnt[e] : 0;
+  const int items = (c + a.chunk - 1) / a.chunk;
+  int c_inc = c, a_inc = c > 0, i_inc = items;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int cc = __shfl_up_sync(0xffffffffu, c_inc, o);
+    const int ac = __shfl_up_sync(0xffffffffu, a_inc, o);
+    const int ic = __shfl_up_sync(0xffffffffu, i_inc, o);
+    if (lane >= o) c_inc += cc, a_inc += ac, i_inc += ic;
+  }
+  if (lane == 31) wsum[0][warp] = c_inc, wsum[1][warp] = a_inc, wsum[2][warp] = i_inc;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (int)(blockDim.x >> 5);
+    int x0 = lane < nw ? wsum[0][lane] : 0, x1 = lane < nw ? wsum[1][lane] : 0,
+        x2 = lane < nw ? wsum[2][lane] : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int cc = __shfl_up_sync(0xffffffffu, c_inc, o);
-      const int ac = __shfl_up_sync(0xffffffffu, a_inc, o);
-      const int ic = __shfl_up_sync(0xffffffffu, i_inc, o);
-      if (lane >= o) c_inc += cc, a_inc += ac, i_inc += ic;
+      const int y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o),
+                y2 = __shfl_up_sync(0xffffffffu, x2, o);
+      if (lane >= o) x0 += y0, x1 += y1, x2 += y2;
     }
-    const int c_off = c_run + c_inc - c, a_off = a_run + a_inc - (c > 0), i_off = i_run + i_inc - items;
-    if (e <= E) {
-      a.counts[e] = c;
-      a.offsets[e] = c_off;
-      if (c > 0) a.active[a_off] = e;
-      for (int j = 0; j < items; j++)
-        a.items[i_off + j] = make_int4(e, j * a.chunk, c_off + j * a.chunk, min(a.chunk, c - j * a.chunk));
-      cnt[e] = c_off;  // becomes the bucket's first position
-    }
-    c_run += __shfl_sync(0xffffffffu, c_inc, 31);
-    a_run += __shfl_sync(0xffffffffu, a_inc, 31);
-    i_run += __shfl_sync(0xffffffffu, i_inc, 31);
+    if (lane < nw) wsum[0][lane] = x0, wsum[1][lane] = x1, wsum[2][lane] = x2;  // inclusive
   }
-  const int tot_c = c_run, tot_a = a_run, tot_i = i_run;
-  if (lane == 0) {
-    a.offsets[E + 1] = tot_c;
-    *a.n_active = tot_a;
-    *a.n_items = tot_i;
+  __syncthreads();
+  const int wb0 = warp ? wsum[0][warp - 1] : 0, wb1 = warp ? wsum[1][warp - 1] : 0,
+            wb2 = warp ? wsum[2][warp - 1] : 0;
+  const int c_off = wb0 + c_inc - c, a_off = wb1 + a_inc - (c > 0), i_off = wb2 + i_inc - items;
+  __syncthreads();  // every count is read before it becomes a position
+  if (e <= E) {
+    a.counts[e] = c;
+    a.offsets[e] = c_off;
+    if (c > 0) a.active[a_off] = e;
+    for (int j = 0; j < items; j++)
+      a.items[i_off + j] = make_int4(e, j * a.chunk, c_off + j * a.chunk, min(a.chunk, c - j * a.chunk));
+    cnt[e] = c_off;  // becomes the bucket's first position
   }
-  __syncwarp();
-#pragma unroll
-  for (int j = 0; j < kSmallPairs / 32; j++) {
-    const int p = lane + 32 * j;
-    if (p < P) {
-      const uint32_t e = mine[j];
-      int before = 0;
-      for (int q = 0; q < p; q++) before += a.sel_idx[q] == e || (a.sel_idx[q] >= (uint32_t)EB && e == 0);
-      const int pos = cnt[e] + before;
-      a.sorted[pos] = p;
-      a.inverse[p] = pos;
-    }
+  if (tid == (int)blockDim.x - 1) {
+    a.offsets[E + 1] = wsum[0][(blockDim.x >> 5) - 1];
+    *a.n_active = wsum[1][(blockDim.x >> 5) - 1];
+    *a.n_items = wsum[2][(blockDim.x >> 5) - 1];
+  }
+  __syncthreads();
+  // pair p goes after the earlier pairs of its bucket (stable order)
+  if (tid < P) {
+    const uint32_t ep = sel[tid];
+    int before = 0;
+    for (int q = 0; q < tid; q++) before += sel[q] == ep;
+    const int pos = cnt[ep] + before;
+    a.sorted[pos] = tid;
+    a.inverse[tid] = pos;
   }
   if (a.shared)
-    for (int t = lane; t < a.T; t += 32) {
+    for (int t = tid; t < a.T; t += blockDim.x) {
       a.sorted[P + t] = P + t;
       a.inverse[P + t] = P + t;
     }
@@ -1305,7 +1311,8 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   // 4. dispatch
   mark(kStageDispatch);
   if (a.T * a.k <= kSmallPairs) {
-    launch_pdl(dispatch_small_kernel, dim3(1), dim3(32), (size_t)(a.E + 1) * sizeof(int32_t), stream, a);
+    launch_pdl(dispatch_small_kernel, dim3(1), dim3(std::max(kSmallPairs, (a.E + 1 + 31) / 32 * 32)),
+               0, stream, a);
   } else {
     size_t dsmem = ((size_t)kDispatchWarps * (a.E + 1) + 2 * (a.E + 1)) * sizeof(int32_t);
     set_smem(dispatch_kernel, dsmem);
