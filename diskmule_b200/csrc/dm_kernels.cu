@@ -614,6 +614,11 @@ __global__ void __launch_bounds__(1024) topk_rank_softmax_kernel(const float *lo
   int wr = 0;
 #pragma unroll
   for (int j = 0; j < 32; j++) wr += __shfl_sync(0xffffffffu, key, j) > key ? 1 : 0;
+  // Lanes past E hold key 0 and tie, so they all land on one slot: clear the warp's k
+  // slots first. A zero key loses to every finite logit, and with at least k valid
+  // candidates the zeros never reach the top k.
+  if (lane < k) cand[warp * k + lane] = 0ull;
+  __syncwarp();
   if (wr < k) cand[warp * k + wr] = key;
   __syncthreads();
   if (bad_s) {
@@ -1137,21 +1142,19 @@ static ExpertFn expert_fn(bool up, int kind, int tt) {
 // the pairs before it with the same expert (stable: expert, then pair index).
 constexpr int kSmallPairs = 64;
 
-__global__ void __launch_bounds__(1024) dispatch_small_kernel(ForwardArgs a) {
-  pdl_wait();
-  __shared__ int32_t cnt[1024];       // bucket counts, then first positions
-  __shared__ uint32_t sel[kSmallPairs];
-  __shared__ int32_t wsum[3][32];     // per-warp totals of counts, active buckets, items
+struct SmallDispatchSmem {
+  int32_t cnt[1024];        // bucket counts, then first positions
+  uint32_t sel[kSmallPairs];
+  int32_t wsum[3][32];      // per-warp totals of counts, active buckets, items
+};
+
+// The dispatch of the pairs in sm.sel (already in range, P = T*k of them).
+__device__ __forceinline__ void dispatch_small_body(const ForwardArgs &a, SmallDispatchSmem &sm) {
   const int E = a.E, P = a.T * a.k, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int EB = E + (a.rows_mode ? 1 : 0);
+  int32_t *cnt = sm.cnt;
   if (tid <= E) cnt[tid] = 0;
-  if (tid < P) {
-    uint32_t e = a.sel_idx[tid];
-    if (e >= (uint32_t)EB) e = 0;  // rejected upstream; keep indices in range
-    sel[tid] = e;
-  }
   __syncthreads();
-  if (tid < P) atomicAdd(&cnt[sel[tid]], 1);
+  if (tid < P) atomicAdd(&cnt[sm.sel[tid]], 1);
   __syncthreads();
   if (a.shared && tid == 0) cnt[E] = a.T;
   __syncthreads();
@@ -1167,23 +1170,23 @@ __global__ void __launch_bounds__(1024) dispatch_small_kernel(ForwardArgs a) {
     const int ic = __shfl_up_sync(0xffffffffu, i_inc, o);
     if (lane >= o) c_inc += cc, a_inc += ac, i_inc += ic;
   }
-  if (lane == 31) wsum[0][warp] = c_inc, wsum[1][warp] = a_inc, wsum[2][warp] = i_inc;
+  if (lane == 31) sm.wsum[0][warp] = c_inc, sm.wsum[1][warp] = a_inc, sm.wsum[2][warp] = i_inc;
   __syncthreads();
   if (warp == 0) {
     const int nw = (int)(blockDim.x >> 5);
-    int x0 = lane < nw ? wsum[0][lane] : 0, x1 = lane < nw ? wsum[1][lane] : 0,
-        x2 = lane < nw ? wsum[2][lane] : 0;
+    int x0 = lane < nw ? sm.wsum[0][lane] : 0, x1 = lane < nw ? sm.wsum[1][lane] : 0,
+        x2 = lane < nw ? sm.wsum[2][lane] : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o),
                 y2 = __shfl_up_sync(0xffffffffu, x2, o);
       if (lane >= o) x0 += y0, x1 += y1, x2 += y2;
     }
-    if (lane < nw) wsum[0][lane] = x0, wsum[1][lane] = x1, wsum[2][lane] = x2;  // inclusive
+    if (lane < nw) sm.wsum[0][lane] = x0, sm.wsum[1][lane] = x1, sm.wsum[2][lane] = x2;  // inclusive
   }
   __syncthreads();
-  const int wb0 = warp ? wsum[0][warp - 1] : 0, wb1 = warp ? wsum[1][warp - 1] : 0,
-            wb2 = warp ? wsum[2][warp - 1] : 0;
+  const int wb0 = warp ? sm.wsum[0][warp - 1] : 0, wb1 = warp ? sm.wsum[1][warp - 1] : 0,
+            wb2 = warp ? sm.wsum[2][warp - 1] : 0;
   const int c_off = wb0 + c_inc - c, a_off = wb1 + a_inc - (c > 0), i_off = wb2 + i_inc - items;
   __syncthreads();  // every count is read before it becomes a position
   if (e <= E) {
@@ -1195,16 +1198,16 @@ __global__ void __launch_bounds__(1024) dispatch_small_kernel(ForwardArgs a) {
     cnt[e] = c_off;  // becomes the bucket's first position
   }
   if (tid == (int)blockDim.x - 1) {
-    a.offsets[E + 1] = wsum[0][(blockDim.x >> 5) - 1];
-    *a.n_active = wsum[1][(blockDim.x >> 5) - 1];
-    *a.n_items = wsum[2][(blockDim.x >> 5) - 1];
+    a.offsets[E + 1] = sm.wsum[0][(blockDim.x >> 5) - 1];
+    *a.n_active = sm.wsum[1][(blockDim.x >> 5) - 1];
+    *a.n_items = sm.wsum[2][(blockDim.x >> 5) - 1];
   }
   __syncthreads();
   // pair p goes after the earlier pairs of its bucket (stable order)
   if (tid < P) {
-    const uint32_t ep = sel[tid];
+    const uint32_t ep = sm.sel[tid];
     int before = 0;
-    for (int q = 0; q < tid; q++) before += sel[q] == ep;
+    for (int q = 0; q < tid; q++) before += sm.sel[q] == ep;
     const int pos = cnt[ep] + before;
     a.sorted[pos] = tid;
     a.inverse[tid] = pos;
@@ -1214,6 +1217,86 @@ __global__ void __launch_bounds__(1024) dispatch_small_kernel(ForwardArgs a) {
       a.sorted[P + t] = P + t;
       a.inverse[P + t] = P + t;
     }
+}
+
+__global__ void __launch_bounds__(1024) dispatch_small_kernel(ForwardArgs a) {
+  pdl_wait();
+  __shared__ SmallDispatchSmem sm;
+  const int EB = a.E + (a.rows_mode ? 1 : 0);
+  if ((int)threadIdx.x < a.T * a.k) {
+    uint32_t e = a.sel_idx[threadIdx.x];
+    if (e >= (uint32_t)EB) e = 0;  // rejected upstream; keep indices in range
+    sm.sel[threadIdx.x] = e;
+  }
+  dispatch_small_body(a, sm);
+}
+
+// One decode token (T = 1) of the softmax families: the rank top-k of
+// topk_rank_softmax_kernel, then the small dispatch of its k pairs, in one CTA.
+__global__ void __launch_bounds__(1024) topk_dispatch1_kernel(ForwardArgs a) {
+  pdl_wait();
+  __shared__ SmallDispatchSmem sm;
+  __shared__ unsigned long long cand[32 * 32];
+  __shared__ unsigned long long chosen[32];
+  __shared__ int bad_s;
+  const int E = a.E, k = a.k, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  if (tid == 0) bad_s = 0;
+  __syncthreads();
+  const float v = tid < E ? a.logits[tid] : 0.0f;
+  if (tid < E && !isfinite(v)) bad_s = 1;
+  const unsigned long long key = tid < E ? rank_key(v, (uint32_t)tid) : 0ull;
+  int wr = 0;
+#pragma unroll
+  for (int j = 0; j < 32; j++) wr += __shfl_sync(0xffffffffu, key, j) > key ? 1 : 0;
+  // Lanes past E hold key 0 and tie, so they all land on one slot: clear the warp's k
+  // slots first. A zero key loses to every finite logit, and with at least k valid
+  // candidates the zeros never reach the top k.
+  if (lane < k) cand[warp * k + lane] = 0ull;
+  __syncwarp();
+  if (wr < k) cand[warp * k + wr] = key;
+  __syncthreads();
+  if (bad_s) {
+    // flag the error and dispatch an in-range selection so later kernels stay in bounds
+    if (tid == 0) atomicExch(a.status, kStatusNonFiniteRouter);
+    if (tid < k) {
+      a.sel_idx[tid] = (uint32_t)tid;
+      a.sel_w[tid] = 0.0f;
+      sm.sel[tid] = (uint32_t)tid;
+    }
+  } else {
+    const int C = nwarps * k;
+    for (int c = tid; c < C; c += blockDim.x) {
+      const unsigned long long mine = cand[c];
+      int r = 0;
+      for (int j = 0; j < C; j++) r += cand[j] > mine ? 1 : 0;
+      if (r < k) chosen[r] = mine;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      float val = -INFINITY;
+      uint32_t idx = 0;
+      if (lane < k) {
+        const unsigned long long best = chosen[lane];
+        idx = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+        const int32_t kb = (int32_t)((uint32_t)(best >> 32) ^ 0x80000000u);
+        val = __int_as_float(kb ^ (int32_t)(((uint32_t)(kb >> 31)) >> 1));
+      }
+      float m = val;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float ex = lane < k ? exp_f32_cr(__fsub_rn(val, m)) : 0.0f;
+      float sum = 0.0f;
+      for (int r = 0; r < k; r++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, r));
+      if (lane < k) {
+        a.sel_idx[lane] = idx;
+        a.sel_w[lane] = __fdiv_rn(ex, sum);
+        sm.sel[lane] = idx < (uint32_t)E ? idx : 0u;  // the dispatch indexes by it
+      }
+    }
+  }
+  __syncthreads();
+  dispatch_small_body(a, sm);
 }
 
 // Per-row outputs of the rows mode: out[r] = ysorted[inverse[r]] (k = 1, unweighted).
@@ -1240,6 +1323,9 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
     launches++;
   }
   const bool glm = a.family == kGlm;
+  // one decode token of a softmax family: top-k and dispatch in one kernel
+  const bool fused_dispatch = (mode & kRunRoute) && (mode & kRunExperts) && !glm && !a.rows_mode &&
+                              a.T == 1 && a.k <= kSmallPairs && a.E + 1 <= 1024;
   auto mark = [&](int stage) {
     if (ev) cudaEventRecord(ev[stage], stream);
   };
@@ -1302,15 +1388,20 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
     launch_pdl(topk_sigmoid_kernel, dim3(topk_blocks), dim3(32 * kTopkWarps), 0, stream,
                (const float *)a.logits, a.T, a.E1, a.E, a.k, a.bias, a.n_groups, a.topk_groups,
                a.normalize, a.sel_idx, a.sel_w, a.status);
+  else if (fused_dispatch)
+    launch_pdl(topk_dispatch1_kernel, dim3(1),
+               dim3(std::max(kSmallPairs, (a.E + 1 + 31) / 32 * 32)), 0, stream, a);
   else
     launch_pdl(topk_rank_softmax_kernel, dim3(a.T), dim3(32 * ((a.E + 31) / 32)), 0, stream,
                (const float *)a.logits, a.T, a.E1, a.E, a.k, a.sel_idx, a.sel_w, a.status);
   launches++;
   }
   if (mode & kRunExperts) {
-  // 4. dispatch
+  // 4. dispatch (already done with the top-k of one decode token)
   mark(kStageDispatch);
-  if (a.T * a.k <= kSmallPairs) {
+  if (fused_dispatch) {
+    launches--;  // counted with the top-k
+  } else if (a.T * a.k <= kSmallPairs) {
     launch_pdl(dispatch_small_kernel, dim3(1), dim3(std::max(kSmallPairs, (a.E + 1 + 31) / 32 * 32)),
                0, stream, a);
   } else {

@@ -40,6 +40,9 @@ CONFIGS = {
                             gate_type=N.Q4_K, down_type=N.Q8_0, epsilon=1e-6),
     "qwen35-small": dict(family="qwen35", hidden=512, intermediate=256, experts=32, top_k=4,
                          gate_type=N.Q4_K, down_type=N.Q6_K, shared=True),
+    # 40 experts, top-10: the last top-k warp holds fewer valid experts than k
+    "qwen35-odd": dict(family="qwen35", hidden=256, intermediate=256, experts=40, top_k=10,
+                       gate_type=N.Q4_K, down_type=N.Q6_K, shared=True),
     "glm52-small": dict(family="glm52", hidden=256, intermediate=128, experts=32, top_k=4,
                         gate_type=N.BF16, down_type=N.BF16, shared=True, n_groups=4,
                         topk_groups=2, routed_scale=2.5, normalize=True),

@@ -73,7 +73,8 @@ def check_dispatch(sl, T, idx):
     assert np.array_equal(inverse, i2)
 
 
-SMALL = ["gemma4-small", "gemma4-small-q8", "qwen35-small", "glm52-small", "glm52-small-flat"]
+SMALL = ["gemma4-small", "gemma4-small-q8", "qwen35-small", "qwen35-odd", "glm52-small",
+         "glm52-small-flat"]
 
 
 @pytest.mark.parametrize("name", SMALL)
