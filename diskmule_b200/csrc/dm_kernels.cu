@@ -660,94 +660,6 @@ __global__ void __launch_bounds__(1024) topk_rank_softmax_kernel(const float *lo
   }
 }
 
-// sigmoid + correction bias (+ restated group limit): src/glm52/cpu.rs:731-754
-__global__ void __launch_bounds__(32 * kTopkWarps) topk_sigmoid_kernel(
-    const float *logits, int T, int E1, int E, int k, const float *bias, int n_groups,
-    int topk_groups, int normalize, uint32_t *sel_idx, float *sel_w, int32_t *status) {
-  pdl_wait();
-  __shared__ float choice_s[kTopkWarps][kMaxGlmExperts];
-  __shared__ unsigned char keep_s[kTopkWarps][32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * kTopkWarps + warp;
-  if (t >= T) return;
-  const float *lg = logits + (size_t)t * E1;
-  float *ch = choice_s[warp];
-  bool bad = false;
-  for (int e = lane; e < E; e += 32) {
-    float w = glm_sigmoid(lg[e]);
-    float c = __fadd_rn(w, bias[e]);
-    bad |= !isfinite(w) || !isfinite(c);
-    ch[e] = c;
-  }
-  if (__any_sync(0xffffffffu, bad)) {
-    // flag the error and leave an in-range selection so later kernels stay in bounds
-    if (lane == 0) atomicExch(status, kStatusNonFiniteRouter);
-    for (int r = lane; r < k; r += 32) {
-      sel_idx[(size_t)t * k + r] = (uint32_t)r;
-      sel_w[(size_t)t * k + r] = 0.0f;
-    }
-    return;
-  }
-  __syncwarp();
-  const int per_group = E / n_groups;
-  if (n_groups > 1) {
-    // group score = top1 + top2 of the group's choices; keep the best groups
-    unsigned long long gkey = 0;
-    if (lane < n_groups) {
-      unsigned long long k1 = 0, k2 = 0;
-      for (int i = 0; i < per_group; i++) {
-        int e = lane * per_group + i;
-        unsigned long long key = rank_key(ch[e], (uint32_t)e);
-        if (key > k1) {
-          k2 = k1;
-          k1 = key;
-        } else if (key > k2) {
-          k2 = key;
-        }
-      }
-      float c1 = ch[0xffffffffu - (uint32_t)(k1 & 0xffffffffu)];
-      float c2 = ch[0xffffffffu - (uint32_t)(k2 & 0xffffffffu)];
-      gkey = rank_key(__fadd_rn(c1, c2), (uint32_t)lane);
-    }
-    // rank of this group = number of groups with a larger key
-    int rank = 0;
-    for (int g = 0; g < n_groups; g++) {
-      unsigned long long other = __shfl_sync(0xffffffffu, gkey, g);
-      rank += other > gkey;
-    }
-    if (lane < n_groups) keep_s[warp][lane] = rank < topk_groups;
-    __syncwarp();
-  }
-  unsigned long long last = ~0ull;
-  float weights[32];
-  uint32_t idxs[32];
-  for (int r = 0; r < k; r++) {
-    unsigned long long best = 0;
-    for (int e = lane; e < E; e += 32) {
-      if (n_groups > 1 && !keep_s[warp][e / per_group]) continue;
-      unsigned long long key = rank_key(ch[e], (uint32_t)e);
-      if (key < last && key > best) best = key;
-    }
-    best = warp_max_u64(best);
-    last = best;
-    uint32_t idx = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
-    if (idx >= (uint32_t)E) idx = 0;  // unreachable for k <= eligible experts; keeps reads in range
-    if (r < 32) {
-      idxs[r] = idx;
-      weights[r] = glm_sigmoid(lg[idx]);
-    }
-  }
-  if (lane == 0) {
-    float sum = -0.0f;
-    for (int r = 0; r < k; r++) sum = __fadd_rn(sum, weights[r]);
-    sum = __fadd_rn(sum, 1e-20f);
-    for (int r = 0; r < k; r++) {
-      sel_idx[(size_t)t * k + r] = idxs[r];
-      sel_w[(size_t)t * k + r] = normalize ? __fdiv_rn(weights[r], sum) : weights[r];
-    }
-  }
-}
-
 int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float *prob,
                         int32_t *status, cudaStream_t stream) {
   if (n <= 1024)
@@ -1314,6 +1226,120 @@ __global__ void iota_kernel(int32_t *v, int n) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) v[i] = i;
 }
 
+// GLM routing with one token per CTA and a thread per expert: sigmoid + correction
+// choices computed once (src/glm52/cpu.rs:731-754), group scores (top1 + top2 of the
+// group's choices, the topk_groups best groups kept; restated), then each eligible
+// expert's rank among the eligible ones by key (choice descending, index ascending) --
+// the selection and order of repeated argmax -- and the weights normalised by their sum
+// in selection order. FUSED (one token): the small dispatch follows in the same CTA.
+template <bool FUSED>
+__global__ void __launch_bounds__(1024) topk_sigmoid_rank_kernel(ForwardArgs a) {
+  pdl_wait();
+  __shared__ unsigned long long key_s[kMaxGlmExperts];
+  __shared__ unsigned long long cmp_s[kMaxGlmExperts];
+  __shared__ float w_s[kMaxGlmExperts];
+  __shared__ float c_s[kMaxGlmExperts];
+  __shared__ unsigned long long gkey_s[32];
+  __shared__ unsigned char keep_s[32];
+  __shared__ uint32_t idx_s[32];
+  __shared__ float selw_s[32];
+  __shared__ float sum_s;
+  __shared__ int bad_s;
+  __shared__ SmallDispatchSmem sm;
+  const int t = blockIdx.x, tid = threadIdx.x, E = a.E, k = a.k;
+  const float *lg = a.logits + (size_t)t * a.E1;
+  if (tid == 0) bad_s = 0;
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) {
+    const float w = glm_sigmoid(lg[e]);
+    const float c = __fadd_rn(w, a.bias[e]);
+    if (!isfinite(w) || !isfinite(c)) bad_s = 1;
+    w_s[e] = w;
+    c_s[e] = c;
+    key_s[e] = rank_key(c, (uint32_t)e);
+  }
+  __syncthreads();
+  if (bad_s) {
+    // flag the error and leave an in-range selection so later kernels stay in bounds
+    if (tid == 0) atomicExch(a.status, kStatusNonFiniteRouter);
+    if (tid < k) {
+      a.sel_idx[(size_t)t * k + tid] = (uint32_t)tid;
+      a.sel_w[(size_t)t * k + tid] = 0.0f;
+      if (FUSED) sm.sel[tid] = (uint32_t)tid;
+    }
+  } else {
+    const int ng = a.n_groups > 1 ? a.n_groups : 1, pg = E / ng;
+    if (ng > 1) {
+      if (tid < ng) {
+        unsigned long long k1 = 0, k2 = 0;
+        for (int i = 0; i < pg; i++) {
+          const unsigned long long key = key_s[tid * pg + i];
+          if (key > k1) {
+            k2 = k1;
+            k1 = key;
+          } else if (key > k2) {
+            k2 = key;
+          }
+        }
+        const float c1 = c_s[0xffffffffu - (uint32_t)(k1 & 0xffffffffu)];
+        const float c2 = c_s[0xffffffffu - (uint32_t)(k2 & 0xffffffffu)];
+        gkey_s[tid] = rank_key(__fadd_rn(c1, c2), (uint32_t)tid);
+      }
+      __syncthreads();
+      if (tid < ng) {
+        int rank = 0;
+        for (int g = 0; g < ng; g++) rank += gkey_s[g] > gkey_s[tid];
+        keep_s[tid] = rank < a.topk_groups;
+      }
+      __syncthreads();
+    }
+    // the eligible experts' keys, compacted (kept groups in order) into cmp_s
+    int n_elig = E;
+    if (ng > 1) {
+      int kept_before = 0, kept = 0;
+      for (int g = 0; g < ng; g++) kept += keep_s[g];
+      n_elig = kept * pg;
+      for (int e = tid; e < E; e += blockDim.x) {
+        const int g = e / pg;
+        if (!keep_s[g]) continue;
+        kept_before = 0;
+        for (int h = 0; h < g; h++) kept_before += keep_s[h];
+        cmp_s[kept_before * pg + (e - g * pg)] = key_s[e];
+      }
+    } else {
+      for (int e = tid; e < E; e += blockDim.x) cmp_s[e] = key_s[e];
+    }
+    __syncthreads();
+    for (int i = tid; i < n_elig; i += blockDim.x) {
+      const unsigned long long key = cmp_s[i];
+      int r = 0;
+      for (int j = 0; j < n_elig; j++) r += cmp_s[j] > key;
+      if (r < k) {
+        const uint32_t e = 0xffffffffu - (uint32_t)(key & 0xffffffffu);
+        idx_s[r] = e;
+        selw_s[r] = w_s[e < (uint32_t)E ? e : 0u];
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float sum = -0.0f;
+      for (int r = 0; r < k; r++) sum = __fadd_rn(sum, selw_s[r]);
+      sum_s = __fadd_rn(sum, 1e-20f);
+    }
+    __syncthreads();
+    if (tid < k) {
+      const uint32_t idx = idx_s[tid] < (uint32_t)E ? idx_s[tid] : 0u;
+      a.sel_idx[(size_t)t * k + tid] = idx;
+      a.sel_w[(size_t)t * k + tid] = a.normalize ? __fdiv_rn(selw_s[tid], sum_s) : selw_s[tid];
+      if (FUSED) sm.sel[tid] = idx;
+    }
+  }
+  if (FUSED) {
+    __syncthreads();
+    dispatch_small_body(a, sm);
+  }
+}
+
 int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
                    const GemvPlan *gemv, const TcPlan *tc, int mode) {
   int launches = 0;
@@ -1324,7 +1350,7 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   }
   const bool glm = a.family == kGlm;
   // one decode token of a softmax family: top-k and dispatch in one kernel
-  const bool fused_dispatch = (mode & kRunRoute) && (mode & kRunExperts) && !glm && !a.rows_mode &&
+  const bool fused_dispatch = (mode & kRunRoute) && (mode & kRunExperts) && !a.rows_mode &&
                               a.T == 1 && a.k <= kSmallPairs && a.E + 1 <= 1024;
   auto mark = [&](int stage) {
     if (ev) cudaEventRecord(ev[stage], stream);
@@ -1383,11 +1409,12 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   launches++;
   // 3. top-k
   mark(kStageTopk);
-  int topk_blocks = (a.T + kTopkWarps - 1) / kTopkWarps;
-  if (glm)
-    launch_pdl(topk_sigmoid_kernel, dim3(topk_blocks), dim3(32 * kTopkWarps), 0, stream,
-               (const float *)a.logits, a.T, a.E1, a.E, a.k, a.bias, a.n_groups, a.topk_groups,
-               a.normalize, a.sel_idx, a.sel_w, a.status);
+  if (glm && fused_dispatch)
+    launch_pdl(topk_sigmoid_rank_kernel<true>, dim3(1),
+               dim3(std::max(kSmallPairs, (a.E + 1 + 31) / 32 * 32)), 0, stream, a);
+  else if (glm)
+    launch_pdl(topk_sigmoid_rank_kernel<false>, dim3(a.T), dim3(std::min(1024, (a.E + 31) / 32 * 32)),
+               0, stream, a);
   else if (fused_dispatch)
     launch_pdl(topk_dispatch1_kernel, dim3(1),
                dim3(std::max(kSmallPairs, (a.E + 1 + 31) / 32 * 32)), 0, stream, a);
