@@ -227,16 +227,20 @@ __device__ __forceinline__ float chain_step(float w, float x, float s) {
 
 // Few tokens: a CTA owns 8 experts and up to RT tokens; 8*RT threads run the sequential
 // chains. The experts' router rows ([E1][H] f32 copy made at set-up, so one row is
-// contiguous) are requested up front with cp.async in chunks of kRsChunk columns, each
-// chunk completing an mbarrier, and land in rows padded by 16 bytes (the 8 threads of a
+// contiguous) are requested up front as 1-D bulk copies in chunks of kRsChunk columns,
+// each chunk completing an mbarrier, and land in rows padded by 16 bytes (the 8 threads of a
 // token read 8 rows at the same column without bank conflicts). A chain thread reads 4
 // weights and 4 inputs per 16-byte load, so the chain runs at the FMA latency.
 constexpr int kSmallExperts = 8;
 constexpr int kRsChunk = 256;
 constexpr int kRsMaxChunks = 48;  // H <= 12288
 
-__device__ __forceinline__ void rs_cp16(uint32_t dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+__device__ __forceinline__ void rs_bulk(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
 }
 
 template <bool GLM, bool XBF16>
@@ -246,7 +250,7 @@ __global__ void __launch_bounds__(256) router_small_kernel(const float *rows, co
                                                           float *logits, int32_t *status) {
   pdl_wait();
   extern __shared__ __align__(16) float smem[];
-  __shared__ __align__(8) unsigned long long bars[kRsMaxChunks];
+  __shared__ __align__(8) unsigned long long bars[kRsMaxChunks + 1];  // chunks, then x
   const int HP = H + 4;                                     // padded rows (16 bytes)
   float *xs = smem;                                         // [RT][H + 4]
   float *ws = xs + RT * HP;                                 // [8][H + 4]
@@ -255,41 +259,66 @@ __global__ void __launch_bounds__(256) router_small_kernel(const float *rows, co
   const int ne = min(kSmallExperts, E1 - e0);
   const int nchunks = (H + kRsChunk - 1) / kRsChunk;
   const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(bars);
+  const uint32_t xbar = (uint32_t)__cvta_generic_to_shared(&bars[kRsMaxChunks]);
   if (threadIdx.x == 0) {
     for (int c = 0; c < nchunks; c++)
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar0 + 8 * c), "r"(blockDim.x));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * c));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(xbar));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  // router rows: every thread copies its pieces of each chunk, then arms the chunk's barrier
+  // One thread streams the router rows chunk by chunk as 1-D bulk copies (one per row and
+  // chunk, each completing the chunk's barrier), and an f32 token row the same way: the
+  // copy engine keeps far more bytes in flight per SM than 16-byte copies would.
   const uint32_t wbase = (uint32_t)__cvta_generic_to_shared(ws);
-  constexpr int kPieces = kRsChunk / 4;                     // 16-byte pieces per row chunk
-  for (int c = 0; c < nchunks; c++) {
-    const int h0 = c * kRsChunk, pieces = min(kRsChunk, H - h0) / 4;
-    for (int i = threadIdx.x; i < ne * kPieces; i += blockDim.x) {
-      const int el = i / kPieces, piece = i % kPieces;
-      if (piece < pieces)
-        rs_cp16(wbase + (uint32_t)(el * HP + h0 + 4 * piece) * 4,
-                rows + (size_t)(e0 + el) * H + h0 + 4 * piece);
+  const uint32_t xbase = (uint32_t)__cvta_generic_to_shared(xs);
+  if (threadIdx.x == 0) {
+    if (!XBF16) {
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
+                   "r"((uint32_t)(nt * H * 4))
+                   : "memory");
+      for (int tt = 0; tt < nt; tt++)
+        rs_bulk(xbase + (uint32_t)(tt * HP) * 4,
+                reinterpret_cast<const float *>(x) + (size_t)(t0 + tt) * H, (uint32_t)H * 4, xbar);
     }
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar0 + 8 * c) : "memory");
+    for (int c = 0; c < nchunks; c++) {
+      const int h0 = c * kRsChunk, w = min(kRsChunk, H - h0);
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar0 + 8 * c),
+                   "r"((uint32_t)(ne * w * 4))
+                   : "memory");
+      for (int el = 0; el < ne; el++)
+        rs_bulk(wbase + (uint32_t)(el * HP + h0) * 4, rows + (size_t)(e0 + el) * H + h0,
+                (uint32_t)w * 4, bar0 + 8 * c);
+    }
   }
-  // token rows (converted to f32) while the router rows stream in
-  for (int i = threadIdx.x; i < nt * (H / 4); i += blockDim.x) {
-    const int tt = i / (H / 4), c = i - tt * (H / 4);
-    float4 v;
-    if (XBF16) {
+  if (XBF16) {
+    // bf16 token rows, converted to f32 while the router rows stream in
+    for (int i = threadIdx.x; i < nt * (H / 4); i += blockDim.x) {
+      const int tt = i / (H / 4), c = i - tt * (H / 4);
       const uint2 u = *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(x) +
                                                        (size_t)(t0 + tt) * H + 4 * c);
-      v = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+      *reinterpret_cast<float4 *>(xs + tt * HP + 4 * c) =
+          make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
-    } else {
-      v = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) +
-                                            (size_t)(t0 + tt) * H + 4 * c);
     }
-    *reinterpret_cast<float4 *>(xs + tt * HP + 4 * c) = v;
+    __syncthreads();  // token rows staged
+  } else if (threadIdx.x < kSmallExperts * nt) {
+    // bounded wait for the token rows
+    const long long start = clock64();
+    uint32_t done = 0;
+    while (!done) {
+      asm volatile(
+          "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n"
+          " selp.u32 %0, 1, 0, p;\n}\n"
+          : "=r"(done)
+          : "r"(xbar)
+          : "memory");
+      if (!done && clock64() - start > 200000000ll) {
+        atomicExch(status, kStatusTimeout);
+        break;
+      }
+    }
   }
-  __syncthreads();  // token rows staged
   const int el = threadIdx.x % kSmallExperts, tl = threadIdx.x / kSmallExperts;
   if (tl < nt && el < ne) {
     const float *xr = xs + tl * HP;
@@ -312,31 +341,41 @@ __global__ void __launch_bounds__(256) router_small_kernel(const float *rows, co
         }
       }
       const int h0 = c * kRsChunk, h1 = min(H, h0 + kRsChunk);
-      // 16 steps per round; the next round's operands are loaded before this round's
-      // FMAs so the shared-memory latency hides behind the chain (H % 32 == 0)
-      float4 w[4], xv[4];
+      // Two register sets of 16 steps each: the set for the next 16 columns is loaded
+      // while the other feeds the chain, so shared-memory latency hides behind the FMAs
+      // and no register copies sit in the chain's way (H % 32 == 0).
+      float4 wa[4], xa[4], wb[4], xb[4];
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        w[i] = *reinterpret_cast<const float4 *>(wr + h0 + 4 * i);
-        xv[i] = *reinterpret_cast<const float4 *>(xr + h0 + 4 * i);
+        wa[i] = *reinterpret_cast<const float4 *>(wr + h0 + 4 * i);
+        xa[i] = *reinterpret_cast<const float4 *>(xr + h0 + 4 * i);
       }
-      for (int h = h0; h < h1; h += 16) {
-        float4 wn[4], xn[4];
-        const int hn = h + 16 < h1 ? h + 16 : h;
+      for (int h = h0; h < h1; h += 32) {
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-          wn[i] = *reinterpret_cast<const float4 *>(wr + hn + 4 * i);
-          xn[i] = *reinterpret_cast<const float4 *>(xr + hn + 4 * i);
+          wb[i] = *reinterpret_cast<const float4 *>(wr + h + 16 + 4 * i);
+          xb[i] = *reinterpret_cast<const float4 *>(xr + h + 16 + 4 * i);
         }
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-          s = chain_step<GLM>(w[i].x, xv[i].x, s);
-          s = chain_step<GLM>(w[i].y, xv[i].y, s);
-          s = chain_step<GLM>(w[i].z, xv[i].z, s);
-          s = chain_step<GLM>(w[i].w, xv[i].w, s);
+          s = chain_step<GLM>(wa[i].x, xa[i].x, s);
+          s = chain_step<GLM>(wa[i].y, xa[i].y, s);
+          s = chain_step<GLM>(wa[i].z, xa[i].z, s);
+          s = chain_step<GLM>(wa[i].w, xa[i].w, s);
+        }
+        const int hn = h + 32 < h1 ? h + 32 : h;  // last pass: a harmless reload
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          wa[i] = *reinterpret_cast<const float4 *>(wr + hn + 4 * i);
+          xa[i] = *reinterpret_cast<const float4 *>(xr + hn + 4 * i);
         }
 #pragma unroll
-        for (int i = 0; i < 4; i++) w[i] = wn[i], xv[i] = xn[i];
+        for (int i = 0; i < 4; i++) {
+          s = chain_step<GLM>(wb[i].x, xb[i].x, s);
+          s = chain_step<GLM>(wb[i].y, xb[i].y, s);
+          s = chain_step<GLM>(wb[i].z, xb[i].z, s);
+          s = chain_step<GLM>(wb[i].w, xb[i].w, s);
+        }
       }
     }
     if (lbias && e0 + el < E) s = __fadd_rn(s, lbias[e0 + el]);
