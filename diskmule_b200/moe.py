@@ -218,14 +218,22 @@ class MoeLayer:
                                            C.c_void_p(pair_out_ptr), C.c_void_p(y_ptr),
                                            C.c_void_p(stream) if stream else None))
 
-    def forward_host(self, x: np.ndarray):
-        """Synchronous forward on host arrays (dm_moe_forward_host): (y, indices, weights)."""
+    def forward_host(self, x: np.ndarray, out=None):
+        """Synchronous forward on host arrays (dm_moe_forward_host): (y, indices, weights).
+        `out`, when given, is that triple preallocated (page-locked arrays make the
+        copies direct DMA)."""
         x = np.ascontiguousarray(x)
         T = x.shape[0]
         H, k = self.desc.hidden, self.desc.top_k
-        y = np.zeros((T, H), dtype=np.float32)
-        idx = np.zeros((T, k), dtype=np.uint32)
-        w = np.zeros((T, k), dtype=np.float32)
+        if out is not None:
+            y, idx, w = out
+            assert y.shape == (T, H) and y.dtype == np.float32 and y.flags.c_contiguous
+            assert idx.shape == (T, k) and idx.dtype == np.uint32 and idx.flags.c_contiguous
+            assert w.shape == (T, k) and w.dtype == np.float32 and w.flags.c_contiguous
+        else:
+            y = np.zeros((T, H), dtype=np.float32)
+            idx = np.zeros((T, k), dtype=np.uint32)
+            w = np.zeros((T, k), dtype=np.float32)
         check(N.lib().dm_moe_forward_host(self._h, _ptr(x), _ptr(y), T, _ptr(idx), _ptr(w)))
         return y, idx, w
 
