@@ -1,5 +1,5 @@
 """ctypes declarations of the C ABI (include/diskmule_cuda.h, include/diskmule_stack.h,
-include/diskmule_synth.h).
+include/diskmule_selftest.h, include/diskmule_synth.h).
 
 The product path is the CUDA library `libdiskmule_cuda.so` built next to this file.
 Nothing here falls back to a CPU implementation: if the library is missing the
@@ -148,6 +148,7 @@ SIGNATURES = {
     "dm_stack_embed": ([P, P, I32, I32, I32, P, P, P, P], I32),
     "dm_stack_add_rms_norm": ([P, P, P, P, I32, C.c_float, P, P, P], I32),
     "dm_stack_lm_head_argmax": ([P, P, I32, I32, I32, P, P, P, P, P], I32),
+    "dm_selftest_device_wait": ([P, C.c_int64], I32),
     "dm_synth_fill_host": ([I32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float,
                             C.c_float, P], I32),
     "dm_synth_fill_device": ([I32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float,

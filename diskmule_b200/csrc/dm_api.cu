@@ -16,6 +16,7 @@
 
 #include "../../include/diskmule_cuda.h"
 #include "dm_internal.cuh"
+#include "../../include/diskmule_selftest.h"
 
 namespace dmi {
 
@@ -1335,4 +1336,21 @@ extern "C" int32_t dm_moe_forward_noalloc(dm_moe_layer *L, const void *x, float 
   if (launches < 0) return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "no expert kernel for this format");
   DM_CUDA(cudaGetLastError(), "MoE forward (no allocation) launch");
   return DM_OK;
+}
+
+extern "C" int32_t dm_selftest_device_wait(dm_cuda_context *ctx, int64_t cycles) {
+  if (!ctx) return fail(DM_ERR_INVALID_ARGUMENT, "null context");
+  if (cycles <= 0 || cycles > 4000000000ll)
+    return fail(DM_ERR_INVALID_ARGUMENT, "the wait limit must be 1..4e9 cycles");
+  cudaSetDevice(ctx->device);
+  int32_t *st = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(ctx->status) + 128);
+  DM_CUDA(cudaMemsetAsync(st, 0, 4, ctx->stream), "status reset");
+  dm::launch_selftest_wait((long long)cycles, st, ctx->stream);
+  DM_CUDA(cudaGetLastError(), "self-test launch");
+  int32_t status = 0;
+  DM_CUDA(cudaMemcpyAsync(&status, st, 4, cudaMemcpyDeviceToHost, ctx->stream), "status copy");
+  DM_CUDA(cudaStreamSynchronize(ctx->stream), "self-test");
+  if (status == dm::kStatusTimeout)
+    return fail(DM_ERR_TIMEOUT, "a bounded device wait gave up after %lld cycles", (long long)cycles);
+  return status == 0 ? DM_OK : fail(DM_ERR_COMMAND, "unexpected self-test status %d", status);
 }

@@ -1369,6 +1369,25 @@ static int launch_bf16(const ForwardArgs &a, const TcPlan &p, const TcWeights &w
   return 4;
 }
 
+// Self-test: the bounded wait of the kernels above on a barrier nothing arrives on.
+__global__ void selftest_wait_kernel(long long cycles, int32_t *status) {
+  __shared__ __align__(8) unsigned long long bar;
+  const uint32_t b = (uint32_t)__cvta_generic_to_shared(&bar);
+  tc::mbar_init(b, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  const long long start = clock64();
+  bool done = false;
+  while (!done) {
+    done = tc::mbar_try(b, 0);
+    if (!done && clock64() - start > cycles) break;
+  }
+  *status = done ? 0 : kStatusTimeout;
+}
+
+void launch_selftest_wait(long long cycles, int32_t *status, cudaStream_t s) {
+  selftest_wait_kernel<<<1, 1, 0, s>>>(cycles, status);
+}
+
 int launch_tc_experts(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, cudaStream_t s,
                       cudaEvent_t down_mark) {
   if (p.bf16) return launch_bf16(a, p, w, s, down_mark);

@@ -84,4 +84,8 @@ int make_tc_maps(TcPlan &p, int H, int I, int down_type, int nt);
 int launch_tc_experts(const ForwardArgs &a, const TcPlan &p, const TcWeights &w,
                       cudaStream_t stream, cudaEvent_t down_mark);
 
+// One thread waits, bounded by `cycles`, on a barrier nothing arrives on; *status gets
+// kStatusTimeout (a self-test of the kernels' bounded waits).
+void launch_selftest_wait(long long cycles, int32_t *status, cudaStream_t s);
+
 }  // namespace dm
