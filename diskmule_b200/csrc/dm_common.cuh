@@ -262,10 +262,20 @@ struct F32Unit {
 cudaError_t ensure_smem_limit(const void *kernel);
 
 // Programmatic dependent launch along the forward chain: a kernel launched this way may
-// be scheduled while its predecessor drains, so its first statement is pdl_wait(), which
-// returns once the predecessor has completed and its writes are visible (and at once when
-// the kernel was launched without the attribute).
+// be scheduled while its predecessor runs, so it reads nothing its predecessor writes
+// before pdl_wait(), which returns once the predecessor has completed and its writes are
+// visible (and at once when the kernel was launched without the attribute).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Let the next kernel of the stream launch now. Called right after pdl_wait() by the
+// latency-bound kernels of the decode chain: every CTA of this grid is then resident or
+// done, so the successor's CTAs take only spare room on the SMs and wait there, and its
+// launch latency overlaps this kernel's work. Not called by a kernel whose successor is a
+// one-wave, throughput-bound grid (the many-token router after the input transpose): CTAs
+// placed around a running grid would pile onto the SMs it leaves free.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,

@@ -389,6 +389,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_up_kernel(ForwardArgs a, Ma
                                                               MatrixRef sh_up, int up_row_offset,
                                                               int rows_per_cta) {
   pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) float smem[];
   if ((int)blockIdx.y >= *a.n_items) return;
   const int4 item = a.items[blockIdx.y];  // (expert, first token of the chunk, ...)
@@ -456,19 +457,30 @@ template <int KIND, int NT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_down_kernel(ForwardArgs a, MatrixRef down,
                                                                 MatrixRef sh_down,
                                                                 int rows_per_cta) {
-  pdl_wait();
   extern __shared__ __align__(16) float smem[];
+  const int H = a.H, I = a.I;
+  constexpr int kTask = Task<KIND>::kElems;
+  const int nb = I / kTask;
+  const int r0 = blockIdx.x * rows_per_cta;
+  const int nrows = min(rows_per_cta, H - r0);
+  const int tasks = nrows * nb;
+  // The work items come from the dispatch two launches back, which completed before the
+  // gate/up kernel let this grid launch: while that kernel still runs, ask L2 for this
+  // CTA's down rows (read through L2, and only as prefetch addresses, so a line cached
+  // from an earlier call cannot turn into a wrong result).
+  if (r0 < H && (int)blockIdx.y < __ldcg(a.n_items) && (int)threadIdx.x < tasks) {
+    const int ep = min(max(__ldcg(&a.items[blockIdx.y].x), 0), a.E);
+    prefetch_task<KIND>(ep == a.E ? sh_down : down, ep == a.E ? 0 : ep, r0 + threadIdx.x / nb,
+                        threadIdx.x % nb);
+  }
+  pdl_wait();
+  pdl_trigger();
   if ((int)blockIdx.y >= *a.n_items) return;
   const int4 item = a.items[blockIdx.y];
   const int e = item.x, c0 = item.y;
   const int base = a.offsets[e];
   const int nt = min(NT, a.counts[e] - c0);
-  const int H = a.H, I = a.I;
-  constexpr int kTask = Task<KIND>::kElems;
-  const int nb = I / kTask;
-  const int r0 = blockIdx.x * rows_per_cta;
   if (r0 >= H) return;
-  const int nrows = min(rows_per_cta, H - r0);
   const int kp = pad_index(I, kTask), groups = I / 16;
   float *xs = smem;
   float *s16 = xs + NT * kp;
@@ -476,8 +488,6 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_down_kernel(ForwardArgs a, 
   const bool shared = e == a.E;
   const MatrixRef &D = shared ? sh_down : down;
   const int ex = shared ? 0 : e;
-  const int tasks = nrows * nb;
-  if ((int)threadIdx.x < tasks) prefetch_task<KIND>(D, ex, r0 + threadIdx.x / nb, threadIdx.x % nb);
   stage_rows<NT>(xs, s16, I, kTask, nt,
                  [&](int t, int k) {
                    return *reinterpret_cast<const float4 *>(a.h + (size_t)(base + c0 + t) * I + k);
@@ -592,6 +602,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_up_kernel(ForwardArgs a, 
                                                                  int up_row_offset,
                                                                  int rows_per_cta) {
   pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) float smem[];
   if ((int)blockIdx.y >= *a.n_items) return;
   const int4 item = a.items[blockIdx.y];
@@ -652,17 +663,18 @@ template <int KIND, int NT>
 __global__ void __launch_bounds__(kDenseThreads) dense_down_kernel(ForwardArgs a, MatrixRef down,
                                                                    MatrixRef sh_down,
                                                                    int rows_per_cta) {
-  pdl_wait();
   extern __shared__ __align__(16) float smem[];
+  const int H = a.H, I = a.I;
+  const int r0 = blockIdx.x * rows_per_cta;
+  const int nrows = min(rows_per_cta, H - r0);
+  pdl_wait();
+  pdl_trigger();
   if ((int)blockIdx.y >= *a.n_items) return;
   const int4 item = a.items[blockIdx.y];
   const int e = item.x, c0 = item.y;
   const int base = a.offsets[e];
   const int nt = min(NT, a.counts[e] - c0);
-  const int H = a.H, I = a.I;
-  const int r0 = blockIdx.x * rows_per_cta;
   if (r0 >= H) return;
-  const int nrows = min(rows_per_cta, H - r0);
   const bool shared = e == a.E;
   const MatrixRef &D = shared ? sh_down : down;
   const int ex = shared ? 0 : e;
@@ -743,12 +755,27 @@ static void launch_dense_down(const ForwardArgs &a, const GemvPlan &p, cudaStrea
   launch_pdl(fn, grid, dim3(kDenseThreads), smem, s, a, d, sd, rows);
 }
 
+// Threads per CTA of the quantised GEMVs (a thread per task): halved from 256 while the
+// grid has fewer than four CTAs per SM, so that few-token launches (a decode token reads
+// k experts) spread evenly over the 148 SMs instead of leaving some SMs a third CTA
+// while others idle.
+static int quant_threads(int rows_total, int tasks_per_row, int items) {
+  int threads = kGemvThreads;
+  while (threads > 64) {
+    const int rows = std::max(1, threads / tasks_per_row);
+    if ((long)((rows_total + rows - 1) / rows) * items >= 4L * 148) break;
+    threads >>= 1;
+  }
+  return threads;
+}
+
 template <int KIND, int NT>
 static void launch_up(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s) {
   if (is_dense(KIND)) return launch_dense_up<KIND, NT>(a, p, s);
   constexpr int kTask = Task<KIND>::kElems;
   const int nb = a.H / kTask;
-  const int rows = std::max(1, kGemvThreads / (2 * nb));
+  const int threads = quant_threads(a.I, 2 * nb, p.max_items);
+  const int rows = std::max(1, threads / (2 * nb));
   const size_t smem = (size_t)NT * (pad_index(a.H, kTask) + a.H / 16) * 4 +
                       (size_t)2 * rows * nb * NT * 4;
   auto fn = gemv_up_kernel<KIND, NT>;
@@ -759,7 +786,7 @@ static void launch_up(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s) {
   MatrixRef u = matrix(KIND, a.family == kGemma ? a.gate : a.up, a.up_stride, up_rows, a.H, p.up);
   MatrixRef sg = matrix(KIND, a.sh_gate, 0, a.I, a.H, p.sh_gate);
   MatrixRef su = matrix(KIND, a.sh_up, 0, a.I, a.H, p.sh_up);
-  launch_pdl(fn, grid, dim3(kGemvThreads), smem, s, a, g, u, sg, su, a.family == kGemma ? a.I : 0, rows);
+  launch_pdl(fn, grid, dim3(threads), smem, s, a, g, u, sg, su, a.family == kGemma ? a.I : 0, rows);
 }
 
 template <int KIND, int NT>
@@ -767,7 +794,8 @@ static void launch_down(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s)
   if (is_dense(KIND)) return launch_dense_down<KIND, NT>(a, p, s);
   constexpr int kTask = Task<KIND>::kElems;
   const int nb = a.I / kTask;
-  const int rows = std::max(1, kGemvThreads / nb);
+  const int threads = quant_threads(a.H, nb, p.max_items);
+  const int rows = std::max(1, threads / nb);
   const size_t smem = (size_t)NT * (pad_index(a.I, kTask) + a.I / 16) * 4 +
                       (size_t)rows * nb * NT * 4;
   auto fn = gemv_down_kernel<KIND, NT>;
@@ -775,7 +803,7 @@ static void launch_down(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s)
   dim3 grid((a.H + rows - 1) / rows, p.max_items);
   MatrixRef d = matrix(KIND, a.down, a.down_stride, a.H, a.I, p.down);
   MatrixRef sd = matrix(KIND, a.sh_down, 0, a.H, a.I, p.sh_down);
-  launch_pdl(fn, grid, dim3(kGemvThreads), smem, s, a, d, sd, rows);
+  launch_pdl(fn, grid, dim3(threads), smem, s, a, d, sd, rows);
 }
 
 template <int NT>

@@ -128,6 +128,7 @@ __device__ __forceinline__ void prep_cp16(float *dst, const float *src) {
 
 __global__ void __launch_bounds__(256) gemma_prep_kernel(ForwardArgs a) {
   pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) float ring[];  // [kPrepStages][kPrepTokens][kPrepLd]
   __shared__ float inv_s[kPrepTokens];
   const int H = a.H;
@@ -219,21 +220,20 @@ __global__ void __launch_bounds__(256) gemma_prep_kernel(ForwardArgs a) {
 // router logits: one sequential chain per (token, expert)
 // ---------------------------------------------------------------------------
 
-template <bool GLM>
-__device__ __forceinline__ float chain_step(float w, float x, float s) {
-  if (GLM) return __fadd_rn(s, __fmul_rn(w, x));
-  return __fmaf_rn(w, x, s);
-}
-
-// Few tokens: a CTA owns 8 experts and up to RT tokens; 8*RT threads run the sequential
-// chains. The experts' router rows ([E1][H] f32 copy made at set-up, so one row is
+// Few tokens: a CTA owns EPC <= 8 experts and up to RT <= 4 tokens; EPC*RT threads of
+// warp 0 run the sequential chains. EPC is chosen so that the grid spreads the router rows
+// over most SMs. The experts' router rows ([E1][H] f32 copy made at set-up, so one row is
 // contiguous) are requested up front as 1-D bulk copies in chunks of kRsChunk columns,
-// each chunk completing an mbarrier, and land in rows padded by 16 bytes (the 8 threads of a
-// token read 8 rows at the same column without bank conflicts). A chain thread reads 4
-// weights and 4 inputs per 16-byte load, so the chain runs at the FMA latency.
+// each chunk completing an mbarrier, and land in rows padded by 16 bytes (threads of one
+// token read different rows at the same column without bank conflicts). The token rows
+// arrive the same way, f32 or bf16 as given (a bf16 value is widened in the chain thread,
+// off the chain's critical path). A chain runs at the dependent-add latency (about 4.2
+// cycles per column on B200): weights and inputs for the next 32 or 64 columns are loaded
+// while the current ones feed the chain, and the GLM family's products are formed before
+// their sums.
 constexpr int kSmallExperts = 8;
-constexpr int kRsChunk = 256;
-constexpr int kRsMaxChunks = 48;  // H <= 12288
+constexpr int kRsChunk = 1024;
+constexpr int kRsMaxChunks = 12;  // H <= 12288
 
 __device__ __forceinline__ void rs_bulk(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
   asm volatile(
@@ -243,20 +243,112 @@ __device__ __forceinline__ void rs_bulk(uint32_t dst, const void *src, uint32_t 
       : "memory");
 }
 
+// Bounded wait for the phase with parity 0 of a router barrier; on timeout the status
+// word records it and the caller goes on (its sums are then discarded by the host).
+__device__ __forceinline__ void rs_wait(uint32_t bar, int32_t *status) {
+  const long long start = clock64();
+  uint32_t done = 0;
+  while (!done) {
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar)
+        : "memory");
+    if (!done && clock64() - start > 200000000ll) {
+      atomicExch(status, kStatusTimeout);
+      break;
+    }
+  }
+}
+
+// Eight inputs of a token row in shared memory, as f32, from column h (h % 8 == 0).
+template <bool XBF16>
+__device__ __forceinline__ void rs_x8(const void *xr, int h, float *v) {
+  if (XBF16) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(xr) + h);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(xr) + h);
+    const float4 b = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(xr) + h + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  }
+}
+
+template <int N, bool XBF16>
+__device__ __forceinline__ void rs_load(const float *wr, const void *xr, int h, float *w, float *xv) {
+#pragma unroll
+  for (int i = 0; i < N / 4; i++) {
+    const float4 a = *reinterpret_cast<const float4 *>(wr + h + 4 * i);
+    w[4 * i] = a.x, w[4 * i + 1] = a.y, w[4 * i + 2] = a.z, w[4 * i + 3] = a.w;
+  }
+#pragma unroll
+  for (int i = 0; i < N / 8; i++) rs_x8<XBF16>(xr, h + 8 * i, xv + 8 * i);
+}
+
+// Columns [h0, h1) of one chain (h1 - h0 a multiple of 32), in order.
+template <bool GLM, bool XBF16>
+__device__ __forceinline__ float rs_chain(const float *wr, const void *xr, int h0, int h1, float s) {
+  if (GLM) {
+    // products of 64 columns first, then their sums; the next 64 columns load meanwhile
+    constexpr int B = 64;
+    int h = h0;
+    if (h + B <= h1) {
+      float w[B], xv[B];
+      rs_load<B, XBF16>(wr, xr, h, w, xv);
+      for (; h + B <= h1; h += B) {
+        float p[B];
+#pragma unroll
+        for (int j = 0; j < B; j++) p[j] = __fmul_rn(w[j], xv[j]);
+        const int hn = h + 2 * B <= h1 ? h + B : h;  // last batch: a harmless reload
+        rs_load<B, XBF16>(wr, xr, hn, w, xv);
+#pragma unroll
+        for (int j = 0; j < B; j++) s = __fadd_rn(s, p[j]);
+      }
+    }
+    for (; h < h1; h += 32) {  // a 32-column tail
+      float w[32], xv[32];
+      rs_load<32, XBF16>(wr, xr, h, w, xv);
+#pragma unroll
+      for (int j = 0; j < 32; j++) s = __fadd_rn(s, __fmul_rn(w[j], xv[j]));
+    }
+    return s;
+  }
+  // fma chain: two register sets of 16 columns, one loading while the other feeds the chain
+  float wa[16], xa[16], wb[16], xb[16];
+  rs_load<16, XBF16>(wr, xr, h0, wa, xa);
+  for (int h = h0; h < h1; h += 32) {
+    rs_load<16, XBF16>(wr, xr, h + 16, wb, xb);
+#pragma unroll
+    for (int j = 0; j < 16; j++) s = __fmaf_rn(wa[j], xa[j], s);
+    const int hn = h + 32 < h1 ? h + 32 : h;  // last pass: a harmless reload
+    rs_load<16, XBF16>(wr, xr, hn, wa, xa);
+#pragma unroll
+    for (int j = 0; j < 16; j++) s = __fmaf_rn(wb[j], xb[j], s);
+  }
+  return s;
+}
+
 template <bool GLM, bool XBF16>
 __global__ void __launch_bounds__(256) router_small_kernel(const float *rows, const void *x, int T,
-                                                          int H, int E1, int RT,
+                                                          int H, int E1, int RT, int EPC,
                                                           const float *lbias, int E,
                                                           float *logits, int32_t *status) {
-  pdl_wait();
   extern __shared__ __align__(16) float smem[];
   __shared__ __align__(8) unsigned long long bars[kRsMaxChunks + 1];  // chunks, then x
-  const int HP = H + 4;                                     // padded rows (16 bytes)
-  float *xs = smem;                                         // [RT][H + 4]
-  float *ws = xs + RT * HP;                                 // [8][H + 4]
-  const int e0 = blockIdx.x * kSmallExperts, t0 = blockIdx.y * RT;
+  constexpr int kXb = XBF16 ? 2 : 4;                       // bytes per input value
+  const int HP = H + 4;                                     // padded weight rows (16 bytes)
+  const int XP = H + 16 / kXb;                              // padded token rows (16 bytes)
+  float *ws = smem;                                         // [EPC][H + 4] f32
+  uint8_t *xs = reinterpret_cast<uint8_t *>(ws + EPC * HP);  // [RT][XP] f32 or bf16
+  const int e0 = blockIdx.x * EPC, t0 = blockIdx.y * RT;
   const int nt = min(RT, T - t0);
-  const int ne = min(kSmallExperts, E1 - e0);
+  const int ne = min(EPC, E1 - e0);
   const int nchunks = (H + kRsChunk - 1) / kRsChunk;
   const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(bars);
   const uint32_t xbar = (uint32_t)__cvta_generic_to_shared(&bars[kRsMaxChunks]);
@@ -267,21 +359,15 @@ __global__ void __launch_bounds__(256) router_small_kernel(const float *rows, co
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  // One thread streams the router rows chunk by chunk as 1-D bulk copies (one per row and
-  // chunk, each completing the chunk's barrier), and an f32 token row the same way: the
-  // copy engine keeps far more bytes in flight per SM than 16-byte copies would.
+  // One thread of warp 1 (no chain runs there) issues the copies: issuing stalls while the
+  // copy engine's queue is full, so it stays off the chain warp. The rows are layer
+  // weights, so the first chunk is requested before pdl_wait(), while the kernel that
+  // writes the token rows still runs; then the token rows, then the other chunks.
   const uint32_t wbase = (uint32_t)__cvta_generic_to_shared(ws);
   const uint32_t xbase = (uint32_t)__cvta_generic_to_shared(xs);
-  if (threadIdx.x == 0) {
-    if (!XBF16) {
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
-                   "r"((uint32_t)(nt * H * 4))
-                   : "memory");
-      for (int tt = 0; tt < nt; tt++)
-        rs_bulk(xbase + (uint32_t)(tt * HP) * 4,
-                reinterpret_cast<const float *>(x) + (size_t)(t0 + tt) * H, (uint32_t)H * 4, xbar);
-    }
-    for (int c = 0; c < nchunks; c++) {
+  constexpr int kIssuer = 32;
+  auto issue_chunks = [&](int c_begin, int c_end) {
+    for (int c = c_begin; c < c_end; c++) {
       const int h0 = c * kRsChunk, w = min(kRsChunk, H - h0);
       asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar0 + 8 * c),
                    "r"((uint32_t)(ne * w * 4))
@@ -290,98 +376,34 @@ __global__ void __launch_bounds__(256) router_small_kernel(const float *rows, co
         rs_bulk(wbase + (uint32_t)(el * HP + h0) * 4, rows + (size_t)(e0 + el) * H + h0,
                 (uint32_t)w * 4, bar0 + 8 * c);
     }
+  };
+  if (threadIdx.x == kIssuer) issue_chunks(0, 1);
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == kIssuer) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
+                 "r"((uint32_t)(nt * H * kXb))
+                 : "memory");
+    for (int tt = 0; tt < nt; tt++)
+      rs_bulk(xbase + (uint32_t)(tt * XP * kXb),
+              reinterpret_cast<const uint8_t *>(x) + (size_t)(t0 + tt) * H * kXb, (uint32_t)(H * kXb),
+              xbar);
+    issue_chunks(1, nchunks);
   }
-  if (XBF16) {
-    // bf16 token rows, converted to f32 while the router rows stream in
-    for (int i = threadIdx.x; i < nt * (H / 4); i += blockDim.x) {
-      const int tt = i / (H / 4), c = i - tt * (H / 4);
-      const uint2 u = *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(x) +
-                                                       (size_t)(t0 + tt) * H + 4 * c);
-      *reinterpret_cast<float4 *>(xs + tt * HP + 4 * c) =
-          make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
-                      __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
-    }
-    __syncthreads();  // token rows staged
-  } else if (threadIdx.x < kSmallExperts * nt) {
-    // bounded wait for the token rows
-    const long long start = clock64();
-    uint32_t done = 0;
-    while (!done) {
-      asm volatile(
-          "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n"
-          " selp.u32 %0, 1, 0, p;\n}\n"
-          : "=r"(done)
-          : "r"(xbar)
-          : "memory");
-      if (!done && clock64() - start > 200000000ll) {
-        atomicExch(status, kStatusTimeout);
-        break;
-      }
-    }
-  }
-  const int el = threadIdx.x % kSmallExperts, tl = threadIdx.x / kSmallExperts;
+  const int el = threadIdx.x % EPC, tl = threadIdx.x / EPC;
   if (tl < nt && el < ne) {
-    const float *xr = xs + tl * HP;
+    const void *xr = xs + (size_t)tl * XP * kXb;
     const float *wr = ws + el * HP;
+    rs_wait(xbar, status);
     float s = GLM ? -0.0f : 0.0f;
     for (int c = 0; c < nchunks; c++) {
-      // bounded wait for chunk c (its copies complete by themselves)
-      const long long start = clock64();
-      uint32_t done = 0;
-      while (!done) {
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n"
-            " selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(done)
-            : "r"(bar0 + 8 * c)
-            : "memory");
-        if (!done && clock64() - start > 200000000ll) {
-          atomicExch(status, kStatusTimeout);
-          break;
-        }
-      }
-      const int h0 = c * kRsChunk, h1 = min(H, h0 + kRsChunk);
-      // Two register sets of 16 steps each: the set for the next 16 columns is loaded
-      // while the other feeds the chain, so shared-memory latency hides behind the FMAs
-      // and no register copies sit in the chain's way (H % 32 == 0).
-      float4 wa[4], xa[4], wb[4], xb[4];
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        wa[i] = *reinterpret_cast<const float4 *>(wr + h0 + 4 * i);
-        xa[i] = *reinterpret_cast<const float4 *>(xr + h0 + 4 * i);
-      }
-      for (int h = h0; h < h1; h += 32) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          wb[i] = *reinterpret_cast<const float4 *>(wr + h + 16 + 4 * i);
-          xb[i] = *reinterpret_cast<const float4 *>(xr + h + 16 + 4 * i);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          s = chain_step<GLM>(wa[i].x, xa[i].x, s);
-          s = chain_step<GLM>(wa[i].y, xa[i].y, s);
-          s = chain_step<GLM>(wa[i].z, xa[i].z, s);
-          s = chain_step<GLM>(wa[i].w, xa[i].w, s);
-        }
-        const int hn = h + 32 < h1 ? h + 32 : h;  // last pass: a harmless reload
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          wa[i] = *reinterpret_cast<const float4 *>(wr + hn + 4 * i);
-          xa[i] = *reinterpret_cast<const float4 *>(xr + hn + 4 * i);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          s = chain_step<GLM>(wb[i].x, xb[i].x, s);
-          s = chain_step<GLM>(wb[i].y, xb[i].y, s);
-          s = chain_step<GLM>(wb[i].z, xb[i].z, s);
-          s = chain_step<GLM>(wb[i].w, xb[i].w, s);
-        }
-      }
+      rs_wait(bar0 + 8 * c, status);  // its copies complete by themselves
+      const int h0 = c * kRsChunk;
+      s = rs_chain<GLM, XBF16>(wr, xr, h0, min(H, h0 + kRsChunk), s);
     }
     if (lbias && e0 + el < E) s = __fadd_rn(s, lbias[e0 + el]);
     logits[(size_t)(t0 + tl) * E1 + e0 + el] = s;
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // router [E][H] (f32 or bf16) + optional extra row (Qwen shared gate) -> [E1][H] f32
@@ -640,7 +662,8 @@ __global__ void __launch_bounds__(1024) topk_rank_softmax_kernel(const float *lo
                                                                 int E, int k, uint32_t *sel_idx,
                                                                 float *sel_w, int32_t *status) {
   pdl_wait();
-  __shared__ unsigned long long cand[32 * 32];
+  pdl_trigger();
+  __shared__ __align__(16) unsigned long long cand[32 * 32];
   __shared__ unsigned long long chosen[32];
   __shared__ int bad_s;
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -670,10 +693,15 @@ __global__ void __launch_bounds__(1024) topk_rank_softmax_kernel(const float *lo
     return;
   }
   const int C = nwarps * k;
+  const ulonglong2 *cand2 = reinterpret_cast<const ulonglong2 *>(cand);
   for (int c = tid; c < C; c += blockDim.x) {
     const unsigned long long mine = cand[c];
-    int r = 0;
-    for (int j = 0; j < C; j++) r += cand[j] > mine ? 1 : 0;
+    int r = (C & 1) && cand[C - 1] > mine ? 1 : 0;
+#pragma unroll 8
+    for (int j = 0; j < C / 2; j++) {  // two keys per 16-byte load, loads pipelined
+      const ulonglong2 q = cand2[j];
+      r += (q.x > mine ? 1 : 0) + (q.y > mine ? 1 : 0);
+    }
     if (r < k) chosen[r] = mine;
   }
   __syncthreads();
@@ -996,6 +1024,7 @@ constexpr int kCombineThreads = 64;
 
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(ForwardArgs a) {
   pdl_wait();
+  pdl_trigger();
   __shared__ int pos_s[32];
   __shared__ float w_s[32];
   __shared__ float gate_s;
@@ -1172,6 +1201,7 @@ __device__ __forceinline__ void dispatch_small_body(const ForwardArgs &a, SmallD
 
 __global__ void __launch_bounds__(1024) dispatch_small_kernel(ForwardArgs a) {
   pdl_wait();
+  pdl_trigger();
   __shared__ SmallDispatchSmem sm;
   const int EB = a.E + (a.rows_mode ? 1 : 0);
   if ((int)threadIdx.x < a.T * a.k) {
@@ -1186,8 +1216,9 @@ __global__ void __launch_bounds__(1024) dispatch_small_kernel(ForwardArgs a) {
 // topk_rank_softmax_kernel, then the small dispatch of its k pairs, in one CTA.
 __global__ void __launch_bounds__(1024) topk_dispatch1_kernel(ForwardArgs a) {
   pdl_wait();
+  pdl_trigger();
   __shared__ SmallDispatchSmem sm;
-  __shared__ unsigned long long cand[32 * 32];
+  __shared__ __align__(16) unsigned long long cand[32 * 32];
   __shared__ unsigned long long chosen[32];
   __shared__ int bad_s;
   const int E = a.E, k = a.k, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1217,10 +1248,15 @@ __global__ void __launch_bounds__(1024) topk_dispatch1_kernel(ForwardArgs a) {
     }
   } else {
     const int C = nwarps * k;
+    const ulonglong2 *cand2 = reinterpret_cast<const ulonglong2 *>(cand);
     for (int c = tid; c < C; c += blockDim.x) {
       const unsigned long long mine = cand[c];
-      int r = 0;
-      for (int j = 0; j < C; j++) r += cand[j] > mine ? 1 : 0;
+      int r = (C & 1) && cand[C - 1] > mine ? 1 : 0;
+#pragma unroll 8
+      for (int j = 0; j < C / 2; j++) {  // two keys per 16-byte load, loads pipelined
+        const ulonglong2 q = cand2[j];
+        r += (q.x > mine ? 1 : 0) + (q.y > mine ? 1 : 0);
+      }
       if (r < k) chosen[r] = mine;
     }
     __syncthreads();
@@ -1274,6 +1310,7 @@ __global__ void iota_kernel(int32_t *v, int n) {
 template <bool FUSED>
 __global__ void __launch_bounds__(1024) topk_sigmoid_rank_kernel(ForwardArgs a) {
   pdl_wait();
+  pdl_trigger();
   __shared__ unsigned long long key_s[kMaxGlmExperts];
   __shared__ unsigned long long cmp_s[kMaxGlmExperts];
   __shared__ float w_s[kMaxGlmExperts];
@@ -1410,17 +1447,21 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   // 2. router logits
   mark(kStageRouter);
   if (a.T <= 16 || !a.xT || !a.router_dup || a.H % kRgChunk) {
-    int RT = 4;
-    auto bytes = [&](int rt) { return ((size_t)rt + kSmallExperts) * (a.H + 4) * 4; };
+    int RT = std::min(4, a.T);
+    const int epc = std::max(1, std::min(kSmallExperts, a.E1 / 256));
+    const int xb = router_x_bf16 ? 2 : 4;
+    auto bytes = [&](int rt) {
+      return (size_t)epc * (a.H + 4) * 4 + (size_t)rt * (a.H + 16 / xb) * xb;
+    };
     while (RT > 1 && bytes(RT) > 200 * 1024) RT >>= 1;
     const size_t smem = bytes(RT);
-    dim3 grid((a.E1 + kSmallExperts - 1) / kSmallExperts, (a.T + RT - 1) / RT);
+    dim3 grid((a.E1 + epc - 1) / epc, (a.T + RT - 1) / RT);
 #define DM_ROUTER_SMALL(G, X)                                                               \
   {                                                                                         \
     auto fn = router_small_kernel<G, X>;                                                    \
     set_smem(fn, smem);                                                                     \
     launch_pdl(fn, grid, dim3(256), smem, stream, (const float *)a.router_rows, router_x, a.T,  \
-               a.H, a.E1, RT, a.logit_bias, a.E, a.logits, a.status);                       \
+               a.H, a.E1, RT, epc, a.logit_bias, a.E, a.logits, a.status);                  \
   }
     if (glm && router_x_bf16) DM_ROUTER_SMALL(true, true)
     else if (glm) DM_ROUTER_SMALL(true, false)
