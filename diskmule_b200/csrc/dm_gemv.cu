@@ -363,8 +363,8 @@ __device__ __forceinline__ void stage_rows(float *xs, float *s16, int K, int gro
 
 __device__ __forceinline__ float act_fn(const ForwardArgs &a, int expert, float g, float u);
 
-// Ask L2 for the bytes of this thread's first task before x is staged, so the weight
-// fetch from HBM overlaps the staging and the barriers.
+// Ask for the bytes of this thread's first task before x is staged, so the weight fetch
+// from HBM overlaps the staging and the barriers.
 template <int KIND>
 __device__ __forceinline__ void prefetch_task(const MatrixRef &m, int expert, int row, int task) {
   const uint8_t *p;
@@ -380,7 +380,11 @@ __device__ __forceinline__ void prefetch_task(const MatrixRef &m, int expert, in
     p = m.base + (uint64_t)expert * m.stride + (uint64_t)row * m.row_bytes + (uint64_t)task * tb;
     bytes = tb;
   }
-  for (int o = 0; o < bytes; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + o));
+  // every 128-byte line the task touches, into L1 (and L2 on the way): the task's loads
+  // then find it on the SM once x is staged
+  const uintptr_t first = (uintptr_t)p & ~(uintptr_t)127, last = ((uintptr_t)p + bytes - 1) & ~(uintptr_t)127;
+  for (uintptr_t l = first; l <= last; l += 128)
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(l));
 }
 
 template <int KIND, int NT>
