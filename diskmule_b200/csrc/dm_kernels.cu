@@ -431,9 +431,11 @@ int launch_router_rows(const void *router, int bf16, int E, int H, const float *
 // two experts at a time with packed f32x2 instructions (one rounding per element, as
 // scalar code). Operands come from x transposed and duplicated per forward, [h][t][2]
 // (a 16-byte load yields two (x, x) pairs; a warp reads only two distinct x chunks), and
-// the router padded to f32 [h][64k] at set-up, through a 4-stage cp.async pipeline of
-// 32-wide h chunks.
-constexpr int kRgTokens = 32, kRgExperts = 64, kRgChunk = 32, kRgThreads = 128, kRgStages = 4;
+// the router padded to f32 [h][64k] at set-up, through a 3-stage cp.async pipeline of
+// 64-wide h chunks (one block barrier per 64 steps of the chains); operands are read with
+// plain shared-memory loads, so the compiler can issue the next step's loads ahead of the
+// current step's FMAs.
+constexpr int kRgTokens = 32, kRgExperts = 64, kRgChunk = 64, kRgThreads = 128, kRgStages = 3;
 constexpr int kRgXBytes = kRgChunk * kRgTokens * 8;
 constexpr int kRgStageBytes = kRgXBytes + kRgChunk * kRgExperts * 4;
 
@@ -454,12 +456,6 @@ __device__ __forceinline__ void rg_cp16(uint32_t dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
-__device__ __forceinline__ ulonglong2 rg_lds(uint32_t addr) {
-  ulonglong2 v;
-  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "r"(addr));
-  return v;
-}
-
 template <bool GLM>
 __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w32, int wld,
                                                                  const float *xT2, int xld, int T,
@@ -476,12 +472,12 @@ __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w3
       const uint32_t st = sbase + (uint32_t)(c % kRgStages) * kRgStageBytes;
       const int h0 = c * kRgChunk;
 #pragma unroll
-      for (int i = 0; i < 4; i++) {  // x: 32 rows x 16 pieces (32 tokens x 8 bytes)
+      for (int i = 0; i < kRgChunk * 16 / kRgThreads; i++) {  // x: rows of 32 tokens x 8 bytes
         const int f = tid + kRgThreads * i, row = f >> 4, piece = f & 15;
         rg_cp16(st + row * 256 + piece * 16, xT2 + ((size_t)(h0 + row) * xld + t0) * 2 + 4 * piece);
       }
 #pragma unroll
-      for (int i = 0; i < 4; i++) {  // w: 32 rows x 16 pieces (64 experts x 4 bytes)
+      for (int i = 0; i < kRgChunk * 16 / kRgThreads; i++) {  // w: rows of 64 experts x 4 bytes
         const int f = tid + kRgThreads * i, row = f >> 4, piece = f & 15;
         rg_cp16(st + kRgXBytes + row * 256 + piece * 16, w32 + (size_t)(h0 + row) * wld + e0 + 4 * piece);
       }
@@ -499,12 +495,12 @@ __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w3
     asm volatile("cp.async.wait_group %0;" ::"n"(kRgStages - 2) : "memory");
     __syncthreads();  // chunk c is in; every thread is done with chunk c - 1
     issue(c + kRgStages - 1);
-    const uint32_t st = sbase + (uint32_t)(c % kRgStages) * kRgStageBytes;
+    const uint8_t *stp = rg_smem + (size_t)(c % kRgStages) * kRgStageBytes;
 #pragma unroll
     for (int kk = 0; kk < kRgChunk; kk++) {
-      const ulonglong2 xa = rg_lds(st + kk * 256 + ty * 32);
-      const ulonglong2 xb = rg_lds(st + kk * 256 + ty * 32 + 16);
-      const ulonglong2 w = rg_lds(st + kRgXBytes + kk * 256 + tx * 16);
+      const ulonglong2 xa = *reinterpret_cast<const ulonglong2 *>(stp + kk * 256 + ty * 32);
+      const ulonglong2 xb = *reinterpret_cast<const ulonglong2 *>(stp + kk * 256 + ty * 32 + 16);
+      const ulonglong2 w = *reinterpret_cast<const ulonglong2 *>(stp + kRgXBytes + kk * 256 + tx * 16);
       const uint64_t xp[4] = {xa.x, xa.y, xb.x, xb.y};
 #pragma unroll
       for (int i = 0; i < 4; i++) {
