@@ -557,10 +557,16 @@ struct Cfg {
   // of NI issuers x NB columns. Four issuers (one per SM sub-partition) when their
   // accumulators fit beside three A stages, single-buffered if need be (the epilogue
   // then reads all partial sums before it stores); otherwise two or one, double-buffered.
-  static constexpr int NI4_AB = 3 * 128 + 2 * 4 * NB <= 512 ? 2 : (3 * 128 + 4 * NB <= 512 ? 1 : 0);
-  static constexpr int NA = NI4_AB ? 3 : (3 * 128 + 4 * NB <= 512 ? 3 : 2);
-  static constexpr int NI = NI4_AB ? 4 : (NA * 128 + 4 * NB <= 512 ? 2 : 1);
-  static constexpr int AB = NI4_AB ? NI4_AB : 2;
+  // The down products (K = I: two or three K steps per unit) use two issuers with
+  // double-buffered accumulators at NB = 32 instead: a unit boundary every few steps costs
+  // more than the slower issue (measured on the Qwen shape: 189 -> 178 us).
+  static constexpr bool kShortK = KIND != kUpQ4K && NB == 32;
+  static constexpr int NI4_AB =
+      kShortK ? 0 : (3 * 128 + 2 * 4 * NB <= 512 ? 2 : (3 * 128 + 4 * NB <= 512 ? 1 : 0));
+  static constexpr int NA = kShortK ? 3 : (NI4_AB ? 3 : (3 * 128 + 4 * NB <= 512 ? 3 : 2));
+  static constexpr int NI = kShortK ? 2 : (NI4_AB ? 4 : (NA * 128 + 4 * NB <= 512 ? 2 : 1));
+  static constexpr int AB = kShortK ? 2 : (NI4_AB ? NI4_AB : 2);
+  static_assert(NB % 16 == 0 && NA * 128 + AB * NI * NB <= 512, "tensor memory layout");
   static constexpr int kAccCol = NA * 128;
   static constexpr int kBStage = (kStepK / 64) * NB * 128;  // 4 swizzle atoms of NB rows
   static constexpr int kFixed = 1024 + NA * kBStage + kBarBytes;
@@ -862,7 +868,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
       // column n of each issuer's accumulator: token n (or, with the split, hi of token
       // n/2 at even n and lo at odd n); the issuers' partial sums are added in order
       const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + C::kAccCol + (uint32_t)(acc * NI * NB);
-      constexpr int CW = NB < 32 / NI ? NB : 32 / NI;  // columns per chunk and issuer
+      // columns per chunk and issuer (a tcgen05.ld here moves 16 columns)
+      constexpr int CW = NB < 16 ? NB : (32 / NI < 16 ? 16 : 32 / NI);
       constexpr int TPC = SPLIT ? CW / 2 : CW;         // tokens per chunk
       // gate/up rows: A rows 2i and 2i+1 hold index 0 and 1 of the gate|up axis
       const bool swapped = un.e == a.E ? side.sh_up_swapped : side.up_swapped;
