@@ -216,7 +216,7 @@ def run_reference(args):
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -439,7 +439,7 @@ def run_ours(args):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     sl.close()
     ctx.close()
     if world > 1:
@@ -595,7 +595,7 @@ def run_ep(args):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     sl.close()
     ctx.close()
     dist.barrier()
@@ -750,12 +750,27 @@ def run_stack(args):
                          "sample": f"{check_n} greedy steps of the same stack on the oracle "
                                    "(experts read from the host pool)"},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     st.close()
     ctx.close()
 
 
+_RESULT_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Print the one JSON result line on the process's original standard output."""
+    print(json.dumps(line), file=_RESULT_OUT or sys.stdout, flush=True)
+
+
 def main():
+    global _RESULT_OUT
+    # Libraries write banners to standard output from C (NCCL prints its version when a
+    # communicator starts): keep the original stdout for the result line alone and send
+    # everything else written to file descriptor 1 to stderr.
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
