@@ -166,13 +166,24 @@ __global__ void __launch_bounds__(256) gemma_prep_kernel(ForwardArgs a) {
     if (threadIdx.x < nt) {
       const float *row = ring + (flat ? 0 : (c % kPrepStages) * kPrepTokens * kPrepLd) + threadIdx.x * ld;
       const int w = min(cw, H - c * cw);
-#pragma unroll 4
-      for (int i = 0; i < w; i += 4) {  // 16-byte reads: padded rows spread the banks
-        const float4 v = *reinterpret_cast<const float4 *>(row + i);
-        s = __fmaf_rn(v.x, v.x, s);
-        s = __fmaf_rn(v.y, v.y, s);
-        s = __fmaf_rn(v.z, v.z, s);
-        s = __fmaf_rn(v.w, v.w, s);
+      // 16-byte reads (padded rows spread the banks) from two register sets of 16 values:
+      // the next 16 load while the current 16 feed the chain (w % 32 == 0)
+      float va[16], vb[16];
+      auto load16 = [&](int i, float *v) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float4 q = *reinterpret_cast<const float4 *>(row + i + 4 * j);
+          v[4 * j] = q.x, v[4 * j + 1] = q.y, v[4 * j + 2] = q.z, v[4 * j + 3] = q.w;
+        }
+      };
+      load16(0, va);
+      for (int i = 0; i < w; i += 32) {
+        load16(i + 16, vb);
+#pragma unroll
+        for (int j = 0; j < 16; j++) s = __fmaf_rn(va[j], va[j], s);
+        load16(i + 32 < w ? i + 32 : i, va);  // last pass: a harmless reload
+#pragma unroll
+        for (int j = 0; j < 16; j++) s = __fmaf_rn(vb[j], vb[j], s);
       }
     }
     __syncthreads();  // the stage is refilled by the next iteration's issue
