@@ -143,6 +143,27 @@ def measured_tensor_peak():
 FORMAT_NAMES = {0: "F32", 1: "F16", 6: "Q5_0", 8: "Q8_0", 12: "Q4_K", 14: "Q6_K", 30: "BF16"}
 
 
+def choose_roofline(kernel, flops, nbytes, ms, hbm, tensor, traffic):
+    """Roofline of one stage: the tensor peak when its FLOP per byte is above the ridge
+    (peak FLOP/s / peak bytes/s), else HBM. hbm = (GB/s, source), tensor = (TFLOP/s, source)."""
+    (peak, peak_src), (tpeak, tpeak_src) = hbm, tensor
+    intensity = flops / nbytes
+    if intensity > tpeak * 1e12 / (peak * 1e9):
+        achieved = flops / (ms / 1e3) / 1e12
+        r = {"bound": "tensor", "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
+             "frac": achieved / tpeak, "traffic": traffic, "kernel": kernel,
+             "algorithmic_flops": flops, "algorithmic_bytes": nbytes, "peak_source": tpeak_src,
+             "note": "fp16 MMAs on hi + lo activation halves: the tensor pipe does twice "
+                     "the algorithmic FLOPs"}
+    else:
+        achieved = nbytes / (ms / 1e3) / 1e9
+        r = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+             "frac": achieved / peak, "traffic": traffic, "kernel": kernel,
+             "algorithmic_bytes": nbytes, "peak_source": peak_src}
+    r["flop_per_byte"] = round(intensity, 1)
+    return r
+
+
 def stage_flops(sl, T):
     """Algorithmic FLOPs (2 per multiply-add) of the expert stages."""
     cfg = sl.cfg
@@ -323,23 +344,8 @@ def run_ours(args):
     nflops = stage_flops(sl, T)
     workload = f"{args.config}-T{T}"
     traffic = ncu_traffic(dominant, workload)
-    # the bound is the one the stage's arithmetic intensity puts it under (ridge = peak
-    # FLOP/s / peak bytes/s)
-    intensity = nflops[dominant] / nbytes[dominant]
-    if intensity > tpeak * 1e12 / (peak * 1e9):
-        achieved = nflops[dominant] / (avg[dominant] / 1e3) / 1e12
-        roofline = {"bound": "tensor", "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
-                    "frac": achieved / tpeak, "traffic": traffic, "kernel": dominant,
-                    "algorithmic_flops": nflops[dominant], "algorithmic_bytes": nbytes[dominant],
-                    "peak_source": tpeak_src,
-                    "note": "fp16 MMAs on hi + lo activation halves: the tensor pipe does twice "
-                            "the algorithmic FLOPs"}
-    else:
-        achieved = nbytes[dominant] / (avg[dominant] / 1e3) / 1e9
-        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                    "frac": achieved / peak, "traffic": traffic, "kernel": dominant,
-                    "algorithmic_bytes": nbytes[dominant], "peak_source": peak_src}
-    roofline["flop_per_byte"] = round(intensity, 1)
+    roofline = choose_roofline(dominant, nflops[dominant], nbytes[dominant], avg[dominant],
+                               (peak, peak_src), (tpeak, tpeak_src), traffic)
     roofline["stage_ms"] = {n: round(v, 4) for n, v in avg.items()}
 
     # ---- decode (T=1) ----

@@ -27,3 +27,17 @@ def test_reference_arm_prints_one_json_line():
     assert d["impl"] == "reference" and d["value"] > 0
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def test_roofline_follows_the_arithmetic_intensity():
+    sys.path.insert(0, ROOT)
+    import bench
+    hbm, tensor = (6456.8, "measured"), (1666.2, "measured")
+    # Qwen T=512 gate/up: 36.5 FLOP/byte, under the ridge (258) -> HBM
+    r = bench.choose_roofline("expert_up", 2.2e10, 6.2e8, 0.228, hbm, tensor, None)
+    assert r["bound"] == "hbm" and r["unit"] == "GB/s"
+    assert abs(r["achieved"] - 6.2e8 / 0.228e-3 / 1e9) < 1e-6 and abs(r["frac"] - r["achieved"] / 6456.8) < 1e-12
+    # Gemma T=4096 gate/up: 613 FLOP/byte -> tensor peak, TFLOP/s
+    r = bench.choose_roofline("expert_up", 2.598e11, 4.239e8, 0.718, hbm, tensor, 1.0)
+    assert r["bound"] == "tensor" and r["unit"] == "TFLOP/s" and r["traffic"] == 1.0
+    assert abs(r["achieved"] - 2.598e11 / 0.718e-3 / 1e12) < 1e-9 and r["flop_per_byte"] > 258
