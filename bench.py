@@ -30,19 +30,31 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 
+DEFAULT_TOKENS = {"glm52": 8192, "qwen35": 512, "gemma4": 4096}
+
+
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=600)  # ~0.3 s timed: the clock sampler sees it
+    p.add_argument("--steps", type=int, default=None,
+                   help="timed steps (default: 100 for glm52, 600 for the GGUF blocks)")
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--config", default="qwen35")
-    p.add_argument("--tokens", type=int, default=512)
+    p.add_argument("--config", default="glm52",
+                   help="glm52 (configuration 4, expert parallel over the ranks; the default), "
+                        "qwen35 or gemma4 (GGUF blocks, one replica per rank)")
+    p.add_argument("--tokens", type=int, default=None,
+                   help="tokens per step (default 8192 for glm52 in total over the ranks, "
+                        "512 for qwen35 and 4096 for gemma4 per rank)")
     p.add_argument("--decode-steps", type=int, default=200)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
-    p.add_argument("--ep", action="store_true",
-                   help="expert parallelism over the ranks (config 4: --config glm52 --tokens 8192 "
-                        "tokens in total, split over the GPUs)")
+    p.add_argument("--sample", type=int, default=4,
+                   help="tokens per step of the CPU reference arm and of the parity check")
+    p.add_argument("--profile-pass", type=int, default=0, metavar="R",
+                   help="untimed: R forwards of --config/--tokens on one GPU with CUDA graphs "
+                        "off, so every kernel is its own launch (the command profiled by ncu)")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the GGUF-block and decode figures reported beside the headline")
     p.add_argument("--stack", action="store_true",
                    help="out-of-core decode (config 5): a stack of GLM-5.2 layers with experts in "
                         "pinned host memory and --slots HBM slots per layer; --steps decode steps")
@@ -54,7 +66,17 @@ def parse_args():
                         "allows)")
     p.add_argument("--check-steps", type=int, default=16,
                    help="decode steps replayed on the CPU oracle (token parity, CPU baseline)")
-    return p.parse_args()
+    a = p.parse_args()
+    if a.tokens is None:
+        a.tokens = DEFAULT_TOKENS.get(a.config, 512)
+    if a.steps is None:
+        a.steps = 256 if a.stack else (100 if a.config == "glm52" else 600)
+    return a
+
+
+def metric_name(config: str, tokens: int) -> str:
+    """The metric string, the same for both arms and every GPU count."""
+    return f"MoE-layer tokens/s ({config} prefill T={tokens})"
 
 
 CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -129,21 +151,27 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def measured_tensor_peak():
-    """Dense bf16/fp16 TFLOP/s (burst: the stage is timed inside a short forward)."""
+def measured_tensor_peak(sustained: bool = False):
+    """Dense bf16/fp16 TFLOP/s: the burst figure for a stage timed inside a short forward,
+    the sustained one (a seconds-long GEMM loop under the power cap) for a long step."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         with open(path) as f:
             d = json.load(f)
-        if "bf16_tflops" in d:
-            return d["bf16_tflops"], "measured"
-    return 1590.0, "fallback"
+        key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
+        if key in d:
+            return d[key], "measured" + (" (sustained)" if sustained else " (burst)")
+    return (1400.0, "fallback (sustained)") if sustained else (1590.0, "fallback (burst)")
 
 
 FORMAT_NAMES = {0: "F32", 1: "F16", 6: "Q5_0", 8: "Q8_0", 12: "Q4_K", 14: "Q6_K", 30: "BF16"}
+KERNEL_NAMES = {"gguf": {"expert_up": "tc_expert_kernel (gate/up)",
+                         "expert_down": "tc_expert_kernel (down)"},
+                "bf16": {"expert_up": "tc_bf16_kernel (gate/up)",
+                         "expert_down": "tc_bf16_kernel (down)"}}
 
 
-def choose_roofline(kernel, flops, nbytes, ms, hbm, tensor, traffic):
+def choose_roofline(kernel, flops, nbytes, ms, hbm, tensor, traffic, note=None):
     """Roofline of one stage: the tensor peak when its FLOP per byte is above the ridge
     (peak FLOP/s / peak bytes/s), else HBM. hbm = (GB/s, source), tensor = (TFLOP/s, source)."""
     (peak, peak_src), (tpeak, tpeak_src) = hbm, tensor
@@ -152,15 +180,16 @@ def choose_roofline(kernel, flops, nbytes, ms, hbm, tensor, traffic):
         achieved = flops / (ms / 1e3) / 1e12
         r = {"bound": "tensor", "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
              "frac": achieved / tpeak, "traffic": traffic, "kernel": kernel,
-             "algorithmic_flops": flops, "algorithmic_bytes": nbytes, "peak_source": tpeak_src,
-             "note": "fp16 MMAs on hi + lo activation halves: the tensor pipe does twice "
-                     "the algorithmic FLOPs"}
+             "algorithmic_flops": flops, "algorithmic_bytes": nbytes, "peak_source": tpeak_src}
+        if note:
+            r["note"] = note
     else:
         achieved = nbytes / (ms / 1e3) / 1e9
         r = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
              "frac": achieved / peak, "traffic": traffic, "kernel": kernel,
              "algorithmic_bytes": nbytes, "peak_source": peak_src}
     r["flop_per_byte"] = round(intensity, 1)
+    r["kernel_ms"] = round(ms, 4)
     return r
 
 
@@ -183,65 +212,138 @@ def ncu_traffic(kernel: str, workload: str):
 
 
 # ---------------------------------------------------------------------------
-# reference arm: the CPU restatement of the reference path (the oracle)
+# the CPU restatement of the reference path (the oracle): reference arm, CPU baseline
+# and parity checker. The reference arm generates its inputs with the oracle library's
+# copy of the seeded generator, so it never loads the CUDA library.
 # ---------------------------------------------------------------------------
 
-def cpu_tokens_per_second(cfg_name: str, seconds: float, threads: int, seed: int = 1,
-                          sample: int | None = None):
-    from diskmule_b200.synthetic import CONFIGS, SyntheticLayer, input_spec, layer_specs, vectors
+def glm_sample(cfg_name: str, x32: np.ndarray, threads: int, fill=None, seed: int = 1):
+    """Oracle GLM block over the token rows x32 [n, H] (f32 values of bf16 rows), with
+    host weights for the experts those tokens select only (the whole pool is tens of GB).
+    Returns (seconds of the block call, y, idx, w)."""
+    from diskmule_b200.synthetic import CONFIGS, SyntheticLayer, layer_specs, vectors
+    from oracle import oracle as O
+    cfg = dict(CONFIGS[cfg_name])
+    specs = layer_specs(cfg, seed)
+    sl = SyntheticLayer(cfg_name, cfg, seed, None, specs, vectors(cfg, seed))
+    router = specs["router"].host(fill=fill)
+    bias = specs["bias"].host(fill=fill).view(np.float32)
+    chosen = set()
+    for t in range(x32.shape[0]):
+        _, lg = O.glm_matvec(O.BF16, cfg["experts"], cfg["hidden"], router, x32[t], threads)
+        _, idx, _ = O.glm_select(lg, bias, cfg["top_k"], cfg["n_groups"], cfg["topk_groups"],
+                                 cfg["normalize"])
+        chosen.update(int(i) for i in idx)
+    w = sl.host_weights(sorted(chosen), fill=fill)
+    t0 = time.perf_counter()
+    rc, y, idx, wt = O.glm_moe(w, x32, threads=threads)
+    el = time.perf_counter() - t0
+    assert rc == O.OK
+    return el, y, idx, wt
+
+
+def gguf_sample(cfg_name: str, x32: np.ndarray, threads: int, fill=None, seed: int = 1,
+                logit_bias=None):
+    """Oracle GGUF block (Qwen / Gemma) over x32 [n, H] with whole host weights."""
+    from diskmule_b200.synthetic import CONFIGS, SyntheticLayer, layer_specs, vectors
     from oracle import oracle as O
     cfg = dict(CONFIGS[cfg_name])
     sl = SyntheticLayer(cfg_name, cfg, seed, None, layer_specs(cfg, seed), vectors(cfg, seed))
-    w = sl.host_weights()
-    fn = {"gemma4": O.gemma_moe, "qwen35": O.qwen_moe, "glm52": O.glm_moe}[cfg["family"]]
-    n = sample or max(threads, 8)
-    spec = input_spec(cfg, n, 21)
-    raw = spec.host()
-    x = raw.view(np.float32).reshape(n, -1)
-    fn(w, x[:1], threads=threads)  # touch the weights once
-    done, t0 = 0, time.perf_counter()
-    while True:
-        rc, _, _, _ = fn(w, x, threads=threads)
-        assert rc == O.OK
-        done += n
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
-    return done / el, n, el
+    sl.logit_bias = logit_bias
+    w = sl.host_weights(fill=fill)
+    fn = {"gemma4": O.gemma_moe, "qwen35": O.qwen_moe}[cfg["family"]]
+    fn(w, x32[:1], threads=threads)  # touch the weights once
+    t0 = time.perf_counter()
+    rc, y, idx, wt = fn(w, x32, threads=threads)
+    el = time.perf_counter() - t0
+    assert rc == O.OK
+    return el, y, idx, wt
+
+
+def x32_rows(cfg: dict, rows: np.ndarray) -> np.ndarray:
+    """f32 values of token rows (bf16 bits for GLM, f32 otherwise)."""
+    if cfg["family"] == "glm52":
+        return (rows.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+    return rows.view(np.float32)
 
 
 def run_reference(args):
+    """The reference arm: the oracle on the host cores, on a bounded token sample per step
+    of the same workload (tokens are independent in the reference, which runs one token
+    at a time: src/glm52/cpu.rs:462-524, src/gemma4/cpu.rs:358-378)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    from diskmule_b200.synthetic import CONFIGS, input_spec
+    from oracle import oracle as O
     threads = os.cpu_count() or 1
+    cfg = CONFIGS[args.config]
+    n = args.sample if cfg["family"] == "glm52" else max(args.sample, 16)
+    # the first n rows of the step's input (row t of a seeded input is the same for any T)
+    x32 = x32_rows(cfg, input_spec(cfg, n, 21).host(fill=O.synth_fill)).reshape(n, -1)
     per_step = []
-    sample = max(threads, 8)
-    for i in range(args.warmup + args.steps):
-        tps, n, el = cpu_tokens_per_second(args.config, 0.0, threads, sample=sample)
-        if i >= args.warmup:
-            per_step.append(n / tps)
-    total_tokens = sample * args.steps
+    if cfg["family"] == "glm52":
+        from diskmule_b200.synthetic import SyntheticLayer, layer_specs, vectors
+        # weights once (the same sample every step), then the block call timed per step
+        sl = SyntheticLayer(args.config, dict(cfg), 1, None, layer_specs(dict(cfg), 1),
+                            vectors(dict(cfg), 1))
+        el, _, idx, _ = glm_sample(args.config, x32, threads, fill=O.synth_fill)
+        w = sl.host_weights(sorted(set(idx.ravel().tolist())), fill=O.synth_fill)
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            rc, _, _, _ = O.glm_moe(w, x32, threads=threads)
+            assert rc == O.OK
+            if i >= args.warmup:
+                per_step.append(time.perf_counter() - t0)
+    else:
+        from diskmule_b200.synthetic import SyntheticLayer, layer_specs, vectors
+        sl = SyntheticLayer(args.config, dict(cfg), 1, None, layer_specs(dict(cfg), 1),
+                            vectors(dict(cfg), 1))
+        w = sl.host_weights(fill=O.synth_fill)
+        fn = {"gemma4": O.gemma_moe, "qwen35": O.qwen_moe}[cfg["family"]]
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            rc, _, _, _ = fn(w, x32, threads=threads)
+            assert rc == O.OK
+            if i >= args.warmup:
+                per_step.append(time.perf_counter() - t0)
     secs = sum(per_step)
-    value = total_tokens / secs
+    value = n * args.steps / secs
+    sample = (f"{n} tokens per step of the {args.config} block (the first {n} rows of the "
+              "step's input; tokens are independent in the reference)")
     line = {
-        "impl": "reference", "metric": f"MoE-layer tokens/s ({args.config}, CPU reference path)",
+        "impl": "reference", "metric": metric_name(args.config, args.tokens),
         "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.config} MoE block, {sample}-token sample per step",
-                   "parallelism": "cpu"},
+        "scaling": "strong" if cfg["family"] == "glm52" else "weak", "vs_baseline": None,
+        "dtype": "bf16" if cfg["family"] == "glm52" else "f32", "data": "synthetic",
+        "config": {"workload": f"{args.config} MoE block, CPU oracle on a {n}-token sample "
+                               "per step", "parallelism": f"cpu ({threads} threads)"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{sample} tokens per step of the {args.config} block "
-                                   "(tokens are independent in the reference)"},
+                         "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     emit(line)
 
 
+def parity_summary(cfg, y, idx, w, y_ref, idx_ref, w_ref):
+    """The north-star bar on a token sample: indices and order bit-exact, selection weights
+    within 2e-7, outputs within 1e-3 relative L2."""
+    num = np.linalg.norm((y - y_ref).astype(np.float64), axis=-1)
+    den = np.linalg.norm(y_ref.astype(np.float64), axis=-1)
+    tok = num / np.maximum(den, 1e-30)
+    layer = float(np.linalg.norm((y - y_ref).astype(np.float64)) /
+                  np.linalg.norm(y_ref.astype(np.float64)))
+    same = bool(np.array_equal(idx, idx_ref))
+    wmax = float(np.max(np.abs(w - w_ref)))
+    return {"tokens": int(y.shape[0]), "indices_equal": same, "weights_max_abs": wmax,
+            "rel_l2": layer, "rel_l2_token_max": float(tok.max()),
+            "pass": same and wmax <= 2e-7 and layer <= 1e-3}
+
+
 # ---------------------------------------------------------------------------
-# our arm
+# our arm: shared measurement helpers
 # ---------------------------------------------------------------------------
 
 def stage_bytes(sl, T, counts):
@@ -260,7 +362,134 @@ def stage_bytes(sl, T, counts):
     return {"expert_up": up, "expert_down": down, "router": router}
 
 
-def run_ours(args):
+def profile_stages(layer, step, n):
+    """Average per-stage device times (ms) over n profiled forwards (CUDA events recorded
+    by the library on the launching stream at every stage boundary)."""
+    layer.set_profiling(True)
+    totals = {}
+    for _ in range(n):
+        step()
+        for name, t in layer.stage_times().items():
+            totals[name] = totals.get(name, 0.0) + t
+    layer.set_profiling(False)
+    return {name: v / n for name, v in totals.items()}
+
+
+def block_roofline(sl, T, avg, workload, sustained):
+    """Roofline of the dominant expert stage from the profiled stage times."""
+    counts, _, _, _ = sl.layer.last_dispatch(T)
+    nbytes = stage_bytes(sl, T, counts)
+    nflops = stage_flops(sl, T)
+    dominant = max(("expert_up", "expert_down"), key=lambda n: avg[n])
+    hbm = measured_peaks()
+    tensor = measured_tensor_peak(sustained)
+    bf16 = sl.cfg["gate_type"] == 30
+    note = None if bf16 else ("fp16 MMAs on hi + lo activation halves: the tensor pipe does "
+                              "twice the algorithmic FLOPs")
+    r = choose_roofline(dominant, nflops[dominant], nbytes[dominant], avg[dominant], hbm,
+                        tensor, ncu_traffic(dominant, workload), note)
+    r["kernel"] = KERNEL_NAMES["bf16" if bf16 else "gguf"][dominant]
+    r["stage_ms"] = {n: round(v, 4) for n, v in avg.items()}
+    return r
+
+
+def decode_block(sl, steps, warmup, rank, seed=33):
+    """Decode (T = 1): distinct tokens, L2 flushed (a 256 MB write) before every timed
+    token, so each token's router and expert weights come from HBM; tokens are timed one
+    by one with events on the launching stream and the flushes stay outside the spans."""
+    import torch
+    cfg = sl.cfg
+    H = cfg["hidden"]
+    xdt = torch.bfloat16 if cfg["family"] == "glm52" else torch.float32
+    from diskmule_b200.synthetic import input_spec
+    n_dec = 12  # forward() keeps up to 16 CUDA graphs keyed by buffers
+    x1 = torch.empty((n_dec, H), dtype=xdt, device="cuda")
+    input_spec(cfg, n_dec, seed + rank).device_fill(x1.data_ptr())
+    y1 = torch.empty((n_dec, H), dtype=torch.float32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    xrow = x1.element_size() * H
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    torch.cuda.synchronize()
+
+    def dec(i):
+        j = i % n_dec
+        sl.layer.forward(x1.data_ptr() + j * xrow, y1.data_ptr() + j * H * 4, 1, stream=sptr)
+
+    for i in range(warmup):
+        dec(i)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(i & 0xFF)
+        ev[i][0].record(stream)
+        dec(i)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    dms = sum(a.elapsed_time(b) for a, b in ev)
+    dec(0)
+    torch.cuda.synchronize()
+    c1, _, _, _ = sl.layer.last_dispatch(1)
+    b1 = stage_bytes(sl, 1, c1)
+    dec_bytes = b1["expert_up"] + b1["expert_down"] + b1["router"]
+    sl.layer.set_profiling(True)
+    dtot = {}
+    for i in range(20):
+        flush.fill_(i & 0xFF)
+        dec(i)
+        for name, t in sl.layer.stage_times().items():
+            dtot[name] = dtot.get(name, 0.0) + t
+    sl.layer.set_profiling(False)
+    del flush
+    peak, _ = measured_peaks()
+    dstage = {n: round(1e3 * v / 20, 2) for n, v in dtot.items()}
+    up_bw = b1["expert_up"] / (dstage["expert_up"] * 1e-6) / 1e9 if dstage.get("expert_up") else 0
+    dn_bw = (b1["expert_down"] / (dstage["expert_down"] * 1e-6) / 1e9
+             if dstage.get("expert_down") else 0)
+    return {"tokens_per_s": steps / (dms / 1e3), "us_per_token": 1e3 * dms / steps,
+            "algorithmic_bytes_per_token": dec_bytes,
+            "hbm_frac": dec_bytes / (dms / steps / 1e3) / 1e9 / peak,
+            "stage_us": dstage,
+            "expert_up_hbm_frac": up_bw / peak, "expert_down_hbm_frac": dn_bw / peak}
+
+
+def prefill_block(sl, T, steps, warmup, rank, seed=21):
+    """Prefill of T tokens on one GPU through dm_moe_forward: value, stage roofline."""
+    import torch
+    from diskmule_b200.synthetic import input_spec
+    cfg = sl.cfg
+    H = cfg["hidden"]
+    xdt = torch.bfloat16 if cfg["family"] == "glm52" else torch.float32
+    x = torch.empty((T, H), dtype=xdt, device="cuda")
+    y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    input_spec(cfg, T, seed + rank).device_fill(x.data_ptr())
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+
+    def step():
+        sl.layer.forward(x.data_ptr(), y.data_ptr(), T, stream=sptr)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    avg = profile_stages(sl.layer, step, min(steps, 20))
+    r = block_roofline(sl, T, avg, f"{sl.name}-T{T}", sustained=False)
+    return {"tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "tokens": T, "roofline": r}
+
+
+# ---------------------------------------------------------------------------
+# GGUF blocks (configurations 1-3): one replica per rank
+# ---------------------------------------------------------------------------
+
+def run_gguf(args):
     import torch
     import torch.distributed as dist
 
@@ -284,29 +513,31 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    from diskmule_b200 import _native as N
     from diskmule_b200.moe import CudaContext
-    from diskmule_b200.synthetic import build_layer, input_spec
+    from diskmule_b200.synthetic import build_layer, input_spec, zipf_bias
 
     ctx = CudaContext(local)
-    sl = build_layer(ctx, args.config, seed=1)
+    bias = zipf_bias(128, 1.1, 5) if args.config == "gemma4" else None
+    sl = build_layer(ctx, args.config, seed=1, logit_bias=bias)
     cfg = sl.cfg
     T, H, k = args.tokens, cfg["hidden"], cfg["top_k"]
-    xdt = torch.bfloat16 if cfg["family"] == "glm52" else torch.float32
+    xdt = torch.float32
     x = torch.empty((T, H), dtype=xdt, device="cuda")
     y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    sel_i = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    sel_w = torch.empty((T, k), dtype=torch.float32, device="cuda")
     xs = input_spec(cfg, T, 21 + rank)
     xs.device_fill(x.data_ptr())
     ctx.synchronize()
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
 
-    def step(tokens, xp, yp):
-        sl.layer.forward(xp, yp, tokens, stream=sptr)
+    def step():
+        sl.layer.forward(x.data_ptr(), y.data_ptr(), T, sel_i.data_ptr(), sel_w.data_ptr(),
+                         stream=sptr)
 
-    # ---- prefill: the headline value ----
     for _ in range(args.warmup):
-        step(T, x.data_ptr(), y.data_ptr())
+        step()
     torch.cuda.synchronize()
     launches = sl.layer.last_launch_count()
     barrier()
@@ -317,130 +548,67 @@ def run_ours(args):
         torch.cuda.synchronize()
         start.record(stream)
         for _ in range(args.steps):
-            step(T, x.data_ptr(), y.data_ptr())
+            step()
         end.record(stream)
         torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(start.elapsed_time(end))
     value = world * T * args.steps / (ms / 1e3)
-
-    # ---- per-stage times (same workload, profiled pass) for the roofline ----
-    counts, _, _, _ = sl.layer.last_dispatch(T)
-    sl.layer.set_profiling(True)
-    totals = {}
-    n_prof = min(args.steps, 50)
-    for _ in range(n_prof):
-        step(T, x.data_ptr(), y.data_ptr())
-        for name, t in sl.layer.stage_times().items():
-            totals[name] = totals.get(name, 0.0) + t
-    sl.layer.set_profiling(False)
-    avg = {n: v / n_prof for n, v in totals.items()}
-    nbytes = stage_bytes(sl, T, counts)
+    avg = profile_stages(sl.layer, step, min(args.steps, 50))
+    roofline = block_roofline(sl, T, avg, f"{args.config}-T{T}", sustained=False)
     weight_gb = sum(sl.specs[n].expert_bytes for n in ("gate", "up", "down") if n in sl.specs) * \
         (cfg["experts"] + (1 if cfg.get("shared") else 0)) / 1e9
-    dominant = max(("expert_up", "expert_down"), key=lambda n: avg[n])
-    peak, peak_src = measured_peaks()
-    tpeak, tpeak_src = measured_tensor_peak()
-    nflops = stage_flops(sl, T)
-    workload = f"{args.config}-T{T}"
-    traffic = ncu_traffic(dominant, workload)
-    roofline = choose_roofline(dominant, nflops[dominant], nbytes[dominant], avg[dominant],
-                               (peak, peak_src), (tpeak, tpeak_src), traffic)
-    roofline["stage_ms"] = {n: round(v, 4) for n, v in avg.items()}
-
-    # ---- decode (T=1) ----
-    # Distinct tokens, and L2 flushed (a 256 MB write) before every timed token, so each
-    # token's router and expert weights come from HBM; tokens are timed one by one with
-    # events on the launching stream and the flushes stay outside the timed spans.
-    n_dec = 12  # forward() keeps up to 16 CUDA graphs keyed by buffers
-    x1 = torch.empty((n_dec, H), dtype=xdt, device="cuda")
-    input_spec(cfg, n_dec, 33 + rank).device_fill(x1.data_ptr())
-    y1 = torch.empty((n_dec, H), dtype=torch.float32, device="cuda")
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-    xrow = x1.element_size() * H
-    ctx.synchronize()
-
-    def dec(i):
-        j = i % n_dec
-        step(1, x1.data_ptr() + j * xrow, y1.data_ptr() + j * H * 4)
-
-    for i in range(args.warmup):
-        dec(i)
     barrier()
-    torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.decode_steps)]
-    for i in range(args.decode_steps):
-        flush.fill_(i & 0xFF)
-        ev[i][0].record(stream)
-        dec(i)
-        ev[i][1].record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    dms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev))
-    decode_tps = world * args.decode_steps / (dms / 1e3)
-    dec(0)
-    c1, _, _, _ = sl.layer.last_dispatch(1)
-    b1 = stage_bytes(sl, 1, c1)
-    dec_bytes = b1["expert_up"] + b1["expert_down"] + b1["router"]
-    sl.layer.set_profiling(True)
-    dtot = {}
-    for i in range(20):
-        flush.fill_(i & 0xFF)
-        dec(i)
-        for name, t in sl.layer.stage_times().items():
-            dtot[name] = dtot.get(name, 0.0) + t
-    sl.layer.set_profiling(False)
-    del flush
-    dstage = {n: round(1e3 * v / 20, 2) for n, v in dtot.items()}
-    up_bw = b1["expert_up"] / (dstage["expert_up"] * 1e-6) / 1e9 if dstage.get("expert_up") else 0
-    dn_bw = b1["expert_down"] / (dstage["expert_down"] * 1e-6) / 1e9 if dstage.get("expert_down") else 0
-    decode = {"tokens_per_s": decode_tps, "us_per_token": 1e3 * dms / args.decode_steps,
-              "algorithmic_bytes_per_token": dec_bytes,
-              "hbm_frac": dec_bytes / (dms / args.decode_steps / 1e3) / 1e9 / peak,
-              "stage_us": dstage,
-              "expert_up_hbm_frac": up_bw / peak, "expert_down_hbm_frac": dn_bw / peak}
+    decode = decode_block(sl, args.decode_steps, args.warmup, rank)
 
-    # ---- end to end through the public host API (pinned host buffers) ----
+    # e2e through the public host API: pipelined batches (page-locked host buffers)
     xh = torch.empty((T, H), dtype=xdt, pin_memory=True)
     xh.copy_(x.cpu())
-    xnp = xh.view(torch.int16).numpy() if xdt == torch.bfloat16 else xh.numpy()
-    # page-locked outputs, as a host that keeps its buffers would pass
-    out = (torch.empty((T, H), dtype=torch.float32, pin_memory=True).numpy(),
-           torch.empty((T, k), dtype=torch.int32, pin_memory=True).numpy().view(np.uint32),
-           torch.empty((T, k), dtype=torch.float32, pin_memory=True).numpy())
-    for _ in range(2):
-        sl.layer.forward_host(xnp, out=out)
+    nb = 8
+    xs_h = [xh.numpy()] * nb
+    ys_h = [torch.empty((T, H), dtype=torch.float32, pin_memory=True).numpy() for _ in range(2)]
+    ys_h = [ys_h[i & 1] for i in range(nb)]
+    sl.layer.forward_host_batches(xs_h[:2], ys_h[:2])
     barrier()
+    reps = max(1, args.steps // nb)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        sl.layer.forward_host(xnp, out=out)
+    for _ in range(reps):
+        sl.layer.forward_host_batches(xs_h, ys_h)
     el = max_over_ranks(time.perf_counter() - t0)
-    e2e = {"value": world * T * args.steps / el, "unit": "tokens/s",
-           "h2d_bytes_per_step": int(T * H * (2 if xdt == torch.bfloat16 else 4)),
-           "d2h_bytes_per_step": int(T * H * 4 + T * k * 8)}
+    e2e = {"value": world * T * nb * reps / el, "unit": "tokens/s",
+           "h2d_bytes_per_step": int(T * H * 4), "d2h_bytes_per_step": int(T * H * 4),
+           "api": f"dm_moe_forward_host_batches, {nb} batches per call"}
 
-    line = None
     if rank == 0:
         cpu = None
+        parity = None
         if world == 1:
             threads = os.cpu_count() or 1
-            tps, n, secs = cpu_tokens_per_second(args.config, args.cpu_seconds, threads)
-            cpu = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
-                   "sample": f"{n}-token batches of the {args.config} block for {secs:.1f} s"}
+            n = max(args.sample, 16)
+            x32 = x32_rows(cfg, xs.host()[: n * H * 4]).reshape(n, H)
+            el_c, y_ref, i_ref, w_ref = gguf_sample(args.config, x32, threads, logit_bias=bias)
+            step()
+            torch.cuda.synchronize()
+            # the first n tokens of the benchmarked T-token forward
+            parity = parity_summary(cfg, y[:n].cpu().numpy(),
+                                    sel_i[:n].cpu().numpy().view(np.uint32),
+                                    sel_w[:n].cpu().numpy(), y_ref, i_ref, w_ref)
+            cpu = {"value": n / el_c, "unit": "tokens/s", "cores": threads, "kind": "port",
+                   "sample": f"{n} tokens of the {args.config} block in one oracle call"}
         line = {
-            "metric": f"MoE-layer tokens/s ({args.config} prefill T={T})",
+            "metric": metric_name(args.config, T),
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{args.config} MoE block, prefill T={T} per GPU",
+            "config": {"workload": f"{args.config} MoE block, prefill T={T} per GPU"
+                                   + (", Zipf(1.1)-biased routing" if bias is not None else ""),
                        "tokens_per_step": T, "hidden": H, "experts": cfg["experts"],
                        "top_k": k, "intermediate": cfg["intermediate"],
                        "formats": f"{FORMAT_NAMES.get(cfg['gate_type'], cfg['gate_type'])} gate/up, "
                                   f"{FORMAT_NAMES.get(cfg['down_type'], cfg['down_type'])} down",
                        "parallelism": f"replicas x{world}",
                        "l2": f"expert weights ({weight_gb:.2f} GB) larger than L2; no flush needed"},
-            "roofline": roofline, "decode": decode, "e2e": e2e,
+            "roofline": roofline, "decode": decode, "e2e": e2e, "parity": parity,
             "gpu_launches": launches * args.steps,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
@@ -454,36 +622,10 @@ def run_ours(args):
 
 
 # ---------------------------------------------------------------------------
-# expert parallelism (config 4)
+# configuration 4 (the headline): GLM-5.2 bf16 layer, T = 8192, expert parallel
 # ---------------------------------------------------------------------------
 
-def cpu_glm_sample_tokens_per_second(cfg_name: str, sample: int, threads: int, seed: int = 1):
-    """The oracle GLM block on `sample` tokens, with host weights for the experts those
-    tokens select only (the full pool is tens of GB)."""
-    from diskmule_b200 import _native as N
-    from diskmule_b200.synthetic import CONFIGS, SyntheticLayer, input_spec, layer_specs, vectors
-    from oracle import oracle as O
-    cfg = dict(CONFIGS[cfg_name])
-    specs = layer_specs(cfg, seed)
-    sl = SyntheticLayer(cfg_name, cfg, seed, None, specs, vectors(cfg, seed))
-    raw = input_spec(cfg, sample, 21).host()
-    x = (raw.view(np.uint16).reshape(sample, -1).astype(np.uint32) << 16).view(np.float32)
-    router = specs["router"].host()
-    bias = specs["bias"].host().view(np.float32)
-    chosen = set()
-    for t in range(sample):
-        _, lg = O.glm_matvec(N.BF16, cfg["experts"], cfg["hidden"], router, x[t], threads)
-        _, idx, _ = O.glm_select(lg, bias, cfg["top_k"], cfg["n_groups"], cfg["topk_groups"],
-                                 cfg["normalize"])
-        chosen.update(int(i) for i in idx)
-    w = sl.host_weights(sorted(chosen))
-    t0 = time.perf_counter()
-    rc, _, _, _ = O.glm_moe(w, x, threads=threads)
-    assert rc == O.OK
-    return sample / (time.perf_counter() - t0)
-
-
-def run_ep(args):
+def run_glm(args):
     import datetime
     import torch
     import torch.distributed as dist
@@ -492,14 +634,17 @@ def run_ep(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    if "MASTER_ADDR" not in os.environ:  # a single process: a one-rank group
-        os.environ["MASTER_ADDR"] = "127.0.0.1"
-        os.environ.setdefault("MASTER_PORT", "29533")
-    dist.init_process_group("nccl", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=120),
-                            device_id=torch.device("cuda", local))
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
 
     def max_over_ranks(v):
+        if world == 1:
+            return v
         t = torch.tensor([v], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
@@ -510,102 +655,173 @@ def run_ep(args):
 
     cfg = dict(CONFIGS[args.config])
     E, H, I, k = cfg["experts"], cfg["hidden"], cfg["intermediate"], cfg["top_k"]
+    if E % world or args.tokens % world:
+        raise SystemExit(f"{E} experts / {args.tokens} tokens do not split over {world} GPUs")
     per = E // world
     T_total = args.tokens
     T = T_total // world
     ctx = CudaContext(local)
-    sl = build_layer(ctx, args.config, seed=1, expert_range=(rank * per, per))
-    xdt = torch.bfloat16 if cfg["family"] == "glm52" else torch.float32
-    x = torch.empty((T, H), dtype=xdt, device="cuda")
-    input_spec(cfg, T, 21 + rank).device_fill(x.data_ptr())
+    # one GPU holds every expert; with several, rank g holds [g*per, (g+1)*per)
+    sl = build_layer(ctx, args.config, seed=1,
+                     expert_range=None if world == 1 else (rank * per, per))
+    x = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+    xs = input_spec(cfg, T, 21 + rank)
+    xs.device_fill(x.data_ptr())
     ctx.synchronize()
-    backend = cuda_backend_for(sl)
-    ep = ExpertParallel(backend, E, k)
     stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    if world == 1:
+        y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        sel_i = torch.empty((T, k), dtype=torch.int32, device="cuda")
+        sel_w = torch.empty((T, k), dtype=torch.float32, device="cuda")
+
+        def step():
+            sl.layer.forward(x.data_ptr(), y.data_ptr(), T, sel_i.data_ptr(), sel_w.data_ptr(),
+                             stream=sptr)
+            return y
+    else:
+        ep = ExpertParallel(cuda_backend_for(sl), E, k)
+
+        def step():
+            return ep.forward(x)
 
     for _ in range(args.warmup):
-        y = ep.forward(x)
+        step()
     torch.cuda.synchronize()
-    dist.barrier()
+    barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local, active=rank == 0) as clk:
-        dist.barrier()  # rank 0 entered after the sampler settled
+        barrier()  # rank 0 entered after the sampler settled
         torch.cuda.synchronize()
         start.record(stream)
         for _ in range(args.steps):
-            y = ep.forward(x)
+            yy = step()
         end.record(stream)
         torch.cuda.synchronize()
-    dist.barrier()
+    barrier()
     ms = max_over_ranks(start.elapsed_time(end))
     value = T_total * args.steps / (ms / 1e3)
-    # launches of one step (route + received rows + shared rows + combine)
-    launches = 0
-    T_probe = T
-    ep.forward(x)
-    launches = sl.layer.last_launch_count()  # combine; the others are counted below
-    routed = backend.route(x)
-    launches += sl.layer.last_launch_count()
-    ids = torch.zeros((T_probe,), dtype=torch.int32, device="cuda")
-    backend.expert_rows(x if cfg["family"] != "gemma4" else routed.expert_in, ids)
-    launches += 2 * sl.layer.last_launch_count()
 
-    # e2e: host input copied in and output copied back every step
-    xh = torch.empty((T, H), dtype=xdt, pin_memory=True)
+    # kernels of one step, and the dominant kernel's event-timed duration
+    if world == 1:
+        launches = sl.layer.last_launch_count()
+        avg = profile_stages(sl.layer, step, min(args.steps, 20))
+        roofline = block_roofline(sl, T, avg, f"{args.config}-T{T}", sustained=True)
+    else:
+        launches, stage = ep.profile_step(x)
+        avg = {n: v for n, v in stage.items()}
+        roofline = ep_roofline(sl, stage, ep)
+    barrier()
+
+    # e2e: every step's input comes from page-locked host memory and its output returns
+    xh = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
     xh.copy_(x.cpu())
-    yh = torch.empty((T, H), dtype=torch.float32, pin_memory=True)
-    torch.cuda.synchronize()
-    dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        xd = xh.to("cuda", non_blocking=True)
-        yh.copy_(ep.forward(xd), non_blocking=True)
+    nb = 4
+    if world == 1:
+        xs_h = [xh.view(torch.int16).numpy()] * nb
+        yb = [torch.empty((T, H), dtype=torch.float32, pin_memory=True).numpy() for _ in range(2)]
+        ys_h = [yb[i & 1] for i in range(nb)]
+        sl.layer.forward_host_batches(xs_h[:2], ys_h[:2])
+        reps = max(1, args.steps // nb)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            sl.layer.forward_host_batches(xs_h, ys_h)
+        el = time.perf_counter() - t0
+        e2e_steps = reps * nb
+        api = f"dm_moe_forward_host_batches, {nb} batches per call"
+    else:
+        yh = [torch.empty((T, H), dtype=torch.float32, pin_memory=True) for _ in range(2)]
+        e2e_steps = max(4, min(args.steps, 40))
+        ep.forward_host_stream(xh, yh, 2)
+        barrier()
         torch.cuda.synchronize()
-    el = max_over_ranks(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        ep.forward_host_stream(xh, yh, e2e_steps)
+        el = time.perf_counter() - t0
+        api = "ExpertParallel.forward_host_stream (copies on side streams)"
+    el = max_over_ranks(el)
+    e2e = {"value": T_total * e2e_steps / el, "unit": "tokens/s",
+           "h2d_bytes_per_step": int(T_total * H * 2), "d2h_bytes_per_step": int(T_total * H * 4),
+           "api": api}
 
-    # tensor roofline: useful FLOPs per GPU per step / time
-    shared = 1 if cfg.get("shared") else 0
-    flops = T * (k + shared) * 3 * 2 * H * I
-    peaks = {}
-    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(path):
-        with open(path) as f:
-            peaks = json.load(f)
-    peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops") or 1590.0
-    achieved = flops / (ms / args.steps / 1e3) / 1e12
+    # parity of a seeded sample of rank 0's tokens against the oracle (after timing)
+    parity = cpu = None
+    n = args.sample
     if rank == 0:
-        cpu = None
-        if world == 1 and cfg["family"] == "glm52":
-            threads = os.cpu_count() or 1
-            sample = 8
-            cpu = {"value": cpu_glm_sample_tokens_per_second(args.config, sample, threads),
-                   "unit": "tokens/s", "cores": threads, "kind": "port",
-                   "sample": f"{sample} tokens of the {args.config} block (host weights of the "
-                             "experts they select)"}
+        yy = step()
+        torch.cuda.synchronize()
+        if world == 1:
+            idx_d, w_d = sel_i[:n].cpu().numpy().view(np.uint32), sel_w[:n].cpu().numpy()
+        else:
+            idx_d, w_d = ep.last_selection(n)
+        y_d = yy[:n].float().cpu().numpy()
+        threads = os.cpu_count() or 1
+        x32 = x32_rows(cfg, xs.host()[: n * H * 2]).reshape(n, H)
+        el_c, y_ref, i_ref, w_ref = glm_sample(args.config, x32, threads)
+        parity = parity_summary(cfg, y_d, idx_d, w_d, y_ref, i_ref, w_ref)
+        if world == 1:
+            cpu = {"value": n / el_c, "unit": "tokens/s", "cores": threads, "kind": "port",
+                   "sample": f"{n} tokens of the {args.config} block in one oracle call (host "
+                             "weights of the experts they select)"}
+    barrier()
+
+    extras = None
+    if world == 1 and not args.no_extras:
+        extras = {"glm52_decode_T1": decode_block(sl, args.decode_steps, args.warmup, rank)}
+    sl.close()
+    if world == 1 and not args.no_extras:
+        from diskmule_b200.synthetic import zipf_bias
+        for name, T_x, bias in (("qwen35", 512, None), ("gemma4", 4096, zipf_bias(128, 1.1, 5))):
+            s2 = build_layer(ctx, name, seed=1, logit_bias=bias)
+            pre = prefill_block(s2, T_x, max(20, args.steps), args.warmup, rank)
+            dec = decode_block(s2, args.decode_steps, args.warmup, rank)
+            key = f"{name}_prefill_T{T_x}" + ("_zipf" if bias is not None else "")
+            extras[key] = pre
+            extras[f"{name}_decode_T1"] = dec
+            s2.close()
+
+    if rank == 0:
         line = {
-            "metric": f"MoE-layer tokens/s ({args.config} prefill T={T_total}, expert parallel)",
+            "metric": metric_name(args.config, T_total),
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"{args.config} MoE block, prefill T={T_total} split over "
-                                   f"{world} GPU(s), experts sharded {per} per GPU",
-                       "parallelism": f"ep{world}", "tokens_per_gpu": T,
-                       "l2": "weights larger than L2; no flush needed"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
-                         "kernel": "whole EP step", "algorithmic_flops_per_gpu": flops},
-            "e2e": {"value": T_total * args.steps / el, "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(T * H * (2 if xdt == torch.bfloat16 else 4)),
-                    "d2h_bytes_per_step": int(T * H * 4)},
+            "config": {"workload": f"{args.config} MoE layer (configuration 4), prefill "
+                                   f"T={T_total} in total"
+                                   + (f", split over {world} GPUs, experts sharded {per} per GPU"
+                                      if world > 1 else " on one GPU holding every expert"),
+                       "parallelism": f"ep{world}", "tokens_per_gpu": T, "hidden": H,
+                       "experts": E, "top_k": k, "intermediate": I,
+                       "formats": "BF16 router, gate/up, down, shared expert; f32 accumulate",
+                       "l2": "expert weights (19.3 GB) larger than L2; no flush needed"},
+            "roofline": roofline, "e2e": e2e, "parity": parity,
             "gpu_launches": launches * args.steps,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "extras": extras,
         }
         emit(line)
-    sl.close()
     ctx.close()
-    dist.barrier()
-    dist.destroy_process_group()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def ep_roofline(sl, stage, ep):
+    """Roofline of the local expert GEMMs inside an expert-parallel step: useful FLOPs of
+    the rows this rank's experts ran ÷ their event-timed duration, against the sustained
+    bf16 peak (the GEMMs run inside a long step)."""
+    cfg = sl.cfg
+    H, I = cfg["hidden"], cfg["intermediate"]
+    rows = ep.last_rows
+    flops = 2.0 * rows * 3 * H * I
+    ms = stage["experts"]
+    tpeak, src = measured_tensor_peak(True)
+    achieved = flops / (ms / 1e3) / 1e12
+    return {"bound": "tensor", "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
+            "frac": achieved / tpeak, "traffic": None, "kernel": "tc_bf16_kernel (local experts)",
+            "algorithmic_flops": flops, "peak_source": src, "kernel_ms": round(ms, 4),
+            "stage_ms": {n: round(v, 4) for n, v in stage.items()}}
 
 
 # ---------------------------------------------------------------------------
@@ -664,7 +880,8 @@ def pinned_h2d_gbs(ctx, pool_ptr: int, nbytes: int, reps: int = 3) -> float:
 def run_stack(args):
     import torch
     from diskmule_b200.moe import CudaContext
-    from diskmule_b200.stack import GlmStack, OracleStack
+    from diskmule_b200.stack import GlmStack
+    from oracle.stack import OracleStack
     from diskmule_b200.synthetic import CONFIGS
 
     cfg = CONFIGS["glm52"]
@@ -769,6 +986,34 @@ def emit(line: dict) -> None:
     print(json.dumps(line), file=_RESULT_OUT or sys.stdout, flush=True)
 
 
+def run_profile_pass(args):
+    """R forwards of one block (one GPU, graphs off) for ncu's launch lists and captures;
+    the same kernels as the timed steps. Prints one JSON line."""
+    os.environ["DISKMULE_CUDA_GRAPHS"] = "0"
+    import torch
+    from diskmule_b200.moe import CudaContext
+    from diskmule_b200.synthetic import build_layer, input_spec, zipf_bias
+
+    torch.cuda.set_device(0)
+    ctx = CudaContext(0)
+    bias = zipf_bias(128, 1.1, 5) if args.config == "gemma4" else None
+    sl = build_layer(ctx, args.config, seed=1, logit_bias=bias)
+    cfg, T = sl.cfg, args.tokens
+    xdt = torch.bfloat16 if cfg["family"] == "glm52" else torch.float32
+    x = torch.empty((T, cfg["hidden"]), dtype=xdt, device="cuda")
+    y = torch.empty((T, cfg["hidden"]), dtype=torch.float32, device="cuda")
+    input_spec(cfg, T, 21).device_fill(x.data_ptr())
+    ctx.synchronize()
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(args.profile_pass):
+        sl.layer.forward(x.data_ptr(), y.data_ptr(), T, stream=stream)
+    torch.cuda.synchronize()
+    emit({"profile_pass": args.profile_pass, "config": args.config, "tokens": T,
+          "launches_per_forward": sl.layer.last_launch_count()})
+    sl.close()
+    ctx.close()
+
+
 def main():
     global _RESULT_OUT
     # Libraries write banners to standard output from C (NCCL prints its version when a
@@ -780,12 +1025,14 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
-    elif args.ep:
-        run_ep(args)
+    elif args.profile_pass:
+        run_profile_pass(args)
     elif args.stack:
         run_stack(args)
+    elif args.config == "glm52":
+        run_glm(args)
     else:
-        run_ours(args)
+        run_gguf(args)
 
 
 if __name__ == "__main__":

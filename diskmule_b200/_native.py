@@ -115,9 +115,11 @@ SIGNATURES = {
     "dm_moe_layer_destroy": ([P], None),
     "dm_moe_forward": ([P, P, P, I32, P, P, P], I32),
     "dm_moe_forward_host": ([P, P, P, I32, P, P], I32),
+    "dm_moe_forward_host_batches": ([P, I32, C.POINTER(P), C.POINTER(P), I32], I32),
     "dm_moe_last_dispatch": ([P, P, P, P, P], I32),
     "dm_moe_last_launch_count": ([P], I32),
     "dm_moe_forward_noalloc": ([P, P, P, I32, P, P, P], I32),
+    "dm_moe_forward_noalloc_status": ([P, P], I32),
     "dm_moe_set_profiling": ([P, I32], I32),
     "dm_moe_stage_times": ([P, P, I32], I32),
     "dm_moe_stage_name": ([I32], C.c_char_p),

@@ -635,7 +635,6 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   a.inverse = arena.take<int32_t>(pairs);
   a.active = arena.take<int32_t>(E + 1);
   a.n_active = arena.take<int32_t>(1);
-  a.status = arena.take<int32_t>(1);
   a.items = arena.take<int4>(pairs + E + 1);
   a.n_items = arena.take<int32_t>(1);
   a.h = arena.take<float>(pairs * I);
@@ -777,6 +776,14 @@ void dm_moe_layer_destroy(dm_moe_layer *L) {
   if (L->router_rows) cudaFree(L->router_rows);
   if (L->scratch) cudaFree(L->scratch);
   if (L->io) cudaFree(L->io);
+  if (L->pipe_in) cudaStreamSynchronize(L->pipe_in);
+  if (L->pipe_out) cudaStreamSynchronize(L->pipe_out);
+  if (L->pipe) cudaFree(L->pipe);
+  for (auto &e : L->pipe_ev)
+    if (e) cudaEventDestroy(e);
+  if (L->pipe_in) cudaStreamDestroy(L->pipe_in);
+  if (L->pipe_out) cudaStreamDestroy(L->pipe_out);
+  if (L->pipe_status) cudaFreeHost(L->pipe_status);
   for (auto &e : L->events)
     if (e) cudaEventDestroy(e);
   for (void *p : L->owned) cudaFree(p);
@@ -1018,6 +1025,7 @@ int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
     DM_CUDA(cudaGetLastError(), "MoE forward launch");
   }
   L->last_tokens = tokens;
+  L->last_noalloc = 0;
   L->last_launches = launches;
   return DM_OK;
 }
@@ -1065,6 +1073,83 @@ int32_t dm_moe_forward_host(dm_moe_layer *L, const void *x, float *y, int32_t to
   return DM_OK;
 }
 
+int32_t dm_moe_forward_host_batches(dm_moe_layer *L, int32_t batches, const void *const *x,
+                                    float *const *y, int32_t tokens) {
+  if (!L || !x || !y) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
+  if (batches < 0 || tokens < 0) return fail(DM_ERR_INVALID_ARGUMENT, "negative count");
+  if (batches == 0 || tokens == 0) return DM_OK;
+  for (int b = 0; b < batches; b++)
+    if (!x[b] || !y[b]) return fail(DM_ERR_INVALID_ARGUMENT, "null batch pointer %d", b);
+  DM_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  const dm_moe_desc &d = L->desc;
+  auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const size_t xb = (size_t)tokens * d.hidden * (d.input_type == DM_BF16 ? 2 : 4);
+  const size_t yb = (size_t)tokens * d.hidden * 4;
+  const size_t slot = al(xb) + al(yb);
+  if (2 * slot > L->pipe_bytes) {
+    if (L->pipe) cudaFree(L->pipe);
+    L->pipe = nullptr;
+    L->pipe_bytes = 0;
+    if (cudaMalloc(&L->pipe, 2 * slot) != cudaSuccess)
+      return fail(DM_ERR_ALLOCATION, "could not allocate %zu bytes of staging", 2 * slot);
+    L->pipe_bytes = 2 * slot;
+  }
+  if (!L->pipe_in) {
+    DM_CUDA(cudaStreamCreateWithFlags(&L->pipe_in, cudaStreamNonBlocking), "copy-in stream");
+    DM_CUDA(cudaStreamCreateWithFlags(&L->pipe_out, cudaStreamNonBlocking), "copy-out stream");
+    for (auto &e : L->pipe_ev)
+      DM_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "pipeline event");
+  }
+  if (batches > L->pipe_status_n) {
+    if (L->pipe_status) cudaFreeHost(L->pipe_status);
+    L->pipe_status = nullptr;
+    L->pipe_status_n = 0;
+    DM_CUDA(cudaHostAlloc((void **)&L->pipe_status, (size_t)batches * 4, cudaHostAllocDefault),
+            "status words");
+    L->pipe_status_n = batches;
+  }
+  cudaStream_t cs = L->ctx->stream;
+  cudaEvent_t *ev_in = L->pipe_ev, *ev_fwd = L->pipe_ev + 2, *ev_out = L->pipe_ev + 4;
+  for (int b = 0; b < batches; b++) {
+    const int s = b & 1;
+    uint8_t *xd = (uint8_t *)L->pipe + s * slot;
+    float *yd = (float *)(xd + al(xb));
+    // slot s was last used by batch b-2: its forward must have read the input before
+    // the copy-in overwrites it, and its copy-out must be done before the forward
+    // overwrites the output
+    if (b >= 2) DM_CUDA(cudaStreamWaitEvent(L->pipe_in, ev_fwd[s], 0), "wait");
+    DM_CUDA(cudaMemcpyAsync(xd, x[b], xb, cudaMemcpyHostToDevice, L->pipe_in), "input copy");
+    DM_CUDA(cudaEventRecord(ev_in[s], L->pipe_in), "record");
+    DM_CUDA(cudaStreamWaitEvent(cs, ev_in[s], 0), "wait");
+    if (b >= 2) DM_CUDA(cudaStreamWaitEvent(cs, ev_out[s], 0), "wait");
+    int32_t rc = dm_moe_forward(L, xd, yd, tokens, nullptr, nullptr, cs);
+    if (rc != DM_OK) {
+      cudaStreamSynchronize(cs);
+      cudaStreamSynchronize(L->pipe_in);
+      cudaStreamSynchronize(L->pipe_out);
+      return rc;
+    }
+    DM_CUDA(cudaMemcpyAsync(&L->pipe_status[b], L->args.status, 4, cudaMemcpyDeviceToHost, cs),
+            "status copy");
+    DM_CUDA(cudaEventRecord(ev_fwd[s], cs), "record");
+    DM_CUDA(cudaStreamWaitEvent(L->pipe_out, ev_fwd[s], 0), "wait");
+    DM_CUDA(cudaMemcpyAsync(y[b], yd, yb, cudaMemcpyDeviceToHost, L->pipe_out), "output copy");
+    DM_CUDA(cudaEventRecord(ev_out[s], L->pipe_out), "record");
+  }
+  DM_CUDA(cudaStreamSynchronize(L->pipe_out), "output copies");
+  DM_CUDA(cudaStreamSynchronize(cs), "MoE forward");
+  for (int b = 0; b < batches; b++) {
+    const int32_t status = L->pipe_status[b];
+    if (status == dm::kStatusNonFiniteRouter)
+      return fail(DM_ERR_NON_FINITE, "batch %d: router produced a non-finite score", b);
+    if (status == dm::kStatusTimeout)
+      return fail(DM_ERR_TIMEOUT, "batch %d: a bounded wait in the tensor-core GEMM ran out", b);
+    if (status == dm::kStatusNonFiniteNorm)
+      return fail(DM_ERR_NON_FINITE, "batch %d: RMSNorm received a non-finite value", b);
+  }
+  return DM_OK;
+}
+
 // ---------------------------------------------------------------------------
 // expert parallelism: route, experts on received rows, combine of returned rows
 // ---------------------------------------------------------------------------
@@ -1075,6 +1160,7 @@ int32_t finish_launch(dm_moe_layer *L, int launches, int tokens) {
   if (launches < 0) return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "no expert kernel for this format");
   DM_CUDA(cudaGetLastError(), "MoE launch");
   L->last_tokens = tokens;
+  L->last_noalloc = 0;
   L->last_launches = launches;
   return DM_OK;
 }
@@ -1169,6 +1255,9 @@ int32_t dm_moe_local_experts(const dm_moe_layer *L, int32_t *first_expert, int32
 int32_t dm_moe_last_dispatch(dm_moe_layer *L, int32_t *counts, int32_t *offsets,
                              int32_t *sorted_pairs, int32_t *inverse) {
   if (!L) return fail(DM_ERR_INVALID_ARGUMENT, "null layer");
+  if (L->last_noalloc)
+    return fail(DM_ERR_INVALID_ARGUMENT,
+                "the last call was dm_moe_forward_noalloc, whose dispatch lists are not kept");
   if (L->last_tokens == 0) return DM_OK;
   cudaSetDevice(L->ctx->device);
   const int E = L->desc.experts;
@@ -1232,18 +1321,28 @@ extern "C" int32_t dm_moe_forward_noalloc(dm_moe_layer *L, const void *x, float 
   if (!L || !x || !y) return fail(DM_ERR_INVALID_ARGUMENT, "null argument");
   if (tokens < 0) return fail(DM_ERR_INVALID_ARGUMENT, "negative token count");
   if (tokens == 0) return DM_OK;
+  // The same refusals as dm_moe_forward: a layer holding only some experts (an
+  // expert-parallel shard, or a cache layer's slots) would index weights it lacks.
+  if (L->local_experts != L->desc.experts)
+    return fail(DM_ERR_INVALID_ARGUMENT,
+                "this layer holds experts %d..%d only: use dm_moe_route / dm_moe_expert_rows",
+                L->first_expert, L->first_expert + L->local_experts - 1);
+  if ((int64_t)tokens * L->desc.top_k > INT32_MAX / 2 || tokens > (1 << 22))
+    return fail(DM_ERR_OVERFLOW, "too many tokens in one call (limit 4194304)");
   if (((uintptr_t)y & 15) || ((uintptr_t)x & 15))
     return fail(DM_ERR_INVALID_ARGUMENT, "x and y must be 16-byte aligned device pointers");
   const dm_moe_desc &d = L->desc;
   // the same scratch layout as the allocating forward, carved from the static array
+  // after the status word, which sits at a fixed offset (0) so that
+  // dm_moe_forward_noalloc_status can find it
   const size_t T = (size_t)tokens, H = d.hidden, I = d.intermediate, E = d.experts,
                k = d.top_k;
   const size_t pairs = T * k + (L->shared ? T : 0);
   auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
-  size_t need = 0;
+  size_t need = al(4);
   if (d.family == DM_FAMILY_GEMMA4) need += 2 * al(T * H * 4);
   need += al(T * L->E1 * 4) + 2 * al(T * k * 4);
-  need += al((E + 1) * 4) + al((E + 2) * 4) + 2 * al(pairs * 4) + al((E + 1) * 4) + 2 * al(4);
+  need += al((E + 1) * 4) + al((E + 2) * 4) + 2 * al(pairs * 4) + al((E + 1) * 4) + al(4);
   need += al((pairs + E + 1) * sizeof(int4)) + al(4);
   need += al(pairs * I * 4) + al(pairs * H * 4);
   if (need > kNoAllocScratchBytes)
@@ -1257,6 +1356,7 @@ extern "C" int32_t dm_moe_forward_noalloc(dm_moe_layer *L, const void *x, float 
   if (rc != DM_OK) return rc;
   dm::Arena arena{base, 0, kNoAllocScratchBytes};
   dm::ForwardArgs a{};
+  a.status = arena.take<int32_t>(1);
   a.router_in = d.family == DM_FAMILY_GEMMA4 ? arena.take<float>(T * H) : nullptr;
   a.expert_in = d.family == DM_FAMILY_GEMMA4 ? arena.take<float>(T * H) : nullptr;
   a.logits = arena.take<float>(T * L->E1);
@@ -1268,7 +1368,6 @@ extern "C" int32_t dm_moe_forward_noalloc(dm_moe_layer *L, const void *x, float 
   a.inverse = arena.take<int32_t>(pairs);
   a.active = arena.take<int32_t>(E + 1);
   a.n_active = arena.take<int32_t>(1);
-  a.status = arena.take<int32_t>(1);
   a.items = arena.take<int4>(pairs + E + 1);
   a.n_items = arena.take<int32_t>(1);
   a.h = arena.take<float>(pairs * I);
@@ -1335,7 +1434,31 @@ extern "C" int32_t dm_moe_forward_noalloc(dm_moe_layer *L, const void *x, float 
   const int launches = dm::launch_forward(a, s, nullptr, gemv_ok ? &plan : nullptr);
   if (launches < 0) return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "no expert kernel for this format");
   DM_CUDA(cudaGetLastError(), "MoE forward (no allocation) launch");
+  // The dispatch lists of this call live in the shared array, not in the layer's
+  // scratch: dm_moe_last_dispatch refuses until the next allocating call.
+  L->last_tokens = tokens;
+  L->last_launches = launches;
+  L->last_noalloc = 1;
   return DM_OK;
+}
+
+extern "C" int32_t dm_moe_forward_noalloc_status(dm_moe_layer *L, void *stream) {
+  if (!L) return fail(DM_ERR_INVALID_ARGUMENT, "null layer");
+  DM_CUDA(cudaSetDevice(L->ctx->device), "cudaSetDevice");
+  uint8_t *base = nullptr;
+  int32_t rc = noalloc_scratch(L->ctx->device, &base);
+  if (rc != DM_OK) return rc;
+  int32_t status = 0;  // a host stack word: the copy allocates nothing
+  cudaStream_t s = (cudaStream_t)stream;
+  DM_CUDA(cudaMemcpyAsync(&status, base, 4, cudaMemcpyDeviceToHost, s), "status copy");
+  DM_CUDA(cudaStreamSynchronize(s), "MoE forward (no allocation)");
+  if (status == dm::kStatusNonFiniteRouter)
+    return fail(DM_ERR_NON_FINITE, "router produced a non-finite score");
+  if (status == dm::kStatusTimeout)
+    return fail(DM_ERR_TIMEOUT, "a bounded wait in an expert kernel ran out");
+  if (status == dm::kStatusNonFiniteNorm)
+    return fail(DM_ERR_NON_FINITE, "RMSNorm received a non-finite value");
+  return status == 0 ? DM_OK : fail(DM_ERR_COMMAND, "unexpected status %d", status);
 }
 
 extern "C" int32_t dm_selftest_device_wait(dm_cuda_context *ctx, int64_t cycles) {

@@ -118,9 +118,18 @@ struct dm_moe_layer {
   dm::ForwardArgs args{};
   int last_tokens = 0;
   int last_launches = 0;
+  int last_noalloc = 0;  // the last call was dm_moe_forward_noalloc
   // host-call staging
   void *io = nullptr;
   size_t io_bytes = 0;
+  // pipelined host calls (dm_moe_forward_host_batches): two staging slots, a copy-in
+  // and a copy-out stream, and a page-locked status word per batch
+  void *pipe = nullptr;
+  size_t pipe_bytes = 0;
+  cudaStream_t pipe_in = nullptr, pipe_out = nullptr;
+  cudaEvent_t pipe_ev[6] = {};
+  int32_t *pipe_status = nullptr;
+  int pipe_status_n = 0;
   // per-stage device timers (GenerationProfile analog)
   bool profiling = false;
   cudaEvent_t events[dm::kStageCount + 1] = {};

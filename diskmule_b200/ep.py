@@ -18,6 +18,7 @@ through the C ABI (dm_moe_route / dm_moe_expert_rows / dm_moe_combine_rows).
 """
 from __future__ import annotations
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -55,10 +56,15 @@ class ExpertParallel:
         if experts % self.world:
             raise ValueError(f"{experts} experts do not split over {self.world} ranks")
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, marks=None) -> torch.Tensor:
+        """One expert-parallel forward of this rank's tokens x [T, H]. `marks`, when
+        given, is called with a stage name at every stage boundary (profiling)."""
         b, k = self.backend, self.top_k
+        mark = marks or (lambda name: None)
         T = x.shape[0]
+        mark("route")
         routed = b.route(x)
+        mark("exchange")
         order, counts, local_ids = exchange_plan(routed.sel_idx, self.experts, self.world)
         counts_dev = counts.to(x.device)
         recv_counts_dev = torch.empty_like(counts_dev)
@@ -69,17 +75,78 @@ class ExpertParallel:
         send_rows = rows.index_select(0, torch.div(order, k, rounding_mode="floor").to(rows.device))
         recv_rows = all_to_all(send_rows, send_counts, recv_counts, self.group)
         recv_ids = all_to_all(local_ids.to(x.device), send_counts, recv_counts, self.group)
+        mark("experts")
         out = b.expert_rows(recv_rows, recv_ids)       # [R, H] f32
-        back = all_to_all(out, recv_counts, send_counts, self.group)
+        self.last_rows = int(recv_rows.shape[0]) + (T if b.has_shared else 0)
         P = T * k
         shared = b.has_shared
-        pair_out = back.new_empty((P + (T if shared else 0), back.shape[1]))
-        pair_out.index_copy_(0, order.to(back.device), back)
+        pair_out = out.new_empty((P + (T if shared else 0), out.shape[1]))
         if shared:
             _, local = b.local_experts()
             ids = torch.full((T,), local, dtype=torch.int32, device=x.device)
             pair_out[P:] = b.expert_rows(rows, ids)
-        return b.combine(routed, pair_out)
+        mark("return")
+        back = all_to_all(out, recv_counts, send_counts, self.group)
+        pair_out[:P].index_copy_(0, order.to(back.device), back)
+        mark("combine")
+        y = b.combine(routed, pair_out)
+        mark("end")
+        self.last_routed = routed
+        return y
+
+    def last_selection(self, n: int):
+        """Selected expert ids and weights of the first n tokens of the last forward."""
+        r = self.last_routed
+        return (r.sel_idx[:n].cpu().numpy().view(np.uint32), r.sel_w[:n].cpu().numpy())
+
+    def profile_step(self, x: torch.Tensor):
+        """One forward with CUDA events at its stage boundaries: (kernel launches of the
+        step counted by the backend, {stage: ms})."""
+        ev = {}
+        names = []
+        stream = torch.cuda.current_stream()
+
+        def mark(name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            ev[name] = e
+            names.append(name)
+
+        self.backend.launches = 0
+        self.forward(x, marks=mark)
+        torch.cuda.synchronize()
+        stage = {a: ev[a].elapsed_time(ev[b]) for a, b in zip(names, names[1:])}
+        return self.backend.launches, stage
+
+    def forward_host_stream(self, x_host: torch.Tensor, y_host, steps: int):
+        """`steps` forwards of the page-locked host rows x_host, each output copied back
+        into y_host[i % len(y_host)]: the input copy of step i+1 runs on a side stream
+        while step i computes, and the output copy of step i on another."""
+        dev = torch.device("cuda", torch.cuda.current_device())
+        cs = torch.cuda.current_stream()
+        s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+        bufs = [torch.empty_like(x_host, device=dev) for _ in range(2)]
+        ready = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
+        with torch.cuda.stream(s_in):
+            bufs[0].copy_(x_host, non_blocking=True)
+            ready[0].record(s_in)
+        for i in range(steps):
+            j = i & 1
+            if i + 1 < steps:
+                with torch.cuda.stream(s_in):
+                    if i >= 1:
+                        s_in.wait_event(done[1 - j])
+                    bufs[1 - j].copy_(x_host, non_blocking=True)
+                    ready[1 - j].record(s_in)
+            cs.wait_event(ready[j])
+            y = self.forward(bufs[j])
+            done[j].record(cs)
+            s_out.wait_stream(cs)
+            with torch.cuda.stream(s_out):
+                y_host[i % len(y_host)].copy_(y, non_blocking=True)
+                y.record_stream(s_out)
+        torch.cuda.synchronize()
 
 
 class Routed:
@@ -100,6 +167,7 @@ class CudaBackend:
         self.top_k = top_k
         self.router_columns = router_columns
         self.has_shared = shared
+        self.launches = 0  # kernels launched through this backend (a count for benchmarks)
 
     def _stream(self) -> int:
         return torch.cuda.current_stream().cuda_stream
@@ -118,6 +186,7 @@ class CudaBackend:
         self.layer.route(x.data_ptr(), T, sel_idx.data_ptr(), sel_w.data_ptr(),
                          expert_in.data_ptr() if expert_in is not None else 0,
                          logits.data_ptr() if logits is not None else 0, self._stream())
+        self.launches += self.layer.last_launch_count()
         return Routed(sel_idx, sel_w, expert_in, logits)
 
     def rows(self, x: torch.Tensor, routed: Routed) -> torch.Tensor:
@@ -128,6 +197,7 @@ class CudaBackend:
         if rows.shape[0]:
             self.layer.expert_rows(rows.contiguous().data_ptr(), ids.contiguous().data_ptr(),
                                    rows.shape[0], out.data_ptr(), self._stream())
+            self.launches += self.layer.last_launch_count()
         return out
 
     def combine(self, routed: Routed, pair_out: torch.Tensor) -> torch.Tensor:
@@ -137,6 +207,7 @@ class CudaBackend:
                                 pair_out.contiguous().data_ptr(), y.data_ptr(),
                                 routed.logits.data_ptr() if routed.logits is not None else 0,
                                 self._stream())
+        self.launches += self.layer.last_launch_count()
         return y
 
 

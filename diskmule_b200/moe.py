@@ -237,6 +237,23 @@ class MoeLayer:
         check(N.lib().dm_moe_forward_host(self._h, _ptr(x), _ptr(y), T, _ptr(idx), _ptr(w)))
         return y, idx, w
 
+    def forward_host_batches(self, xs, ys):
+        """Pipelined forwards of equal-size host batches (dm_moe_forward_host_batches):
+        xs[b] [T, hidden] (input type) -> ys[b] [T, hidden] f32, written in place."""
+        n = len(xs)
+        if n != len(ys):
+            raise ValueError("xs and ys differ in length")
+        if n == 0:
+            return
+        T = xs[0].shape[0]
+        H = self.desc.hidden
+        for a, b in zip(xs, ys):
+            assert a.shape[0] == T and a.flags.c_contiguous
+            assert b.shape == (T, H) and b.dtype == np.float32 and b.flags.c_contiguous
+        xp = (C.c_void_p * n)(*[a.ctypes.data for a in xs])
+        yp = (C.c_void_p * n)(*[b.ctypes.data for b in ys])
+        check(N.lib().dm_moe_forward_host_batches(self._h, n, xp, yp, T))
+
     def last_dispatch(self, tokens: int):
         E, k = self.desc.experts, self.desc.top_k
         counts = np.zeros(E, np.int32)

@@ -88,9 +88,15 @@ class TensorSpec:
         per = self.rows * self.blocks_per_row
         return (0, per * self.experts) if expert is None else (expert * per, per * count)
 
-    def host(self, expert: int | None = None) -> np.ndarray:
-        """Bytes of the whole tensor, or of one expert's slice, generated on the CPU."""
+    def host(self, expert: int | None = None, fill=None) -> np.ndarray:
+        """Bytes of the whole tensor, or of one expert's slice, generated on the CPU.
+        `fill(kind, seed, first_block, n_blocks, sigma, lo, hi, block_bytes)` replaces
+        the library's host fill (the CPU reference arm passes the oracle's, so that it
+        never loads the CUDA library); both evaluate the same generator."""
         first, n = self._range(expert)
+        if fill is not None:
+            return fill(self.kind, self.seed, first, n, self.sigma, SCALE_LO, SCALE_HI,
+                        _BLOCK[self.kind][1])
         out = np.empty(n * _BLOCK[self.kind][1], dtype=np.uint8)
         N.check(N.lib().dm_synth_fill_host(self.kind, self.seed, first, n, self.sigma,
                                            SCALE_LO, SCALE_HI, out.ctypes.data_as(C.c_void_p)))
@@ -178,18 +184,19 @@ class SyntheticLayer:
     def ptr(self, key: str) -> int:
         return self.buffers[key].device_pointer if key in self.buffers else 0
 
-    def host_weights(self, experts=None) -> dict:
-        """Oracle inputs: full tensors (or the listed experts, others zero)."""
+    def host_weights(self, experts=None, fill=None) -> dict:
+        """Oracle inputs: full tensors (or the listed experts, others zero). `fill` as in
+        `TensorSpec.host`."""
         cfg = self.cfg
         w = dict(hidden=cfg["hidden"], intermediate=cfg["intermediate"], experts=cfg["experts"],
                  top_k=cfg["top_k"], epsilon=cfg.get("epsilon", 1e-6))
         for key, spec in self.specs.items():
             if experts is None or spec.experts == 1:
-                w[key] = spec.host()
+                w[key] = spec.host(fill=fill)
             else:
                 full = np.zeros(spec.nbytes, dtype=np.uint8)
                 for e in experts:
-                    full[e * spec.expert_bytes:(e + 1) * spec.expert_bytes] = spec.host(e)
+                    full[e * spec.expert_bytes:(e + 1) * spec.expert_bytes] = spec.host(e, fill)
                 w[key] = full
         for key in ("router", "shared_gate_vector"):
             if key in w and self.specs[key].kind == N.F32:
@@ -216,9 +223,9 @@ class SyntheticLayer:
                 w["shared_intermediate"] = cfg["intermediate"]
         return w
 
-    def inputs(self, tokens: int, seed: int) -> tuple[TensorSpec, np.ndarray]:
+    def inputs(self, tokens: int, seed: int, fill=None) -> tuple[TensorSpec, np.ndarray]:
         spec = input_spec(self.cfg, tokens, seed)
-        return spec, spec.host()
+        return spec, spec.host(fill=fill)
 
     def close(self):
         if self.layer is not None:

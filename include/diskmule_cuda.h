@@ -195,6 +195,16 @@ DM_API int32_t dm_moe_forward(dm_moe_layer *layer, const void *x, float *y, int3
 /* The same on host slices, synchronous (the Metal call convention). */
 DM_API int32_t dm_moe_forward_host(dm_moe_layer *layer, const void *x, float *y, int32_t tokens,
                             uint32_t *sel_idx, float *sel_weight);
+/* `batches` independent forwards of `tokens` rows each on host slices x[b] -> y[b],
+ * pipelined: the input copy of batch b+1 and the output copy of batch b-1 run on their
+ * own streams while batch b computes (two device staging slots). Synchronous: returns
+ * when every output is on the host, with the first failing batch's status. Page-locked
+ * host slices make the copies overlap. The reference runs one token at a time through
+ * `forward_token_inner` (src/gemma4/cpu.rs:358-378, src/glm52/cpu.rs:462-524); this is
+ * the streaming form of that loop for a host that holds whole batches. */
+DM_API int32_t dm_moe_forward_host_batches(dm_moe_layer *layer, int32_t batches,
+                                           const void *const *x, float *const *y,
+                                           int32_t tokens);
 /* Token -> expert dispatch of the last forward, copied to the host: counts[experts],
  * offsets[experts + 1], sorted_pairs[tokens * top_k] (pair p = t*top_k + j, ordered by
  * expert, then p) and inverse[tokens * top_k]. Synchronous. */
@@ -223,10 +233,21 @@ DM_API int32_t dm_moe_last_launch_count(const dm_moe_layer *layer);
  * with DM_ERR_OVERFLOW. The first call on a device looks up the array's device
  * address, so make that first call before any stream capture. All calls share the
  * array: calls whose GPU work overlaps in time (other streams, other threads) race
- * on it and must be serialised by the caller. */
+ * on it and must be serialised by the caller. Layers holding only some experts
+ * (expert-parallel shards, cache layers) are refused with DM_ERR_INVALID_ARGUMENT,
+ * as by dm_moe_forward. The call returns once its kernels are queued; it does not
+ * wait for them, so device-side failures (a non-finite router score, a bounded wait
+ * that ran out) are read with dm_moe_forward_noalloc_status. dm_moe_last_dispatch
+ * refuses after a no-allocation call: its dispatch lists are not kept. */
 DM_API int32_t dm_moe_forward_noalloc(dm_moe_layer *layer, const void *x, float *y,
                                       int32_t tokens, uint32_t *sel_idx, float *sel_weight,
                                       void *stream);
+/* Outcome of the last dm_moe_forward_noalloc on the layer's device: waits for
+ * `stream`, then returns DM_OK, DM_ERR_NON_FINITE (a non-finite router score or
+ * RMSNorm input) or DM_ERR_TIMEOUT (a bounded device wait ran out), as
+ * dm_moe_forward_host reports them. Allocates nothing. No counterpart in the
+ * reference. */
+DM_API int32_t dm_moe_forward_noalloc_status(dm_moe_layer *layer, void *stream);
 
 /* ---- expert parallelism --------------------------------------------------------
  * The reference runs every expert of a layer in one process (src/glm52/cpu.rs:711-778,

@@ -35,8 +35,9 @@ ERR_ALL_PINNED = -13
 
 def build() -> str:
     """Compile the oracle with its Makefile if the library is missing or stale."""
-    src = os.path.join(HERE, "dm_oracle.c")
-    if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
+    srcs = [os.path.join(HERE, f) for f in ("dm_oracle.c", "dm_oracle.h", "dm_oracle_synth.cpp")]
+    if not os.path.exists(LIB_PATH) or any(os.path.getmtime(LIB_PATH) < os.path.getmtime(f)
+                                           for f in srcs if os.path.exists(f)):
         subprocess.run(["make", "-s", "-C", HERE], check=True)
     return LIB_PATH
 
@@ -89,10 +90,24 @@ def _declare(L):
     L.dmo_lru_acquire.argtypes = [P, I32, I32, C.POINTER(I32), C.POINTER(I32)]
     L.dmo_lru_set_pinned.argtypes = [P, I32, I32, I32]
     L.dmo_lru_stats.argtypes = [P, P]
+    L.dmo_synth_fill.argtypes = [I32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float,
+                                 C.c_float, P]
+    L.dmo_synth_fill.restype = I32
 
 
 def _ptr(a):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def synth_fill(kind: int, seed: int, first_block: int, n_blocks: int, sigma: float,
+               lo: float, hi: float, block_bytes: int) -> np.ndarray:
+    """Bytes of blocks [first_block, first_block + n_blocks) of a seeded synthetic tensor
+    (the generator of include/diskmule_synth.h, evaluated in this library)."""
+    out = np.empty(n_blocks * block_bytes, dtype=np.uint8)
+    rc = lib().dmo_synth_fill(kind, seed, first_block, n_blocks, sigma, lo, hi, _ptr(out))
+    if rc != OK:
+        raise ValueError(f"synthetic fill of kind {kind} failed ({rc})")
+    return out
 
 
 def _f32(a):

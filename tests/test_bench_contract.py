@@ -13,9 +13,19 @@ import sys
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
+# Runs bench.py's main() in this interpreter, then reports whether the CUDA library was
+# mapped into the process (it must not be on the reference arm).
+_RUN = (
+    "import runpy, sys; sys.argv = ['bench.py'] + sys.argv[1:]; "
+    "runpy.run_path('bench.py', run_name='__main__'); "
+    "loaded = 'libdiskmule_cuda' in open('/proc/self/maps').read(); "
+    "sys.stderr.write('CUDA_LIBRARY_LOADED=%d\\n' % loaded)"
+)
+
+
 def test_reference_arm_prints_one_json_line():
-    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1",
-                        "--warmup", "0"], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    r = subprocess.run([sys.executable, "-c", _RUN, "--impl", "reference", "--steps", "1",
+                        "--warmup", "0"], cwd=ROOT, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [l for l in r.stdout.splitlines() if l.strip()]
     assert len(lines) == 1, r.stdout
@@ -27,6 +37,12 @@ def test_reference_arm_prints_one_json_line():
     assert d["impl"] == "reference" and d["value"] > 0
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    # the same metric string as the GPU arm's default line (configuration 4)
+    sys.path.insert(0, ROOT)
+    import bench
+    assert d["metric"] == bench.metric_name("glm52", 8192)
+    # the reference arm generates its inputs with the oracle library only
+    assert "CUDA_LIBRARY_LOADED=0" in r.stderr, r.stderr[-2000:]
 
 
 def test_roofline_follows_the_arithmetic_intensity():

@@ -14,7 +14,8 @@ import torch
 from diskmule_b200 import _native as N
 from diskmule_b200.cache import Cancellation, ExpertCache, PinnedHost, layout
 from diskmule_b200.moe import CudaContext
-from diskmule_b200.stack import GlmStack, OracleStack
+from diskmule_b200.stack import GlmStack
+from oracle.stack import OracleStack
 from diskmule_b200.synthetic import EXPERT_TENSORS, build_cached_layer
 from oracle import oracle as O
 

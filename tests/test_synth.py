@@ -54,3 +54,17 @@ def test_zipf_bias_is_a_log_distribution():
     b = zipf_bias(128, 1.1, 3)
     assert np.isclose(np.exp(b.astype(np.float64)).sum(), 1.0, rtol=1e-5)
     assert b.max() > b.min() + 4
+
+
+@pytest.mark.parametrize("name", ["glm52-small", "qwen35-small", "gemma4-small"])
+def test_oracle_fill_equals_the_library_fill(name):
+    """The CPU reference arm generates its inputs with the oracle library's copy of the
+    generator (it never loads the CUDA library): the bytes must be the same."""
+    from diskmule_b200.synthetic import input_spec
+    cfg = CONFIGS[name]
+    for key, spec in layer_specs(cfg, 4).items():
+        assert np.array_equal(spec.host(), spec.host(fill=O.synth_fill)), key
+        if spec.experts > 1:
+            assert np.array_equal(spec.host(1), spec.host(1, O.synth_fill)), key
+    x = input_spec(cfg, 7, 5)
+    assert np.array_equal(x.host(), x.host(fill=O.synth_fill))
