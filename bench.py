@@ -649,7 +649,7 @@ def run_glm(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    from diskmule_b200.ep import ExpertParallel, cuda_backend_for
+    from diskmule_b200.ep import PeerExpertParallel
     from diskmule_b200.moe import CudaContext
     from diskmule_b200.synthetic import CONFIGS, build_layer, input_spec
 
@@ -680,10 +680,15 @@ def run_glm(args):
                              stream=sptr)
             return y
     else:
-        ep = ExpertParallel(cuda_backend_for(sl), E, k)
+        # token rows and expert outputs travel as stores into the peers' memory
+        ep = PeerExpertParallel(sl.layer, rank, world, T)
+        ep.connect_ipc()
+        y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        sel_i = torch.empty((T, k), dtype=torch.int32, device="cuda")
+        sel_w = torch.empty((T, k), dtype=torch.float32, device="cuda")
 
         def step():
-            return ep.forward(x)
+            return ep.forward(x, y, sel_i, sel_w, stream=sptr)
 
     for _ in range(args.warmup):
         step()
@@ -708,9 +713,10 @@ def run_glm(args):
         avg = profile_stages(sl.layer, step, min(args.steps, 20))
         roofline = block_roofline(sl, T, avg, f"{args.config}-T{T}", sustained=True)
     else:
-        launches, stage = ep.profile_step(x)
-        avg = {n: v for n, v in stage.items()}
-        roofline = ep_roofline(sl, stage, ep)
+        ep.status()
+        launches = ep.last_launch_count()
+        stage = ep_profile(ep, x, y, n=min(args.steps, 20))
+        roofline = ep_roofline(sl, stage, T_total * k // world + T)
     barrier()
 
     # e2e: every step's input comes from page-locked host memory and its output returns
@@ -732,13 +738,15 @@ def run_glm(args):
     else:
         yh = [torch.empty((T, H), dtype=torch.float32, pin_memory=True) for _ in range(2)]
         e2e_steps = max(4, min(args.steps, 40))
-        ep.forward_host_stream(xh, yh, 2)
+        host_stream(lambda xd, yd: ep.forward(xd, yd), xh, yh, 2, H)
         barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        ep.forward_host_stream(xh, yh, e2e_steps)
+        host_stream(lambda xd, yd: ep.forward(xd, yd), xh, yh, e2e_steps, H)
         el = time.perf_counter() - t0
-        api = "ExpertParallel.forward_host_stream (copies on side streams)"
+        ep.status()
+        api = ("PeerExpertParallel.forward, input and output copies of neighbouring steps on "
+               "side streams")
     el = max_over_ranks(el)
     e2e = {"value": T_total * e2e_steps / el, "unit": "tokens/s",
            "h2d_bytes_per_step": int(T_total * H * 2), "d2h_bytes_per_step": int(T_total * H * 4),
@@ -750,10 +758,7 @@ def run_glm(args):
     if rank == 0:
         yy = step()
         torch.cuda.synchronize()
-        if world == 1:
-            idx_d, w_d = sel_i[:n].cpu().numpy().view(np.uint32), sel_w[:n].cpu().numpy()
-        else:
-            idx_d, w_d = ep.last_selection(n)
+        idx_d, w_d = sel_i[:n].cpu().numpy().view(np.uint32), sel_w[:n].cpu().numpy()
         y_d = yy[:n].float().cpu().numpy()
         threads = os.cpu_count() or 1
         x32 = x32_rows(cfg, xs.host()[: n * H * 2]).reshape(n, H)
@@ -764,6 +769,10 @@ def run_glm(args):
                    "sample": f"{n} tokens of the {args.config} block in one oracle call (host "
                              "weights of the experts they select)"}
     barrier()
+    if world > 1:
+        barrier()  # no rank unmaps its peers' regions while another still stores into them
+        ep.close()
+        barrier()
 
     extras = None
     if world == 1 and not args.no_extras:
@@ -807,19 +816,78 @@ def run_glm(args):
         dist.destroy_process_group()
 
 
-def ep_roofline(sl, stage, ep):
+def ep_profile(ep, x, y, n):
+    """Average device time (ms) of the three phases of an expert-parallel forward
+    (events on the launching stream): dispatch (router, top-k, row stores to the peers),
+    experts (wait for every rank's rows, local GEMMs, output stores), combine (wait for
+    every rank's outputs, weighted combine)."""
+    import torch
+    stream = torch.cuda.current_stream()
+    tot = {"dispatch": 0.0, "experts": 0.0, "combine": 0.0}
+    for _ in range(n):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record(stream)
+        ep.dispatch(x)
+        ev[1].record(stream)
+        ep.experts()
+        ev[2].record(stream)
+        ep.combine(y)
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+        for i, name in enumerate(("dispatch", "experts", "combine")):
+            tot[name] += ev[i].elapsed_time(ev[i + 1])
+    return {name: v / n for name, v in tot.items()}
+
+
+def host_stream(forward, x_host, y_host, steps, hidden):
+    """`steps` forwards of the page-locked rows x_host: the input copy of step i+1 runs
+    on a side stream while step i computes, and the output copy of step i on another."""
+    import torch
+    cs = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    T = x_host.shape[0]
+    xb = [torch.empty_like(x_host, device="cuda") for _ in range(2)]
+    yb = [torch.empty((T, hidden), dtype=torch.float32, device="cuda") for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]     # forward i finished reading xb / writing yb
+    copied = [torch.cuda.Event() for _ in range(2)]   # output copy of step i finished
+    with torch.cuda.stream(s_in):
+        xb[0].copy_(x_host, non_blocking=True)
+        ready[0].record(s_in)
+    for i in range(steps):
+        j = i & 1
+        if i + 1 < steps:
+            with torch.cuda.stream(s_in):
+                if i >= 1:
+                    s_in.wait_event(used[1 - j])
+                xb[1 - j].copy_(x_host, non_blocking=True)
+                ready[1 - j].record(s_in)
+        cs.wait_event(ready[j])
+        if i >= 2:
+            cs.wait_event(copied[j])
+        forward(xb[j], yb[j])
+        used[j].record(cs)
+        s_out.wait_event(used[j])
+        with torch.cuda.stream(s_out):
+            y_host[i % len(y_host)].copy_(yb[j], non_blocking=True)
+            copied[j].record(s_out)
+    torch.cuda.synchronize()
+
+
+def ep_roofline(sl, stage, rows):
     """Roofline of the local expert GEMMs inside an expert-parallel step: useful FLOPs of
-    the rows this rank's experts ran ÷ their event-timed duration, against the sustained
-    bf16 peak (the GEMMs run inside a long step)."""
+    the rows this rank's experts run (`rows`: the expected T*k/world routed rows plus the
+    shared expert's T) ÷ the experts phase's event-timed duration (which also holds the
+    wait for the peers' rows and the output stores), against the sustained bf16 peak."""
     cfg = sl.cfg
     H, I = cfg["hidden"], cfg["intermediate"]
-    rows = ep.last_rows
     flops = 2.0 * rows * 3 * H * I
     ms = stage["experts"]
     tpeak, src = measured_tensor_peak(True)
     achieved = flops / (ms / 1e3) / 1e12
     return {"bound": "tensor", "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
-            "frac": achieved / tpeak, "traffic": None, "kernel": "tc_bf16_kernel (local experts)",
+            "frac": achieved / tpeak, "traffic": None,
+            "kernel": "tc_bf16_kernel (local experts, experts phase)",
             "algorithmic_flops": flops, "peak_source": src, "kernel_ms": round(ms, 4),
             "stage_ms": {n: round(v, 4) for n, v in stage.items()}}
 

@@ -128,6 +128,17 @@ SIGNATURES = {
     "dm_moe_route": ([P, P, I32, P, P, P, P, P], I32),
     "dm_moe_expert_rows": ([P, P, P, I32, P, P], I32),
     "dm_moe_combine_rows": ([P, I32, P, P, P, P, P, P], I32),
+    "dm_ep_create": ([P, I32, I32, I32, C.POINTER(P)], I32),
+    "dm_ep_ipc_handle": ([P, P], I32),
+    "dm_ep_connect_ipc": ([P, P], I32),
+    "dm_ep_connect_local": ([P, C.POINTER(P)], I32),
+    "dm_ep_dispatch": ([P, P, I32, P], I32),
+    "dm_ep_experts": ([P, P], I32),
+    "dm_ep_combine": ([P, P, P, P, P], I32),
+    "dm_ep_forward": ([P, P, P, I32, P, P, P], I32),
+    "dm_ep_status": ([P, P], I32),
+    "dm_ep_last_launch_count": ([P], I32),
+    "dm_ep_destroy": ([P], None),
     "dm_cuda_host_alloc": ([P, SZ, C.POINTER(P)], I32),
     "dm_cuda_host_free": ([P, P], None),
     "dm_cuda_host_register": ([P, P, SZ], I32),

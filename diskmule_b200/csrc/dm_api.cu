@@ -594,6 +594,10 @@ int32_t build_plan(dm_moe_layer *L) {
   return rc;
 }
 
+}  // namespace
+
+namespace dmi {
+
 int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   if (tokens <= L->capacity) return DM_OK;
   const dm_moe_desc &d = L->desc;
@@ -635,6 +639,7 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   a.inverse = arena.take<int32_t>(pairs);
   a.active = arena.take<int32_t>(E + 1);
   a.n_active = arena.take<int32_t>(1);
+  a.status = arena.take<int32_t>(1);
   a.items = arena.take<int4>(pairs + E + 1);
   a.n_items = arena.take<int32_t>(1);
   a.h = arena.take<float>(pairs * I);
@@ -671,7 +676,8 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   return DM_OK;
 }
 
-}  // namespace
+}  // namespace dmi
+using dmi::ensure_layer_scratch;
 
 extern "C" {
 
@@ -862,7 +868,9 @@ const char *dm_moe_stage_name(int32_t stage) {
   return stage >= 0 && stage < dm::kStageCount ? names[stage] : "";
 }
 
-namespace {
+}  // extern "C"
+
+namespace dmi {
 
 // Forward arguments for `tokens` rows of `x` (the scratch is already sized).
 dm::ForwardArgs fill_args(dm_moe_layer *L, const void *x, float *y, int32_t tokens) {
@@ -912,13 +920,6 @@ dm::ForwardArgs fill_args(dm_moe_layer *L, const void *x, float *y, int32_t toke
 
 // Expert-kernel plans for the dispatch described by `a` (tokens, k, experts, shared or
 // rows mode); sets a.chunk. `gp` / `tp` are null when that path does not apply.
-struct Plans {
-  dm::GemvPlan plan;
-  dm::TcPlan tcp;
-  const dm::GemvPlan *gp = nullptr;
-  const dm::TcPlan *tp = nullptr;
-};
-
 void choose_plans(dm_moe_layer *L, dm::ForwardArgs &a, Plans &P) {
   const dm_moe_desc &d = L->desc;
   const int pairs = a.T * a.k + (a.shared ? a.T : 0);
@@ -955,7 +956,12 @@ void choose_plans(dm_moe_layer *L, dm::ForwardArgs &a, Plans &P) {
   }
 }
 
-}  // namespace
+}  // namespace dmi
+using dmi::Plans;
+using dmi::choose_plans;
+using dmi::fill_args;
+
+extern "C" {
 
 int32_t dm_moe_forward(dm_moe_layer *L, const void *x, float *y, int32_t tokens,
                        uint32_t *sel_idx, float *sel_weight, void *stream) {

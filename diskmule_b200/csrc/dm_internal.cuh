@@ -54,6 +54,18 @@ int32_t cache_layer_view(const dm_expert_cache *cache, int layer, int *tensors, 
 bool cache_on_device(const dm_expert_cache *cache, int device);
 void release_cached_scratch(CachedScratch &scratch);
 
+// Layer scratch for `tokens` tokens (dm_api.cu), forward arguments over it, and the
+// expert-kernel plans (GEMV or tcgen05) for the dispatch `a` describes.
+int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens);
+dm::ForwardArgs fill_args(dm_moe_layer *L, const void *x, float *y, int32_t tokens);
+struct Plans {
+  dm::GemvPlan plan;
+  dm::TcPlan tcp;
+  const dm::GemvPlan *gp = nullptr;
+  const dm::TcPlan *tp = nullptr;
+};
+void choose_plans(dm_moe_layer *L, dm::ForwardArgs &a, Plans &P);
+
 }  // namespace dmi
 
 #define DM_CUDA(call, what)                                        \

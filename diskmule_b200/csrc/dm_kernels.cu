@@ -857,6 +857,11 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs 
     int p = base + lane;
     bool valid = p < end;
     unsigned vmask = __ballot_sync(0xffffffffu, valid);
+    if (valid && a.drop_invalid && a.sel_idx[p] >= (uint32_t)EB) {
+      a.inverse[p] = -1;  // a slot this rank does not run
+      valid = false;
+    }
+    vmask = __ballot_sync(0xffffffffu, valid);
     if (valid) {
       uint32_t e = a.sel_idx[p];
       if (e >= (uint32_t)EB) e = 0;  // rejected upstream; keep indices in range
@@ -1515,7 +1520,7 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   mark(kStageDispatch);
   if (fused_dispatch) {
     launches--;  // counted with the top-k
-  } else if (a.T * a.k <= kSmallPairs) {
+  } else if (a.T * a.k <= kSmallPairs && !a.drop_invalid) {
     launch_pdl(dispatch_small_kernel, dim3(1), dim3(std::max(kSmallPairs, (a.E + 1 + 31) / 32 * 32)),
                0, stream, a);
   } else {

@@ -46,6 +46,8 @@ struct ForwardArgs {
   int32_t *active;         // [E + 1] experts with tokens, ascending
   int32_t *n_active;       // [1]
   int rows_mode;           // sel_idx are explicit expert ids (id E = shared), k = 1
+  int drop_invalid;        // rows mode: ids above E take no bucket and get no position
+                           // (expert-parallel receivers: slots owned by other ranks)
   int chunk;               // tokens per work item
   int4 *items;             // [T*k + T + E + 1] work items: (expert, first token within the
                            // expert, first sorted position, tokens)

@@ -1,5 +1,15 @@
 """Expert parallelism: experts sharded over the ranks of a process group.
 
+Two data planes share the same split of the block:
+
+* `PeerExpertParallel` (the default): the library's own kernels move the token rows
+  and the expert outputs by direct stores into the other GPUs' memory over NVLink
+  (CUDA IPC mappings of each rank's exchange region) with device-side epoch flags, so
+  one forward has no host synchronisation and no collective-library call
+  (dm_ep_* in include/diskmule_cuda.h).
+* `ExpertParallel`: the collective baseline, torch.distributed all_to_all_single
+  (NCCL on GPUs, gloo on CPU in the tests), described below.
+
 Rank g holds experts [g*E/n, (g+1)*E/n) of every layer plus the replicated router and
 shared expert, and routes its own T/n tokens. One forward (the GLM block of
 src/glm52/cpu.rs:711-778 split across GPUs):
@@ -18,9 +28,14 @@ through the C ABI (dm_moe_route / dm_moe_expert_rows / dm_moe_combine_rows).
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import numpy as np
 import torch
 import torch.distributed as dist
+
+from . import _native as N
+from ._native import check
 
 
 def exchange_plan(sel_idx: torch.Tensor, experts: int, world: int):
@@ -217,3 +232,92 @@ def cuda_backend_for(sl) -> CudaBackend:
     shared = bool(cfg.get("shared"))
     columns = cfg["experts"] + (1 if cfg["family"] == "qwen35" and shared else 0)
     return CudaBackend(sl.layer, cfg["family"], cfg["hidden"], cfg["top_k"], columns, shared)
+
+
+class PeerExpertParallel:
+    """Expert parallelism over NVLink peer memory (dm_ep_*): rank `rank` of `world` holds
+    the experts of `layer` (a shard built for [rank*E/world, (rank+1)*E/world)) and
+    runs up to `max_tokens` tokens per forward. Call `connect_ipc` on every rank (one
+    process per GPU), or `connect_local` once with every rank of one process, before
+    the first forward."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, layer, rank: int, world: int, max_tokens: int):
+        self.layer = layer
+        self.rank, self.world, self.max_tokens = rank, world, max_tokens
+        self.hidden = layer.desc.hidden
+        self.top_k = layer.desc.top_k
+        h = C.c_void_p()
+        check(N.lib().dm_ep_create(layer.handle, rank, world, max_tokens, C.byref(h)))
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def ipc_handle(self) -> bytes:
+        buf = (C.c_uint8 * self.HANDLE_BYTES)()
+        check(N.lib().dm_ep_ipc_handle(self._h, buf))
+        return bytes(buf)
+
+    def connect_ipc(self, group=None):
+        """Exchange exchange-region handles with every rank of `group` and map them."""
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.ipc_handle(), group=group)
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check(N.lib().dm_ep_connect_ipc(self._h, buf))
+        dist.barrier(group=group)  # every rank mapped before anyone sends
+
+    @staticmethod
+    def connect_local(ranks):
+        """Connect the ranks of one process (one GPU or several)."""
+        arr = (C.c_void_p * len(ranks))(*[r.handle.value for r in ranks])
+        for r in ranks:
+            check(N.lib().dm_ep_connect_local(r.handle, arr))
+
+    @staticmethod
+    def _stream(stream):
+        if stream is None:
+            stream = torch.cuda.current_stream().cuda_stream
+        return C.c_void_p(stream) if stream else None
+
+    def dispatch(self, x: torch.Tensor, stream=None):
+        self.tokens = x.shape[0]
+        check(N.lib().dm_ep_dispatch(self._h, C.c_void_p(x.data_ptr()), self.tokens,
+                                     self._stream(stream)))
+
+    def experts(self, stream=None):
+        check(N.lib().dm_ep_experts(self._h, self._stream(stream)))
+
+    def combine(self, y=None, sel_idx=None, sel_w=None, stream=None) -> torch.Tensor:
+        if y is None:
+            y = torch.empty((self.tokens, self.hidden), dtype=torch.float32, device="cuda")
+        ptr = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+        check(N.lib().dm_ep_combine(self._h, ptr(y), ptr(sel_idx), ptr(sel_w),
+                                    self._stream(stream)))
+        return y
+
+    def forward(self, x: torch.Tensor, y=None, sel_idx=None, sel_w=None,
+                stream=None) -> torch.Tensor:
+        """One expert-parallel forward of this rank's tokens x [T, H] (device)."""
+        T = x.shape[0]
+        if y is None:
+            y = torch.empty((T, self.hidden), dtype=torch.float32, device=x.device)
+        ptr = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+        self.tokens = T
+        check(N.lib().dm_ep_forward(self._h, ptr(x), ptr(y), T, ptr(sel_idx), ptr(sel_w),
+                                    self._stream(stream)))
+        return y
+
+    def status(self, stream=None):
+        check(N.lib().dm_ep_status(self._h, self._stream(stream)))
+
+    def last_launch_count(self) -> int:
+        return N.lib().dm_ep_last_launch_count(self._h)
+
+    def close(self):
+        if self._h:
+            N.lib().dm_ep_destroy(self._h)
+            self._h = None

@@ -290,6 +290,54 @@ DM_API int32_t dm_moe_combine_rows(dm_moe_layer *layer, int32_t tokens, const ui
                                    const float *sel_weight, const float *logits,
                                    const float *pair_out, float *y, void *stream);
 
+/* ---- expert parallelism over NVLink peer memory -----------------------------------
+ * The same split as above with the token exchange done by this library's own kernels:
+ * each rank stores token rows straight into the other ranks' memory (CUDA IPC mappings
+ * over NVLink / NVSwitch) and raises per-rank epoch flags, so a forward has no host
+ * synchronisation and no collective-library call. The reference runs every expert in
+ * one process (src/glm52/cpu.rs:711-778, src/glm52/expert.rs:183-267); composed over
+ * the ranks, a forward gives dm_moe_forward's result for each rank's tokens (the
+ * combine is the same selection-order kernel on the same pair outputs).
+ *
+ * dm_ep_create takes a layer made by dm_moe_layer_create_ep for experts
+ * [rank*E/world, (rank+1)*E/world) and sizes an exchange region for up to
+ * `max_tokens` tokens per rank per forward. Every rank then connects to every other:
+ * dm_ep_ipc_handle writes this rank's 64-byte handle, and dm_ep_connect_ipc takes all
+ * ranks' handles [world][64] (exchanged by the caller, e.g. an all-gather); ranks
+ * that live in one process use dm_ep_connect_local with every rank's dm_ep. All ranks
+ * must be connected before any rank starts a forward, and stay alive until every rank
+ * has finished its last one.
+ *
+ * A forward is dm_ep_forward on every rank (or its three phases in order: dispatch,
+ * experts, combine). Every rank runs the same number of forwards; a rank with no
+ * tokens passes tokens = 0. Waits on other ranks are bounded (about two seconds):
+ * dm_ep_status returns DM_ERR_TIMEOUT after a forward in which a rank's rows or
+ * outputs did not arrive. Ranks on one GPU are run phase by phase in one stream
+ * (every rank's dispatch, then every rank's experts, then every rank's combine), so no
+ * kernel ever waits on a kernel launched after it. */
+typedef struct dm_ep dm_ep;
+DM_API int32_t dm_ep_create(dm_moe_layer *layer, int32_t rank, int32_t world,
+                            int32_t max_tokens, dm_ep **out);
+DM_API int32_t dm_ep_ipc_handle(dm_ep *ep, void *handle);
+DM_API int32_t dm_ep_connect_ipc(dm_ep *ep, const void *handles);
+DM_API int32_t dm_ep_connect_local(dm_ep *ep, dm_ep *const *peers);
+/* Router + top-k of x [tokens, hidden] (input_type, device) and the send of rows. */
+DM_API int32_t dm_ep_dispatch(dm_ep *ep, const void *x, int32_t tokens, void *stream);
+/* Wait for every rank's rows, run this rank's experts on them, return the outputs. */
+DM_API int32_t dm_ep_experts(dm_ep *ep, void *stream);
+/* Wait for every rank's outputs and combine them into y [tokens, hidden] f32;
+ * optional copies of the selection [tokens, top_k]. */
+DM_API int32_t dm_ep_combine(dm_ep *ep, float *y, uint32_t *sel_idx, float *sel_weight,
+                             void *stream);
+DM_API int32_t dm_ep_forward(dm_ep *ep, const void *x, float *y, int32_t tokens,
+                             uint32_t *sel_idx, float *sel_weight, void *stream);
+/* Waits for `stream`; DM_OK, DM_ERR_TIMEOUT (a rank did not arrive) or the layer's own
+ * device status (non-finite router score, tensor-core wait) of the last forward. */
+DM_API int32_t dm_ep_status(dm_ep *ep, void *stream);
+/* Kernel launches of the last forward (a count for benchmarks). */
+DM_API int32_t dm_ep_last_launch_count(const dm_ep *ep);
+DM_API void dm_ep_destroy(dm_ep *ep);
+
 /* ---- pinned host memory ----------------------------------------------------------
  * The out-of-core expert pool lives in page-locked host memory so that a cache miss
  * is one DMA copy over PCIe (the reference reads the file with pread instead,

@@ -26,14 +26,21 @@ from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
-REL_L2 = 1e-3       # layer-output tolerance used by the parity tests
-WEIGHT_ATOL = 2e-7  # selection-weight tolerance used by the parity tests
+REL_L2 = 1e-3        # layer-output tolerance used by the parity tests
+REL_L2_TOKEN = 2e-3  # bound on any single token, as in the parity tests
+WEIGHT_ATOL = 2e-7   # selection-weight tolerance used by the parity tests
 
 
-def _rel_l2(y, ref):
-    num = np.linalg.norm((y - ref).astype(np.float64), axis=-1)
-    den = np.linalg.norm(ref.astype(np.float64), axis=-1)
-    return float((num / np.maximum(den, 1e-30)).max())
+def _close(y, ref):
+    """The parity tests' output bar: relative L2 of the whole output within 1e-3 and of
+    every token within 2e-3. (Above a few tokens per expert the allocating forward runs
+    the tensor-core GEMM with fp16 operands while the no-allocation forward runs the
+    CUDA-core GEMV, so the two differ by the tensor-core path's rounding.)"""
+    d = (y - ref).astype(np.float64)
+    r = ref.astype(np.float64)
+    layer = np.linalg.norm(d) / np.linalg.norm(r)
+    token = (np.linalg.norm(d, axis=-1) / np.maximum(np.linalg.norm(r, axis=-1), 1e-30)).max()
+    return layer <= REL_L2 and token <= REL_L2_TOKEN, (float(layer), float(token))
 
 
 def _as_f32(sl, raw, T):
@@ -108,7 +115,8 @@ def _compare(ctx, sl, T, check_oracle=True):
             assert np.isfinite(y).all()
             assert np.array_equal(i, i_ref)
             assert np.max(np.abs(w - w_ref)) <= WEIGHT_ATOL
-            assert _rel_l2(y, y_ref) <= REL_L2
+            ok, err = _close(y, y_ref)
+            assert ok, err
         # the dispatch lists of a no-allocation call are not kept
         assert L.dm_moe_last_dispatch(sl.layer.handle, None, None, None, None) == \
             N.ERR_INVALID_ARGUMENT
@@ -116,7 +124,8 @@ def _compare(ctx, sl, T, check_oracle=True):
             y_o, i_o, w_o = _oracle(sl, _as_f32(sl, raw, T), sorted(set(i_ref.ravel().tolist())))
             assert np.array_equal(i, i_o)
             assert np.max(np.abs(w - w_o)) <= WEIGHT_ATOL
-            assert _rel_l2(y, y_o) <= 2 * REL_L2  # per token
+            ok, err = _close(y, y_o)
+            assert ok, err
     finally:
         for b in out.values():
             b.free()
