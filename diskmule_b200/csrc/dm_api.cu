@@ -533,10 +533,31 @@ int32_t make_split(dm_moe_layer *L, int kind, const void *src, uint64_t blocks,
 int32_t build_tc_weights(dm_moe_layer *L) {
   const dm_moe_desc &d = L->desc;
   if (d.down_type == DM_BF16) {
+    // fp16 copies of the down weights: bf16 -> fp16 is exact for magnitudes in fp16's
+    // normal range, and the down product then takes one fp16 MMA per K step on single
+    // fp16 intermediates instead of two bf16 MMAs on hi + lo halves
+    uint8_t *down16 = nullptr, *sh_down16 = nullptr;
+    if (L->tc_f16_down && ((uintptr_t)d.down | (uintptr_t)d.shared_down) % 16 == 0) {
+      const uint64_t n = (uint64_t)L->local_experts * d.hidden * d.intermediate;
+      const uint64_t n_sh = L->shared ? (uint64_t)d.hidden * d.intermediate : 0;
+      void *mem = nullptr;
+      if (cudaMalloc(&mem, (n + n_sh) * 2) == cudaSuccess) {
+        L->owned.push_back(mem);
+        down16 = (uint8_t *)mem;
+        dm::launch_bf16_to_f16(d.down, down16, n, L->ctx->stream);
+        if (n_sh) {
+          sh_down16 = down16 + n * 2;
+          dm::launch_bf16_to_f16(d.shared_down, sh_down16, n_sh, L->ctx->stream);
+        }
+      } else {
+        cudaGetLastError();  // no room for the copies: the hi + lo bf16 down path
+      }
+    }
     if (dm::make_tc_weights_bf16(L->tcw, (const uint8_t *)d.gate, L->up_base, L->gate_stride,
                                  (const uint8_t *)d.shared_gate, (const uint8_t *)d.shared_up,
                                  (const uint8_t *)d.down, (const uint8_t *)d.shared_down,
-                                 L->local_experts, d.hidden, d.intermediate) != 0) {
+                                 L->local_experts, d.hidden, d.intermediate, down16,
+                                 sh_down16) != 0) {
       fprintf(stderr, "diskmule_cuda: tensor-core path off for this layer (weight maps refused)\n");
       L->tc_ok = false;
     }
@@ -758,6 +779,8 @@ static int32_t create_layer(dm_cuda_context *ctx, const dm_moe_desc *desc, int32
                             (uintptr_t)d.shared_gate | (uintptr_t)d.shared_up;
     // Slots of an expert cache change under the layer: only the bf16 kernels, which
     // read the weights through TMA maps alone, keep no per-expert side arrays.
+    const char *f16_env = getenv("DISKMULE_CUDA_F16_DOWN");
+    L->tc_f16_down = !cached && !(f16_env && (!strcmp(f16_env, "0") || !strcmp(f16_env, "false")));
     L->tc_ok = rc == DM_OK && align % 16 == 0 && (!cached || d.down_type == DM_BF16) &&
                dm::tc_supported(d.gate_type, d.down_type, d.hidden, d.intermediate) &&
                !(tc_env && (!strcmp(tc_env, "0") || !strcmp(tc_env, "false")));

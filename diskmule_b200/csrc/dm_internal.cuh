@@ -152,6 +152,9 @@ struct dm_moe_layer {
   bool tc_ok = false;
   dm::TcPlan tc[3];
   dm::TcWeights tcw;  // tensor-core weight views (valid while tc_ok)
+  // bf16 layers: run the down product on fp16 copies of the down weights (held in
+  // `owned`) with single fp16 intermediates; off for cache layers, whose slots refill
+  bool tc_f16_down = false;
   // CUDA graphs of repeated calls (keyed by buffers and token count)
   struct GraphEntry {
     const void *x;

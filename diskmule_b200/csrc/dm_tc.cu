@@ -1011,10 +1011,13 @@ __device__ __forceinline__ void mma_ss(uint32_t d, uint64_t adesc, uint64_t bdes
 // holds up to 2 x TPT tokens and each (item, row tile) is two units of TPT tokens; a unit
 // without tokens is skipped by every warp role alike, and the accumulator buffers and
 // barrier phases follow the count of units actually run.
-template <bool UP, int NB, bool SPLIT, int HALVES>
+// F16 (down only): A = fp16 copies of the down weights, B = single fp16 intermediate rows
+// scaled by a power of two per row (row_inv = 1 / scale, applied in the epilogue).
+template <bool UP, int NB, bool SPLIT, int HALVES, bool F16 = false>
 __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
     const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap wmap,
-    const __grid_constant__ CUtensorMap sh_wmap, ForwardArgs a, TcSide side, float *gu) {
+    const __grid_constant__ CUtensorMap sh_wmap, ForwardArgs a, TcSide side, float *gu,
+    const float *row_inv) {
   using C = BfCfg<NB>;
   constexpr int S = C::kStages;
   constexpr int TPT = SPLIT ? NB / 2 : NB;  // tokens per tile
@@ -1122,7 +1125,7 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
         // N sized to the unit's tokens (a multiple of 16): ragged tiles cost less
         const int rows = SPLIT ? 2 * un.ntok : un.ntok;
         const int n = min(NB, (rows + 15) & ~15);
-        const uint32_t idesc = idesc_bf16(n);
+        const uint32_t idesc = F16 ? idesc_f16(n) : idesc_bf16(n);
         const uint32_t dcol = tmem + (uint32_t)(acc * NB);
         for (int ks = 0; ks < nsteps; ks++, t++) {
           const int i = t % S;
@@ -1175,8 +1178,11 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
 #pragma unroll
           for (int j = 0; j < (SPLIT ? 16 : 32); j++) {
             const int n = nbase + j;
-            const float v = SPLIT ? w[2 * j] + w[2 * j + 1] : w[j];
-            if (n < un.ntok) out[(size_t)(un.pos0 + n) * ld + col] = v;
+            float v = SPLIT ? w[2 * j] + w[2 * j + 1] : w[j];
+            if (n < un.ntok) {
+              if (F16) v *= row_inv[un.pos0 + n];  // exact: a power of two
+              out[(size_t)(un.pos0 + n) * ld + col] = v;
+            }
           }
         }
       }
@@ -1297,6 +1303,8 @@ int make_tc_maps(TcPlan &p, int H, int I, int down_type, int nt) {
     // x tiles: nt tokens; h tiles: nt rows = nt / 2 tokens as hi/lo pairs
     if (!encode_bf16_rows(&p.x_map, p.x16, H, (uint64_t)p.rows, nt)) return -1;
     if (!encode_bf16_rows(&p.h_map, p.h16, I, 2 * (uint64_t)p.rows, nt)) return -1;
+    // the same buffer as single fp16 rows (2-byte elements either way for the copy)
+    if (!encode_bf16_rows(&p.h1_map, p.h16, I, (uint64_t)p.rows, nt)) return -1;
     return 0;
   }
   p.split_x = p.split && fits_split<tc::kUpQ4K>(nt);
@@ -1367,16 +1375,30 @@ static int launch_bf16(const ForwardArgs &a, const TcPlan &p, const TcWeights &w
     auto fn = tc::tc_bf16_kernel<true, NT, false, 1>;
     ensure_smem_limit((const void *)fn);
     const int grid = std::max(1, std::min(p.n_sm, p.max_items * (a.I / 64)));
-    fn<<<grid, tc::kBfThreads, tc::BfCfg<NT>::kSmem, s>>>(p.x_map, w.up, w.sh_up, a, w.side, p.gu);
+    fn<<<grid, tc::kBfThreads, tc::BfCfg<NT>::kSmem, s>>>(p.x_map, w.up, w.sh_up, a, w.side, p.gu,
+                                                              nullptr);
   }
   if (down_mark) cudaEventRecord(down_mark, s);
+  if (w.f16_down) {
+    // h = act(gate, up) as one fp16 row per pair, scaled by a power of two per row
+    const size_t hsmem = (size_t)tc::kPackRows * a.I * sizeof(float);
+    if (hsmem > 48 * 1024) ensure_smem_limit((const void *)tc::pack_kernel<false>);
+    tc::pack_kernel<false><<<(rows_bound + tc::kPackRows - 1) / tc::kPackRows, 32 * tc::kPackRows,
+                             hsmem, s>>>(a, p.gu, p.h16, p.h_inv, a.I, 0);
+    auto fn = tc::tc_bf16_kernel<false, NT, false, 1, true>;
+    ensure_smem_limit((const void *)fn);
+    const int grid = std::max(1, std::min(p.n_sm, p.max_items * (a.H / 128)));
+    fn<<<grid, tc::kBfThreads, tc::BfCfg<NT>::kSmem, s>>>(p.h1_map, w.down16, w.sh_down16, a,
+                                                              w.side, p.gu, p.h_inv);
+    return 4;
+  }
   tc::pack_h_bf16_kernel<<<rows_bound, 256, 0, s>>>(a, p.gu, reinterpret_cast<__nv_bfloat16 *>(p.h16));
   {
     auto fn = tc::tc_bf16_kernel<false, NT, true, 2>;
     ensure_smem_limit((const void *)fn);
     const int grid = std::max(1, std::min(p.n_sm, 2 * p.max_items * (a.H / 128)));
     fn<<<grid, tc::kBfThreads, tc::BfCfg<NT>::kSmem, s>>>(p.h_map, w.down, w.sh_down, a, w.side,
-                                                              p.gu);
+                                                              p.gu, nullptr);
   }
   return 4;
 }
@@ -1470,7 +1492,8 @@ static bool encode_up_bf16(CUtensorMap *map, const uint8_t *gate, const uint8_t 
 
 int make_tc_weights_bf16(TcWeights &w, const uint8_t *gate, const uint8_t *up, uint64_t expert_stride,
                          const uint8_t *sh_gate, const uint8_t *sh_up, const uint8_t *down,
-                         const uint8_t *sh_down, int experts, int H, int I) {
+                         const uint8_t *sh_down, int experts, int H, int I,
+                         const uint8_t *down16, const uint8_t *sh_down16) {
   if (!encode_up_bf16(&w.up, gate, up, H, I, experts, expert_stride, &w.side.up_swapped)) return -1;
   if (!encode_bf16_rows(&w.down, down, I, (uint64_t)experts * H, 128)) return -1;
   const bool shared = sh_gate != nullptr;
@@ -1482,7 +1505,39 @@ int make_tc_weights_bf16(TcWeights &w, const uint8_t *gate, const uint8_t *up, u
     w.sh_up = w.up;
     w.sh_down = w.down;
   }
+  w.f16_down = false;
+  if (down16 && (!shared || sh_down16)) {
+    if (!encode_bf16_rows(&w.down16, down16, I, (uint64_t)experts * H, 128)) return -1;
+    if (shared) {
+      if (!encode_bf16_rows(&w.sh_down16, sh_down16, I, (uint64_t)H, 128)) return -1;
+    } else {
+      w.sh_down16 = w.down16;
+    }
+    w.f16_down = true;
+  }
   return 0;
+}
+
+namespace tc {
+__global__ void bf16_to_f16_kernel(const uint4 *src, uint4 *dst, uint64_t n8) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n8;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint4 v = src[i];
+    const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float lo = __uint_as_float(in[j] << 16), hi = __uint_as_float(in[j] & 0xffff0000u);
+      o[j] = h2u(__halves2half2(__float2half_rn(lo), __float2half_rn(hi)));
+    }
+    dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+}  // namespace tc
+
+void launch_bf16_to_f16(const void *src, void *dst, uint64_t n, cudaStream_t stream) {
+  const uint64_t n8 = n / 8;  // callers pass whole 16-byte pieces (rows of 8k elements)
+  tc::bf16_to_f16_kernel<<<148 * 8, 256, 0, stream>>>((const uint4 *)src, (uint4 *)dst, n8);
 }
 
 int make_tc_weights(TcWeights &w, const uint8_t *gate, const uint8_t *up, uint64_t expert_stride,

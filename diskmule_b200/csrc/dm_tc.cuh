@@ -39,6 +39,7 @@ struct TcPlan {
   float *gu = nullptr;     // [rows][2I] gate/up outputs (gate i at 2i, up i at 2i + 1)
   CUtensorMap x_map;       // TMA view of x16: box {64, nb, 4 atoms}, 128-byte swizzle
   CUtensorMap h_map;       // TMA view of h16
+  CUtensorMap h1_map;      // bf16 layers: h16 as single fp16 rows [rows][I] (f16 down path)
 };
 
 // Device-side pointers of the per-step transposed down arrays (see TcWeights).
@@ -53,6 +54,8 @@ struct TcWeights {
   CUtensorMap up, sh_up;      // Q4_K gate/up: {row bytes, gate|up, row, expert},
                               // box {144, 2, 64, 1} = 64 interleaved gate/up row pairs
   CUtensorMap down, sh_down;  // down quant bytes: {row bytes, expert*H + row}, box {., 128}
+  CUtensorMap down16, sh_down16;  // bf16 layers: fp16 copies of the down weights
+  bool f16_down = false;          // bf16 layers: down product on fp16 copies (one MMA per step)
   TcSide side;
 };
 
@@ -69,9 +72,16 @@ int make_tc_weights(TcWeights &w, const uint8_t *gate, const uint8_t *up, uint64
                     cudaStream_t stream);
 
 // bf16 weights (no side arrays): gate/up {K, gate|up, row, expert}, down {K, expert*H + row}.
+// down16 / sh_down16, when given, are fp16 copies of the down weights (same layout): the
+// down product then runs on them with single fp16 intermediates.
 int make_tc_weights_bf16(TcWeights &w, const uint8_t *gate, const uint8_t *up, uint64_t expert_stride,
                          const uint8_t *sh_gate, const uint8_t *sh_up, const uint8_t *down,
-                         const uint8_t *sh_down, int experts, int H, int I);
+                         const uint8_t *sh_down, int experts, int H, int I,
+                         const uint8_t *down16 = nullptr, const uint8_t *sh_down16 = nullptr);
+
+// bf16 -> fp16 copy of n elements (exact for magnitudes in fp16's normal range, 2^-14 to
+// 65504; smaller ones round to fp16's subnormal grid of 2^-24).
+void launch_bf16_to_f16(const void *src, void *dst, uint64_t n, cudaStream_t stream);
 
 // Whether the tensor-core path covers these formats / shapes.
 bool tc_supported(int gate_type, int down_type, int H, int I);
