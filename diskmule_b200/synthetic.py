@@ -46,6 +46,11 @@ CONFIGS = {
     "glm52-small": dict(family="glm52", hidden=256, intermediate=128, experts=32, top_k=4,
                         gate_type=N.BF16, down_type=N.BF16, shared=True, n_groups=4,
                         topk_groups=2, routed_scale=2.5, normalize=True),
+    # the GLM shapes with 32 experts (2.4 GB): at T=1024 each expert gets the ~256 tokens
+    # it gets at T=8192 with 256 experts, so its GEMM tiles match config 4's (profiling)
+    "glm52-e32": dict(family="glm52", hidden=6144, intermediate=2048, experts=32, top_k=8,
+                      gate_type=N.BF16, down_type=N.BF16, shared=True, n_groups=8,
+                      topk_groups=4, routed_scale=2.5, normalize=True),
     "glm52-small-flat": dict(family="glm52", hidden=256, intermediate=128, experts=16, top_k=2,
                              gate_type=N.BF16, down_type=N.BF16, shared=True, n_groups=1,
                              topk_groups=1, routed_scale=2.5, normalize=True),
