@@ -15,6 +15,8 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 #include "dm_kernels.cuh"
 #include "dm_tc.cuh"
@@ -1199,6 +1201,293 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// The same bf16 / fp16 grouped GEMM on CTA pairs (tcgen05 cta_group::2).
+//
+// A cluster of two CTAs on two SMs computes a 256-row x up-to-256-token unit: CTA r holds
+// the 128 weight rows of tile 2 pt + r and half of the unit's tokens (each CTA loads only
+// its own halves, with plain non-multicast TMA), and one thread of CTA 0 issues
+// M = 256 MMAs that read both CTAs' shared memory and accumulate into both CTAs' tensor
+// memory (each its 128 rows x N tokens). Per K step and SM that moves 32 KB for the
+// 4.2 MFLOP the SM's tensor core does (48 KB on the single-CTA kernel), and seven 32 KB
+// stages fit where four 48 KB ones did, so more of the L2 / HBM latency is covered.
+//   full[s]     (CTA 0) CTA 0's producer expects both CTAs' bytes; both CTAs' TMA loads
+//               complete on it
+//   empty[s]    (each CTA) the MMA issuer's commit arrives on both CTAs' copies
+//   accfull[b]  (each CTA) the last commit of a unit arrives on both
+//   accempty[b] (CTA 0) the four epilogue warps of each CTA arrive (CTA 1's remotely)
+// Token split of a unit of n tokens: h = n/2 rounded up to 16; CTA 0's B rows are tokens
+// 0..h-1, CTA 1's tokens h..2h-1, so accumulator column c is token c (N = 2h).
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int c0,
+                                                 int c1, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(bar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const CUtensorMap *map, int c0,
+                                                 int c1, int c2, int c3, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
+               : "memory");
+}
+
+// completion of this thread's MMAs so far arrives once on the barrier at cluster address
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar_cluster)
+               : "memory");
+}
+
+__device__ __forceinline__ void mma_ss_pair(uint32_t d, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// M = 256 (two CTAs x 128 rows), N = n, f32 D; bf16 or fp16 A and B (one type for both)
+__host__ __device__ constexpr uint32_t idesc_pair(int n, bool f16) {
+  return (1u << 4) | (f16 ? 0u : (1u << 7) | (1u << 10)) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(256 >> 4) << 24);
+}
+
+struct PairCfg {
+  static constexpr int kA = 128 * 128;  // 128 rows x 64 elements
+  static constexpr int kB = 128 * 128;  // 128 tokens x 64 elements
+  static constexpr int kStage = kA + kB;
+  static constexpr int kStages = 7;
+  static constexpr int kSmem = 1024 + kStages * kStage + 256;
+  static_assert(kSmem <= kSmemLimit, "stages exceed shared memory");
+};
+
+template <bool UP, bool F16>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBfThreads, 1) tc_bf16_pair_kernel(
+    const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap wmap,
+    const __grid_constant__ CUtensorMap sh_wmap, ForwardArgs a, TcSide side, float *gu,
+    const float *row_inv) {
+  using C = PairCfg;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t dsm[];
+  __shared__ int abort_flag;
+  const uint32_t rank = cluster_rank();
+  const int K = UP ? a.H : a.I;
+  const int n_pt = UP ? a.I / 128 : a.H / 256;  // pair tiles of 256 weight rows
+  const int n_units = *a.n_items * n_pt;
+  const int cid = (int)blockIdx.x >> 1, nclusters = (int)gridDim.x >> 1;
+  const int my_units = cid < n_units ? (n_units - cid + nclusters - 1) / nclusters : 0;
+  const int nsteps = K / kBfStepK;
+  auto unit_at = [&](int lu) {
+    const int u = cid + lu * nclusters;
+    const int item = u / n_pt;
+    const int4 rec = a.items[item];
+    Unit un;
+    un.e = rec.x;
+    un.tile = 2 * (u - item * n_pt) + (int)rank;  // this CTA's 128-row tile
+    un.pos0 = rec.z;
+    un.ntok = min(256, rec.w);
+    return un;
+  };
+  auto half_of = [](int ntok) { return (((ntok + 1) >> 1) + 15) & ~15; };
+
+  const uint32_t raw = smem_u32(dsm);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t bars = base + S * C::kStage;  // full[S], empty[S], accfull[2], accempty[2], slot
+  auto full = [&](int i) { return bars + 8u * i; };
+  auto empty = [&](int i) { return bars + 8u * (S + i); };
+  auto accfull = [&](int i) { return bars + 8u * (2 * S + i); };
+  auto accempty = [&](int i) { return bars + 8u * (2 * S + 2 + i); };
+  const uint32_t slot = bars + 8u * (2 * S + 4);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    abort_flag = *reinterpret_cast<const volatile int32_t *>(a.status) == kStatusTimeout;
+    for (int i = 0; i < S; i++) {
+      mbar_init(full(i), 1);
+      mbar_init(empty(i), 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(accfull(i), 1);
+      mbar_init(accempty(i), 8);  // four epilogue warps in each CTA (used in CTA 0)
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  constexpr uint32_t kCols = 512;  // two 256-column accumulators
+  if (warp == 0) tmem_alloc_pair(slot, kCols);
+  fence_before();
+  cluster_sync();  // barriers and tensor memory of both CTAs ready
+  fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(dsm + (slot - raw));
+
+  if (warp == 4) {
+    if (lane == 0) {
+      int t = 0;
+      bool stop = false;
+      for (int lu = 0; lu < my_units && !stop; lu++) {
+        const Unit un = unit_at(lu);
+        if (un.ntok <= 0) continue;
+        if (*reinterpret_cast<const volatile int32_t *>(a.status) == kStatusTimeout)
+          atomicExch(&abort_flag, 1);
+        const bool shared = un.e == a.E;
+        const int ex = shared ? 0 : un.e;
+        const int h = half_of(un.ntok);
+        const int brow = un.pos0 + (int)rank * h;
+        for (int ks = 0; ks < nsteps; ks++, t++) {
+          const int i = t % S;
+          if ((t >= S && !wait_or_abort<64>(empty(i), (uint32_t)((t / S - 1) & 1), &abort_flag)) ||
+              aborted(&abort_flag)) {
+            atomicExch(&abort_flag, 1);
+            stop = true;
+            break;
+          }
+          const uint32_t st = base + (uint32_t)i * C::kStage;
+          const uint32_t fb = map_to_rank(full(i), 0);
+          if (rank == 0) mbar_expect_tx(full(i), (uint32_t)(2 * C::kStage));
+          if (UP)
+            tma_load_4d_pair(st, shared ? &sh_wmap : &wmap, kBfStepK * ks, 0, un.tile * 64, ex, fb);
+          else
+            tma_load_2d_pair(st, shared ? &sh_wmap : &wmap, kBfStepK * ks, ex * a.H + un.tile * 128,
+                             fb);
+          tma_load_2d_pair(st + C::kA, &bmap, kBfStepK * ks, brow, fb);
+        }
+      }
+      // CTA 0 drains both CTAs' loads in flight (they all complete on its full barriers)
+      if (rank == 0)
+        for (int i = max(0, t - S); i < t; i++) mbar_wait(full(i % S), (uint32_t)((i / S) & 1));
+    }
+  } else if (warp == 5) {
+    if (lane == 0 && rank == 0) {
+      int t = 0, pu = 0;
+      bool stop = false;
+      for (int lu = 0; lu < my_units && !stop; lu++) {
+        const Unit un = unit_at(lu);
+        if (un.ntok <= 0) continue;
+        const int acc = pu & 1;
+        if (pu >= 2 && !wait_or_abort(accempty(acc), (uint32_t)(((pu >> 1) - 1) & 1), &abort_flag)) {
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        pu++;
+        fence_after();
+        const int n = 2 * half_of(un.ntok);
+        const uint32_t idesc = idesc_pair(n, F16);
+        const uint32_t dcol = tmem + (uint32_t)(acc * 256);
+        for (int ks = 0; ks < nsteps; ks++, t++) {
+          const int i = t % S;
+          if (!wait_or_abort(full(i), (uint32_t)((t / S) & 1), &abort_flag)) {
+            atomicExch(&abort_flag, 1);
+            stop = true;
+            break;
+          }
+          fence_after();
+          const uint32_t st = base + (uint32_t)i * C::kStage;
+          const uint64_t a0 = sw128_desc(st), b0 = sw128_desc(st + C::kA);
+#pragma unroll
+          for (int s = 0; s < kBfStepK / 16; s++)
+            mma_ss_pair(dcol, a0 + 2u * s, b0 + 2u * s, idesc, (ks | s) ? 1u : 0u);
+          mma_commit_pair(empty(i));
+          mma_commit_pair(map_to_rank(empty(i), 1));
+        }
+        if (!stop) {
+          mma_commit_pair(accfull(acc));
+          mma_commit_pair(map_to_rank(accfull(acc), 1));
+        }
+      }
+      // every issued MMA is done before either CTA may free its stages or exit
+      if (t > 0) mbar_wait(empty((t - 1) % S), (uint32_t)(((t - 1) / S) & 1));
+    }
+  } else if (warp < 4) {
+    const int q = warp, r = 32 * q + lane;
+    const uint32_t ae0 = map_to_rank(accempty(0), 0), ae1 = map_to_rank(accempty(1), 0);
+    int pu = 0;
+    for (int lu = 0; lu < my_units; lu++) {
+      const Unit un = unit_at(lu);
+      if (un.ntok <= 0) continue;
+      const int acc = pu & 1;
+      const bool ok = wait_or_abort<128>(accfull(acc), (uint32_t)((pu >> 1) & 1), &abort_flag);
+      pu++;
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) atomicExch(&abort_flag, 1);
+        break;
+      }
+      fence_after();
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * 256);
+      const bool swapped = un.e == a.E ? side.sh_up_swapped : side.up_swapped;
+      float *out = UP ? gu : a.ysorted;
+      const int ld = UP ? 2 * a.I : a.H;
+      const int col = UP ? un.tile * 128 + (r ^ (swapped ? 1 : 0)) : un.tile * 128 + r;
+#pragma unroll 1
+      for (int c0 = 0; c0 < un.ntok; c0 += 32) {
+        float w[32];
+        tmem_ld16(taddr + c0, reinterpret_cast<uint32_t *>(w));
+        tmem_ld16(taddr + c0 + 16, reinterpret_cast<uint32_t *>(w + 16));
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const int n = c0 + j;
+          if (n < un.ntok) {
+            float v = w[j];
+            if (F16) v *= row_inv[un.pos0 + n];  // exact: a power of two
+            out[(size_t)(un.pos0 + n) * ld + col] = v;
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? ae1 : ae0);
+    }
+  }
+  fence_before();
+  cluster_sync();  // no CTA frees tensor memory or leaves while its pair still works
+  if (tid == 0 && abort_flag) atomicExch(a.status, kStatusTimeout);
+  if (warp == 0) {
+    fence_after();
+    tmem_dealloc_pair(tmem, kCols);
+  }
+}
+
 // bf16 inputs gathered into sorted order: out[pos] = x[token of pos] (bf16 copy).
 __global__ void __launch_bounds__(256) gather_bf16_kernel(ForwardArgs a, __nv_bfloat16 *out) {
   const int pos = blockIdx.x;
@@ -1305,6 +1594,9 @@ int make_tc_maps(TcPlan &p, int H, int I, int down_type, int nt) {
     if (!encode_bf16_rows(&p.h_map, p.h16, I, 2 * (uint64_t)p.rows, nt)) return -1;
     // the same buffer as single fp16 rows (2-byte elements either way for the copy)
     if (!encode_bf16_rows(&p.h1_map, p.h16, I, (uint64_t)p.rows, nt)) return -1;
+    // CTA pairs load half a 256-token tile each: 128-row boxes
+    if (!encode_bf16_rows(&p.x_map_pair, p.x16, H, (uint64_t)p.rows, 128)) return -1;
+    if (!encode_bf16_rows(&p.h1_map_pair, p.h16, I, (uint64_t)p.rows, 128)) return -1;
     return 0;
   }
   p.split_x = p.split && fits_split<tc::kUpQ4K>(nt);
@@ -1365,12 +1657,44 @@ static int launch_nt(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, 
 // Work items of up to 256 tokens: gate/up takes a whole item per unit (N = 256, every
 // weight tile read once per item); down, whose hi/lo rows double N, takes each item as
 // two units of 128 tokens.
+// Persistent grid of CTA pairs for tc_bf16_pair_kernel: at most one pair per two SMs.
+static int pair_grid(const TcPlan &p, int tiles) {
+  const int pairs = std::max(1, std::min(p.n_sm / 2, p.max_items * tiles));
+  return 2 * pairs;
+}
+
+static bool use_pairs() {
+  static int v = -1;
+  if (v < 0) {
+    const char *e = getenv("DISKMULE_CUDA_TC_PAIRS");
+    v = e && (!strcmp(e, "1") || !strcmp(e, "true"));
+  }
+  return v == 1;
+}
+
 static int launch_bf16(const ForwardArgs &a, const TcPlan &p, const TcWeights &w, cudaStream_t s,
                        cudaEvent_t down_mark) {
   constexpr int NT = 256;
   if (p.nt != NT) return -1;
   const int rows_bound = a.T * a.k + (a.shared ? a.T : 0);
   tc::gather_bf16_kernel<<<rows_bound, 256, 0, s>>>(a, reinterpret_cast<__nv_bfloat16 *>(p.x16));
+  if (use_pairs() && w.f16_down && a.I % 128 == 0 && a.H % 256 == 0) {
+    // CTA pairs: 256-row weight tiles over both gate/up and down
+    auto up = tc::tc_bf16_pair_kernel<true, false>;
+    ensure_smem_limit((const void *)up);
+    up<<<pair_grid(p, a.I / 128), tc::kBfThreads, tc::PairCfg::kSmem, s>>>(
+        p.x_map_pair, w.up, w.sh_up, a, w.side, p.gu, nullptr);
+    if (down_mark) cudaEventRecord(down_mark, s);
+    const size_t hsmem = (size_t)tc::kPackRows * a.I * sizeof(float);
+    if (hsmem > 48 * 1024) ensure_smem_limit((const void *)tc::pack_kernel<false>);
+    tc::pack_kernel<false><<<(rows_bound + tc::kPackRows - 1) / tc::kPackRows, 32 * tc::kPackRows,
+                             hsmem, s>>>(a, p.gu, p.h16, p.h_inv, a.I, 0);
+    auto down = tc::tc_bf16_pair_kernel<false, true>;
+    ensure_smem_limit((const void *)down);
+    down<<<pair_grid(p, a.H / 256), tc::kBfThreads, tc::PairCfg::kSmem, s>>>(
+        p.h1_map_pair, w.down16, w.sh_down16, a, w.side, p.gu, p.h_inv);
+    return 4;
+  }
   {
     auto fn = tc::tc_bf16_kernel<true, NT, false, 1>;
     ensure_smem_limit((const void *)fn);

@@ -40,6 +40,7 @@ struct TcPlan {
   CUtensorMap x_map;       // TMA view of x16: box {64, nb, 4 atoms}, 128-byte swizzle
   CUtensorMap h_map;       // TMA view of h16
   CUtensorMap h1_map;      // bf16 layers: h16 as single fp16 rows [rows][I] (f16 down path)
+  CUtensorMap x_map_pair, h1_map_pair;  // the same with 128-row boxes (CTA-pair kernels)
 };
 
 // Device-side pointers of the per-step transposed down arrays (see TcWeights).
