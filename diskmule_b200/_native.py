@@ -1,5 +1,5 @@
 """ctypes declarations of the C ABI (include/diskmule_cuda.h, include/diskmule_stack.h,
-include/diskmule_selftest.h, include/diskmule_synth.h).
+include/diskmule_selftest.h, include/diskmule_synth.h, include/diskmule_gguf.h).
 
 The product path is the CUDA library `libdiskmule_cuda.so` built next to this file.
 Nothing here falls back to a CPU implementation: if the library is missing the
@@ -40,6 +40,7 @@ ERR_TIMEOUT = -22
 ERR_NOT_BUILT = -23
 ERR_COMMUNICATOR = -24
 ERR_IO = -25
+ERR_FORMAT = -26
 
 # dm_tensor_type (GGML ids)
 F32, F16, Q5_0, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 6, 8, 12, 14, 30
@@ -162,6 +163,24 @@ SIGNATURES = {
     "dm_stack_add_rms_norm": ([P, P, P, P, I32, C.c_float, P, P, P], I32),
     "dm_stack_lm_head_argmax": ([P, P, I32, I32, I32, P, P, P, P, P], I32),
     "dm_selftest_device_wait": ([P, C.c_int64], I32),
+    "dm_gguf_open": ([C.c_char_p, C.c_char_p, C.POINTER(P)], I32),
+    "dm_gguf_parse": ([P, C.c_uint64, C.c_char_p, C.POINTER(P)], I32),
+    "dm_gguf_close": ([P], None),
+    "dm_gguf_header": ([P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_uint64),
+                        C.POINTER(C.c_uint64)], I32),
+    "dm_gguf_tensor_count": ([P], C.c_int64),
+    "dm_gguf_find_tensor": ([P, C.c_char_p, C.POINTER(C.c_int64)], I32),
+    "dm_gguf_tensor": ([P, C.c_int64, P], I32),
+    "dm_gguf_tensor_bytes": ([P, C.c_int64, C.POINTER(P), C.POINTER(C.c_uint64)], I32),
+    "dm_gguf_read_tensor_at": ([P, C.c_char_p, C.c_uint64, P, C.c_uint64], I32),
+    "dm_gguf_metadata_type": ([P, C.c_char_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                               C.POINTER(C.c_uint64)], I32),
+    "dm_gguf_metadata_u64": ([P, C.c_char_p, C.POINTER(C.c_uint64)], I32),
+    "dm_gguf_metadata_f64": ([P, C.c_char_p, C.POINTER(C.c_double)], I32),
+    "dm_gguf_metadata_string": ([P, C.c_char_p, C.c_char_p, C.c_uint64], I32),
+    "dm_gguf_metadata_array": ([P, C.c_char_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint64),
+                                C.POINTER(P)], I32),
+    "dm_gguf_expert_layout": ([P, C.c_char_p, C.c_char_p, I32, P], I32),
     "dm_synth_fill_host": ([I32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float,
                             C.c_float, P], I32),
     "dm_synth_fill_device": ([I32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float,

@@ -72,6 +72,7 @@ const char *dm_status_string(int32_t status) {
     case DM_ERR_NOT_BUILT: return "component not built";
     case DM_ERR_COMMUNICATOR: return "expert-parallel exchange failed";
     case DM_ERR_IO: return "expert source read failed";
+    case DM_ERR_FORMAT: return "malformed model file index";
     default: return "unknown status";
   }
 }

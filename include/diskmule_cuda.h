@@ -61,6 +61,7 @@ typedef enum {
   DM_ERR_NOT_BUILT = -23,             /* the call needs a component this build lacks */
   DM_ERR_COMMUNICATOR = -24,          /* NCCL / expert-parallel exchange failed */
   DM_ERR_IO = -25,                    /* ExpertCacheError::Io: a source read failed or was short */
+  DM_ERR_FORMAT = -26,                /* GgufError: a malformed model-file index, a missing tensor */
 } dm_status;
 
 /* GGML tensor type ids (src/gguf.rs:295-318) on the path. */
