@@ -44,6 +44,7 @@ ERR_FORMAT = -26
 
 # dm_tensor_type (GGML ids)
 F32, F16, Q5_0, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 6, 8, 12, 14, 30
+U8_QUANT, F8_E4M3 = 200, 201  # GLM-5.2 safetensors storage (dm_cuda_matvec_safetensor)
 # dm_moe_family
 FAMILY_GEMMA4, FAMILY_QWEN35_MOE, FAMILY_GLM52 = 1, 2, 3
 
@@ -108,6 +109,7 @@ SIGNATURES = {
     "dm_buffer_free": ([P], None),
     "dm_cuda_matvec": ([P, I32, SZ, SZ, P, SZ, P, SZ, P, SZ], I32),
     "dm_cuda_matvec_mapped": ([P, I32, SZ, SZ, P, SZ, SZ, P, SZ, P, SZ], I32),
+    "dm_cuda_matvec_safetensor": ([P, I32, SZ, SZ, P, SZ, P, SZ, P, SZ, P, SZ], I32),
     "dm_cuda_top_k_softmax": ([P, P, SZ, SZ, P, P], I32),
     "dm_cuda_gelu_mul": ([P, P, P, P, SZ], I32),
     "dm_cuda_silu_mul": ([P, P, P, P, SZ], I32),

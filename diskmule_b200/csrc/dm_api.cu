@@ -341,6 +341,97 @@ int32_t dm_cuda_matvec_mapped(dm_cuda_context *ctx, int32_t kind, size_t rows, s
                     output);
 }
 
+// u8_matrix_encoding (src/metal.rs:1893-1942): int8 rows when rows * columns bytes and
+// one scale per row; otherwise int4 with rows * ceil(columns / 2) bytes and one scale per
+// row (one group spanning the row) or the first group size of {16, 32, 48, 64, 96, 128,
+// 192, 256} (not above `columns`) whose scale count matches.
+static int32_t u8_encoding(size_t rows, size_t columns, size_t encoded_length, size_t scales,
+                           int *enc, int *group) {
+  if (columns && rows > SIZE_MAX / columns) return fail(DM_ERR_OVERFLOW, "matrix size overflows");
+  if (encoded_length == rows * columns && scales == rows) {
+    *enc = dm::kQuantI8Row;
+    *group = 0;
+    return DM_OK;
+  }
+  const size_t int4_bytes = rows * ((columns + 1) / 2);
+  if (encoded_length != int4_bytes)
+    return fail(DM_ERR_BYTE_LENGTH, "U8 quantized matrix requires %zu encoded bytes, got %zu",
+                int4_bytes, encoded_length);
+  if (scales == rows) {
+    *enc = dm::kQuantI4;
+    *group = (int)std::max<size_t>(columns, 1);
+    return DM_OK;
+  }
+  static const size_t groups[8] = {16, 32, 48, 64, 96, 128, 192, 256};
+  for (size_t g : groups) {
+    if (g > columns) break;
+    if (scales == rows * ((columns + g - 1) / g)) {
+      *enc = dm::kQuantI4;
+      *group = (int)g;
+      return DM_OK;
+    }
+  }
+  return fail(DM_ERR_BYTE_LENGTH, "U8 quantization scales require %zu bytes, got %zu", rows * 4,
+              scales * 4);
+}
+
+int32_t dm_cuda_matvec_safetensor(dm_cuda_context *ctx, int32_t dtype, size_t rows,
+                                  size_t columns, const uint8_t *encoded, size_t encoded_length,
+                                  const float *scales, size_t scale_count, const float *input,
+                                  size_t input_length, float *output, size_t output_length) {
+  if (!ctx) return fail(DM_ERR_INVALID_ARGUMENT, "null context");
+  if (dtype == DM_F32 || dtype == DM_F16 || dtype == DM_BF16)
+    return dm_cuda_matvec(ctx, dtype, rows, columns, encoded, encoded_length, input, input_length,
+                          output, output_length);
+  if (dtype != DM_U8_QUANT && dtype != DM_F8_E4M3)
+    return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "safetensors dtype %d is not supported", dtype);
+  if (input_length != columns)
+    return fail(DM_ERR_INPUT_LENGTH, "matvec input has %zu columns; expected %zu", input_length,
+                columns);
+  if (output_length != rows)
+    return fail(DM_ERR_OUTPUT_LENGTH, "matvec output has %zu rows; expected %zu", output_length,
+                rows);
+  int enc = dm::kQuantF8, group = 0;
+  size_t expect_scales = 0;
+  if (dtype == DM_U8_QUANT) {
+    if (!scales)
+      return fail(DM_ERR_BYTE_LENGTH, "U8 quantization scales require %zu bytes, got 0", rows * 4);
+    int32_t rc = u8_encoding(rows, columns, encoded_length, scale_count, &enc, &group);
+    if (rc != DM_OK) return rc;
+    expect_scales = scale_count;
+  } else {
+    if (columns && rows > SIZE_MAX / columns) return fail(DM_ERR_OVERFLOW, "matrix size overflows");
+    if (encoded_length != rows * columns)
+      return fail(DM_ERR_BYTE_LENGTH, "F8_E4M3FN requires %zu encoded bytes, got %zu",
+                  rows * columns, encoded_length);
+    expect_scales = ((rows + 127) / 128) * ((columns + 127) / 128);
+    if (!scales || scale_count != expect_scales)
+      return fail(DM_ERR_VECTOR_LENGTH, "F8_E4M3FN matvec scales: expected %zu, got %zu",
+                  expect_scales, scales ? scale_count : (size_t)0);
+  }
+  if (rows == 0) return DM_OK;
+  if (input_length == 0) return fail(DM_ERR_EMPTY_INPUT, "safetensors matvec requires a non-empty input");
+  if (rows > INT32_MAX || columns > INT32_MAX) return fail(DM_ERR_OVERFLOW, "shape too large");
+  cudaSetDevice(ctx->device);
+  auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+  const size_t need = al(encoded_length) + al(expect_scales * 4) + al(columns * 4) + al(rows * 4);
+  int32_t rc = ctx->ensure_scratch(need);
+  if (rc != DM_OK) return rc;
+  uint8_t *w = (uint8_t *)ctx->scratch;
+  float *sc = (float *)(w + al(encoded_length));
+  float *x = (float *)((uint8_t *)sc + al(expect_scales * 4));
+  float *y = (float *)((uint8_t *)x + al(columns * 4));
+  cudaStream_t s = ctx->stream;
+  DM_CUDA(cudaMemcpyAsync(w, encoded, encoded_length, cudaMemcpyHostToDevice, s), "matrix copy");
+  DM_CUDA(cudaMemcpyAsync(sc, scales, expect_scales * 4, cudaMemcpyHostToDevice, s), "scale copy");
+  DM_CUDA(cudaMemcpyAsync(x, input, columns * 4, cudaMemcpyHostToDevice, s), "input copy");
+  dm::launch_quant_gemv(enc, w, sc, (int)rows, (int)columns, group, x, y, s);
+  DM_CUDA(cudaGetLastError(), "matvec launch");
+  DM_CUDA(cudaMemcpyAsync(output, y, rows * 4, cudaMemcpyDeviceToHost, s), "output copy");
+  DM_CUDA(cudaStreamSynchronize(s), "matvec");
+  return DM_OK;
+}
+
 int32_t dm_cuda_top_k_softmax(dm_cuda_context *ctx, const float *logits, size_t length, size_t k,
                               uint32_t *indices, float *probabilities) {
   if (!ctx) return fail(DM_ERR_INVALID_ARGUMENT, "null context");

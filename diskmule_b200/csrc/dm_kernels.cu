@@ -1618,6 +1618,60 @@ __global__ void __launch_bounds__(256) gemv_dense_kernel(const uint8_t *w, int k
   if (lane == 0) y[warp] = acc;
 }
 
+// GLM-5.2 checkpoint encodings, one warp per row (lanes stride the columns, so a
+// warp's byte loads are one coalesced 32-byte piece), products summed with fma and a
+// warp reduction (a tolerance-bound result, like the reference's Metal kernels,
+// metal/kernels.metal:273-344):
+//   kQuantI8Row:  w = int8 * scales[row]
+//   kQuantI4:     w = (nibble - 8) * scales[row * ceil(cols / group) + col / group],
+//                 low nibble for even columns
+//   kQuantF8:     w = e4m3fn(byte) * scales[(row / 128) * ceil(cols / 128) + col / 128],
+//                 decoded through a 256-entry table built per block; the two invalid
+//                 codes (exponent 15, fraction 7) decode to NaN.
+__global__ void __launch_bounds__(256) quant_gemv_kernel(int enc, const uint8_t *w,
+                                                        const float *scales, int rows, int cols,
+                                                        int group, const float *x, float *y) {
+  __shared__ float lut[256];
+  if (enc == kQuantF8) {
+    const int v = threadIdx.x;
+    const int e = (v >> 3) & 15, f = v & 7;
+    const float mag = e == 0 ? (float)f * 0.001953125f
+                             : __fmul_rn(1.0f + (float)f * 0.125f, ldexpf(1.0f, e - 7));
+    lut[v] = (e == 15 && f == 7) ? __int_as_float(0x7fc00000) : ((v & 0x80) ? -mag : mag);
+    __syncthreads();
+  }
+  const int row = (int)(blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float acc = 0.0f;
+  if (enc == kQuantI8Row) {
+    const int8_t *q = reinterpret_cast<const int8_t *>(w) + (size_t)row * cols;
+    const float s = scales[row];
+    for (int c = lane; c < cols; c += 32) acc = fmaf(__fmul_rn((float)q[c], s), x[c], acc);
+  } else if (enc == kQuantI4) {
+    const int rb = (cols + 1) / 2, sc = (cols + group - 1) / group;
+    const uint8_t *q = w + (size_t)row * rb;
+    const float *srow = scales + (size_t)row * sc;
+    for (int c = lane; c < cols; c += 32) {
+      const uint8_t b = q[c >> 1];
+      const int nib = (c & 1) ? (b >> 4) : (b & 15);
+      acc = fmaf(__fmul_rn((float)(nib - 8), srow[c / group]), x[c], acc);
+    }
+  } else {
+    const uint8_t *q = w + (size_t)row * cols;
+    const float *srow = scales + (size_t)(row / 128) * ((cols + 127) / 128);
+    for (int c = lane; c < cols; c += 32)
+      acc = fmaf(__fmul_rn(lut[q[c]], srow[c >> 7]), x[c], acc);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) y[row] = acc;
+}
+
+int launch_quant_gemv(int enc, const uint8_t *w, const float *scales, int rows, int cols,
+                      int group, const float *x, float *y, cudaStream_t stream) {
+  quant_gemv_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(enc, w, scales, rows, cols, group, x, y);
+  return 1;
+}
+
 int launch_gemv(int kind, const uint8_t *w, int rows, int cols, const float *x, float *y,
                 cudaStream_t stream) {
   int blocks = (rows + 7) / 8;

@@ -102,6 +102,11 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
                    const GemvPlan *gemv, const TcPlan *tc = nullptr, int mode = kRunAll);
 int launch_gemv(int kind, const uint8_t *w, int rows, int cols, const float *x, float *y,
                 cudaStream_t stream);
+// GLM-5.2 checkpoint encodings (int8 rows, grouped int4, fp8 e4m3 with 128 x 128 block
+// scales) times x: one launch.
+enum QuantEncoding { kQuantI8Row = 1, kQuantI4 = 2, kQuantF8 = 3 };
+int launch_quant_gemv(int enc, const uint8_t *w, const float *scales, int rows, int cols,
+                      int group, const float *x, float *y, cudaStream_t stream);
 int launch_topk_softmax(const float *logits, int n, int k, uint32_t *idx, float *prob,
                         int32_t *status, cudaStream_t stream);
 int launch_elementwise(int op, const float *a, const float *b, float *out, int n,

@@ -1667,7 +1667,7 @@ static bool use_pairs() {
   static int v = -1;
   if (v < 0) {
     const char *e = getenv("DISKMULE_CUDA_TC_PAIRS");
-    v = e && (!strcmp(e, "1") || !strcmp(e, "true"));
+    v = !(e && (!strcmp(e, "0") || !strcmp(e, "false")));
   }
   return v == 1;
 }
@@ -1679,7 +1679,8 @@ static int launch_bf16(const ForwardArgs &a, const TcPlan &p, const TcWeights &w
   const int rows_bound = a.T * a.k + (a.shared ? a.T : 0);
   tc::gather_bf16_kernel<<<rows_bound, 256, 0, s>>>(a, reinterpret_cast<__nv_bfloat16 *>(p.x16));
   if (use_pairs() && w.f16_down && a.I % 128 == 0 && a.H % 256 == 0) {
-    // CTA pairs: 256-row weight tiles over both gate/up and down
+    // CTA pairs for the gate/up product: 256-row weight tiles (DISKMULE_CUDA_TC_PAIRS=0
+    // turns them off)
     auto up = tc::tc_bf16_pair_kernel<true, false>;
     ensure_smem_limit((const void *)up);
     up<<<pair_grid(p, a.I / 128), tc::kBfThreads, tc::PairCfg::kSmem, s>>>(
@@ -1689,10 +1690,12 @@ static int launch_bf16(const ForwardArgs &a, const TcPlan &p, const TcWeights &w
     if (hsmem > 48 * 1024) ensure_smem_limit((const void *)tc::pack_kernel<false>);
     tc::pack_kernel<false><<<(rows_bound + tc::kPackRows - 1) / tc::kPackRows, 32 * tc::kPackRows,
                              hsmem, s>>>(a, p.gu, p.h16, p.h_inv, a.I, 0);
-    auto down = tc::tc_bf16_pair_kernel<false, true>;
+    // the down product (K = I: few K steps per unit) measured faster on single CTAs
+    auto down = tc::tc_bf16_kernel<false, NT, false, 1, true>;
     ensure_smem_limit((const void *)down);
-    down<<<pair_grid(p, a.H / 256), tc::kBfThreads, tc::PairCfg::kSmem, s>>>(
-        p.h1_map_pair, w.down16, w.sh_down16, a, w.side, p.gu, p.h_inv);
+    const int grid = std::max(1, std::min(p.n_sm, p.max_items * (a.H / 128)));
+    down<<<grid, tc::kBfThreads, tc::BfCfg<NT>::kSmem, s>>>(p.h1_map, w.down16, w.sh_down16, a,
+                                                                w.side, p.gu, p.h_inv);
     return 4;
   }
   {

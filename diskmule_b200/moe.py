@@ -113,6 +113,19 @@ class CudaContext:
 
     matvec_owned = matvec_mapped
 
+    def matvec_safetensor(self, dtype, rows, columns, encoded, scales, input):
+        """MetalContext::matvec_safetensor (src/metal.rs:883-992): F32 / F16 / BF16 rows,
+        or the GLM-5.2 checkpoint storage N.U8_QUANT (int8 rows / grouped int4 with `.qs`
+        scales) and N.F8_E4M3 (with 128 x 128 block `_scale_inv` scales)."""
+        enc = np.ascontiguousarray(np.frombuffer(encoded, np.uint8) if isinstance(encoded, (bytes, bytearray)) else encoded).view(np.uint8).reshape(-1)
+        sc = None if scales is None else np.ascontiguousarray(scales, dtype=np.float32)
+        x = np.ascontiguousarray(input, dtype=np.float32)
+        out = np.zeros(rows, dtype=np.float32)
+        check(N.lib().dm_cuda_matvec_safetensor(self._h, dtype, rows, columns, _ptr(enc), enc.size,
+                                                _ptr(sc), 0 if sc is None else sc.size, _ptr(x),
+                                                x.size, _ptr(out), out.size))
+        return out
+
     def top_k_softmax(self, logits, k):
         lg = np.ascontiguousarray(logits, dtype=np.float32)
         idx = np.zeros(max(k, 1), dtype=np.uint32)

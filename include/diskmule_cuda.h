@@ -73,6 +73,9 @@ typedef enum {
   DM_Q4_K = 12,
   DM_Q6_K = 14,
   DM_BF16 = 30,
+  /* safetensors storage of the GLM-5.2 checkpoints (src/glm52/quant.rs, SafeDtype) */
+  DM_U8_QUANT = 200, /* U8: int8 rows or grouped int4, with a flat F32 `.qs` scale tensor */
+  DM_F8_E4M3 = 201,  /* F8_E4M3 with an F32 `_scale_inv` tensor of 128 x 128 blocks */
 } dm_tensor_type;
 
 typedef struct dm_cuda_context dm_cuda_context;
@@ -121,6 +124,17 @@ DM_API int32_t dm_cuda_matvec_mapped(dm_cuda_context *ctx, int32_t kind, size_t 
                               size_t columns, const dm_buffer *mapped, size_t offset,
                               size_t encoded_length, const float *input, size_t input_length,
                               float *output, size_t output_length);
+/* MetalContext::matvec_safetensor (src/metal.rs:883-992, matvec_u8 :1070-1147):
+ * F32 / F16 / BF16 as dm_cuda_matvec; DM_U8_QUANT resolved to int8 rows or grouped int4
+ * from the byte and scale counts as u8_matrix_encoding does (src/metal.rs:1893-1942);
+ * DM_F8_E4M3 with [ceil(rows/128)][ceil(columns/128)] scales. Values decode as the CPU
+ * reference's rows (src/glm52/cpu.rs:1278-1410); the dot products are f32 (tolerance). */
+DM_API int32_t dm_cuda_matvec_safetensor(dm_cuda_context *ctx, int32_t dtype, size_t rows,
+                                         size_t columns, const uint8_t *encoded,
+                                         size_t encoded_length, const float *scales,
+                                         size_t scale_count, const float *input,
+                                         size_t input_length, float *output,
+                                         size_t output_length);
 /* MetalContext::top_k_softmax (src/metal.rs:1392-1434); indices are bit-exact with
  * cpu::top_k_softmax (src/cpu.rs:234-260). */
 DM_API int32_t dm_cuda_top_k_softmax(dm_cuda_context *ctx, const float *logits, size_t length,

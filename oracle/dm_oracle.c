@@ -430,6 +430,117 @@ int dmo_glm_matvec(int kind, size_t rows, size_t columns, const uint8_t *encoded
   return DMO_OK;
 }
 
+/* GLM-5.2 checkpoint encodings.
+ * decode_f8_e4m3fn (src/glm52/cpu.rs:1397-1410): finite-only E4M3; 0x7f / 0xff (exponent
+ * 15, fraction 7) are invalid. Subnormals fraction * 2^-9, normals (1 + f/8) * 2^(e-7). */
+int dmo_f8_e4m3fn(uint8_t v, float *out) {
+  const float sign = (v & 0x80) ? -1.0f : 1.0f;
+  const int e = (v >> 3) & 0x0f, f = v & 0x07;
+  if (e == 0x0f && f == 0x07) return DMO_ERR_NONFINITE;
+  const float mag = e == 0 ? (float)f * ldexpf(1.0f, -9) : (1.0f + (float)f / 8.0f) * ldexpf(1.0f, e - 7);
+  *out = sign * mag;
+  return DMO_OK;
+}
+
+/* matching_quantizations + resolve_quantization (src/glm52/quant.rs:63-76, :148-176):
+ * int8 rows when rows * columns bytes and one scale per row, else int4 grouped with the
+ * first group size of {16, 32, 48, 64, 96, 128, 192, 256} whose scale count matches.
+ * kind: 1 int8 row, 2 int4 grouped. */
+int dmo_glm_u8_encoding(size_t rows, size_t columns, size_t encoded_bytes, size_t scales,
+                        int *kind, int *group_size) {
+  static const size_t groups[8] = {16, 32, 48, 64, 96, 128, 192, 256};
+  if (rows * columns == encoded_bytes && scales == rows) {
+    *kind = 1;
+    *group_size = 0;
+    return DMO_OK;
+  }
+  if (rows * ((columns + 1) / 2) == encoded_bytes) {
+    for (int i = 0; i < 8; i++)
+      if (rows * ((columns + groups[i] - 1) / groups[i]) == scales) {
+        *kind = 2;
+        *group_size = (int)groups[i];
+        return DMO_OK;
+      }
+  }
+  return DMO_ERR_BYTE_LENGTH;
+}
+
+/* One decoded row (read_quantized_row, src/glm52/cpu.rs:1339-1395; read_fp8_row,
+ * :1278-1337). fp8: scales [ceil(rows/128)][ceil(columns/128)] of `scale_inv` values. */
+static int quant_row(int enc, int group, size_t rows, size_t columns, const uint8_t *w,
+                     const float *scales, size_t r, float *out) {
+  if (enc == 1) {
+    const uint8_t *q = w + r * columns;
+    for (size_t c = 0; c < columns; c++) out[c] = (float)(int8_t)q[c] * scales[r];
+  } else if (enc == 2) {
+    const size_t rb = (columns + 1) / 2, sc = (columns + (size_t)group - 1) / (size_t)group;
+    const uint8_t *q = w + r * rb;
+    for (size_t c = 0; c < columns; c++) {
+      const uint8_t b = q[c / 2];
+      const int nib = (c % 2 == 0) ? (b & 0x0f) : (b >> 4);
+      out[c] = ((float)nib - 8.0f) * scales[r * sc + c / (size_t)group];
+    }
+  } else {
+    const size_t sc = (columns + 127) / 128;
+    const uint8_t *q = w + r * columns;
+    for (size_t c = 0; c < columns; c++) {
+      float d;
+      if (dmo_f8_e4m3fn(q[c], &d) != DMO_OK) return DMO_ERR_NONFINITE;
+      out[c] = d * scales[(r / 128) * sc + c / 128];
+    }
+  }
+  (void)rows;
+  return DMO_OK;
+}
+
+/* TensorReader::matvec_into over the quantized dtypes (src/glm52/cpu.rs:1121-1187):
+ * each row decoded, then a sequential non-fused sum of `weight * value` from -0.0.
+ * fp8 != 0: F8_E4M3 weights [rows][columns] with block scales; otherwise U8 storage
+ * (int8 row or int4 grouped, resolved as above) with `.qs` scales. */
+int dmo_glm_quant_matvec(int fp8, size_t rows, size_t columns, const uint8_t *encoded,
+                         size_t encoded_bytes, const float *scales, size_t n_scales,
+                         const float *input, float *output, int threads) {
+  int enc = 3, group = 0;
+  if (!fp8) {
+    int rc = dmo_glm_u8_encoding(rows, columns, encoded_bytes, n_scales, &enc, &group);
+    if (rc != DMO_OK) return rc;
+  } else {
+    if (encoded_bytes != rows * columns) return DMO_ERR_BYTE_LENGTH;
+    if (n_scales != ((rows + 127) / 128) * ((columns + 127) / 128)) return DMO_ERR_BYTE_LENGTH;
+  }
+  if (threads < 1) threads = 1;
+  int bad = 0;
+#pragma omp parallel num_threads(threads) if (threads > 1 && rows > 1) reduction(| : bad)
+  {
+    float *row = (float *)malloc((columns ? columns : 1) * sizeof(float));
+#pragma omp for schedule(static)
+    for (long r = 0; r < (long)rows; r++) {
+      if (quant_row(enc, group, rows, columns, encoded, scales, (size_t)r, row) != DMO_OK) {
+        bad = 1;
+        continue;
+      }
+      float sum = -0.0f;
+      for (size_t c = 0; c < columns; c++) sum = sum + row[c] * input[c];
+      output[r] = sum;
+    }
+    free(row);
+  }
+  return bad ? DMO_ERR_NONFINITE : DMO_OK;
+}
+
+/* A decoded row (matrix_row_into) of the same encodings. */
+int dmo_glm_quant_row(int fp8, size_t rows, size_t columns, const uint8_t *encoded,
+                      size_t encoded_bytes, const float *scales, size_t n_scales, size_t r,
+                      float *out) {
+  int enc = 3, group = 0;
+  if (!fp8) {
+    int rc = dmo_glm_u8_encoding(rows, columns, encoded_bytes, n_scales, &enc, &group);
+    if (rc != DMO_OK) return rc;
+  }
+  if (r >= rows) return DMO_ERR_OUTPUT_LENGTH;
+  return quant_row(enc, group, rows, columns, encoded, scales, r, out);
+}
+
 /* Sigmoid + correction-bias selection.
  *   n_groups == 1: src/glm52/cpu.rs:731-754 exactly (sigmoid, `choice = weight +
  *   correction`, non-finite -> error, sort by choice desc / index asc, truncate,

@@ -82,6 +82,15 @@ int dmo_argmax(const float *values, size_t n, size_t *index);
 /* ---- GLM-5.2 helpers (src/glm52/cpu.rs, src/glm52/expert.rs) ---- */
 int dmo_glm_rms_norm(const float *input, const float *weight, size_t n, float epsilon,
                      float *output);
+int dmo_f8_e4m3fn(uint8_t v, float *out);
+int dmo_glm_u8_encoding(size_t rows, size_t columns, size_t encoded_bytes, size_t scales,
+                        int *kind, int *group_size);
+int dmo_glm_quant_matvec(int fp8, size_t rows, size_t columns, const uint8_t *encoded,
+                         size_t encoded_bytes, const float *scales, size_t n_scales,
+                         const float *input, float *output, int threads);
+int dmo_glm_quant_row(int fp8, size_t rows, size_t columns, const uint8_t *encoded,
+                      size_t encoded_bytes, const float *scales, size_t n_scales, size_t r,
+                      float *out);
 int dmo_glm_matvec(int kind, size_t rows, size_t columns, const uint8_t *encoded,
                    const float *input, float *output, int threads);
 float dmo_glm_sigmoid(float value);

@@ -90,6 +90,10 @@ def _declare(L):
     L.dmo_lru_acquire.argtypes = [P, I32, I32, C.POINTER(I32), C.POINTER(I32)]
     L.dmo_lru_set_pinned.argtypes = [P, I32, I32, I32]
     L.dmo_lru_stats.argtypes = [P, P]
+    L.dmo_f8_e4m3fn.argtypes = [C.c_uint8, C.POINTER(C.c_float)]
+    L.dmo_glm_u8_encoding.argtypes = [SZ, SZ, SZ, SZ, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+    L.dmo_glm_quant_matvec.argtypes = [C.c_int, SZ, SZ, P, SZ, P, SZ, P, P, C.c_int]
+    L.dmo_glm_quant_row.argtypes = [C.c_int, SZ, SZ, P, SZ, P, SZ, SZ, P]
     L.dmo_synth_fill.argtypes = [I32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_float,
                                  C.c_float, P]
     L.dmo_synth_fill.restype = I32
@@ -199,6 +203,38 @@ def glm_matvec(kind: int, rows: int, columns: int, encoded, x, threads: int = 1)
     x = _f32(x)
     out = np.zeros(rows, dtype=np.float32)
     rc = lib().dmo_glm_matvec(kind, rows, columns, _ptr(enc), _ptr(x), _ptr(out), threads)
+    return rc, out
+
+
+def f8_e4m3fn(byte: int):
+    v = C.c_float()
+    rc = lib().dmo_f8_e4m3fn(byte, C.byref(v))
+    return None if rc != OK else v.value
+
+
+def glm_u8_encoding(rows, columns, encoded_bytes, scales):
+    """(1, 0) int8 rows, (2, group) int4 grouped, or None (src/glm52/quant.rs)."""
+    k, g = C.c_int(), C.c_int()
+    rc = lib().dmo_glm_u8_encoding(rows, columns, encoded_bytes, scales, C.byref(k), C.byref(g))
+    return None if rc != OK else (k.value, g.value)
+
+
+def glm_quant_matvec(fp8: bool, rows: int, columns: int, encoded, scales, x, threads: int = 1):
+    enc = _u8(encoded)
+    sc = _f32(scales)
+    xv = _f32(x)
+    out = np.zeros(rows, np.float32)
+    rc = lib().dmo_glm_quant_matvec(int(fp8), rows, columns, _ptr(enc), enc.size, _ptr(sc),
+                                    sc.size, _ptr(xv), _ptr(out), threads)
+    return rc, out
+
+
+def glm_quant_row(fp8: bool, rows: int, columns: int, encoded, scales, r: int):
+    enc = _u8(encoded)
+    sc = _f32(scales)
+    out = np.zeros(columns, np.float32)
+    rc = lib().dmo_glm_quant_row(int(fp8), rows, columns, _ptr(enc), enc.size, _ptr(sc), sc.size,
+                                 r, _ptr(out))
     return rc, out
 
 

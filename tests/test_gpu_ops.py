@@ -8,6 +8,7 @@ import numpy as np
 import pytest
 
 from diskmule_b200 import _native as N
+from diskmule_b200._native import DmError
 from diskmule_b200.moe import CudaContext
 from diskmule_b200.synthetic import TensorSpec
 from oracle import oracle as O
@@ -132,3 +133,58 @@ def test_synthetic_device_bytes_equal_host_bytes(ctx, kind):
     spec.device_fill(buf.device_pointer)
     ctx.synchronize()
     assert np.array_equal(buf.read(), spec.host())
+
+
+# ---------------------------------------------------------------------------
+# GLM-5.2 checkpoint encodings (dm_cuda_matvec_safetensor)
+# ---------------------------------------------------------------------------
+
+def _glm_quant_case(kind, rows, cols, group, rng):
+    if kind == "fp8":
+        enc = rng.integers(0, 256, rows * cols, dtype=np.uint8)
+        enc[(enc & 0x7F) == 0x7F] = 0x38  # no invalid codes
+        scales = rng.uniform(0.5, 2.0, ((rows + 127) // 128) * ((cols + 127) // 128)).astype(np.float32)
+    elif kind == "i8":
+        enc = rng.integers(0, 256, rows * cols, dtype=np.uint8)
+        scales = rng.uniform(1e-3, 1e-2, rows).astype(np.float32)
+    else:
+        enc = rng.integers(0, 256, rows * ((cols + 1) // 2), dtype=np.uint8)
+        scales = rng.uniform(1e-3, 1e-2, rows * ((cols + group - 1) // group)).astype(np.float32)
+    x = rng.standard_normal(cols).astype(np.float32)
+    return enc, scales, x
+
+
+def test_safetensor_matvec_known_answers(ctx):
+    w = np.full(129 * 130, 0x38, np.uint8)
+    x = np.ones(130, np.float32)
+    x[129] = 2.0
+    y = ctx.matvec_safetensor(N.F8_E4M3, 129, 130, w, [2.0, 3.0, 5.0, 7.0], x)
+    np.testing.assert_allclose(y[:128], 265.0, atol=1e-5, rtol=0)
+    assert abs(y[128] - 661.0) < 1e-5
+    i8 = np.array([-127, 0, 127, -2, 3, 4], np.int8).view(np.uint8)
+    np.testing.assert_allclose(ctx.matvec_safetensor(N.U8_QUANT, 2, 3, i8, [0.1, 0.5], [1, 2, -1]),
+                               [-25.4, 0.0], atol=1e-5)
+    i4 = np.array([0x40, 0xC8, 0x0F, 0xA9, 0xCB, 0x0D], np.uint8)
+    np.testing.assert_allclose(ctx.matvec_safetensor(N.U8_QUANT, 2, 5, i4, [0.5, 2.0], [1] * 5),
+                               [-0.5, 30.0], atol=1e-5)
+    with pytest.raises(DmError) as e:
+        ctx.matvec_safetensor(N.U8_QUANT, 1, 256, np.zeros(196, np.uint8), [6.0], np.ones(256))
+    assert e.value.status == N.ERR_BYTE_LENGTH
+
+
+@pytest.mark.parametrize("kind,rows,cols,group", [
+    ("i8", 300, 2048, 0), ("i4", 257, 6144, 32), ("i4", 64, 1000, 128), ("i4", 33, 515, 16),
+    ("fp8", 384, 2048, 0), ("fp8", 129, 300, 0)])
+def test_safetensor_matvec_matches_the_oracle(ctx, kind, rows, cols, group):
+    rng = np.random.default_rng(rows * 7 + cols)
+    enc, scales, x = _glm_quant_case(kind, rows, cols, group, rng)
+    dtype = N.F8_E4M3 if kind == "fp8" else N.U8_QUANT
+    y = ctx.matvec_safetensor(dtype, rows, cols, enc, scales, x)
+    rc, y_ref = O.glm_quant_matvec(kind == "fp8", rows, cols, enc, scales, x, threads=8)
+    assert rc == O.OK
+    # per row: |error| within 1e-5 of the row's sum of |w * x| (reordered f32 sums)
+    mag = np.zeros(rows)
+    for r in range(rows):
+        _, row = O.glm_quant_row(kind == "fp8", rows, cols, enc, scales, r)
+        mag[r] = np.abs(row.astype(np.float64) * x).sum()
+    assert np.all(np.abs(y.astype(np.float64) - y_ref) <= 1e-5 * mag + 1e-30)
