@@ -131,6 +131,10 @@ SIGNATURES = {
     "dm_moe_route": ([P, P, I32, P, P, P, P, P], I32),
     "dm_moe_expert_rows": ([P, P, P, I32, P, P], I32),
     "dm_moe_combine_rows": ([P, I32, P, P, P, P, P, P], I32),
+    "dm_gemma_ffn_create": ([P, P, C.POINTER(P)], I32),
+    "dm_gemma_ffn_forward": ([P, P, P, I32, P, P, P], I32),
+    "dm_gemma_ffn_status": ([P, P], I32),
+    "dm_gemma_ffn_destroy": ([P], None),
     "dm_ep_create": ([P, I32, I32, I32, C.POINTER(P)], I32),
     "dm_ep_ipc_handle": ([P, P], I32),
     "dm_ep_connect_ipc": ([P, P], I32),

@@ -17,7 +17,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdiskmule_cuda.so")
 BUILD = os.path.join(HERE, "_build")
 
-SOURCES = ["dm_kernels.cu", "dm_gemv.cu", "dm_tc.cu", "dm_api.cu", "dm_cache.cu", "dm_stack.cu", "dm_synth.cu", "dm_ep.cu", "dm_gguf.cu"]
+SOURCES = ["dm_kernels.cu", "dm_gemv.cu", "dm_tc.cu", "dm_api.cu", "dm_cache.cu", "dm_stack.cu", "dm_synth.cu", "dm_ep.cu", "dm_gguf.cu", "dm_gemma.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -169,6 +169,40 @@ class CudaContext:
             pass
 
 
+class GemmaFfnDesc(C.Structure):
+    _fields_ = [("width", C.c_int32), ("gate_type", C.c_int32), ("up_type", C.c_int32),
+                ("down_type", C.c_int32), ("gate", C.c_void_p), ("up", C.c_void_p),
+                ("down", C.c_void_p), ("feed_forward_norm", C.c_void_p),
+                ("shared_post_norm", C.c_void_p), ("routed_post_norm", C.c_void_p),
+                ("post_feed_forward_norm", C.c_void_p), ("layer_output_scale", C.c_float)]
+
+
+class GemmaFfnBlock:
+    """Gemma 4's whole feed-forward block (dm_gemma_ffn_*): the routed `layer` plus the
+    dense shared FFN and the norms around it (src/gemma4/cpu.rs:547-620)."""
+
+    def __init__(self, layer, desc: GemmaFfnDesc):
+        self.layer, self.desc = layer, desc
+        h = C.c_void_p()
+        check(N.lib().dm_gemma_ffn_create(layer.handle, C.byref(desc), C.byref(h)))
+        self._h = h
+
+    def forward(self, x_ptr: int, hidden_ptr: int, tokens: int, sel_idx_ptr=0, sel_w_ptr=0,
+                stream: int = 0):
+        check(N.lib().dm_gemma_ffn_forward(self._h, C.c_void_p(x_ptr), C.c_void_p(hidden_ptr),
+                                           tokens, C.c_void_p(sel_idx_ptr) if sel_idx_ptr else None,
+                                           C.c_void_p(sel_w_ptr) if sel_w_ptr else None,
+                                           C.c_void_p(stream) if stream else None))
+
+    def status(self, stream: int = 0):
+        check(N.lib().dm_gemma_ffn_status(self._h, C.c_void_p(stream) if stream else None))
+
+    def close(self):
+        if self._h:
+            N.lib().dm_gemma_ffn_destroy(self._h)
+            self._h = None
+
+
 class MoeLayer:
     """The batched routed-expert block behind dm_moe_layer_create / dm_moe_forward.
 

@@ -312,6 +312,76 @@ def build_layer(ctx: CudaContext, name: str, seed: int = 1, logit_bias=None,
     return sl
 
 
+GEMMA_FFN_WIDTH = {"gemma4": 2112, "gemma4-small": 192, "gemma4-small-q8": 192}
+
+
+@dataclass
+class SyntheticGemmaBlock:
+    """A synthetic Gemma 4 feed-forward block: a routed layer plus the dense shared FFN
+    (Q4_K gate / up [W][H], Q5_0 down [H][W]; Gemma-4-26B's feed_forward_length is 2112),
+    the four norm vectors U[0.5, 1.5) and a layer output scale."""
+
+    sl: SyntheticLayer
+    width: int
+    specs: dict
+    norms: dict
+    layer_scale: float
+    buffers: dict = field(default_factory=dict)
+    block: object = None
+
+    def host_ffn(self) -> dict:
+        """Oracle inputs of the shared FFN and norms (oracle.gemma_ffn_block's `f`)."""
+        f = dict(width=self.width, gate_type=self.specs["gate"].kind,
+                 up_type=self.specs["up"].kind, down_type=self.specs["down"].kind,
+                 gate=self.specs["gate"].host(), up=self.specs["up"].host(),
+                 down=self.specs["down"].host(), layer_output_scale=self.layer_scale)
+        f.update(self.norms)
+        return f
+
+    def close(self):
+        if self.block is not None:
+            self.block.close()
+            self.block = None
+        for b in self.buffers.values():
+            b.free()
+        self.buffers.clear()
+        self.sl.close()
+
+
+def build_gemma_block(ctx: CudaContext, name: str = "gemma4", seed: int = 1,
+                      logit_bias=None) -> SyntheticGemmaBlock:
+    from .moe import GemmaFfnBlock, GemmaFfnDesc
+    cfg = CONFIGS[name]
+    H, W = cfg["hidden"], GEMMA_FFN_WIDTH[name]
+    sl = build_layer(ctx, name, seed, logit_bias=logit_bias)
+    s = lambda i: seed * 1009 + 50 + i  # noqa: E731
+    specs = {"gate": TensorSpec("ffn_gate", cfg["gate_type"], W, H, 1, s(1)),
+             "up": TensorSpec("ffn_up", cfg["gate_type"], W, H, 1, s(2)),
+             "down": TensorSpec("ffn_down", cfg["down_type"], H, W, 1, s(3))}
+    rng = np.random.default_rng(seed * 7919 + 23)
+    norms = {n: rng.uniform(0.5, 1.5, H).astype(np.float32)
+             for n in ("feed_forward_norm", "shared_post_norm", "routed_post_norm",
+                       "post_feed_forward_norm")}
+    gb = SyntheticGemmaBlock(sl, W, specs, norms, float(rng.uniform(0.5, 1.5)))
+    for key, spec in specs.items():
+        buf = ctx.new_owned_buffer(spec.nbytes)
+        spec.device_fill(buf.device_pointer)
+        gb.buffers[key] = buf
+    for key, v in norms.items():
+        gb.buffers[key] = ctx.map_read_only(v)
+    ctx.synchronize()
+    d = GemmaFfnDesc()
+    d.width = W
+    d.gate_type = d.up_type = cfg["gate_type"]
+    d.down_type = cfg["down_type"]
+    d.gate, d.up, d.down = (gb.buffers[k].device_pointer for k in ("gate", "up", "down"))
+    for key in norms:
+        setattr(d, key, gb.buffers[key].device_pointer)
+    d.layer_output_scale = gb.layer_scale
+    gb.block = GemmaFfnBlock(sl.layer, d)
+    return gb
+
+
 EXPERT_TENSORS = {"gemma4": ("gate", "down"), "qwen35": ("gate", "up", "down"),
                   "glm52": ("gate", "up", "down")}
 

@@ -305,6 +305,32 @@ DM_API int32_t dm_moe_combine_rows(dm_moe_layer *layer, int32_t tokens, const ui
                                    const float *sel_weight, const float *logits,
                                    const float *pair_out, float *y, void *stream);
 
+/* ---- Gemma 4's whole feed-forward block ---------------------------------------------
+ * The routed layer above plus what surrounds it in the reference (src/gemma4/cpu.rs:
+ * 547-558, :613-620): the dense shared FFN on rms_norm(x, feed_forward_norm)
+ * (feed_forward, :693-712: gelu_tanh(gate) * up, then down), its post norm, the routed
+ * branch's post norm, their sum and post feed-forward norm, the residual add and the
+ * layer output scale. x and hidden are [tokens, hidden] f32 device rows; sel_idx /
+ * sel_weight as in dm_moe_forward. Weight pointers are device memory in GGUF row
+ * layout ([width][hidden] gate and up, [hidden][width] down); norm vectors [hidden] f32.
+ * The block keeps pointers, not copies (the gate and up rows are copied once into one
+ * fused buffer). dm_gemma_ffn_status waits for `stream` and reports a non-finite norm. */
+typedef struct {
+  int32_t width;                 /* feed_forward_length */
+  int32_t gate_type, up_type, down_type;
+  const void *gate, *up, *down;
+  const float *feed_forward_norm, *shared_post_norm, *routed_post_norm, *post_feed_forward_norm;
+  float layer_output_scale;
+} dm_gemma_ffn_desc;
+typedef struct dm_gemma_ffn dm_gemma_ffn;
+DM_API int32_t dm_gemma_ffn_create(dm_moe_layer *routed, const dm_gemma_ffn_desc *desc,
+                                   dm_gemma_ffn **out);
+DM_API int32_t dm_gemma_ffn_forward(dm_gemma_ffn *block, const float *x, float *hidden,
+                                    int32_t tokens, uint32_t *sel_idx, float *sel_weight,
+                                    void *stream);
+DM_API int32_t dm_gemma_ffn_status(dm_gemma_ffn *block, void *stream);
+DM_API void dm_gemma_ffn_destroy(dm_gemma_ffn *block);
+
 /* ---- expert parallelism over NVLink peer memory -----------------------------------
  * The same split as above with the token exchange done by this library's own kernels:
  * each rank stores token rows straight into the other ranks' memory (CUDA IPC mappings

@@ -724,6 +724,52 @@ int dmo_gemma_moe(const dmo_gemma_layer *L, const float *x, size_t tokens, float
                          tokens == 1 ? threads : 1))
 }
 
+/* One token of the whole Gemma 4 feed-forward block (src/gemma4/cpu.rs:547-620). */
+static int gemma_ffn_token(const dmo_gemma_ffn *F, const dmo_gemma_layer *L, const float *x,
+                           float *hidden, uint32_t *sel_idx, float *sel_prob, int threads) {
+  const size_t H = (size_t)L->hidden, W = (size_t)F->width;
+  float *shared_input = (float *)malloc(H * sizeof(float));
+  float *gate = (float *)malloc(W * sizeof(float));
+  float *up = (float *)malloc(W * sizeof(float));
+  float *shared_raw = (float *)malloc(H * sizeof(float));
+  float *shared = (float *)malloc(H * sizeof(float));
+  float *routed_raw = (float *)malloc(H * sizeof(float));
+  float *routed = (float *)malloc(H * sizeof(float));
+  float *combined = (float *)malloc(H * sizeof(float));
+  int rc = dmo_rms_norm(x, F->feed_forward_norm, H, L->epsilon, shared_input);
+  if (rc == DMO_OK)
+    rc = dmo_matvec(F->gate_type, W, H, F->gate, W * row_bytes_of(F->gate_type, H), shared_input,
+                    H, gate, W, threads);
+  if (rc == DMO_OK)
+    rc = dmo_matvec(F->up_type, W, H, F->up, W * row_bytes_of(F->up_type, H), shared_input, H,
+                    up, W, threads);
+  if (rc == DMO_OK) {
+    for (size_t i = 0; i < W; i++) gate[i] = dmo_gelu_tanh(gate[i]) * up[i];
+    rc = dmo_matvec(F->down_type, H, W, F->down, H * row_bytes_of(F->down_type, W), gate, W,
+                    shared_raw, H, threads);
+  }
+  if (rc == DMO_OK) rc = dmo_rms_norm(shared_raw, F->shared_post_norm, H, L->epsilon, shared);
+  if (rc == DMO_OK) rc = gemma_token(L, x, routed_raw, sel_idx, sel_prob, threads);
+  if (rc == DMO_OK) rc = dmo_rms_norm(routed_raw, F->routed_post_norm, H, L->epsilon, routed);
+  if (rc == DMO_OK) {
+    for (size_t i = 0; i < H; i++) routed_raw[i] = shared[i] + routed[i];  /* combined */
+    rc = dmo_rms_norm(routed_raw, F->post_feed_forward_norm, H, L->epsilon, combined);
+  }
+  if (rc == DMO_OK)
+    for (size_t i = 0; i < H; i++) hidden[i] = (x[i] + combined[i]) * F->layer_output_scale;
+  free(shared_input); free(gate); free(up); free(shared_raw); free(shared);
+  free(routed_raw); free(routed); free(combined);
+  return rc;
+}
+
+int dmo_gemma_ffn_block(const dmo_gemma_ffn *F, const dmo_gemma_layer *L, const float *x,
+                        size_t tokens, float *hidden, uint32_t *sel_idx, float *sel_prob,
+                        int threads) {
+  size_t H = (size_t)L->hidden, k = (size_t)L->top_k;
+  TOKEN_LOOP(gemma_ffn_token(F, L, x + t * H, hidden + t * H, sel_idx + t * k, sel_prob + t * k,
+                             tokens == 1 ? threads : 1))
+}
+
 /* dense SiLU-GLU expert on GGUF tensors: the Qwen3.5 FFN form of
  * src/qwen35/cpu.rs:415-428 (gate, up, silu(gate)*up, down). */
 static int qwen_expert(int gate_type, int up_type, int down_type, const uint8_t *gate,

@@ -127,6 +127,25 @@ typedef struct {
 int dmo_gemma_moe(const dmo_gemma_layer *layer, const float *x, size_t tokens,
                   float *routed, uint32_t *sel_idx, float *sel_prob, int threads);
 
+/* The rest of Gemma 4's feed-forward block around the routed branch
+ * (src/gemma4/cpu.rs:547-558, :613-620): the dense shared FFN on
+ * rms_norm(x, feed_forward_norm) (feed_forward, :693-712: gelu_tanh(gate) * up, then
+ * down), its post norm, the routed post norm, their sum, the post feed-forward norm,
+ * the residual add and the layer output scale. */
+typedef struct {
+  int32_t width;                    /* feed_forward_length */
+  int32_t gate_type, up_type, down_type;
+  const uint8_t *gate, *up;         /* [width][hidden] GGUF rows */
+  const uint8_t *down;              /* [hidden][width] */
+  const float *feed_forward_norm, *shared_post_norm, *routed_post_norm,
+      *post_feed_forward_norm;      /* [hidden] */
+  float layer_output_scale;
+} dmo_gemma_ffn;
+
+int dmo_gemma_ffn_block(const dmo_gemma_ffn *ffn, const dmo_gemma_layer *layer, const float *x,
+                        size_t tokens, float *hidden, uint32_t *sel_idx, float *sel_prob,
+                        int threads);
+
 typedef struct {
   int32_t hidden, intermediate, experts, top_k;
   const float *router;      /* [experts, hidden] f32 */

@@ -90,6 +90,7 @@ def _declare(L):
     L.dmo_lru_acquire.argtypes = [P, I32, I32, C.POINTER(I32), C.POINTER(I32)]
     L.dmo_lru_set_pinned.argtypes = [P, I32, I32, I32]
     L.dmo_lru_stats.argtypes = [P, P]
+    L.dmo_gemma_ffn_block.argtypes = [P, P, P, SZ, P, P, P, C.c_int]
     L.dmo_f8_e4m3fn.argtypes = [C.c_uint8, C.POINTER(C.c_float)]
     L.dmo_glm_u8_encoding.argtypes = [SZ, SZ, SZ, SZ, C.POINTER(C.c_int), C.POINTER(C.c_int)]
     L.dmo_glm_quant_matvec.argtypes = [C.c_int, SZ, SZ, P, SZ, P, SZ, P, P, C.c_int]
@@ -267,6 +268,13 @@ class GemmaLayer(C.Structure):
                 ("router_logit_bias", P)]
 
 
+class GemmaFfn(C.Structure):
+    _fields_ = [("width", I32), ("gate_type", I32), ("up_type", I32), ("down_type", I32),
+                ("gate", P), ("up", P), ("down", P), ("feed_forward_norm", P),
+                ("shared_post_norm", P), ("routed_post_norm", P),
+                ("post_feed_forward_norm", P), ("layer_output_scale", C.c_float)]
+
+
 class QwenLayer(C.Structure):
     _fields_ = [("hidden", I32), ("intermediate", I32), ("experts", I32), ("top_k", I32),
                 ("router", P), ("gate_type", I32), ("up_type", I32), ("down_type", I32),
@@ -297,6 +305,30 @@ def gemma_moe(w: dict, x, threads: int = 1):
     idx = np.zeros((T, k), dtype=np.uint32)
     prob = np.zeros((T, k), dtype=np.float32)
     rc = lib().dmo_gemma_moe(C.byref(layer), _ptr(x), T, _ptr(y), _ptr(idx), _ptr(prob), threads)
+    return rc, y, idx, prob
+
+
+def gemma_ffn_block(w: dict, f: dict, x, threads: int = 1):
+    """Gemma-4 feed-forward block (src/gemma4/cpu.rs:547-620): the routed branch of `w`
+    (as gemma_moe) plus the shared FFN, norms, residual and layer scale of `f`."""
+    x = _f32(x)
+    T, H = x.shape
+    k = w["top_k"]
+    layer = GemmaLayer(H, w["intermediate"], w["experts"], k, w.get("epsilon", 1e-6),
+                       _ptr(w["router"]), _ptr(w["router_scale"]), _ptr(w["routed_pre_norm"]),
+                       w["gate_up_type"], _ptr(w["gate_up"]), w["down_type"], _ptr(w["down"]),
+                       _ptr(w["expert_scale"]), _ptr(w.get("router_logit_bias")))
+    norms = {n: _f32(f[n]) for n in ("feed_forward_norm", "shared_post_norm", "routed_post_norm",
+                                     "post_feed_forward_norm")}
+    ffn = GemmaFfn(f["width"], f["gate_type"], f["up_type"], f["down_type"], _ptr(f["gate"]),
+                   _ptr(f["up"]), _ptr(f["down"]), _ptr(norms["feed_forward_norm"]),
+                   _ptr(norms["shared_post_norm"]), _ptr(norms["routed_post_norm"]),
+                   _ptr(norms["post_feed_forward_norm"]), f["layer_output_scale"])
+    y = np.zeros((T, H), dtype=np.float32)
+    idx = np.zeros((T, k), dtype=np.uint32)
+    prob = np.zeros((T, k), dtype=np.float32)
+    rc = lib().dmo_gemma_ffn_block(C.byref(ffn), C.byref(layer), _ptr(x), T, _ptr(y), _ptr(idx),
+                                   _ptr(prob), threads)
     return rc, y, idx, prob
 
 

@@ -24,8 +24,10 @@ _RUN = (
 
 
 def test_reference_arm_prints_one_json_line():
+    # one token per step keeps the host weights it generates small (its 8 experts)
     r = subprocess.run([sys.executable, "-c", _RUN, "--impl", "reference", "--steps", "1",
-                        "--warmup", "0"], cwd=ROOT, capture_output=True, text=True, timeout=900)
+                        "--warmup", "0", "--sample", "1"], cwd=ROOT, capture_output=True,
+                       text=True, timeout=900)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [l for l in r.stdout.splitlines() if l.strip()]
     assert len(lines) == 1, r.stdout
