@@ -17,7 +17,10 @@
 //              r's own tokens); slots of other ranks' experts are dropped
 //   experts    dispatch + grouped gate/up and down GEMMs on r's experts (dm_tc.cu)
 //   return     each output row is stored into its source rank's pair-ordered output
-//              table; the last CTA publishes r's done flag at every rank
+//              table: on the bf16 tensor-core path by the down GEMM's own epilogue (a
+//              destination table built right after the dispatch; the NVLink stores
+//              overlap the GEMM), otherwise by a copy kernel after it; then r's done
+//              flag is raised at every rank
 //   wait       until every rank's done flag holds this epoch (bounded)
 //   combine    selection-order weighted combine of r's returned rows + shared expert
 //
@@ -169,6 +172,15 @@ __global__ void ep_plan_kernel(EpDev e, uint32_t *recv_sel, const int32_t *statu
   }
 }
 
+// The down product already stored every output row into its source rank's memory
+// (ForwardArgs::ydest) and fenced: raise this rank's done flag at every rank.
+__global__ void ep_signal_done_kernel(EpDev e) {
+  const int d = threadIdx.x;
+  if (d >= e.world) return;
+  __threadfence_system();
+  st_release_sys(flags_of(e, d) + kDone + e.rank, e.epoch);
+}
+
 // Warp per output row: row `pos` of the sorted outputs goes to its source rank's pair
 // table (pair t*k + j, or T_s*k + t for the shared expert). The last CTA raises done.
 __global__ void __launch_bounds__(256) ep_return_kernel(EpDev e, const int32_t *n_rows,
@@ -206,6 +218,7 @@ struct dm_ep {
   uint32_t *sel = nullptr;
   float *sel_w = nullptr;
   uint32_t *recv_sel = nullptr;
+  float **ydest = nullptr;  // per received pair: its output row in the source rank's memory
   int32_t *status = nullptr;
   uint32_t epoch = 0;
   int tokens = 0;
@@ -291,7 +304,7 @@ int32_t dm_ep_create(dm_moe_layer *L, int32_t rank, int32_t world, int32_t max_t
                         ep->region_bytes));
   }
   const size_t local = al(kMaxRanks * sizeof(void *)) + 2 * al((size_t)max_tokens * ep->k * 4) +
-                       al(rows * ep->k1 * 4) + al(4);
+                       al(rows * ep->k1 * 4) + al(rows * ep->k1 * sizeof(float *)) + al(4);
   if (cudaMalloc(&ep->local, local) != cudaSuccess) {
     ep->local = nullptr;
     return cleanup(fail(DM_ERR_ALLOCATION, "could not allocate %zu bytes of scratch", local));
@@ -301,6 +314,7 @@ int32_t dm_ep_create(dm_moe_layer *L, int32_t rank, int32_t world, int32_t max_t
   ep->sel = a.take<uint32_t>((size_t)max_tokens * ep->k);
   ep->sel_w = a.take<float>((size_t)max_tokens * ep->k);
   ep->recv_sel = a.take<uint32_t>(rows * ep->k1);
+  ep->ydest = a.take<float *>(rows * ep->k1);
   ep->status = a.take<int32_t>(1);
   if (a.overflow) return cleanup(fail(DM_ERR_ALLOCATION, "scratch carve overflow"));
   // flags and counters start at zero (epoch 0 = nothing sent yet)
@@ -430,9 +444,25 @@ int32_t dm_ep_experts(dm_ep *ep, void *stream) {
   if (L->desc.family == DM_FAMILY_GEMMA4) a.expert_in = (float *)(ep->region + ep->off_x);
   dmi::Plans plans;
   dmi::choose_plans(L, a, plans);
+  // On the bf16 tensor-core path with fp16 down weights the down GEMM's epilogue stores
+  // each output row straight into its source rank's output table (the transfer overlaps
+  // the GEMM); otherwise a return kernel copies the rows after it.
+  const bool fused = plans.tp && plans.tp->bf16 && L->tcw.f16_down;
+  if (fused) {
+    a.ydest = ep->ydest;
+    a.ret.peer = ep->peer_dev;
+    a.ret.tokens = reinterpret_cast<const uint32_t *>(ep->region) + kTokens;
+    a.ret.off_ret = ep->off_ret;
+    a.ret.tmax = ep->tmax;
+    a.ret.k1 = ep->k1;
+    a.ret.k = ep->k;
+  }
   const int m = dm::launch_forward(a, s, nullptr, plans.gp, plans.tp, dm::kRunExperts);
   if (m < 0) return fail(DM_ERR_UNSUPPORTED_TENSOR_TYPE, "no expert kernel for this format");
-  ep_return_kernel<<<ep->n_sm * 4, 256, 0, s>>>(e, a.offsets + a.E + 1, a.sorted, a.ysorted);
+  if (fused)
+    ep_signal_done_kernel<<<1, 32, 0, s>>>(e);
+  else
+    ep_return_kernel<<<ep->n_sm * 4, 256, 0, s>>>(e, a.offsets + a.E + 1, a.sorted, a.ysorted);
   ep->launches += m + 3;
   DM_CUDA(cudaGetLastError(), "expert-parallel experts");
   return DM_OK;

@@ -1428,6 +1428,21 @@ __global__ void __launch_bounds__(1024) topk_sigmoid_rank_kernel(ForwardArgs a) 
   }
 }
 
+// ydest[pos] = the output row of sorted position pos in its source rank's output table
+// (EpReturnMap); positions past the received count are left alone.
+__global__ void __launch_bounds__(256) ep_dest_kernel(ForwardArgs a) {
+  pdl_wait();
+  const int count = a.offsets[a.E + 1];
+  const EpReturnMap m = a.ret;
+  for (int pos = blockIdx.x * blockDim.x + threadIdx.x; pos < count; pos += gridDim.x * blockDim.x) {
+    const int p = a.sorted[pos];
+    const int r = p / m.k1, j = p - r * m.k1;
+    const int s = r / m.tmax, t = r - s * m.tmax;
+    const size_t row = j < m.k ? (size_t)t * m.k + j : (size_t)m.tokens[s] * m.k + t;
+    a.ydest[pos] = reinterpret_cast<float *>(m.peer[s] + m.off_ret) + row * a.H;
+  }
+}
+
 int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
                    const GemvPlan *gemv, const TcPlan *tc, int mode) {
   int launches = 0;
@@ -1529,6 +1544,11 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
     launch_pdl(dispatch_kernel, dim3(1), dim3(kDispatchThreads), dsmem, stream, a);
   }
   launches++;
+  if (a.ydest) {  // expert-parallel return: each sorted row's destination in peer memory
+    const int n = a.T * a.k;
+    launch_pdl(ep_dest_kernel, dim3((n + 255) / 256), dim3(256), 0, stream, a);
+    launches++;
+  }
   // 5. gate/up (+activation) and 6. down, over the active experts
   const int max_active = std::min(a.E + (a.shared ? 1 : 0), a.T * a.k + (a.shared ? 1 : 0));
   mark(kStageUp);

@@ -8,6 +8,16 @@ namespace dm {
 
 enum Family { kGemma = DM_FAMILY_GEMMA4, kQwen = DM_FAMILY_QWEN35_MOE, kGlm = DM_FAMILY_GLM52 };
 
+// Expert-parallel return map (dm_ep.cu): where the output row of received pair p goes.
+// Pair p = (s * tmax + t) * k1 + j (rank s's token t, slot j; slot k is the shared
+// expert) lands in rank s's output table at row t * k + j (j < k) or tokens[s] * k + t.
+struct EpReturnMap {
+  uint8_t *const *peer;     // [ranks] exchange-region bases
+  const uint32_t *tokens;   // [ranks] token counts of the current forward
+  size_t off_ret;           // byte offset of the output table in a region
+  int tmax, k1, k;
+};
+
 // Everything a forward needs on the device, by value.
 struct ForwardArgs {
   int family;
@@ -55,6 +65,11 @@ struct ForwardArgs {
   int32_t *status;         // [1] device error word (0 = ok)
   float *h;                // [(T*k + T), I]
   float *ysorted;          // [(T*k + T), H]
+  // expert-parallel receivers whose down product stores each output row straight into
+  // its source rank's memory: ydest[pos] is that row (filled after the dispatch from
+  // `ret`); null everywhere else
+  float **ydest;
+  EpReturnMap ret;
 };
 
 // Row stride (elements) of the transposed router [H][ld]: E1 rounded up to 8 so

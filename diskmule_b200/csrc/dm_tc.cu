@@ -1218,7 +1218,10 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
             float v = SPLIT ? w[2 * j] + w[2 * j + 1] : w[j];
             if (n < un.ntok) {
               if (F16) v *= row_inv[un.pos0 + n];  // exact: a power of two
-              out[(size_t)(un.pos0 + n) * ld + col] = v;
+              // expert-parallel receivers store the row into its source rank's memory
+              float *orow = (!UP && a.ydest) ? a.ydest[un.pos0 + n]
+                                             : out + (size_t)(un.pos0 + n) * ld;
+              orow[col] = v;
             }
           }
         }
@@ -1228,6 +1231,9 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
       if (lane == 0) mbar_arrive(accempty(acc));
     }
   }
+  // stores into other GPUs' memory are visible system-wide before the kernel ends (the
+  // signal that follows it raises the ranks' done flags)
+  if (!UP && a.ydest) __threadfence_system();
   __syncthreads();
   if (tid == 0 && abort_flag) atomicExch(a.status, kStatusTimeout);
   if (warp == 0) {
