@@ -189,13 +189,16 @@ class SyntheticLayer:
     def ptr(self, key: str) -> int:
         return self.buffers[key].device_pointer if key in self.buffers else 0
 
-    def host_weights(self, experts=None, fill=None) -> dict:
+    def host_weights(self, experts=None, fill=None, router_only=False) -> dict:
         """Oracle inputs: full tensors (or the listed experts, others zero). `fill` as in
-        `TensorSpec.host`."""
+        `TensorSpec.host`. `router_only` leaves out every expert and shared-expert tensor
+        (for `oracle.route`, which reads the router alone)."""
         cfg = self.cfg
         w = dict(hidden=cfg["hidden"], intermediate=cfg["intermediate"], experts=cfg["experts"],
                  top_k=cfg["top_k"], epsilon=cfg.get("epsilon", 1e-6))
         for key, spec in self.specs.items():
+            if router_only and key not in ("router", "bias"):
+                continue
             if experts is None or spec.experts == 1:
                 w[key] = spec.host(fill=fill)
             else:
@@ -213,7 +216,7 @@ class SyntheticLayer:
             w["router_logit_bias"] = self.logit_bias
         fam = cfg["family"]
         if fam == "gemma4":
-            w["gate_up_type"], w["gate_up"] = cfg["gate_type"], w.pop("gate")
+            w["gate_up_type"], w["gate_up"] = cfg["gate_type"], w.pop("gate", None)
             w["down_type"] = cfg["down_type"]
         elif fam == "qwen35":
             w["gate_type"] = w["up_type"] = cfg["gate_type"]
@@ -284,10 +287,12 @@ def _desc(sl: SyntheticLayer) -> N.MoeDesc:
 
 
 def build_layer(ctx: CudaContext, name: str, seed: int = 1, logit_bias=None,
-                expert_range=None) -> SyntheticLayer:
+                expert_range=None, edit=None) -> SyntheticLayer:
     """A device-resident synthetic layer. `expert_range=(first, count)` builds a shard
     holding only those experts' weights (the same bytes as in the whole layer) for
-    expert parallelism; the router and shared expert stay whole."""
+    expert parallelism; the router and shared expert stay whole. `edit(sl)` runs after
+    the device buffers are filled and before the layer is created, so it may overwrite
+    their bytes (through `sl.buffers[key].write`)."""
     cfg = dict(CONFIGS[name])
     specs = layer_specs(cfg, seed)
     vecs = vectors(cfg, seed)
@@ -307,6 +312,9 @@ def build_layer(ctx: CudaContext, name: str, seed: int = 1, logit_bias=None,
         sl.logit_bias = np.ascontiguousarray(logit_bias, dtype=np.float32)
         sl.buffers["router_logit_bias"] = ctx.map_read_only(sl.logit_bias)
     ctx.synchronize()
+    if edit is not None:
+        edit(sl)
+        ctx.synchronize()
     d = _desc(sl)
     sl.layer = MoeLayer(ctx, d, expert_range=expert_range)
     return sl

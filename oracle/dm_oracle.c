@@ -656,18 +656,15 @@ static size_t row_bytes_of(int kind, size_t columns) {
 /* Gemma 4 routed branch for one token: src/gemma4/cpu.rs:559-611, with
  * tensor_expert_matvec (src/cpu.rs:474-509) slicing expert `e` at
  * `e * rows * row_bytes`. Output is `routed` at :612 (before routed_post_norm). */
-static int gemma_token(const dmo_gemma_layer *L, const float *x, float *routed,
-                       uint32_t *sel_idx, float *sel_prob, int threads) {
-  size_t H = (size_t)L->hidden, I = (size_t)L->intermediate, E = (size_t)L->experts;
-  size_t k = (size_t)L->top_k;
-  float *routed_input = (float *)malloc(H * sizeof(float));
+/* The Gemma 4 router for one token (src/gemma4/cpu.rs:562-576): unweighted rms_norm,
+ * router_scale / sqrt(hidden), the f32 router matvec, the optional logit bias, then
+ * top_k_softmax. */
+static int gemma_route_token(const dmo_gemma_layer *L, const float *x, uint32_t *sel_idx,
+                             float *sel_prob, int threads) {
+  size_t H = (size_t)L->hidden, E = (size_t)L->experts, k = (size_t)L->top_k;
   float *router_input = (float *)malloc(H * sizeof(float));
   float *logits = (float *)malloc(E * sizeof(float));
-  float *gate_up = (float *)malloc(2 * I * sizeof(float));
-  float *activated = (float *)malloc(I * sizeof(float));
-  float *expert_output = (float *)malloc(H * sizeof(float));
-  int rc = dmo_rms_norm(x, L->routed_pre_norm, H, L->epsilon, routed_input);
-  if (rc == DMO_OK) rc = dmo_rms_norm(x, NULL, H, L->epsilon, router_input);
+  int rc = dmo_rms_norm(x, NULL, H, L->epsilon, router_input);
   if (rc == DMO_OK) {
     float inverse_hidden_scale = 1.0f / sqrtf((float)H);
     for (size_t i = 0; i < H; i++)
@@ -678,6 +675,20 @@ static int gemma_token(const dmo_gemma_layer *L, const float *x, float *routed,
   if (rc == DMO_OK && L->router_logit_bias)
     for (size_t e = 0; e < E; e++) logits[e] = logits[e] + L->router_logit_bias[e];
   if (rc == DMO_OK) rc = dmo_top_k_softmax(logits, E, k, sel_idx, sel_prob);
+  free(router_input); free(logits);
+  return rc;
+}
+
+static int gemma_token(const dmo_gemma_layer *L, const float *x, float *routed,
+                       uint32_t *sel_idx, float *sel_prob, int threads) {
+  size_t H = (size_t)L->hidden, I = (size_t)L->intermediate;
+  size_t k = (size_t)L->top_k;
+  float *routed_input = (float *)malloc(H * sizeof(float));
+  float *gate_up = (float *)malloc(2 * I * sizeof(float));
+  float *activated = (float *)malloc(I * sizeof(float));
+  float *expert_output = (float *)malloc(H * sizeof(float));
+  int rc = dmo_rms_norm(x, L->routed_pre_norm, H, L->epsilon, routed_input);
+  if (rc == DMO_OK) rc = gemma_route_token(L, x, sel_idx, sel_prob, threads);
   for (size_t i = 0; i < H; i++) routed[i] = 0.0f;
   size_t gu_row = row_bytes_of(L->gate_up_type, H), down_row = row_bytes_of(L->down_type, I);
   for (size_t j = 0; rc == DMO_OK && j < k; j++) {
@@ -693,7 +704,7 @@ static int gemma_token(const dmo_gemma_layer *L, const float *x, float *routed,
     float scale = sel_prob[j] * L->expert_scale[e];
     for (size_t i = 0; i < H; i++) routed[i] = fmaf(expert_output[i], scale, routed[i]);
   }
-  free(routed_input); free(router_input); free(logits); free(gate_up);
+  free(routed_input); free(gate_up);
   free(activated); free(expert_output);
   return rc;
 }
@@ -722,6 +733,13 @@ int dmo_gemma_moe(const dmo_gemma_layer *L, const float *x, size_t tokens, float
   size_t H = (size_t)L->hidden, k = (size_t)L->top_k;
   TOKEN_LOOP(gemma_token(L, x + t * H, routed + t * H, sel_idx + t * k, sel_prob + t * k,
                          tokens == 1 ? threads : 1))
+}
+
+int dmo_gemma_route(const dmo_gemma_layer *L, const float *x, size_t tokens, uint32_t *sel_idx,
+                    float *sel_prob, int threads) {
+  size_t H = (size_t)L->hidden, k = (size_t)L->top_k;
+  TOKEN_LOOP(gemma_route_token(L, x + t * H, sel_idx + t * k, sel_prob + t * k,
+                               tokens == 1 ? threads : 1))
 }
 
 /* One token of the whole Gemma 4 feed-forward block (src/gemma4/cpu.rs:547-620). */
@@ -799,17 +817,25 @@ static int qwen_expert(int gate_type, int up_type, int down_type, const uint8_t 
  *   g = qwen_sigmoid(fma-chain dot(shared_gate_vector, x))
  *   y = fma(shared(x), g, routed)
  * with expert(x) = down(silu(gate x) * (up x)). */
-static int qwen_token(const dmo_qwen_layer *L, const float *x, float *y, uint32_t *sel_idx,
-                      float *sel_prob, int threads) {
-  size_t H = (size_t)L->hidden, I = (size_t)L->intermediate, E = (size_t)L->experts;
-  size_t k = (size_t)L->top_k;
+static int qwen_route_token(const dmo_qwen_layer *L, const float *x, uint32_t *sel_idx,
+                            float *sel_prob, int threads) {
+  size_t H = (size_t)L->hidden, E = (size_t)L->experts, k = (size_t)L->top_k;
   float *logits = (float *)malloc(E * sizeof(float));
-  float *out = (float *)malloc(H * sizeof(float));
   int rc = dmo_matvec(DMO_F32, E, H, (const uint8_t *)L->router, E * H * 4, x, H, logits, E,
                       threads);
   if (rc == DMO_OK && L->router_logit_bias)
     for (size_t e = 0; e < E; e++) logits[e] = logits[e] + L->router_logit_bias[e];
   if (rc == DMO_OK) rc = dmo_top_k_softmax(logits, E, k, sel_idx, sel_prob);
+  free(logits);
+  return rc;
+}
+
+static int qwen_token(const dmo_qwen_layer *L, const float *x, float *y, uint32_t *sel_idx,
+                      float *sel_prob, int threads) {
+  size_t H = (size_t)L->hidden, I = (size_t)L->intermediate;
+  size_t k = (size_t)L->top_k;
+  float *out = (float *)malloc(H * sizeof(float));
+  int rc = qwen_route_token(L, x, sel_idx, sel_prob, threads);
   for (size_t i = 0; i < H; i++) y[i] = 0.0f;
   size_t gate_bytes = I * row_bytes_of(L->gate_type, H);
   size_t up_bytes = I * row_bytes_of(L->up_type, H);
@@ -830,7 +856,6 @@ static int qwen_token(const dmo_qwen_layer *L, const float *x, float *y, uint32_
     if (rc == DMO_OK)
       for (size_t i = 0; i < H; i++) y[i] = fmaf(out[i], g, y[i]);
   }
-  free(logits);
   free(out);
   return rc;
 }
@@ -842,25 +867,42 @@ int dmo_qwen_moe(const dmo_qwen_layer *L, const float *x, size_t tokens, float *
                         tokens == 1 ? threads : 1))
 }
 
+int dmo_qwen_route(const dmo_qwen_layer *L, const float *x, size_t tokens, uint32_t *sel_idx,
+                   float *sel_prob, int threads) {
+  size_t H = (size_t)L->hidden, k = (size_t)L->top_k;
+  TOKEN_LOOP(qwen_route_token(L, x + t * H, sel_idx + t * k, sel_prob + t * k,
+                              tokens == 1 ? threads : 1))
+}
+
+/* The GLM-5.2 router for one token (src/glm52/cpu.rs:731-754): the router matvec on
+ * the raw hidden state, then the grouped sigmoid + correction-bias selection. */
+static int glm_route_token(const dmo_glm_layer *L, const float *x, uint32_t *sel_idx,
+                           float *sel_weight, int threads) {
+  size_t H = (size_t)L->hidden, E = (size_t)L->experts, k = (size_t)L->top_k;
+  float *logits = (float *)malloc(E * sizeof(float));
+  int rc = dmo_glm_matvec(L->weight_type, E, H, L->router, x, logits, threads);
+  if (rc == DMO_OK)
+    rc = dmo_glm_select(logits, L->correction_bias, E, k, (size_t)L->n_groups,
+                        (size_t)L->topk_groups, L->normalize, sel_idx, sel_weight);
+  free(logits);
+  return rc;
+}
+
 /* GLM-5.2 sparse feed-forward for one token: src/glm52/cpu.rs:711-778.
  * Routed experts go through CachedExpert::mlp (src/glm52/expert.rs:260-267, silu
  * written `g / (1 + exp(-g))`); the shared expert through `mlp`
  * (src/glm52/cpu.rs:897-910, silu written `g * sigmoid(g)`). */
 static int glm_token(const dmo_glm_layer *L, const float *x, float *y, uint32_t *sel_idx,
                      float *sel_weight, int threads) {
-  size_t H = (size_t)L->hidden, I = (size_t)L->intermediate, E = (size_t)L->experts;
+  size_t H = (size_t)L->hidden, I = (size_t)L->intermediate;
   size_t k = (size_t)L->top_k;
   size_t width = L->weight_type == DMO_F32 ? 4 : 2;
-  float *logits = (float *)malloc(E * sizeof(float));
   size_t SI = L->shared_intermediate > 0 ? (size_t)L->shared_intermediate : 0;
   size_t maxI = I > SI ? I : SI;
   float *gate = (float *)malloc(maxI * sizeof(float));
   float *up = (float *)malloc(maxI * sizeof(float));
   float *out = (float *)malloc(H * sizeof(float));
-  int rc = dmo_glm_matvec(L->weight_type, E, H, L->router, x, logits, threads);
-  if (rc == DMO_OK)
-    rc = dmo_glm_select(logits, L->correction_bias, E, k, (size_t)L->n_groups,
-                        (size_t)L->topk_groups, L->normalize, sel_idx, sel_weight);
+  int rc = glm_route_token(L, x, sel_idx, sel_weight, threads);
   for (size_t i = 0; i < H; i++) y[i] = 0.0f;
   size_t expert_in = I * H * width;
   for (size_t j = 0; rc == DMO_OK && j < k; j++) {
@@ -881,7 +923,7 @@ static int glm_token(const dmo_glm_layer *L, const float *x, float *y, uint32_t 
     dmo_glm_matvec(L->weight_type, H, SI, L->shared_down, gate, out, threads);
     for (size_t i = 0; i < H; i++) y[i] = y[i] + out[i];
   }
-  free(logits); free(gate); free(up); free(out);
+  free(gate); free(up); free(out);
   return rc;
 }
 
@@ -890,6 +932,13 @@ int dmo_glm_moe(const dmo_glm_layer *L, const float *x, size_t tokens, float *y,
   size_t H = (size_t)L->hidden, k = (size_t)L->top_k;
   TOKEN_LOOP(glm_token(L, x + t * H, y + t * H, sel_idx + t * k, sel_weight + t * k,
                        tokens == 1 ? threads : 1))
+}
+
+int dmo_glm_route(const dmo_glm_layer *L, const float *x, size_t tokens, uint32_t *sel_idx,
+                  float *sel_weight, int threads) {
+  size_t H = (size_t)L->hidden, k = (size_t)L->top_k;
+  TOKEN_LOOP(glm_route_token(L, x + t * H, sel_idx + t * k, sel_weight + t * k,
+                             tokens == 1 ? threads : 1))
 }
 
 /* ------------------------------------------------------------------------ */

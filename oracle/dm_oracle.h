@@ -126,6 +126,9 @@ typedef struct {
 
 int dmo_gemma_moe(const dmo_gemma_layer *layer, const float *x, size_t tokens,
                   float *routed, uint32_t *sel_idx, float *sel_prob, int threads);
+/* The router and top-k alone (no expert weights read): selection of `tokens` tokens. */
+int dmo_gemma_route(const dmo_gemma_layer *layer, const float *x, size_t tokens,
+                    uint32_t *sel_idx, float *sel_prob, int threads);
 
 /* The rest of Gemma 4's feed-forward block around the routed branch
  * (src/gemma4/cpu.rs:547-558, :613-620): the dense shared FFN on
@@ -161,6 +164,8 @@ typedef struct {
 
 int dmo_qwen_moe(const dmo_qwen_layer *layer, const float *x, size_t tokens, float *y,
                  uint32_t *sel_idx, float *sel_prob, int threads);
+int dmo_qwen_route(const dmo_qwen_layer *layer, const float *x, size_t tokens,
+                   uint32_t *sel_idx, float *sel_prob, int threads);
 
 typedef struct {
   int32_t hidden, intermediate, experts, top_k;
@@ -180,6 +185,8 @@ typedef struct {
 
 int dmo_glm_moe(const dmo_glm_layer *layer, const float *x, size_t tokens, float *y,
                 uint32_t *sel_idx, float *sel_weight, int threads);
+int dmo_glm_route(const dmo_glm_layer *layer, const float *x, size_t tokens,
+                  uint32_t *sel_idx, float *sel_weight, int threads);
 
 /* ---- expert residency (src/expert.rs, src/glm52/expert.rs) ---- */
 typedef struct {

@@ -84,6 +84,9 @@ def _declare(L):
     L.dmo_gemma_moe.argtypes = [P, P, SZ, P, P, P, C.c_int]
     L.dmo_qwen_moe.argtypes = [P, P, SZ, P, P, P, C.c_int]
     L.dmo_glm_moe.argtypes = [P, P, SZ, P, P, P, C.c_int]
+    L.dmo_gemma_route.argtypes = [P, P, SZ, P, P, C.c_int]
+    L.dmo_qwen_route.argtypes = [P, P, SZ, P, P, C.c_int]
+    L.dmo_glm_route.argtypes = [P, P, SZ, P, P, C.c_int]
     L.dmo_lru_create.argtypes = [I32, I32, I32, I32, C.c_uint64, I32]
     L.dmo_lru_create.restype = P
     L.dmo_lru_destroy.argtypes = [P]
@@ -292,15 +295,20 @@ class GlmLayer(C.Structure):
                 ("shared_down", P), ("expert_blobs", C.POINTER(P))]
 
 
+def _gemma_layer(w: dict, H: int):
+    return GemmaLayer(H, w["intermediate"], w["experts"], w["top_k"], w.get("epsilon", 1e-6),
+                      _ptr(w["router"]), _ptr(w["router_scale"]), _ptr(w["routed_pre_norm"]),
+                      w["gate_up_type"], _ptr(w.get("gate_up")), w["down_type"],
+                      _ptr(w.get("down")), _ptr(w["expert_scale"]),
+                      _ptr(w.get("router_logit_bias")))
+
+
 def gemma_moe(w: dict, x, threads: int = 1):
     """Gemma-4 routed branch (src/gemma4/cpu.rs:559-611). `w` holds numpy arrays."""
     x = _f32(x)
     T, H = x.shape
     k = w["top_k"]
-    layer = GemmaLayer(H, w["intermediate"], w["experts"], k, w.get("epsilon", 1e-6),
-                       _ptr(w["router"]), _ptr(w["router_scale"]), _ptr(w["routed_pre_norm"]),
-                       w["gate_up_type"], _ptr(w["gate_up"]), w["down_type"], _ptr(w["down"]),
-                       _ptr(w["expert_scale"]), _ptr(w.get("router_logit_bias")))
+    layer = _gemma_layer(w, H)
     y = np.zeros((T, H), dtype=np.float32)
     idx = np.zeros((T, k), dtype=np.uint32)
     prob = np.zeros((T, k), dtype=np.float32)
@@ -314,10 +322,7 @@ def gemma_ffn_block(w: dict, f: dict, x, threads: int = 1):
     x = _f32(x)
     T, H = x.shape
     k = w["top_k"]
-    layer = GemmaLayer(H, w["intermediate"], w["experts"], k, w.get("epsilon", 1e-6),
-                       _ptr(w["router"]), _ptr(w["router_scale"]), _ptr(w["routed_pre_norm"]),
-                       w["gate_up_type"], _ptr(w["gate_up"]), w["down_type"], _ptr(w["down"]),
-                       _ptr(w["expert_scale"]), _ptr(w.get("router_logit_bias")))
+    layer = _gemma_layer(w, H)
     norms = {n: _f32(f[n]) for n in ("feed_forward_norm", "shared_post_norm", "routed_post_norm",
                                      "post_feed_forward_norm")}
     ffn = GemmaFfn(f["width"], f["gate_type"], f["up_type"], f["down_type"], _ptr(f["gate"]),
@@ -332,17 +337,21 @@ def gemma_ffn_block(w: dict, f: dict, x, threads: int = 1):
     return rc, y, idx, prob
 
 
+def _qwen_layer(w: dict, H: int):
+    return QwenLayer(H, w["intermediate"], w["experts"], w["top_k"], _ptr(w["router"]),
+                     w["gate_type"], w["up_type"], w["down_type"], _ptr(w.get("gate")),
+                     _ptr(w.get("up")), _ptr(w.get("down")), w.get("shared_intermediate", 0),
+                     _ptr(w.get("shared_gate")), _ptr(w.get("shared_up")),
+                     _ptr(w.get("shared_down")), _ptr(w.get("shared_gate_vector")),
+                     _ptr(w.get("router_logit_bias")))
+
+
 def qwen_moe(w: dict, x, threads: int = 1):
     """Restated Qwen3.5-shaped MoE block (see dm_oracle.c for the definition)."""
     x = _f32(x)
     T, H = x.shape
     k = w["top_k"]
-    si = w.get("shared_intermediate", 0)
-    layer = QwenLayer(H, w["intermediate"], w["experts"], k, _ptr(w["router"]),
-                      w["gate_type"], w["up_type"], w["down_type"], _ptr(w["gate"]),
-                      _ptr(w["up"]), _ptr(w["down"]), si, _ptr(w.get("shared_gate")),
-                      _ptr(w.get("shared_up")), _ptr(w.get("shared_down")),
-                      _ptr(w.get("shared_gate_vector")), _ptr(w.get("router_logit_bias")))
+    layer = _qwen_layer(w, H)
     y = np.zeros((T, H), dtype=np.float32)
     idx = np.zeros((T, k), dtype=np.uint32)
     prob = np.zeros((T, k), dtype=np.float32)
@@ -350,18 +359,22 @@ def qwen_moe(w: dict, x, threads: int = 1):
     return rc, y, idx, prob
 
 
+def _glm_layer(w: dict, H: int):
+    return GlmLayer(H, w["intermediate"], w["experts"], w["top_k"], w.get("n_groups", 1),
+                    w.get("topk_groups", 1), int(w.get("normalize", True)),
+                    w.get("routed_scale", 1.0), w.get("weight_type", BF16), _ptr(w["router"]),
+                    _ptr(w["correction_bias"]), _ptr(w.get("gate")), _ptr(w.get("up")),
+                    _ptr(w.get("down")), w.get("shared_intermediate", 0),
+                    _ptr(w.get("shared_gate")), _ptr(w.get("shared_up")),
+                    _ptr(w.get("shared_down")))
+
+
 def glm_moe(w: dict, x, threads: int = 1):
     """GLM-5.2 sparse feed-forward (src/glm52/cpu.rs:711-778)."""
     x = _f32(x)
     T, H = x.shape
     k = w["top_k"]
-    si = w.get("shared_intermediate", 0)
-    layer = GlmLayer(H, w["intermediate"], w["experts"], k, w.get("n_groups", 1),
-                     w.get("topk_groups", 1), int(w.get("normalize", True)),
-                     w.get("routed_scale", 1.0), w.get("weight_type", BF16), _ptr(w["router"]),
-                     _ptr(w["correction_bias"]), _ptr(w.get("gate")), _ptr(w.get("up")),
-                     _ptr(w.get("down")), si, _ptr(w.get("shared_gate")), _ptr(w.get("shared_up")),
-                     _ptr(w.get("shared_down")))
+    layer = _glm_layer(w, H)
     blobs = w.get("expert_blobs")  # host addresses of per-expert gate|up|down blobs
     if blobs is not None:
         keep = (P * len(blobs))(*[int(b) for b in blobs])
@@ -371,6 +384,23 @@ def glm_moe(w: dict, x, threads: int = 1):
     wt = np.zeros((T, k), dtype=np.float32)
     rc = lib().dmo_glm_moe(C.byref(layer), _ptr(x), T, _ptr(y), _ptr(idx), _ptr(wt), threads)
     return rc, y, idx, wt
+
+
+def route(family: str, w: dict, x, threads: int = 1):
+    """The router and top-k of `family` ("gemma4", "qwen35", "glm52") alone, for every token
+    of `x`: (rc, indices [T, k], weights [T, k]). Reads only the router tensors of `w`
+    (src/gemma4/cpu.rs:562-576, src/cpu.rs:234-260, src/glm52/cpu.rs:731-754)."""
+    x = _f32(x)
+    T, H = x.shape
+    k = w["top_k"]
+    make, fn = {"gemma4": (_gemma_layer, lib().dmo_gemma_route),
+                "qwen35": (_qwen_layer, lib().dmo_qwen_route),
+                "glm52": (_glm_layer, lib().dmo_glm_route)}[family]
+    layer = make(w, H)
+    idx = np.zeros((T, k), dtype=np.uint32)
+    wt = np.zeros((T, k), dtype=np.float32)
+    rc = fn(C.byref(layer), _ptr(x), T, _ptr(idx), _ptr(wt), threads)
+    return rc, idx, wt
 
 
 class CacheStats(C.Structure):

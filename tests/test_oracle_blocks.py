@@ -137,3 +137,20 @@ def test_qwen_block_runs_and_is_deterministic(name):
     assert rc == rc2 == O.OK
     assert np.array_equal(y1, y2) and np.array_equal(i1, i2)
     assert np.all(np.isfinite(y1)) and np.allclose(p1.sum(axis=1), 1.0, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", ["gemma4-small", "qwen35-small", "qwen35-odd", "glm52-small",
+                                  "glm52-small-flat"])
+def test_route_alone_selects_what_the_whole_block_selects(name):
+    # oracle.route is the router + top-k of the block, run without any expert weights;
+    # the full-size GPU parity tests compare every token's selection against it
+    hl = HostLayer(name, seed=4)
+    x = hl.x(40, seed=9)
+    fam = hl.cfg["family"]
+    block = {"gemma4": O.gemma_moe, "qwen35": O.qwen_moe, "glm52": O.glm_moe}[fam]
+    rc, _, idx, wt = block(hl.weights(), x, threads=4)
+    assert rc == O.OK
+    rc, idx2, wt2 = O.route(fam, hl.sl.host_weights(router_only=True), x, threads=4)
+    assert rc == O.OK
+    assert np.array_equal(idx, idx2)
+    assert np.array_equal(wt, wt2)
