@@ -653,6 +653,26 @@ int32_t build_tc_weights(dm_moe_layer *L) {
       fprintf(stderr, "diskmule_cuda: tensor-core path off for this layer (weight maps refused)\n");
       L->tc_ok = false;
     }
+    // the largest gate-row and up-row norms of each expert (index E: the shared expert),
+    // from which the fused gate/up epilogue scales the intermediates into fp16
+    const int E = L->local_experts;
+    void *norms = nullptr;
+    if (L->tc_ok && down16 && cudaMalloc(&norms, 2 * (size_t)(E + 1) * sizeof(float)) == cudaSuccess) {
+      L->owned.push_back(norms);
+      float *gn = (float *)norms, *un = gn + E + 1;
+      cudaMemsetAsync(norms, 0, 2 * (size_t)(E + 1) * sizeof(float), L->ctx->stream);
+      const int H = d.hidden, I = d.intermediate;
+      dm::launch_row_norm_max(d.gate, L->gate_stride, E, I, H, gn, L->ctx->stream);
+      dm::launch_row_norm_max(L->up_base, L->up_stride, E, I, H, un, L->ctx->stream);
+      if (L->shared) {
+        dm::launch_row_norm_max(d.shared_gate, 0, 1, I, H, gn + E, L->ctx->stream);
+        dm::launch_row_norm_max(d.shared_up, 0, 1, I, H, un + E, L->ctx->stream);
+      }
+      L->tcw.side.gate_norm = gn;
+      L->tcw.side.up_norm = un;
+    } else {
+      cudaGetLastError();  // without the norms the gate/up product keeps the separate pack
+    }
     return DM_OK;
   }
   uint64_t qh_bytes = 0, d_bytes = 0, sh_qh_bytes = 0, sh_d_bytes = 0;
@@ -725,7 +745,7 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   bytes += al((pairs + E + 1) * sizeof(int4)) + al(4);
   bytes += al(pairs * I * 4) + al(pairs * H * 4);
   const uint64_t xld = (T + 31) / 32 * 32;  // transposed router input for many tokens
-  bytes += al(H * xld * 8);
+  bytes += al(H * xld * 8) + al((xld / 32) * ((H + 31) / 32));
   if (L->tc_ok)
     bytes += al(2 * pairs * H * 2) + al(2 * pairs * I * 2) + 2 * al(pairs * 4) + al(2 * pairs * I * 4);
   L->drop_graphs();
@@ -744,6 +764,7 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
   a.expert_in = d.family == DM_FAMILY_GEMMA4 ? arena.take<float>(T * H) : nullptr;
   a.logits = arena.take<float>(T * L->E1);
   a.xT = arena.take<float>(H * xld * 2);
+  a.x_tiny = arena.take<uint8_t>((xld / 32) * ((H + 31) / 32));
   a.sel_idx = arena.take<uint32_t>(T * k);
   a.sel_w = arena.take<float>(T * k);
   a.counts = arena.take<int32_t>(E + 1);
@@ -860,6 +881,21 @@ static int32_t create_layer(dm_cuda_context *ctx, const dm_moe_desc *desc, int32
                           ctx->stream);
   else
     L->router_dup = nullptr;  // the many-token router then runs the chain-per-thread kernel
+  if (d.family == DM_FAMILY_GLM52 && d.router_type == DM_BF16) {
+    int32_t *flag = nullptr, bad = 1;
+    if (cudaMalloc(&flag, sizeof(int32_t)) == cudaSuccess) {
+      if (cudaMemsetAsync(flag, 0, sizeof(int32_t), ctx->stream) == cudaSuccess) {
+        dm::launch_bf16_range_check((const uint16_t *)d.router, (size_t)d.experts * H, flag,
+                                    ctx->stream);
+        if (cudaMemcpyAsync(&bad, flag, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+          bad = 1;
+      }
+      cudaFree(flag);
+    }
+    L->router_exact_products = bad == 0;
+  }
   rc = build_plan(L);
   if (cudaStreamCreateWithFlags(&L->capture, cudaStreamNonBlocking) != cudaSuccess) L->capture = nullptr;
   {
@@ -1012,6 +1048,7 @@ dm::ForwardArgs fill_args(dm_moe_layer *L, const void *x, float *y, int32_t toke
   a.router_bf16 = d.router_type == DM_BF16;
   a.router_t = L->router_t;
   a.router_dup = L->router_dup;
+  a.router_exact_products = L->router_exact_products;
   a.router_rows = L->router_rows;
   a.bias = d.correction_bias;
   a.router_scale = d.router_scale;

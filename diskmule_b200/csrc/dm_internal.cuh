@@ -120,6 +120,9 @@ struct dm_moe_layer {
   bool shared = false;
   void *router_t = nullptr;  // transposed router [H][E1]
   float *router_dup = nullptr;  // [H][router_dup_ld(E1)] f32 router for many tokens
+  // GLM: the router is bf16 with every nonzero |w| in [2^-60, 2^60), so its products
+  // with bf16 inputs are exact and the router chains may use fused steps
+  int router_exact_products = 0;
   float *router_rows = nullptr; // [E1][H] f32 router rows for few tokens
   uint64_t gate_stride = 0, up_stride = 0, down_stride = 0;
   const uint8_t *up_base = nullptr;

@@ -442,18 +442,27 @@ int launch_router_rows(const void *router, int bf16, int E, int H, const float *
 // two experts at a time with packed f32x2 instructions (one rounding per element, as
 // scalar code). Operands come from x transposed and duplicated per forward, [h][t][2]
 // (a 16-byte load yields two (x, x) pairs; a warp reads only two distinct x chunks), and
-// the router padded to f32 [h][64k] at set-up, through a 3-stage cp.async pipeline of
+// the router padded to f32 [h][128k] at set-up, through a 3-stage cp.async pipeline of
 // 64-wide h chunks (one block barrier per 64 steps of the chains); operands are read with
 // plain shared-memory loads, so the compiler can issue the next step's loads ahead of the
 // current step's FMAs.
+//
+// Step arithmetic. The softmax families' reference chains are fused multiply-adds. GLM's
+// is `s + w * x` with the product rounded first (src/glm52/cpu.rs:1121-1187). When w and
+// x are both bf16 (8 significant bits each) the product has at most 16 significant bits,
+// so it is an exact f32 value unless it leaves the normal range; with every nonzero |w|
+// and |x| in [2^-60, 2^60) it cannot, the first rounding is the identity, and
+// fma(w, x, s) == s + w * x bit for bit. The GLM kernels then take the fused step (half
+// the FP32 instructions); otherwise (an f32 router or input, or a tile holding a value
+// outside that range) they keep the two-instruction step.
 constexpr int kRgTokens = 32, kRgExperts = 64, kRgChunk = 64, kRgThreads = 128, kRgStages = 3;
 constexpr int kRgXBytes = kRgChunk * kRgTokens * 8;
 constexpr int kRgStageBytes = kRgXBytes + kRgChunk * kRgExperts * 4;
 
-template <bool GLM>
+template <bool FMA>
 __device__ __forceinline__ uint64_t rg_step(uint64_t w, uint64_t x, uint64_t s) {
   uint64_t r;
-  if (GLM) {
+  if (!FMA) {
     uint64_t p;
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(w), "l"(x));
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(s), "l"(p));
@@ -463,17 +472,44 @@ __device__ __forceinline__ uint64_t rg_step(uint64_t w, uint64_t x, uint64_t s) 
   return r;
 }
 
+__device__ __forceinline__ bool outside_exact_range(float v) {
+  const float a = fabsf(v);
+  return v != 0.0f && !(a >= 0x1p-60f && a < 0x1p60f);  // NaN and inf fail the range test
+}
+
+// Whether a GLM router CTA over token tile `tile` may take the fused step: the layer's
+// router is in range and no 32x32 input tile of its tokens holds a value out of range.
+__device__ __forceinline__ bool router_fused_step(bool glm, int exact_products,
+                                                  const uint8_t *tiny, int tile, int hblocks) {
+  if (!glm) return true;
+  int bad = !exact_products || !tiny;
+  if (!bad)
+    for (int i = threadIdx.x; i < hblocks; i += blockDim.x) bad |= tiny[(size_t)tile * hblocks + i];
+  return !__syncthreads_or(bad);
+}
+
+__global__ void bf16_range_check_kernel(const uint16_t *v, size_t n, int32_t *flag) {
+  bool bad = false;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    bad |= outside_exact_range(__uint_as_float((uint32_t)v[i] << 16));
+  if (__syncthreads_or(bad) && threadIdx.x == 0) *flag = 1;
+}
+
+int launch_bf16_range_check(const uint16_t *v, size_t n, int32_t *flag, cudaStream_t stream) {
+  bf16_range_check_kernel<<<(int)std::min<size_t>((n + 255) / 256, 1184), 256, 0, stream>>>(
+      v, n, flag);
+  return 1;
+}
+
 __device__ __forceinline__ void rg_cp16(uint32_t dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
-template <bool GLM>
-__global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w32, int wld,
-                                                                 const float *xT2, int xld, int T,
-                                                                 int H, int E1, const float *lbias,
-                                                                 int E, float *logits) {
-  pdl_wait();
-  extern __shared__ __align__(16) uint8_t rg_smem[];
+template <bool FMA>
+__device__ __forceinline__ void router_gemm_chains(uint64_t (&acc)[4][2], const float *w32,
+                                                   int wld, const float *xT2, int xld, int H,
+                                                   uint8_t *rg_smem) {
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int e0 = blockIdx.x * kRgExperts, t0 = blockIdx.y * kRgTokens;
   const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(rg_smem);
@@ -495,11 +531,6 @@ __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w3
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  uint64_t acc[4][2];  // token 4ty + i, experts (4tx + 2jp, 4tx + 2jp + 1)
-  const float z = GLM ? -0.0f : 0.0f;
-  const uint64_t z2 = ((uint64_t)__float_as_uint(z) << 32) | __float_as_uint(z);
-#pragma unroll
-  for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = z2;
 #pragma unroll
   for (int c = 0; c < kRgStages - 1; c++) issue(c);
   for (int c = 0; c < nchunks; c++) {
@@ -515,12 +546,34 @@ __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w3
       const uint64_t xp[4] = {xa.x, xa.y, xb.x, xb.y};
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        acc[i][0] = rg_step<GLM>(w.x, xp[i], acc[i][0]);
-        acc[i][1] = rg_step<GLM>(w.y, xp[i], acc[i][1]);
+        acc[i][0] = rg_step<FMA>(w.x, xp[i], acc[i][0]);
+        acc[i][1] = rg_step<FMA>(w.y, xp[i], acc[i][1]);
       }
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+template <bool GLM>
+__global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w32, int wld,
+                                                                 const float *xT2, int xld, int T,
+                                                                 int H, int E1, const float *lbias,
+                                                                 int E, float *logits,
+                                                                 const uint8_t *tiny,
+                                                                 int exact_products) {
+  pdl_wait();
+  extern __shared__ __align__(16) uint8_t rg_smem[];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int e0 = blockIdx.x * kRgExperts, t0 = blockIdx.y * kRgTokens;
+  uint64_t acc[4][2];  // token 4ty + i, experts (4tx + 2jp, 4tx + 2jp + 1)
+  const float z = GLM ? -0.0f : 0.0f;
+  const uint64_t z2 = ((uint64_t)__float_as_uint(z) << 32) | __float_as_uint(z);
+#pragma unroll
+  for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = z2;
+  if (router_fused_step(GLM, exact_products, tiny, blockIdx.y, (H + 31) / 32))
+    router_gemm_chains<true>(acc, w32, wld, xT2, xld, H, rg_smem);
+  else
+    router_gemm_chains<false>(acc, w32, wld, xT2, xld, H, rg_smem);
 #pragma unroll
   for (int i = 0; i < 4; i++) {
     const int t = t0 + 4 * ty + i;
@@ -534,20 +587,125 @@ __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w3
   }
 }
 
+// The wide form for many tokens and experts: a CTA computes 32 tokens x 128 experts and
+// thread (tx, ty) holds tokens 4ty.. x experts {4tx.., 64 + 4tx..} = 32 chains (the two
+// expert quads sit 256 bytes apart in shared memory, so a quarter-warp's 16-byte loads
+// cover 128 contiguous bytes). Per step of h a thread loads 64 bytes and issues 16
+// packed steps, twice the work per shared-memory byte of the 16-chain form; 16-wide h
+// chunks in 4 stages keep a CTA at 48 KB so four fit on an SM. Chains, operands and the
+// step arithmetic are those of router_gemm_kernel.
+constexpr int kRwTokens = 32, kRwExperts = 128, kRwChunk = 16, kRwThreads = 128, kRwStages = 4;
+constexpr int kRwXBytes = kRwChunk * kRwTokens * 8;
+constexpr int kRwStageBytes = kRwXBytes + kRwChunk * kRwExperts * 4;
+
+template <bool FMA>
+__device__ __forceinline__ void router_wide_chains(uint64_t (&acc)[4][4], const float *w32,
+                                                   int wld, const float *xT2, int xld, int H,
+                                                   uint8_t *smem) {
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int e0 = blockIdx.x * kRwExperts, t0 = blockIdx.y * kRwTokens;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
+  const int nchunks = H / kRwChunk;
+  auto issue = [&](int c) {
+    if (c < nchunks) {
+      const uint32_t st = sbase + (uint32_t)(c % kRwStages) * kRwStageBytes;
+      const int h0 = c * kRwChunk;
+#pragma unroll
+      for (int i = 0; i < kRwChunk * 16 / kRwThreads; i++) {  // x: rows of 32 tokens x 8 bytes
+        const int f = tid + kRwThreads * i, row = f >> 4, piece = f & 15;
+        rg_cp16(st + row * 256 + piece * 16, xT2 + ((size_t)(h0 + row) * xld + t0) * 2 + 4 * piece);
+      }
+#pragma unroll
+      for (int i = 0; i < kRwChunk * 32 / kRwThreads; i++) {  // w: rows of 128 experts x 4 bytes
+        const int f = tid + kRwThreads * i, row = f >> 5, piece = f & 31;
+        rg_cp16(st + kRwXBytes + row * 512 + piece * 16, w32 + (size_t)(h0 + row) * wld + e0 + 4 * piece);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+#pragma unroll
+  for (int c = 0; c < kRwStages - 1; c++) issue(c);
+  for (int c = 0; c < nchunks; c++) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kRwStages - 2) : "memory");
+    __syncthreads();  // chunk c is in; every thread is done with chunk c - 1
+    issue(c + kRwStages - 1);
+    const uint8_t *stp = smem + (size_t)(c % kRwStages) * kRwStageBytes;
+#pragma unroll
+    for (int kk = 0; kk < kRwChunk; kk++) {
+      const ulonglong2 xa = *reinterpret_cast<const ulonglong2 *>(stp + kk * 256 + ty * 32);
+      const ulonglong2 xb = *reinterpret_cast<const ulonglong2 *>(stp + kk * 256 + ty * 32 + 16);
+      const uint8_t *wrow = stp + kRwXBytes + kk * 512 + tx * 16;
+      const ulonglong2 wa = *reinterpret_cast<const ulonglong2 *>(wrow);
+      const ulonglong2 wb = *reinterpret_cast<const ulonglong2 *>(wrow + 256);
+      const uint64_t xp[4] = {xa.x, xa.y, xb.x, xb.y};
+      const uint64_t wp[4] = {wa.x, wa.y, wb.x, wb.y};
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = rg_step<FMA>(wp[j], xp[i], acc[i][j]);
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+template <bool GLM>
+__global__ void __launch_bounds__(kRwThreads) router_wide_kernel(const float *w32, int wld,
+                                                                 const float *xT2, int xld, int T,
+                                                                 int H, int E1, const float *lbias,
+                                                                 int E, float *logits,
+                                                                 const uint8_t *tiny,
+                                                                 int exact_products) {
+  pdl_wait();
+  extern __shared__ __align__(16) uint8_t rw_smem[];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int e0 = blockIdx.x * kRwExperts, t0 = blockIdx.y * kRwTokens;
+  uint64_t acc[4][4];  // token 4ty + i; experts (4tx + 2j, +1) for j < 2, (64 + 4tx + 2(j-2), +1)
+  const float z = GLM ? -0.0f : 0.0f;
+  const uint64_t z2 = ((uint64_t)__float_as_uint(z) << 32) | __float_as_uint(z);
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[i][j] = z2;
+  if (router_fused_step(GLM, exact_products, tiny, blockIdx.y, (H + 31) / 32))
+    router_wide_chains<true>(acc, w32, wld, xT2, xld, H, rw_smem);
+  else
+    router_wide_chains<false>(acc, w32, wld, xT2, xld, H, rw_smem);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int t = t0 + 4 * ty + i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int eb = e0 + (j < 2 ? 4 * tx + 2 * j : 64 + 4 * tx + 2 * (j - 2));
+#pragma unroll
+      for (int q = 0; q < 2; q++) {
+        const int e = eb + q;
+        const float v = __uint_as_float((uint32_t)(acc[i][j] >> (32 * q)));
+        if (e < E1) logits[(size_t)t * E1 + e] = (lbias && e < E) ? __fadd_rn(v, lbias[e]) : v;
+      }
+    }
+  }
+}
+
 // x [T][H] (f32 or bf16) -> xT2 [H][xld][2] f32, each value twice; tokens T..xld-1 zero.
+// With `tiny`, block (bx, by) also writes tiny[by * gridDim.x + bx]: whether its 32x32 tile
+// holds a nonzero |x| outside [2^-60, 2^60) (see the router's step arithmetic).
 __global__ void __launch_bounds__(256) transpose_x_kernel(const void *x, int bf16, int T, int H,
-                                                         int xld, float *xT2) {
+                                                         int xld, float *xT2, uint8_t *tiny) {
   pdl_wait();
   __shared__ float tile[32][33];
   const int h0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
   const int c = threadIdx.x & 31, r0 = threadIdx.x >> 5;
+  bool bad = false;
   for (int r = r0; r < 32; r += 8) {
     const int t = t0 + r, h = h0 + c;
     float v = 0.0f;
     if (t < T && h < H) v = load_as_f32(x, (size_t)t * H + h, bf16 != 0);
+    bad |= outside_exact_range(v);
     tile[r][c] = v;
   }
-  __syncthreads();
+  const int any = __syncthreads_or(bad);  // also the barrier before the tile is read
+  if (tiny && threadIdx.x == 0) tiny[(size_t)blockIdx.y * gridDim.x + blockIdx.x] = any ? 1 : 0;
   for (int r = r0; r < 32; r += 8) {
     const int h = h0 + r, t = t0 + c;
     const float v = tile[c][r];
@@ -1496,21 +1654,36 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
 #undef DM_ROUTER_SMALL
   } else {
     const int xld = (a.T + kRgTokens - 1) / kRgTokens * kRgTokens;
+    // GLM with a bf16 router and bf16 input may take the fused step; the transpose marks
+    // the input tiles that rule it out
+    const int exact = glm && router_x_bf16 && a.router_exact_products;
+    uint8_t *tiny = exact ? a.x_tiny : nullptr;
     launch_pdl(transpose_x_kernel, dim3((a.H + 31) / 32, xld / 32), dim3(256), 0, stream, router_x,
-               router_x_bf16 ? 1 : 0, a.T, a.H, xld, a.xT);
+               router_x_bf16 ? 1 : 0, a.T, a.H, xld, a.xT, tiny);
     launches++;
-    dim3 grid((a.E1 + kRgExperts - 1) / kRgExperts, xld / kRgTokens);
-    const size_t smem = (size_t)kRgStages * kRgStageBytes;
-#define DM_ROUTER_TILED(G)                                                                   \
+    // 32 x 128 tiles when there are enough of them to fill the SMs, else 32 x 64
+    static const int n_sm = [] {
+      int dev = 0, n = 148;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+      return n;
+    }();
+    const int wide_tiles = (a.E1 + kRwExperts - 1) / kRwExperts * (xld / kRwTokens);
+    const bool wide = a.E1 >= kRwExperts && a.H % kRwChunk == 0 && wide_tiles >= n_sm;
+#define DM_ROUTER_TILED(KERNEL, G, EXPERTS, THREADS, SMEM)                                     \
   {                                                                                          \
-    auto fn = router_gemm_kernel<G>;                                                         \
-    set_smem(fn, smem);                                                                      \
-    launch_pdl(fn, grid, dim3(kRgThreads), smem, stream, (const float *)a.router_dup,          \
-               router_dup_ld(a.E1), (const float *)a.xT, xld, a.T, a.H, a.E1, a.logit_bias, a.E,  \
-               a.logits);                                                                    \
+    auto fn = KERNEL<G>;                                                                     \
+    set_smem(fn, SMEM);                                                                      \
+    launch_pdl(fn, dim3((a.E1 + EXPERTS - 1) / EXPERTS, xld / kRgTokens), dim3(THREADS), SMEM, \
+               stream, (const float *)a.router_dup, router_dup_ld(a.E1), (const float *)a.xT,  \
+               xld, a.T, a.H, a.E1, a.logit_bias, a.E, a.logits, (const uint8_t *)tiny, exact); \
   }
-    if (glm) DM_ROUTER_TILED(true)
-    else DM_ROUTER_TILED(false)
+    const size_t rg_smem = (size_t)kRgStages * kRgStageBytes;
+    const size_t rw_smem = (size_t)kRwStages * kRwStageBytes;
+    if (wide && glm) DM_ROUTER_TILED(router_wide_kernel, true, kRwExperts, kRwThreads, rw_smem)
+    else if (wide) DM_ROUTER_TILED(router_wide_kernel, false, kRwExperts, kRwThreads, rw_smem)
+    else if (glm) DM_ROUTER_TILED(router_gemm_kernel, true, kRgExperts, kRgThreads, rg_smem)
+    else DM_ROUTER_TILED(router_gemm_kernel, false, kRgExperts, kRgThreads, rg_smem)
 #undef DM_ROUTER_TILED
   }
   launches++;

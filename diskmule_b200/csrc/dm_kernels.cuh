@@ -38,6 +38,9 @@ struct ForwardArgs {
   const float *router_dup; // [H][router_dup_ld] f32 router copy (many tokens), or null
   const float *router_rows;  // [E1][H] f32 router rows (few tokens)
   float *xT;               // [H][T rounded up to 32][2] transposed, duplicated router input
+  uint8_t *x_tiny;         // [T/32 rounded up][H/32 rounded up]: 1 where a 32x32 tile of a bf16
+                           // router input holds a nonzero |x| outside [2^-60, 2^60) (or null)
+  int router_exact_products;  // GLM: bf16 router whose nonzero |w| all lie in [2^-60, 2^60)
   // experts
   int gate_type, up_type, down_type;
   const uint8_t *gate, *up, *down;
@@ -77,7 +80,7 @@ struct ForwardArgs {
 __host__ __device__ inline int router_ld(int E1) { return (E1 + 7) & ~7; }
 // Row stride of the f32 router copy [H][ld] used for many tokens: E1 rounded up to the
 // 64-expert tile.
-__host__ __device__ inline int router_dup_ld(int E1) { return (E1 + 63) & ~63; }
+__host__ __device__ inline int router_dup_ld(int E1) { return (E1 + 127) & ~127; }
 
 enum DeviceStatus : int32_t {
   kStatusOk = 0,
@@ -132,6 +135,9 @@ int launch_router_rows(const void *router, int bf16, int E, int H, const float *
 // [H][ld] router -> [H][router_dup_ld] f32 (layer set-up)
 int launch_dup_router(const void *router_t, int bf16, int H, int E1, float *dst,
                       cudaStream_t stream);
+// *flag = 1 if any nonzero |v| of n bf16 values lies outside [2^-60, 2^60) (or is not
+// finite); the caller zeroes *flag first (layer set-up)
+int launch_bf16_range_check(const uint16_t *v, size_t n, int32_t *flag, cudaStream_t stream);
 int launch_transpose_router(const void *src, int src_bf16, int E, int H, const float *extra_col,
                             void *dst, cudaStream_t stream);
 

@@ -370,7 +370,17 @@ __device__ __forceinline__ float block_max(float v, float *red) {
 // scale s = 2^(13 - floor(log2 max)) puts the row's largest magnitude in [2^13, 2^14)
 __device__ __forceinline__ float pow2_scale(float m) {
   if (!(m > 0.0f) || !isfinite(m)) return 1.0f;
-  return exp2f((float)(13 - ilogbf(m)));
+  // capped at 2^126 so that the scale and its inverse stay finite for rows below 2^-113
+  return exp2f((float)min(13 - ilogbf(m), 126));
+}
+
+// GLM's silu(g) * u with the hardware exponential and a fast divide: the CUDA-core
+// activations above evaluate exp in double for the reference's exact rounding, which the
+// intermediate h, rounded to fp16 right after, does not need (|error| ~1e-6 relative against
+// fp16's 5e-4). Used where the epilogue of a tensor-core product applies the activation:
+// four warps per SM there, so latency, not throughput, bounds it.
+__device__ __forceinline__ float glm_silu_mul_fast(float g, float u) {
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
 __device__ __forceinline__ float activate(const ForwardArgs &a, int expert, float g, float u) {
@@ -1212,17 +1222,22 @@ __global__ void __launch_bounds__(kBfThreads, 1) tc_bf16_kernel(
           tmem_ld16(taddr + c0 + 16, reinterpret_cast<uint32_t *>(w + 16));
           tmem_wait_ld();
           const int nbase = SPLIT ? c0 / 2 : c0;
+          // the chunk's row scales and destination rows, one per lane, fetched before the
+          // loop so that its stores wait on no load
+          const bool mine = nbase + lane < un.ntok;
+          const float rv = (F16 && mine) ? row_inv[un.pos0 + nbase + lane] : 1.0f;
+          // expert-parallel receivers store the row into its source rank's memory
+          float *dp = !mine ? nullptr
+                            : (!UP && a.ydest) ? a.ydest[un.pos0 + nbase + lane]
+                                               : out + (size_t)(un.pos0 + nbase + lane) * ld;
 #pragma unroll
           for (int j = 0; j < (SPLIT ? 16 : 32); j++) {
             const int n = nbase + j;
             float v = SPLIT ? w[2 * j] + w[2 * j + 1] : w[j];
-            if (n < un.ntok) {
-              if (F16) v *= row_inv[un.pos0 + n];  // exact: a power of two
-              // expert-parallel receivers store the row into its source rank's memory
-              float *orow = (!UP && a.ydest) ? a.ydest[un.pos0 + n]
-                                             : out + (size_t)(un.pos0 + n) * ld;
-              orow[col] = v;
-            }
+            if (F16) v *= __shfl_sync(0xffffffffu, rv, j);  // exact: a power of two
+            float *orow = reinterpret_cast<float *>(
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dp), j));
+            if (n < un.ntok) orow[col] = v;
           }
         }
       }
@@ -1345,11 +1360,16 @@ struct PairCfg {
   static_assert(kSmem <= kSmemLimit, "stages exceed shared memory");
 };
 
+// With UP the epilogue applies the activation: the gate and up rows of an intermediate
+// index sit in adjacent lanes, a lane pair trades one value per two tokens, and each lane
+// writes h = act(gate, up) * h_scale[row] as fp16 (h_out [rows][I], the down product's
+// operand) for one of the two tokens. h_scale is a power of two per row chosen before the
+// product from a bound on |h| (gather_bf16_kernel), so no pass over h is needed to scale it.
 template <bool UP, bool F16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBfThreads, 1) tc_bf16_pair_kernel(
     const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap wmap,
     const __grid_constant__ CUtensorMap sh_wmap, ForwardArgs a, TcSide side, float *gu,
-    const float *row_inv) {
+    const float *row_inv, __half *h_out, const float *h_scale) {
   using C = PairCfg;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t dsm[];
@@ -1498,22 +1518,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBfThreads, 1) tc_bf
       fence_after();
       const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * 256);
       const bool swapped = un.e == a.E ? side.sh_up_swapped : side.up_swapped;
-      float *out = UP ? gu : a.ysorted;
-      const int ld = UP ? 2 * a.I : a.H;
-      const int col = UP ? un.tile * 128 + (r ^ (swapped ? 1 : 0)) : un.tile * 128 + r;
+      // UP: gate|up row `gr` of the tile; even rows are gates
+      const int gr = r ^ (swapped ? 1 : 0);
+      const bool is_gate = (gr & 1) == 0;
+      __half *hcol = h_out + un.tile * 64 + (gr >> 1);
+      const int col = un.tile * 128 + r;
 #pragma unroll 1
       for (int c0 = 0; c0 < un.ntok; c0 += 32) {
         float w[32];
         tmem_ld16(taddr + c0, reinterpret_cast<uint32_t *>(w));
         tmem_ld16(taddr + c0 + 16, reinterpret_cast<uint32_t *>(w + 16));
         tmem_wait_ld();
+        if (UP) {
+          // the chunk's 32 row scales, one per lane (no load waits inside the loop below)
+          const float sc = c0 + lane < un.ntok ? h_scale[un.pos0 + c0 + lane] : 0.0f;
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-          const int n = c0 + j;
-          if (n < un.ntok) {
+          for (int j = 0; j < 32; j += 2) {
+            // the gate lane takes token c0 + j, the up lane token c0 + j + 1
+            const float recv = __shfl_xor_sync(0xffffffffu, is_gate ? w[j + 1] : w[j], 1);
+            const float s_n = __shfl_sync(0xffffffffu, sc, is_gate ? j : j + 1);
+            const float g = is_gate ? w[j] : recv, u = is_gate ? recv : w[j + 1];
+            const int n = c0 + j + (is_gate ? 0 : 1);
+            if (n < un.ntok)
+              hcol[(size_t)(un.pos0 + n) * a.I] = __float2half_rn(glm_silu_mul_fast(g, u) * s_n);
+          }
+        } else {
+          const float rv = (F16 && c0 + lane < un.ntok) ? row_inv[un.pos0 + c0 + lane] : 1.0f;
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            const int n = c0 + j;
             float v = w[j];
-            if (F16) v *= row_inv[un.pos0 + n];  // exact: a power of two
-            out[(size_t)(un.pos0 + n) * ld + col] = v;
+            if (F16) v *= __shfl_sync(0xffffffffu, rv, j);  // exact: a power of two
+            if (n < un.ntok) a.ysorted[(size_t)(un.pos0 + n) * a.H + col] = v;
           }
         }
       }
@@ -1532,14 +1568,77 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kBfThreads, 1) tc_bf
 }
 
 // bf16 inputs gathered into sorted order: out[pos] = x[token of pos] (bf16 copy).
-__global__ void __launch_bounds__(256) gather_bf16_kernel(ForwardArgs a, __nv_bfloat16 *out) {
+//
+// With h_scale, also the power of two that scales row pos of the intermediate h into fp16.
+// |gate_i| <= |gate row i| |x| and |up_i| <= |up row i| |x| (Cauchy-Schwarz), |silu(g)| <= |g|,
+// so |h_i| <= B = gate_norm[e] up_norm[e] |x|^2 for every i of the row. The scale is
+// 2^(13 - floor(log2 B)): every scaled |h| stays below 2^14, a quarter of fp16's largest
+// finite value (room for rounding in the products), and values within 2^24 of the bound
+// keep fp16's full 11-bit precision. h_inv[pos] = 1 / scale (exact).
+__global__ void __launch_bounds__(256) gather_bf16_kernel(ForwardArgs a, __nv_bfloat16 *out,
+                                                          TcSide side, float *h_scale,
+                                                          float *h_inv) {
   const int pos = blockIdx.x;
   if (pos >= a.offsets[a.E + 1]) return;
   const int P = a.T * a.k, pr = a.sorted[pos];
   const int tok = pr < P ? pr / a.k : pr - P;
   const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(a.x) + (size_t)tok * a.H);
   uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)pos * a.H);
-  for (int i = threadIdx.x; i < a.H / 8; i += blockDim.x) dst[i] = src[i];
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < a.H / 8; i += blockDim.x) {
+    const uint4 v = src[i];
+    dst[i] = v;
+    const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float lo = __uint_as_float(p[j] << 16), hi = __uint_as_float(p[j] & 0xffff0000u);
+      ss = fmaf(lo, lo, fmaf(hi, hi, ss));
+    }
+  }
+  if (!h_scale) return;
+  __shared__ float part[8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) sum += part[w];
+    const int e = pr < P ? (int)a.sel_idx[pr] : a.E;
+    const float bound = side.gate_norm[e] * side.up_norm[e] * sum;
+    float s = 1.0f;
+    if (!isfinite(bound)) s = 0x1p-126f;
+    else if (bound > 0.0f) s = exp2f((float)max(-126, min(126, 13 - ilogbf(bound))));
+    h_scale[pos] = s;
+    h_inv[pos] = 1.0f / s;
+  }
+}
+
+// out[e] = max over the rows of expert e of the row's L2 norm (a warp per row).
+__global__ void row_norm_max_kernel(const uint8_t *w, uint64_t expert_stride, int experts,
+                                    int rows, int K, float *out) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t nrows = (uint64_t)experts * rows;
+  const uint64_t step = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  for (uint64_t r = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5; r < nrows; r += step) {
+    const int e = (int)(r / rows), i = (int)(r % rows);
+    const uint4 *row = reinterpret_cast<const uint4 *>(w + e * expert_stride + (uint64_t)i * K * 2);
+    float ss = 0.0f;
+    for (int q = lane; q < K / 8; q += 32) {
+      const uint4 v = row[q];
+      const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float lo = __uint_as_float(p[j] << 16), hi = __uint_as_float(p[j] & 0xffff0000u);
+        ss = fmaf(lo, lo, fmaf(hi, hi, ss));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    // norms are not negative, so their bit patterns order as integers; a NaN or inf norm
+    // (a non-finite weight) pins the bound at inf
+    if (lane == 0) atomicMax(reinterpret_cast<int *>(out + e), __float_as_int(fminf(sqrtf(ss), INFINITY)));
+  }
 }
 
 // h = act(gate, up) from gu, as bf16 hi (row 2 pos) + lo (row 2 pos + 1).
@@ -1720,26 +1819,28 @@ static int launch_bf16(const ForwardArgs &a, const TcPlan &p, const TcWeights &w
   constexpr int NT = 256;
   if (p.nt != NT) return -1;
   const int rows_bound = a.T * a.k + (a.shared ? a.T : 0);
-  tc::gather_bf16_kernel<<<rows_bound, 256, 0, s>>>(a, reinterpret_cast<__nv_bfloat16 *>(p.x16));
-  if (use_pairs() && w.f16_down && a.I % 128 == 0 && a.H % 256 == 0) {
-    // CTA pairs for the gate/up product: 256-row weight tiles (DISKMULE_CUDA_TC_PAIRS=0
-    // turns them off)
+  // (the pair epilogue applies GLM's activation)
+  const bool pairs = use_pairs() && a.family == kGlm && w.f16_down && w.side.gate_norm &&
+                     a.I % 128 == 0 && a.H % 256 == 0;
+  // with CTA pairs, the gather also sets each row's intermediate scale (p.x_inv holds the
+  // scales, p.h_inv their inverses)
+  tc::gather_bf16_kernel<<<rows_bound, 256, 0, s>>>(a, reinterpret_cast<__nv_bfloat16 *>(p.x16),
+                                                    w.side, pairs ? p.x_inv : nullptr, p.h_inv);
+  if (pairs) {
+    // CTA pairs for the gate/up product: 256-row weight tiles, activation in the epilogue
+    // (DISKMULE_CUDA_TC_PAIRS=0 turns them off)
     auto up = tc::tc_bf16_pair_kernel<true, false>;
     ensure_smem_limit((const void *)up);
     up<<<pair_grid(p, a.I / 128), tc::kBfThreads, tc::PairCfg::kSmem, s>>>(
-        p.x_map_pair, w.up, w.sh_up, a, w.side, p.gu, nullptr);
+        p.x_map_pair, w.up, w.sh_up, a, w.side, nullptr, nullptr, p.h16, p.x_inv);
     if (down_mark) cudaEventRecord(down_mark, s);
-    const size_t hsmem = (size_t)tc::kPackRows * a.I * sizeof(float);
-    if (hsmem > 48 * 1024) ensure_smem_limit((const void *)tc::pack_kernel<false>);
-    tc::pack_kernel<false><<<(rows_bound + tc::kPackRows - 1) / tc::kPackRows, 32 * tc::kPackRows,
-                             hsmem, s>>>(a, p.gu, p.h16, p.h_inv, a.I, 0);
     // the down product (K = I: few K steps per unit) measured faster on single CTAs
     auto down = tc::tc_bf16_kernel<false, NT, false, 1, true>;
     ensure_smem_limit((const void *)down);
     const int grid = std::max(1, std::min(p.n_sm, p.max_items * (a.H / 128)));
     down<<<grid, tc::kBfThreads, tc::BfCfg<NT>::kSmem, s>>>(p.h1_map, w.down16, w.sh_down16, a,
                                                                 w.side, p.gu, p.h_inv);
-    return 4;
+    return 3;
   }
   {
     auto fn = tc::tc_bf16_kernel<true, NT, false, 1>;
@@ -1904,6 +2005,12 @@ __global__ void bf16_to_f16_kernel(const uint4 *src, uint4 *dst, uint64_t n8) {
   }
 }
 }  // namespace tc
+
+void launch_row_norm_max(const void *w, uint64_t expert_stride, int experts, int rows, int K,
+                         float *out, cudaStream_t stream) {
+  tc::row_norm_max_kernel<<<148 * 8, 256, 0, stream>>>((const uint8_t *)w, expert_stride, experts,
+                                                       rows, K, out);
+}
 
 void launch_bf16_to_f16(const void *src, void *dst, uint64_t n, cudaStream_t stream) {
   const uint64_t n8 = n / 8;  // callers pass whole 16-byte pieces (rows of 8k elements)

@@ -48,6 +48,9 @@ struct TcSide {
   const uint8_t *qh_t = nullptr, *d_t = nullptr;        // routed experts
   const uint8_t *sh_qh_t = nullptr, *sh_d_t = nullptr;  // shared expert
   int up_swapped = 0, sh_up_swapped = 0;  // 1: index 0 of the gate|up axis is `up`
+  // bf16 layers: the largest L2 norm of a gate row / an up row of each expert (index E:
+  // the shared expert), or null
+  const float *gate_norm = nullptr, *up_norm = nullptr;
 };
 
 // Per-layer tensor-core views of the expert weights, built once.
@@ -79,6 +82,11 @@ int make_tc_weights_bf16(TcWeights &w, const uint8_t *gate, const uint8_t *up, u
                          const uint8_t *sh_gate, const uint8_t *sh_up, const uint8_t *down,
                          const uint8_t *sh_down, int experts, int H, int I,
                          const uint8_t *down16 = nullptr, const uint8_t *sh_down16 = nullptr);
+
+// out[e] = max(out[e], largest L2 norm of the `rows` bf16 rows of K elements of expert e),
+// experts `expert_stride` bytes apart (layer set-up; out starts at zero).
+void launch_row_norm_max(const void *w, uint64_t expert_stride, int experts, int rows, int K,
+                         float *out, cudaStream_t stream);
 
 // bf16 -> fp16 copy of n elements (exact for magnitudes in fp16's normal range, 2^-14 to
 // 65504; smaller ones round to fp16's subnormal grid of 2^-24).

@@ -153,3 +153,44 @@ def test_exact_and_one_ulp_ties_keep_the_reference_order(ctx, name, T):
         check(y[sub], idx[sub], wt[sub], y_ref, idx_ref, wt_ref)
     finally:
         sl.close()
+
+
+# ---- router kernel forms ---------------------------------------------------------
+
+def test_qwen_many_tokens_take_the_wide_router(ctx):
+    # 2048 tokens x 513 router rows: enough 32 x 128 tiles for the wide router kernel
+    T = 2048
+    sl = build_layer(ctx, "qwen35", seed=12)
+    try:
+        spec, raw = sl.inputs(T, seed=23)
+        y, idx, wt = sl.layer.forward_host(device_input(spec, raw, T))
+        x32 = as_f32(spec, raw, T)
+        check_routing(sl, x32, idx, wt)
+        check_dispatch(sl, T, idx)
+        sub = [0, 1023, 2047]
+        y_ref, idx_ref, wt_ref = run_oracle(sl, x32[sub], threads=THREADS)
+        check(y[sub], idx[sub], wt[sub], y_ref, idx_ref, wt_ref)
+    finally:
+        sl.close()
+
+
+def test_glm_input_outside_the_exact_product_range(ctx):
+    # bf16 x bf16 router products are exact f32 values, so the GLM router chains may use
+    # fused steps, unless a value leaves [2^-60, 2^60): tiles holding such values take the
+    # two-rounding step. Plant subnormal, tiny and huge inputs in a few tokens.
+    T = 4096
+    sl = build_layer(ctx, "glm52", seed=2)
+    try:
+        spec, raw = sl.inputs(T, seed=29)
+        x = raw.view(np.uint16).reshape(T, -1).copy()
+        x[5, :] = 0x0001          # smallest bf16 subnormal, every column
+        x[700, ::3] = 0x1F80      # 2^-64
+        x[3001, 17] = 0x5E00      # 2^61
+        x[3001, 18] = 0xDE00      # -2^61
+        y, idx, wt = sl.layer.forward_host(x)
+        assert np.all(np.isfinite(y))
+        x32 = (x.astype(np.uint32) << 16).view(np.float32)
+        check_routing(sl, x32, idx, wt)
+        check_dispatch(sl, T, idx)
+    finally:
+        sl.close()
