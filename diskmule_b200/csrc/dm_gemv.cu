@@ -392,24 +392,38 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_up_kernel(ForwardArgs a, Ma
                                                               MatrixRef up, MatrixRef sh_gate,
                                                               MatrixRef sh_up, int up_row_offset,
                                                               int rows_per_cta) {
-  pdl_wait();
-  pdl_trigger();
   extern __shared__ __align__(16) float smem[];
-  if ((int)blockIdx.y >= *a.n_items) return;
-  const int4 item = a.items[blockIdx.y];  // (expert, first token of the chunk, ...)
-  const int e = item.x, c0 = item.y;
-  const int base = a.offsets[e];
-  const int nt = min(NT, a.counts[e] - c0);
   const int H = a.H, I = a.I;
   constexpr int kTask = Task<KIND>::kElems;
-  const int nb = H / kTask;
-  const int i0 = blockIdx.x * rows_per_cta;
-  if (i0 >= I) return;
-  const int nrows = min(rows_per_cta, I - i0);
   const int kp = pad_index(H, kTask), groups = H / 16;
   float *xs = smem;
   float *s16 = xs + NT * kp;
   float *part = s16 + NT * groups;
+  // One token: every work item reads row 0 of the input (or of Gemma's routed input, which
+  // a kernel before the predecessor wrote), so it is staged before the wait, while the
+  // predecessor finishes, instead of after the chain items -> offsets -> sorted -> row.
+  const bool one = NT == 1 && a.T == 1;
+  if (one && blockIdx.x * rows_per_cta < I)
+    stage_rows<1>(xs, s16, H, kTask, 1, [&](int, int k) {
+      if (a.family == kGemma) return *reinterpret_cast<const float4 *>(a.expert_in + k);
+      if (a.input_bf16) {
+        const uint2 u = *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(a.x) + k);
+        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                           __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+      }
+      return *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + k);
+    });
+  pdl_wait();
+  pdl_trigger();
+  if ((int)blockIdx.y >= *a.n_items) return;
+  const int4 item = a.items[blockIdx.y];  // (expert, first token of the chunk, ...)
+  const int e = item.x, c0 = item.y;
+  const int base = a.offsets[e];
+  const int nt = one ? 1 : min(NT, a.counts[e] - c0);
+  const int nb = H / kTask;
+  const int i0 = blockIdx.x * rows_per_cta;
+  if (i0 >= I) return;
+  const int nrows = min(rows_per_cta, I - i0);
   const bool shared = e == a.E;
   const MatrixRef &G = shared ? sh_gate : gate;
   const MatrixRef &U = shared ? sh_up : up;
@@ -420,7 +434,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_up_kernel(ForwardArgs a, Ma
     const int which = threadIdx.x / (nrows * nb), rem = threadIdx.x - which * nrows * nb;
     prefetch_task<KIND>(which ? U : G, ex, i0 + rem / nb + (which ? up_row_offset : 0), rem % nb);
   }
-  stage_rows<NT>(xs, s16, H, kTask, nt, [&](int t, int k) {
+  if (!one) stage_rows<NT>(xs, s16, H, kTask, nt, [&](int t, int k) {
     int pair = a.sorted[base + c0 + t];
     int tok = pair < P ? pair / a.k : pair - P;
     size_t o = (size_t)tok * H + k;
