@@ -789,13 +789,19 @@ int32_t ensure_layer_scratch(dm_moe_layer *L, int tokens) {
     const int nts[3] = {bf16 ? 256 : 16, bf16 ? 256 : 32, bf16 ? 256 : 64};
     int n_sm = 148;
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, L->ctx->device);
+    // Activation rows as fp16 hi + lo halves (two MMAs per step) for the memory-bound
+    // plans (up to 24 tokens per expert on average), where the second MMA is free; single
+    // fp16 rows with a power-of-two row scale for the 64-token plan, where the products are
+    // compute-bound (Gemma T = 4096: 2.96 -> 3.41 M tokens/s, layer rel-L2 2e-4 -> 5e-4
+    // against the 1e-3 bar). DISKMULE_CUDA_TC_SPLIT=0 makes every plan single, =all split.
     const char *split_env = getenv("DISKMULE_CUDA_TC_SPLIT");
-    const bool split = !(split_env && (!strcmp(split_env, "0") || !strcmp(split_env, "false")));
+    const bool split_off = split_env && (!strcmp(split_env, "0") || !strcmp(split_env, "false"));
+    const bool split_all = split_env && !strcmp(split_env, "all");
     for (int i = 0; i < 3; i++) {
       dm::TcPlan &p = L->tc[i];
       p.nt = nts[i];
       p.n_sm = n_sm;
-      p.split = split;
+      p.split = !split_off && (i < 2 || split_all);
       p.rows = (int)pairs;
       p.x16 = x16;
       p.h16 = h16;
