@@ -1,5 +1,6 @@
 // dm_gemv.cu -- HBM-bound expert GEMV for decode-sized batches (see dm_gemv.cuh).
 #include <algorithm>
+#include <cstdlib>
 
 #include "dm_gemv.cuh"
 #include "dm_kernels.cuh"
@@ -537,6 +538,288 @@ __device__ __forceinline__ float act_fn(const ForwardArgs &a, int expert, float 
 }
 
 // ---------------------------------------------------------------------------
+// Q4_K gate/up on tensor-core tiles (mma.sync m16n8k16, f16 in, f32 accumulate)
+//
+// The f32 dot products above spend about six instructions per weight (byte placement,
+// FMA, shared-memory loads of x), so a decode token's 13 MB of Q4_K rows took 15 us on
+// instruction issue, not on HBM. Here the dot product of a block (256 columns) with up
+// to four tokens is 16 MMAs per 16 rows, and a weight costs about one instruction:
+//
+//   w = d * sc_j * q - dmin * m_j   (q a nibble, sc_j / m_j the 6-bit scale and min of
+//                                    the 32-column sub-block j)
+//   sum_i w_i x_i = d * sum_i (q_i sc_j) x_i - dmin * sum_j m_j X_j,  X_j = sum_{i in j} x_i
+//
+// q * sc_j <= 945 is an integer, exact in f16: a PRMT places two quant bytes under an
+// f16 exponent (1024 + q, or 1024 + 16 q for a high nibble) and one f16x2 FMA with
+// (sc, -1024 sc) or (sc / 16, -64 sc) leaves q * sc exactly. Each token's x, scaled by a
+// power of two per block so its largest value lies in [2^14, 2^15), is split into f16
+// hi + lo halves (x = hi + lo to ~2^-22), two B columns of the MMA; the products are
+// exact and sum in f32. So the result carries no weight rounding at all.
+//
+// Work: a CTA takes 16 gate rows and the same 16 up rows of one (expert, token chunk)
+// item; warp w takes blocks w, w + warps, ... of the row. Lane (r = lane / 4,
+// q = lane % 4) holds rows r and r + 8 of the tile (the A fragment's rows) and bytes
+// [16q, 16q + 16) and [16q + 64, 16q + 80) of each row's 128 quant bytes; the MMA's K
+// order is a permutation of the block's columns (the same one in A and B): MMA c of a
+// piece uses the lane's bytes 2c and 2c + 1, their low nibbles as k = 2q, 2q + 1 and
+// their high nibbles as k = 2q + 8, 2q + 9. A lane's 12 16-byte loads of a block (two
+// rows, header and two quant pieces, gate and up) are all issued before any use. The
+// per-block partial sums of a row are added in block order (deterministic).
+// ---------------------------------------------------------------------------
+
+constexpr int kMmaMaxWarps = 8;
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// two f32 -> f16x2 (lo in bits 0-15), round to nearest even
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+__device__ __forceinline__ float f16_round(float v) {
+  uint16_t h;
+  asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(v));
+  float f;
+  asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+  return f;
+}
+
+// The same f16 value in both halves of a register (v exactly representable).
+__device__ __forceinline__ uint32_t splat_f16(float v) { return pack_f16x2(v, v); }
+
+// Q4_K 6-bit scale (j < 8) and min of a block header (bytes 4..15 in y, z, w).
+__device__ __forceinline__ uint32_t q4k_sc(const uint4 &hd, int j) {
+  return j < 4 ? (hd.y >> (8 * j)) & 0x3F
+               : ((hd.w >> (8 * (j - 4))) & 0x0F) | (((hd.y >> (8 * (j - 4))) >> 2) & 0x30);
+}
+__device__ __forceinline__ uint32_t q4k_m(const uint4 &hd, int j) {
+  return j < 4 ? (hd.z >> (8 * j)) & 0x3F
+               : ((hd.w >> (8 * (j - 4) + 4)) & 0x0F) | (((hd.z >> (8 * (j - 4))) >> 2) & 0x30);
+}
+
+// x of up to NT tokens, scaled and split for the B fragments of one block; see the
+// kernel. Only lanes 0 .. 8 NT - 1 hold nonzero B values (columns 2t, 2t + 1).
+template <int NT>
+struct MmaBlockX {
+  uint2 frag[2][8][8 * NT];  // [piece slot][MMA][lane]: {b0b1, b2b3}
+  float xsum[NT][8];         // [token][sub-block] unscaled sums
+  float inv[NT];             // [token] 2^-s
+};
+
+template <int NT, class RowPtr>
+__device__ __forceinline__ void mma_build_x(MmaBlockX<NT> &bx, int b, int nt, RowPtr row_ptr) {
+  // Lane l converts columns [8l, 8l + 8) of the block for every token. Column e sits in
+  // piece P = 2 (e / 64) + (e % 32) / 16 (lane q = P % 4, slot P / 4), MMA (e % 16) / 2,
+  // register (e % 64) / 32 (low or high nibbles), half e % 2.
+  const int lane = threadIdx.x & 31, e0 = 8 * lane;
+  const int P = 2 * (e0 >> 6) + ((e0 & 31) >> 4);
+  const int q = P & 3, ps = P >> 2, reg = (e0 & 63) >> 5, c0 = (e0 & 15) >> 1;
+  uint32_t *frag = reinterpret_cast<uint32_t *>(&bx.frag[0][0][0]);
+  for (int t = 0; t < nt && t < NT; t++) {
+    const float *xr = row_ptr(t) + 256 * b + e0;
+    const float4 u = *reinterpret_cast<const float4 *>(xr);
+    const float4 w = *reinterpret_cast<const float4 *>(xr + 4);
+    const float x[8] = {u.x, u.y, u.z, u.w, w.x, w.y, w.z, w.w};
+    float mx = 0.0f, sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      mx = fmaxf(mx, fabsf(x[i]));
+      sum = __fadd_rn(sum, x[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    // the 32-column sub-block (lanes 4s .. 4s + 3): sum of the four lanes' sums
+    sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
+    sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
+    // scale 2^s with mx * 2^s in [2^14, 2^15); 1 for zero or non-finite rows
+    int sh = 0;
+    if (mx > 0.0f && mx <= 3.0e38f) {
+      const int ex = (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127;
+      sh = min(max(14 - ex, -126), 126);
+    }
+    const float scale = __uint_as_float((uint32_t)(127 + sh) << 23);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float v0 = x[2 * i] * scale, v1 = x[2 * i + 1] * scale;
+      const float h0 = f16_round(v0), h1 = f16_round(v1);
+      const int slot = ((ps * 8 + c0 + i) * (8 * NT) + 8 * t + q) * 2 + reg;
+      frag[slot] = pack_f16x2(h0, h1);                                   // column 2t: hi
+      frag[slot + 8] = pack_f16x2(__fsub_rn(v0, h0), __fsub_rn(v1, h1));  // column 2t + 1: lo
+    }
+    if ((lane & 3) == 0) bx.xsum[t][lane >> 2] = sum;
+    if (lane == 0) bx.inv[t] = __uint_as_float((uint32_t)(127 - sh) << 23);
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(32 * kMmaMaxWarps, 3) gemv_up_q4k_mma_kernel(
+    ForwardArgs a, MatrixRef gate, MatrixRef up, MatrixRef sh_gate, MatrixRef sh_up,
+    int up_row_offset) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int H = a.H, I = a.I, nb = H / 256;
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int q = lane & 3, rr = lane >> 2;
+  MmaBlockX<NT> *bx = reinterpret_cast<MmaBlockX<NT> *>(smem_raw);    // [nb]
+  float *part = reinterpret_cast<float *>(bx + nb);                   // [nw][NT][32]
+  float *partm = part + nw * NT * 32;                                 // [nw][NT][32]
+  const bool one = NT == 1 && a.T == 1;
+  // One token: every item reads row 0 of the input, which does not depend on the
+  // dispatch, so its fragments are built while the predecessor finishes.
+  auto x_row = [&](int tok) -> const float * {
+    return a.family == kGemma ? a.expert_in + (size_t)tok * H
+                              : reinterpret_cast<const float *>(a.x) + (size_t)tok * H;
+  };
+  if (one)
+    for (int b = warp; b < nb; b += nw) mma_build_x<NT>(bx[b], b, 1, [&](int) { return x_row(0); });
+  pdl_wait();
+  pdl_trigger();
+  if ((int)blockIdx.y >= *a.n_items) return;
+  // (expert, first token within it, its sorted position, tokens): no further lookups
+  const int4 item = a.items[blockIdx.y];
+  const int e = item.x, pos0 = item.z;
+  const int nt = one ? 1 : min(NT, item.w);
+  const int i0 = blockIdx.x * 16;
+  const bool shared = e == a.E;
+  const MatrixRef &G = shared ? sh_gate : gate;
+  const MatrixRef &U = shared ? sh_up : up;
+  const int ex = shared ? 0 : e;
+  const uint8_t *gp0 = G.base + (uint64_t)ex * G.stride + (uint64_t)(i0 + rr) * G.row_bytes;
+  const uint8_t *up0 =
+      U.base + (uint64_t)ex * U.stride + (uint64_t)(i0 + rr + up_row_offset) * U.row_bytes;
+  const uint64_t r8g = 8 * G.row_bytes, r8u = 8 * U.row_bytes;
+  float val[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // gate r, gate r + 8, up r, up r + 8 (token q)
+  // Lane l's row for the prefetches and the min terms: row l % 16 of gate (l < 16) or up.
+  const uint8_t *row_l = lane < 16 ? gp0 + ((int64_t)(lane & 15) - rr) * (int64_t)G.row_bytes
+                                   : up0 + ((int64_t)(lane & 15) - rr) * (int64_t)U.row_bytes;
+  // Every line of the warp's blocks is requested into L1 first, so all of the bytes are in
+  // flight without holding registers; the loads of each matrix then find them there.
+  for (int b = warp; b < nb; b += nw) {
+    const uint8_t *p = row_l + (uint64_t)b * 144;
+    const uintptr_t first = (uintptr_t)p & ~(uintptr_t)127, last = ((uintptr_t)p + 143) & ~(uintptr_t)127;
+    for (uintptr_t l = first; l <= last; l += 128) asm volatile("prefetch.global.L1 [%0];" ::"l"(l));
+  }
+  // several tokens: their rows come from the dispatch (built after the prefetches)
+  if (!one) {
+    const int P = a.T * a.k;
+    for (int b = warp; b < nb; b += nw)
+      mma_build_x<NT>(bx[b], b, nt, [&](int t) {
+        const int pair = a.sorted[pos0 + t];
+        return x_row(pair < P ? pair / a.k : pair - P);
+      });
+  }
+  __syncwarp();
+  float mval[NT];  // lane l's row: sum over blocks of dmin * sum_j m_j X_j, per token
+#pragma unroll
+  for (int t = 0; t < NT; t++) mval[t] = 0.0f;
+  for (int b = warp; b < nb; b += nw) {
+    const MmaBlockX<NT> &X = bx[b];
+#pragma unroll
+    for (int m = 0; m < 2; m++) {
+      // [row][header, piece q, piece q + 4]
+      uint4 v[2][3];
+#pragma unroll
+      for (int r = 0; r < 2; r++) {
+        const uint8_t *p = (m ? up0 + (r ? r8u : 0) : gp0 + (r ? r8g : 0)) + (uint64_t)b * 144;
+        v[r][0] = ldg16(p);
+        v[r][1] = ldg16(p + 16 + 16 * q);
+        v[r][2] = ldg16(p + 16 + 16 * (q + 4));
+      }
+      float dacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int ps = 0; ps < 2; ps++) {
+        const int j = 2 * (ps * 2 + (q >> 1));  // sub-block of the low nibbles; j + 1 high
+        uint32_t ml[2], al[2], mh[2], ah[2];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+          const float scl = (float)q4k_sc(v[r][0], j), sch = (float)q4k_sc(v[r][0], j + 1);
+          ml[r] = splat_f16(scl);
+          al[r] = splat_f16(-1024.0f * scl);
+          mh[r] = splat_f16(0.0625f * sch);
+          ah[r] = splat_f16(-64.0f * sch);
+        }
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          const uint32_t sel = (c & 1) ? 0x4342u : 0x4140u;
+          uint32_t w[2];
+#pragma unroll
+          for (int r = 0; r < 2; r++) {
+            const uint4 &pc = v[r][1 + ps];
+            w[r] = __byte_perm(c < 2 ? pc.x : c < 4 ? pc.y : c < 6 ? pc.z : pc.w, 0x64646464u, sel);
+          }
+          const uint32_t a0 = hfma2_bits(w[0] & 0xFF0FFF0Fu, ml[0], al[0]);
+          const uint32_t a1 = hfma2_bits(w[1] & 0xFF0FFF0Fu, ml[1], al[1]);
+          const uint32_t a2 = hfma2_bits(w[0] & 0xFFF0FFF0u, mh[0], ah[0]);
+          const uint32_t a3 = hfma2_bits(w[1] & 0xFFF0FFF0u, mh[1], ah[1]);
+          const uint2 f = lane < 8 * NT ? X.frag[ps][c][lane] : make_uint2(0u, 0u);
+          mma_16816(dacc, a0, a1, a2, a3, f.x, f.y);
+        }
+      }
+      if (q < nt) {
+        const float inv = X.inv[q];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+          const float d = f16_bits_to_f32((uint16_t)(v[r][0].x & 0xffff));
+          const float dot = __fmul_rn(__fadd_rn(dacc[2 * r], dacc[2 * r + 1]), inv);
+          val[2 * m + r] = __fmaf_rn(d, dot, val[2 * m + r]);
+        }
+      }
+    }
+    // the min terms, one row per lane
+    {
+      const uint4 hd = ldg16(row_l + (uint64_t)b * 144);
+      const float dmin = f16_bits_to_f32((uint16_t)(hd.x >> 16));
+      float mj[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) mj[j] = (float)q4k_m(hd, j);
+#pragma unroll
+      for (int t = 0; t < NT; t++) {
+        if (t < nt) {
+          float mins = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 8; j++) mins = __fmaf_rn(mj[j], X.xsum[t][j], mins);
+          mval[t] = __fmaf_rn(dmin, mins, mval[t]);
+        }
+      }
+    }
+  }
+  if (q < nt) {
+    float *pw = part + ((size_t)warp * NT + q) * 32;
+    pw[rr] = val[0];
+    pw[rr + 8] = val[1];
+    pw[16 + rr] = val[2];
+    pw[16 + rr + 8] = val[3];
+  }
+#pragma unroll
+  for (int t = 0; t < NT; t++)
+    if (t < nt) partm[((size_t)warp * NT + t) * 32 + lane] = mval[t];
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 16 * nt; idx += blockDim.x) {
+    const int r = idx & 15, t = idx >> 4;
+    float g = 0.0f, u = 0.0f;
+    for (int w = 0; w < nw; w++) {
+      const size_t o = ((size_t)w * NT + t) * 32;
+      g = __fadd_rn(g, __fsub_rn(part[o + r], partm[o + r]));
+      u = __fadd_rn(u, __fsub_rn(part[o + 16 + r], partm[o + 16 + r]));
+    }
+    a.h[(size_t)(pos0 + t) * I + i0 + r] = act_fn(a, e, g, u);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // dense weights (BF16 / F16 / F32): one warp per row, coalesced 512-byte loads
 //
 // A warp streams a row as 512-byte pieces (lane l takes bytes 16·(l + 32i) .. +16), with
@@ -787,9 +1070,37 @@ static int quant_threads(int rows_total, int tasks_per_row, int items) {
   return threads;
 }
 
+// Q4_K gate/up through gemv_up_q4k_mma_kernel (DISKMULE_CUDA_GEMV_MMA=0 keeps the f32
+// dot products): rows in tiles of 16, so I must be a multiple of 16.
+static bool use_q4k_mma(const ForwardArgs &a) {
+  static const bool enabled = [] {
+    const char *env = getenv("DISKMULE_CUDA_GEMV_MMA");
+    return !(env && env[0] == '0');
+  }();
+  return enabled && a.I % 16 == 0 && a.H % 256 == 0 && !a.input_bf16;
+}
+
+template <int NT>
+static void launch_up_q4k_mma(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s) {
+  const int nb = a.H / 256;
+  const int per_warp = (nb + kMmaMaxWarps - 1) / kMmaMaxWarps;  // blocks of a row per warp
+  const int warps = (nb + per_warp - 1) / per_warp;
+  const size_t smem = (size_t)nb * sizeof(MmaBlockX<NT>) + (size_t)2 * warps * NT * 32 * sizeof(float);
+  auto fn = gemv_up_q4k_mma_kernel<NT>;
+  if (smem > 48 * 1024) ensure_smem_limit((const void *)fn);
+  const int up_rows = a.family == kGemma ? 2 * a.I : a.I;
+  MatrixRef g = matrix(DM_Q4_K, a.gate, a.gate_stride, up_rows, a.H, p.gate);
+  MatrixRef u = matrix(DM_Q4_K, a.family == kGemma ? a.gate : a.up, a.up_stride, up_rows, a.H, p.up);
+  MatrixRef sg = matrix(DM_Q4_K, a.sh_gate, 0, a.I, a.H, p.sh_gate);
+  MatrixRef su = matrix(DM_Q4_K, a.sh_up, 0, a.I, a.H, p.sh_up);
+  launch_pdl(fn, dim3(a.I / 16, p.max_items), dim3(32 * warps), smem, s, a, g, u, sg, su,
+             a.family == kGemma ? a.I : 0);
+}
+
 template <int KIND, int NT>
 static void launch_up(const ForwardArgs &a, const GemvPlan &p, cudaStream_t s) {
   if (is_dense(KIND)) return launch_dense_up<KIND, NT>(a, p, s);
+  if (KIND == DM_Q4_K && use_q4k_mma(a)) return launch_up_q4k_mma<NT>(a, p, s);
   constexpr int kTask = Task<KIND>::kElems;
   const int nb = a.H / kTask;
   const int threads = quant_threads(a.I, 2 * nb, p.max_items);
