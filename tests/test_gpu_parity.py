@@ -78,7 +78,7 @@ SMALL = ["gemma4-small", "gemma4-small-q8", "qwen35-small", "qwen35-odd", "glm52
 
 
 @pytest.mark.parametrize("name", SMALL)
-@pytest.mark.parametrize("T", [1, 3, 17, 130])
+@pytest.mark.parametrize("T", [1, 2, 3, 17, 130])
 def test_small_layers_match_the_oracle(ctx, name, T):
     sl = build_layer(ctx, name, seed=2)
     try:
@@ -87,6 +87,30 @@ def test_small_layers_match_the_oracle(ctx, name, T):
         y_ref, idx_ref, wt_ref = run_oracle(sl, as_f32(spec, raw, T))
         check(y, idx, wt, y_ref, idx_ref, wt_ref)
         check_dispatch(sl, T, idx)
+    finally:
+        sl.close()
+
+
+@pytest.mark.parametrize("name", ["qwen35-small", "gemma4-small"])
+@pytest.mark.parametrize("T", [1, 2, 5])
+@pytest.mark.parametrize("mode", ["large", "small", "spike"])
+def test_decode_inputs_of_extreme_magnitude_match_the_oracle(ctx, name, T, mode):
+    # The Q4_K decode GEMV scales each token's 256-column block by a power of two and
+    # splits it into f16 hi + lo halves: inputs far from 1 and a block whose values span
+    # many binades must still match the oracle's f32 products.
+    sl = build_layer(ctx, name, seed=4)
+    try:
+        spec, raw = sl.inputs(T, seed=11)
+        x = as_f32(spec, raw, T).copy()
+        if mode == "large":
+            x *= np.float32(2.0 ** 40)
+        elif mode == "small":
+            x *= np.float32(2.0 ** -40)
+        else:  # one column per 64 a thousand times larger than the rest
+            x[:, ::64] *= np.float32(1000.0)
+        y, idx, wt = sl.layer.forward_host(x)
+        y_ref, idx_ref, wt_ref = run_oracle(sl, x)
+        check(y, idx, wt, y_ref, idx_ref, wt_ref)
     finally:
         sl.close()
 
