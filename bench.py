@@ -384,8 +384,15 @@ def block_roofline(sl, T, avg, workload, sustained):
     hbm = measured_peaks()
     tensor = measured_tensor_peak(sustained)
     bf16 = sl.cfg["gate_type"] == 30
-    note = None if bf16 else ("fp16 MMAs on hi + lo activation halves: the tensor pipe does "
-                              "twice the algorithmic FLOPs")
+    # the library's tensor-core plans: hi + lo activation halves up to 24 tokens per expert
+    # on average, single fp16 rows above (DISKMULE_CUDA_TC_SPLIT=0 / =all override)
+    per_expert = T * sl.cfg["top_k"] / sl.cfg["experts"]
+    split_env = os.environ.get("DISKMULE_CUDA_TC_SPLIT", "")
+    split = split_env == "all" or (per_expert <= 24 and split_env not in ("0", "false"))
+    note = None if bf16 else (
+        "fp16 MMAs on hi + lo activation halves: the tensor pipe does twice the algorithmic "
+        "FLOPs" if split else
+        "fp16 MMAs on single fp16 activation rows, each scaled by a power of two")
     r = choose_roofline(dominant, nflops[dominant], nbytes[dominant], avg[dominant], hbm,
                         tensor, ncu_traffic(dominant, workload), note)
     r["kernel"] = KERNEL_NAMES["bf16" if bf16 else "gguf"][dominant]
