@@ -1071,13 +1071,16 @@ static int quant_threads(int rows_total, int tasks_per_row, int items) {
 }
 
 // Q4_K gate/up through gemv_up_q4k_mma_kernel (DISKMULE_CUDA_GEMV_MMA=0 keeps the f32
-// dot products): rows in tiles of 16, so I must be a multiple of 16.
+// dot products): rows in tiles of 16, so I must be a multiple of 16, and the x fragments
+// of a whole row (4.2 KB per 256 columns at four tokens) must fit shared memory.
 static bool use_q4k_mma(const ForwardArgs &a) {
   static const bool enabled = [] {
     const char *env = getenv("DISKMULE_CUDA_GEMV_MMA");
     return !(env && env[0] == '0');
   }();
-  return enabled && a.I % 16 == 0 && a.H % 256 == 0 && !a.input_bf16;
+  const size_t smem_bound = (size_t)(a.H / 256) * sizeof(MmaBlockX<4>) +
+                            (size_t)2 * kMmaMaxWarps * 4 * 32 * sizeof(float);
+  return enabled && a.I % 16 == 0 && a.H % 256 == 0 && !a.input_bf16 && smem_bound <= 200 * 1024;
 }
 
 template <int NT>
