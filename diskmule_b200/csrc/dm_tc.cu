@@ -353,6 +353,44 @@ __device__ __forceinline__ void deq_q50(uint32_t sq, uint32_t sh, uint32_t sd, i
   }
 }
 
+__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// nb (<= 4) Q5_0 blocks whose quants were widened at layer set-up to one byte per value,
+// q5 = low nibble | high bit << 4 (src/cpu.rs:560-574), 32 bytes per block at sq; f16 d
+// at sd. value = d*(q5 - 16): a PRMT puts two bytes under an f16 exponent (1024 + q5,
+// exact), an f16x2 add of -1040 leaves q5 - 16 (exact), an f16x2 multiply by d rounds
+// once -- the value deq_q50 rounds once from f32 -- in three instructions per two values
+// instead of the bit assembly of the 5-bit layout. Columns 16b, natural K order.
+__device__ __forceinline__ void deq_q50b(uint32_t sq, uint32_t sd, int nb, uint32_t tcol) {
+  constexpr uint32_t kMinus1040 = 0xE410E410u;  // (-1040, -1040) as f16x2
+#pragma unroll
+  for (int b = 0; b < 4; b++) {
+    if (b < nb) {
+      const uint4 u0 = lds16(sq + 32 * b), u1 = lds16(sq + 32 * b + 16);
+      const uint32_t dw = lds4(sd + 4 * (b >> 1));
+      const uint32_t dh = (b & 1) ? dw >> 16 : dw & 0xffffu;
+      const uint32_t D = dh | (dh << 16);
+      const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      uint32_t out[16];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        out[2 * i] = hmul2(hadd2(__byte_perm(w[i], 0x64646464u, 0x4140u), kMinus1040), D);
+        out[2 * i + 1] = hmul2(hadd2(__byte_perm(w[i], 0x64646464u, 0x4342u), kMinus1040), D);
+      }
+      tmem_st16(tcol + 16 * b, out);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // pack: sorted activation rows -> fp16 hi + lo pair with a power-of-two scale
 // ---------------------------------------------------------------------------
@@ -545,15 +583,15 @@ enum TcKind { kUpQ4K = 0, kDownQ6K = 1, kDownQ50 = 2 };
 // Raw stage of one K step, 128 weight rows, filled by TMA:
 //   Q4_K: row r (gate/up interleaved) at 144 r: one super-block;
 //   Q6_K: row r at 208 r: ql qh sc of one super-block; then the 128 f16 d;
-//   Q5_0: row r at 144 r: qs of 8 blocks (+16 bytes unused); then qh[128][8 words],
-//         then d[128][8 f16].
+//   Q5_0: row r at 272 r: the 256 quant bytes (one per value, widened at set-up) of 8
+//         blocks (+16 bytes of the next step, unused); then d[128][8 f16].
 // Row strides are odd multiples of 16 bytes, so a warp's 16-byte loads of 32 rows are
 // free of bank conflicts.
 template <int KIND>
 struct RawTile {
-  static constexpr int kRowBytes = KIND == kDownQ6K ? 208 : 144;
+  static constexpr int kRowBytes = KIND == kDownQ6K ? 208 : KIND == kDownQ50 ? 272 : 144;
   static constexpr int kQuant = 128 * kRowBytes;
-  static constexpr int kSide = KIND == kDownQ6K ? 256 : KIND == kDownQ50 ? 128 * 32 + 128 * 16 : 0;
+  static constexpr int kSide = KIND == kDownQ6K ? 256 : KIND == kDownQ50 ? 128 * 16 : 0;
   static constexpr int kBytes = kQuant + kSide;
   static constexpr int kStage = (kBytes + 1023) / 1024 * 1024;
 };
@@ -754,10 +792,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
         const float d = f16_bits_to_f32(lds2(st + RT::kQuant + 2u * r));
         deq_q6k(st + r * 208u, hf, d, tcol);
       } else {
-        const uint32_t sq = st + r * 144u + 64u * hf;
-        const uint32_t sh = st + RT::kQuant + r * 32u + 16u * hf;
-        const uint32_t sd = st + RT::kQuant + 128 * 32 + r * 16u + 8u * hf;
-        deq_q50(sq, sh, sd, min(4, (K - kStepK * ks) / 32 - 4 * hf), tcol);
+        const uint32_t sq = st + r * 272u + 128u * hf;
+        const uint32_t sd = st + RT::kQuant + r * 16u + 8u * hf;
+        deq_q50b(sq, sd, min(4, (K - kStepK * ks) / 32 - 4 * hf), tcol);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bars.rawempty(rs));  // this warp's reads of the stage are done
@@ -803,14 +840,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
               tma_load_4d(dst, map, 144 * ks, 0, un.tile * 64, ex, bar);
             } else {
               const int row0 = ex * a.H + un.tile * 128;
-              tma_load_2d(dst, map, (KIND == kDownQ6K ? 208 : 128) * ks, row0, bar);
+              // x: Q6_K in bytes; Q5_0 in 2-byte elements (a 136-element box is its 272 bytes)
+              tma_load_2d(dst, map, KIND == kDownQ6K ? 208 * ks : 128 * ks, row0, bar);
               const size_t side_row = ((size_t)ex * nsteps + ks) * a.H + un.tile * 128;
               if (KIND == kDownQ6K) {
                 bulk_load(dst + RT::kQuant, (shared ? side.sh_d_t : side.d_t) + side_row * 2, 256, bar);
               } else {
-                bulk_load(dst + RT::kQuant, (shared ? side.sh_qh_t : side.qh_t) + side_row * 32,
-                          128 * 32, bar);
-                bulk_load(dst + RT::kQuant + 128 * 32, (shared ? side.sh_d_t : side.d_t) + side_row * 16,
+                bulk_load(dst + RT::kQuant, (shared ? side.sh_d_t : side.d_t) + side_row * 16,
                           128 * 16, bar);
               }
             }
@@ -957,8 +993,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(
 }
 
 // Per-step transposes of the down side arrays: Q6_K d -> [expert][step][row] f16;
-// Q5_0 qh -> [expert][step][row][8 words], d -> [expert][step][row][8 f16] (zero past
-// the last block of a ragged step).
+// Q5_0: quants widened to one byte per value, q5 = low nibble | high bit << 4, at
+// qh_t [expert][row][I]; d -> [expert][step][row][8 f16] (zero past the last block of a
+// ragged step).
 __global__ void side_transpose_kernel(int kind, SplitTensor src, int experts, int H, int I,
                                       uint8_t *qh_t, uint8_t *d_t) {
   const int nsteps = (I + kStepK - 1) / kStepK;
@@ -976,9 +1013,15 @@ __global__ void side_transpose_kernel(int kind, SplitTensor src, int experts, in
       for (int b = 0; b < 8; b++) {
         const int blk = 8 * ks + b;
         const bool in = blk < nbr;
-        reinterpret_cast<uint32_t *>(qh_t)[idx * 8 + b] =
-            in ? *reinterpret_cast<const uint32_t *>(src.qh + (grow * nbr + blk) * 4) : 0u;
         reinterpret_cast<uint16_t *>(d_t)[idx * 8 + b] = in ? src.d[grow * nbr + blk] : (uint16_t)0;
+        if (!in) continue;
+        const uint8_t *qs = src.quant + (grow * nbr + blk) * 16;
+        const uint32_t qh = *reinterpret_cast<const uint32_t *>(src.qh + (grow * nbr + blk) * 4);
+        uint8_t *q5 = qh_t + grow * I + 32 * blk;
+        for (int j = 0; j < 16; j++) {
+          q5[j] = (uint8_t)((qs[j] & 0x0F) | (((qh >> j) & 1u) << 4));
+          q5[16 + j] = (uint8_t)((qs[j] >> 4) | (((qh >> (16 + j)) & 1u) << 4));
+        }
       }
     }
   }
@@ -1907,7 +1950,7 @@ int launch_tc_experts(const ForwardArgs &a, const TcPlan &p, const TcWeights &w,
 void tc_side_bytes(int down_type, uint64_t experts, int H, int I, uint64_t *qh_bytes,
                    uint64_t *d_bytes) {
   const uint64_t rows = experts * (uint64_t)((I + tc::kStepK - 1) / tc::kStepK) * H;
-  *qh_bytes = down_type == DM_Q5_0 ? rows * 32 : 0;
+  *qh_bytes = down_type == DM_Q5_0 ? experts * (uint64_t)H * I : 0;  // one byte per value
   *d_bytes = down_type == DM_Q5_0 ? rows * 16 : rows * 2;
 }
 
@@ -1939,6 +1982,21 @@ static bool encode_rows(CUtensorMap *map, const uint8_t *base, uint64_t row_byte
   cuuint32_t box[2] = {box_x, 128};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)base, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// widened Q5_0 rows ({I bytes, row}) as 2-byte elements, box {136, 128}: the 256 bytes of
+// one K step plus 16 more, so that rows land 272 bytes apart in shared memory (an odd
+// multiple of 16: conflict-free 16-byte reads of 32 rows); past I the box reads zeros
+static bool encode_rows16(CUtensorMap *map, const uint8_t *base, int row_bytes, uint64_t rows) {
+  auto fn = encode_fn();
+  if (!fn || !base || row_bytes % 16) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)row_bytes / 2, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {136, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void *)base, dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -2028,10 +2086,15 @@ int make_tc_weights(TcWeights &w, const uint8_t *gate, const uint8_t *up, uint64
   if (shared && !encode_up(&w.sh_up, sh_gate, sh_up, up_row, I, 1, up_row * I, &w.side.sh_up_swapped))
     return -1;
   const bool q6 = down_type == DM_Q6_K;
-  const uint64_t down_row = q6 ? (uint64_t)(I / 256) * 208 : (uint64_t)(I / 32) * 16;
-  const uint32_t box_x = q6 ? 208 : 144;
-  if (!encode_rows(&w.down, down.quant, down_row, (uint64_t)experts * H, box_x)) return -1;
-  if (shared && !encode_rows(&w.sh_down, sh_down.quant, down_row, (uint64_t)H, box_x)) return -1;
+  if (q6) {
+    const uint64_t down_row = (uint64_t)(I / 256) * 208;
+    if (!encode_rows(&w.down, down.quant, down_row, (uint64_t)experts * H, 208)) return -1;
+    if (shared && !encode_rows(&w.sh_down, sh_down.quant, down_row, (uint64_t)H, 208)) return -1;
+  } else {
+    // Q5_0 rows widened to I bytes (side_transpose_kernel, below, fills them first)
+    if (!encode_rows16(&w.down, qh_t, I, (uint64_t)experts * H)) return -1;
+    if (shared && !encode_rows16(&w.sh_down, sh_qh_t, I, (uint64_t)H)) return -1;
+  }
   if (!shared) {  // the kernels take both maps; the shared ones are never used
     w.sh_up = w.up;
     w.sh_down = w.down;
