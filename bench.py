@@ -53,6 +53,9 @@ def parse_args():
     p.add_argument("--profile-pass", type=int, default=0, metavar="R",
                    help="untimed: R forwards of --config/--tokens on one GPU with CUDA graphs "
                         "off, so every kernel is its own launch (the command profiled by ncu)")
+    p.add_argument("--uniform", action="store_true",
+                   help="gemma4: no Zipf(1.1) router bias (configuration 1's plain routing; "
+                        "the default is configuration 3's skewed routing)")
     p.add_argument("--no-extras", action="store_true",
                    help="skip the GGUF-block and decode figures reported beside the headline")
     p.add_argument("--stack", action="store_true",
@@ -524,7 +527,7 @@ def run_gguf(args):
     from diskmule_b200.synthetic import build_layer, input_spec, zipf_bias
 
     ctx = CudaContext(local)
-    bias = zipf_bias(128, 1.1, 5) if args.config == "gemma4" else None
+    bias = zipf_bias(128, 1.1, 5) if args.config == "gemma4" and not args.uniform else None
     sl = build_layer(ctx, args.config, seed=1, logit_bias=bias)
     cfg = sl.cfg
     T, H, k = args.tokens, cfg["hidden"], cfg["top_k"]
@@ -1071,7 +1074,7 @@ def run_profile_pass(args):
 
     torch.cuda.set_device(0)
     ctx = CudaContext(0)
-    bias = zipf_bias(128, 1.1, 5) if args.config == "gemma4" else None
+    bias = zipf_bias(128, 1.1, 5) if args.config == "gemma4" and not args.uniform else None
     sl = build_layer(ctx, args.config, seed=1, logit_bias=bias)
     cfg, T = sl.cfg, args.tokens
     xdt = torch.bfloat16 if cfg["family"] == "glm52" else torch.float32
