@@ -73,6 +73,10 @@ template <int KIND> struct Task;
 template <> struct Task<DM_Q4_K> { static constexpr int kElems = 256; };
 template <> struct Task<DM_Q6_K> { static constexpr int kElems = 256; };
 template <> struct Task<DM_Q5_0> { static constexpr int kElems = 32; };
+// Q5_0 with two blocks per task (rows whose length is a multiple of 64): half the threads,
+// each with two blocks' loads in flight. An internal kernel choice, not a format.
+constexpr int kQ50Pair = 1000 + DM_Q5_0;
+template <> struct Task<kQ50Pair> { static constexpr int kElems = 64; };
 template <> struct Task<DM_Q8_0> { static constexpr int kElems = 32; };
 template <> struct Task<DM_BF16> { static constexpr int kElems = 128; };
 template <> struct Task<DM_F16> { static constexpr int kElems = 64; };
@@ -207,6 +211,39 @@ __device__ __forceinline__ uint32_t spread4(uint32_t v) {
   return ((v & 0xfu) * 0x02040810u) & 0x10101010u;
 }
 
+// One Q5_0 block (global block g) dotted with up to NT tokens' 32 x values.
+template <int NT>
+__device__ __forceinline__ void q50_block_dot(const MatrixRef &m, uint64_t g, const float *x, int kp,
+                                              const float *s16, int sp, int nt, float *acc) {
+  const uint4 qs = ldg16(m.split.quant + g * 16);
+  const uint32_t hb = *reinterpret_cast<const uint32_t *>(m.split.qh + g * 4);
+  const float d = f16_bits_to_f32(m.split.d[g]);
+  const uint32_t w[4] = {qs.x, qs.y, qs.z, qs.w};
+  uint32_t lo[4], hi[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    lo[i] = (w[i] & 0x0F0F0F0Fu) | spread4(hb >> (4 * i));
+    hi[i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | spread4(hb >> (16 + 4 * i));
+  }
+#pragma unroll
+  for (int t = 0; t < NT; t++) {
+    if (t < nt) {
+      const float *xp = x + t * kp;
+      float sl = 0.0f, sh = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        sl = dot4(lo[i], *reinterpret_cast<const float4 *>(xp + 4 * i), sl);
+        sh = dot4(hi[i], *reinterpret_cast<const float4 *>(xp + 16 + 4 * i), sh);
+      }
+      const float xl = s16[t * sp], xh = s16[t * sp + 1];
+      float r = acc[t];
+      r = fmaf(d, fmaf(256.0f, fmaf(-0.5f, xl, sl), -16.0f * xl), r);
+      r = fmaf(d, fmaf(256.0f, fmaf(-0.5f, xh, sh), -16.0f * xh), r);
+      acc[t] = r;
+    }
+  }
+}
+
 #define DM_TASK_DOT_Q50(NT)                                                                     \
   template <>                                                                                   \
   __device__ __forceinline__ void task_dot<DM_Q5_0, NT>(const MatrixRef &m, int expert, int row, \
@@ -214,31 +251,17 @@ __device__ __forceinline__ uint32_t spread4(uint32_t v) {
                                                         const float *s16, int sp, int nt,       \
                                                         float *acc) {                           \
     const int nb = (int)(m.row_bytes / 22);                                                     \
-    const uint64_t g = ((uint64_t)expert * m.rows + row) * nb + task;                           \
-    const uint4 qs = ldg16(m.split.quant + g * 16);                                             \
-    const uint32_t hb = *reinterpret_cast<const uint32_t *>(m.split.qh + g * 4);                \
-    const float d = f16_bits_to_f32(m.split.d[g]);                                              \
-    const uint32_t w[4] = {qs.x, qs.y, qs.z, qs.w};                                             \
-    uint32_t lo[4], hi[4];                                                                      \
-    _Pragma("unroll") for (int i = 0; i < 4; i++) {                                             \
-      lo[i] = (w[i] & 0x0F0F0F0Fu) | spread4(hb >> (4 * i));                                   \
-      hi[i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | spread4(hb >> (16 + 4 * i));                        \
-    }                                                                                           \
-    _Pragma("unroll") for (int t = 0; t < NT; t++) {                                            \
-      if (t < nt) {                                                                             \
-        const float *xp = x + t * kp;                                                           \
-        float sl = 0.0f, sh = 0.0f;                                                             \
-        _Pragma("unroll") for (int i = 0; i < 4; i++) {                                         \
-          sl = dot4(lo[i], *reinterpret_cast<const float4 *>(xp + 4 * i), sl);                  \
-          sh = dot4(hi[i], *reinterpret_cast<const float4 *>(xp + 16 + 4 * i), sh);             \
-        }                                                                                       \
-        const float xl = s16[t * sp], xh = s16[t * sp + 1];                                     \
-        float r = acc[t];                                                                       \
-        r = fmaf(d, fmaf(256.0f, fmaf(-0.5f, xl, sl), -16.0f * xl), r);                         \
-        r = fmaf(d, fmaf(256.0f, fmaf(-0.5f, xh, sh), -16.0f * xh), r);                         \
-        acc[t] = r;                                                                             \
-      }                                                                                         \
-    }                                                                                           \
+    q50_block_dot<NT>(m, ((uint64_t)expert * m.rows + row) * nb + task, x, kp, s16, sp, nt, acc); \
+  }                                                                                             \
+  template <>                                                                                   \
+  __device__ __forceinline__ void task_dot<kQ50Pair, NT>(const MatrixRef &m, int expert, int row, \
+                                                         int task, const float *x, int kp,      \
+                                                         const float *s16, int sp, int nt,      \
+                                                         float *acc) {                          \
+    const int nb = (int)(m.row_bytes / 22);                                                     \
+    const uint64_t g = ((uint64_t)expert * m.rows + row) * nb + 2 * (uint64_t)task;             \
+    q50_block_dot<NT>(m, g, x, kp, s16, sp, nt, acc);                                           \
+    q50_block_dot<NT>(m, g + 1, x + 32, kp, s16 + 2, sp, nt, acc);                              \
   }
 DM_TASK_DOT_Q50(1)
 DM_TASK_DOT_Q50(2)
@@ -370,10 +393,12 @@ template <int KIND>
 __device__ __forceinline__ void prefetch_task(const MatrixRef &m, int expert, int row, int task) {
   const uint8_t *p;
   int bytes;
-  if (KIND == DM_Q6_K || KIND == DM_Q5_0 || KIND == DM_Q8_0) {
-    const int nb = (int)(m.row_bytes / (KIND == DM_Q6_K ? 210 : (KIND == DM_Q5_0 ? 22 : 34)));
-    const uint64_t g = ((uint64_t)expert * m.rows + row) * nb + task;
-    const int qb = KIND == DM_Q6_K ? 208 : (KIND == DM_Q5_0 ? 16 : 32);
+  if (KIND == DM_Q6_K || KIND == DM_Q5_0 || KIND == kQ50Pair || KIND == DM_Q8_0) {
+    const bool q50 = KIND == DM_Q5_0 || KIND == kQ50Pair;
+    const int nb = (int)(m.row_bytes / (KIND == DM_Q6_K ? 210 : (q50 ? 22 : 34)));
+    const uint64_t g = ((uint64_t)expert * m.rows + row) * nb +
+                       (uint64_t)task * (KIND == DM_Q6_K ? 1 : Task<KIND>::kElems / 32);
+    const int qb = KIND == DM_Q6_K ? 208 : (q50 ? 16 : 32);
     p = m.split.quant + g * qb;
     bytes = qb * (KIND == DM_Q6_K ? 1 : Task<KIND>::kElems / 32);
   } else {
@@ -1013,7 +1038,7 @@ static MatrixRef matrix(int kind, const uint8_t *base, uint64_t stride, int rows
   MatrixRef m;
   m.base = base;
   m.stride = stride;
-  m.row_bytes = row_bytes(kind, cols);
+  m.row_bytes = row_bytes(kind == kQ50Pair ? DM_Q5_0 : kind, cols);
   m.split = split;
   m.rows = rows;
   return m;
@@ -1143,7 +1168,10 @@ static bool dispatch_up(int kind, const ForwardArgs &a, const GemvPlan &p, cudaS
   switch (kind) {
     case DM_Q4_K: launch_up<DM_Q4_K, NT>(a, p, s); return true;
     case DM_Q6_K: launch_up<DM_Q6_K, NT>(a, p, s); return true;
-    case DM_Q5_0: launch_up<DM_Q5_0, NT>(a, p, s); return true;
+    case DM_Q5_0:
+      if (a.H % 64 == 0) launch_up<kQ50Pair, NT>(a, p, s);
+      else launch_up<DM_Q5_0, NT>(a, p, s);
+      return true;
     case DM_Q8_0: launch_up<DM_Q8_0, NT>(a, p, s); return true;
     case DM_BF16: launch_up<DM_BF16, NT>(a, p, s); return true;
     case DM_F16: launch_up<DM_F16, NT>(a, p, s); return true;
@@ -1157,7 +1185,10 @@ static bool dispatch_down(int kind, const ForwardArgs &a, const GemvPlan &p, cud
   switch (kind) {
     case DM_Q4_K: launch_down<DM_Q4_K, NT>(a, p, s); return true;
     case DM_Q6_K: launch_down<DM_Q6_K, NT>(a, p, s); return true;
-    case DM_Q5_0: launch_down<DM_Q5_0, NT>(a, p, s); return true;
+    case DM_Q5_0:
+      if (a.I % 64 == 0) launch_down<kQ50Pair, NT>(a, p, s);
+      else launch_down<DM_Q5_0, NT>(a, p, s);
+      return true;
     case DM_Q8_0: launch_down<DM_Q8_0, NT>(a, p, s); return true;
     case DM_BF16: launch_down<DM_BF16, NT>(a, p, s); return true;
     case DM_F16: launch_down<DM_F16, NT>(a, p, s); return true;
