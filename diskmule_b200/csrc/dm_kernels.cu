@@ -687,11 +687,112 @@ __global__ void __launch_bounds__(kRwThreads) router_wide_kernel(const float *w3
   }
 }
 
+// The widest form (GLM prefill): a CTA of 64 threads computes 32 tokens x 128 experts and
+// thread (tx, ty) holds tokens 8ty .. 8ty+7 x experts {4tx.., 64 + 4tx..} = 64 chains. The
+// input comes once per value ([H][xld] f32) and is paired in registers for the packed
+// steps, so a step of h loads 64 bytes for 32 packed steps: half the shared-memory bytes
+// per step of router_wide_kernel, whose operand traffic bounded it (shared memory 85%
+// busy). Chains, operands and the step arithmetic are those of router_gemm_kernel.
+constexpr int kRxTokens = 32, kRxExperts = 128, kRxChunk = 16, kRxThreads = 64, kRxStages = 4;
+constexpr int kRxXBytes = kRxChunk * kRxTokens * 4;
+constexpr int kRxStageBytes = kRxXBytes + kRxChunk * kRxExperts * 4;
+
+template <bool FMA>
+__device__ __forceinline__ void router_x8_chains(uint64_t (&acc)[8][4], const float *w32, int wld,
+                                                 const float *xT1, int xld, int H, uint8_t *smem) {
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int e0 = blockIdx.x * kRxExperts, t0 = blockIdx.y * kRxTokens;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
+  const int nchunks = H / kRxChunk;
+  auto issue = [&](int c) {
+    if (c < nchunks) {
+      const uint32_t st = sbase + (uint32_t)(c % kRxStages) * kRxStageBytes;
+      const int h0 = c * kRxChunk;
+#pragma unroll
+      for (int i = 0; i < kRxChunk * 8 / kRxThreads; i++) {  // x: rows of 32 tokens x 4 bytes
+        const int f = tid + kRxThreads * i, row = f >> 3, piece = f & 7;
+        rg_cp16(st + row * 128 + piece * 16, xT1 + (size_t)(h0 + row) * xld + t0 + 4 * piece);
+      }
+#pragma unroll
+      for (int i = 0; i < kRxChunk * 32 / kRxThreads; i++) {  // w: rows of 128 experts x 4 bytes
+        const int f = tid + kRxThreads * i, row = f >> 5, piece = f & 31;
+        rg_cp16(st + kRxXBytes + row * 512 + piece * 16, w32 + (size_t)(h0 + row) * wld + e0 + 4 * piece);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+#pragma unroll
+  for (int c = 0; c < kRxStages - 1; c++) issue(c);
+  for (int c = 0; c < nchunks; c++) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kRxStages - 2) : "memory");
+    __syncthreads();  // chunk c is in; every thread is done with chunk c - 1
+    issue(c + kRxStages - 1);
+    const uint8_t *stp = smem + (size_t)(c % kRxStages) * kRxStageBytes;
+#pragma unroll
+    for (int kk = 0; kk < kRxChunk; kk++) {
+      const float4 xa = *reinterpret_cast<const float4 *>(stp + kk * 128 + ty * 32);
+      const float4 xb = *reinterpret_cast<const float4 *>(stp + kk * 128 + ty * 32 + 16);
+      const uint8_t *wrow = stp + kRxXBytes + kk * 512 + tx * 16;
+      const ulonglong2 wa = *reinterpret_cast<const ulonglong2 *>(wrow);
+      const ulonglong2 wb = *reinterpret_cast<const ulonglong2 *>(wrow + 256);
+      const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      const uint64_t wp[4] = {wa.x, wa.y, wb.x, wb.y};
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const uint64_t xp = ((uint64_t)__float_as_uint(xv[i]) << 32) | __float_as_uint(xv[i]);
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = rg_step<FMA>(wp[j], xp, acc[i][j]);
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+template <bool GLM>
+__global__ void __launch_bounds__(kRxThreads) router_x8_kernel(const float *w32, int wld,
+                                                               const float *xT1, int xld, int T,
+                                                               int H, int E1, const float *lbias,
+                                                               int E, float *logits,
+                                                               const uint8_t *tiny,
+                                                               int exact_products) {
+  pdl_wait();
+  extern __shared__ __align__(16) uint8_t rx_smem[];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int e0 = blockIdx.x * kRxExperts, t0 = blockIdx.y * kRxTokens;
+  uint64_t acc[8][4];  // token 8ty + i; experts (4tx + 2j, +1) for j < 2, (64 + 4tx + 2(j-2), +1)
+  const float z = GLM ? -0.0f : 0.0f;
+  const uint64_t z2 = ((uint64_t)__float_as_uint(z) << 32) | __float_as_uint(z);
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[i][j] = z2;
+  if (router_fused_step(GLM, exact_products, tiny, blockIdx.y, (H + 31) / 32))
+    router_x8_chains<true>(acc, w32, wld, xT1, xld, H, rx_smem);
+  else
+    router_x8_chains<false>(acc, w32, wld, xT1, xld, H, rx_smem);
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int t = t0 + 8 * ty + i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int eb = e0 + (j < 2 ? 4 * tx + 2 * j : 64 + 4 * tx + 2 * (j - 2));
+#pragma unroll
+      for (int q = 0; q < 2; q++) {
+        const int e = eb + q;
+        const float v = __uint_as_float((uint32_t)(acc[i][j] >> (32 * q)));
+        if (e < E1) logits[(size_t)t * E1 + e] = (lbias && e < E) ? __fadd_rn(v, lbias[e]) : v;
+      }
+    }
+  }
+}
+
 // x [T][H] (f32 or bf16) -> xT2 [H][xld][2] f32, each value twice; tokens T..xld-1 zero.
 // With `tiny`, block (bx, by) also writes tiny[by * gridDim.x + bx]: whether its 32x32 tile
 // holds a nonzero |x| outside [2^-60, 2^60) (see the router's step arithmetic).
 __global__ void __launch_bounds__(256) transpose_x_kernel(const void *x, int bf16, int T, int H,
-                                                         int xld, float *xT2, uint8_t *tiny) {
+                                                         int xld, float *xT2, uint8_t *tiny,
+                                                         int single) {
   pdl_wait();
   __shared__ float tile[32][33];
   const int h0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
@@ -709,7 +810,10 @@ __global__ void __launch_bounds__(256) transpose_x_kernel(const void *x, int bf1
   for (int r = r0; r < 32; r += 8) {
     const int h = h0 + r, t = t0 + c;
     const float v = tile[c][r];
-    if (h < H && t < xld) reinterpret_cast<float2 *>(xT2)[(size_t)h * xld + t] = make_float2(v, v);
+    if (h < H && t < xld) {
+      if (single) xT2[(size_t)h * xld + t] = v;
+      else reinterpret_cast<float2 *>(xT2)[(size_t)h * xld + t] = make_float2(v, v);
+    }
   }
 }
 
@@ -1658,9 +1762,6 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
     // the input tiles that rule it out
     const int exact = glm && router_x_bf16 && a.router_exact_products;
     uint8_t *tiny = exact ? a.x_tiny : nullptr;
-    launch_pdl(transpose_x_kernel, dim3((a.H + 31) / 32, xld / 32), dim3(256), 0, stream, router_x,
-               router_x_bf16 ? 1 : 0, a.T, a.H, xld, a.xT, tiny);
-    launches++;
     // 32 x 128 tiles when there are enough of them to fill the SMs, else 32 x 64
     static const int n_sm = [] {
       int dev = 0, n = 148;
@@ -1670,6 +1771,16 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
     }();
     const int wide_tiles = (a.E1 + kRwExperts - 1) / kRwExperts * (xld / kRwTokens);
     const bool wide = a.E1 >= kRwExperts && a.H % kRwChunk == 0 && wide_tiles >= n_sm;
+    // the wide tiles with 64 chains per thread read the input once per value
+    // (DISKMULE_CUDA_ROUTER_X8=0 keeps the 32-chain form over the doubled input)
+    static const bool x8_on = [] {
+      const char *e = getenv("DISKMULE_CUDA_ROUTER_X8");
+      return !(e && e[0] == '0');
+    }();
+    const bool x8 = wide && x8_on;
+    launch_pdl(transpose_x_kernel, dim3((a.H + 31) / 32, xld / 32), dim3(256), 0, stream, router_x,
+               router_x_bf16 ? 1 : 0, a.T, a.H, xld, a.xT, tiny, x8 ? 1 : 0);
+    launches++;
 #define DM_ROUTER_TILED(KERNEL, G, EXPERTS, THREADS, SMEM)                                     \
   {                                                                                          \
     auto fn = KERNEL<G>;                                                                     \
@@ -1680,7 +1791,10 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
   }
     const size_t rg_smem = (size_t)kRgStages * kRgStageBytes;
     const size_t rw_smem = (size_t)kRwStages * kRwStageBytes;
-    if (wide && glm) DM_ROUTER_TILED(router_wide_kernel, true, kRwExperts, kRwThreads, rw_smem)
+    const size_t rx_smem = (size_t)kRxStages * kRxStageBytes;
+    if (x8 && glm) DM_ROUTER_TILED(router_x8_kernel, true, kRxExperts, kRxThreads, rx_smem)
+    else if (x8) DM_ROUTER_TILED(router_x8_kernel, false, kRxExperts, kRxThreads, rx_smem)
+    else if (wide && glm) DM_ROUTER_TILED(router_wide_kernel, true, kRwExperts, kRwThreads, rw_smem)
     else if (wide) DM_ROUTER_TILED(router_wide_kernel, false, kRwExperts, kRwThreads, rw_smem)
     else if (glm) DM_ROUTER_TILED(router_gemm_kernel, true, kRgExperts, kRgThreads, rg_smem)
     else DM_ROUTER_TILED(router_gemm_kernel, false, kRgExperts, kRgThreads, rg_smem)
