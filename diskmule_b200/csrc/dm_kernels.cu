@@ -440,9 +440,10 @@ int launch_router_rows(const void *router, int bf16, int E, int H, const float *
 // thread (tx, ty) holds tokens 4ty.. x experts 4tx.. = 16 chains, each still one
 // sequential chain over h in the reference's order (so logits stay bit-exact), computed
 // two experts at a time with packed f32x2 instructions (one rounding per element, as
-// scalar code). Operands come from x transposed and duplicated per forward, [h][t][2]
-// (a 16-byte load yields two (x, x) pairs; a warp reads only two distinct x chunks), and
-// the router padded to f32 [h][128k] at set-up, through a 3-stage cp.async pipeline of
+// scalar code). Operands come from x transposed once per forward, [h][t] (a 16-byte load
+// yields a thread's four tokens, each paired with itself in registers for the packed
+// steps: 32 bytes of shared memory per 8 packed steps), and the router padded to f32
+// [h][128k] at set-up, through a 3-stage cp.async pipeline of
 // 64-wide h chunks (one block barrier per 64 steps of the chains); operands are read with
 // plain shared-memory loads, so the compiler can issue the next step's loads ahead of the
 // current step's FMAs.
@@ -456,7 +457,7 @@ int launch_router_rows(const void *router, int bf16, int E, int H, const float *
 // the FP32 instructions); otherwise (an f32 router or input, or a tile holding a value
 // outside that range) they keep the two-instruction step.
 constexpr int kRgTokens = 32, kRgExperts = 64, kRgChunk = 64, kRgThreads = 128, kRgStages = 3;
-constexpr int kRgXBytes = kRgChunk * kRgTokens * 8;
+constexpr int kRgXBytes = kRgChunk * kRgTokens * 4;
 constexpr int kRgStageBytes = kRgXBytes + kRgChunk * kRgExperts * 4;
 
 template <bool FMA>
@@ -506,9 +507,15 @@ __device__ __forceinline__ void rg_cp16(uint32_t dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
+// (v, v) as an f32 pair for a packed step
+__device__ __forceinline__ uint64_t pair_same(float v) {
+  const uint64_t u = __float_as_uint(v);
+  return (u << 32) | u;
+}
+
 template <bool FMA>
 __device__ __forceinline__ void router_gemm_chains(uint64_t (&acc)[4][2], const float *w32,
-                                                   int wld, const float *xT2, int xld, int H,
+                                                   int wld, const float *xT1, int xld, int H,
                                                    uint8_t *rg_smem) {
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int e0 = blockIdx.x * kRgExperts, t0 = blockIdx.y * kRgTokens;
@@ -519,9 +526,9 @@ __device__ __forceinline__ void router_gemm_chains(uint64_t (&acc)[4][2], const 
       const uint32_t st = sbase + (uint32_t)(c % kRgStages) * kRgStageBytes;
       const int h0 = c * kRgChunk;
 #pragma unroll
-      for (int i = 0; i < kRgChunk * 16 / kRgThreads; i++) {  // x: rows of 32 tokens x 8 bytes
-        const int f = tid + kRgThreads * i, row = f >> 4, piece = f & 15;
-        rg_cp16(st + row * 256 + piece * 16, xT2 + ((size_t)(h0 + row) * xld + t0) * 2 + 4 * piece);
+      for (int i = 0; i < kRgChunk * 8 / kRgThreads; i++) {  // x: rows of 32 tokens x 4 bytes
+        const int f = tid + kRgThreads * i, row = f >> 3, piece = f & 7;
+        rg_cp16(st + row * 128 + piece * 16, xT1 + (size_t)(h0 + row) * xld + t0 + 4 * piece);
       }
 #pragma unroll
       for (int i = 0; i < kRgChunk * 16 / kRgThreads; i++) {  // w: rows of 64 experts x 4 bytes
@@ -540,10 +547,9 @@ __device__ __forceinline__ void router_gemm_chains(uint64_t (&acc)[4][2], const 
     const uint8_t *stp = rg_smem + (size_t)(c % kRgStages) * kRgStageBytes;
 #pragma unroll
     for (int kk = 0; kk < kRgChunk; kk++) {
-      const ulonglong2 xa = *reinterpret_cast<const ulonglong2 *>(stp + kk * 256 + ty * 32);
-      const ulonglong2 xb = *reinterpret_cast<const ulonglong2 *>(stp + kk * 256 + ty * 32 + 16);
+      const float4 xv = *reinterpret_cast<const float4 *>(stp + kk * 128 + ty * 16);
       const ulonglong2 w = *reinterpret_cast<const ulonglong2 *>(stp + kRgXBytes + kk * 256 + tx * 16);
-      const uint64_t xp[4] = {xa.x, xa.y, xb.x, xb.y};
+      const uint64_t xp[4] = {pair_same(xv.x), pair_same(xv.y), pair_same(xv.z), pair_same(xv.w)};
 #pragma unroll
       for (int i = 0; i < 4; i++) {
         acc[i][0] = rg_step<FMA>(w.x, xp[i], acc[i][0]);
@@ -556,7 +562,7 @@ __device__ __forceinline__ void router_gemm_chains(uint64_t (&acc)[4][2], const 
 
 template <bool GLM>
 __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w32, int wld,
-                                                                 const float *xT2, int xld, int T,
+                                                                 const float *xT1, int xld, int T,
                                                                  int H, int E1, const float *lbias,
                                                                  int E, float *logits,
                                                                  const uint8_t *tiny,
@@ -571,9 +577,9 @@ __global__ void __launch_bounds__(kRgThreads) router_gemm_kernel(const float *w3
 #pragma unroll
   for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = z2;
   if (router_fused_step(GLM, exact_products, tiny, blockIdx.y, (H + 31) / 32))
-    router_gemm_chains<true>(acc, w32, wld, xT2, xld, H, rg_smem);
+    router_gemm_chains<true>(acc, w32, wld, xT1, xld, H, rg_smem);
   else
-    router_gemm_chains<false>(acc, w32, wld, xT2, xld, H, rg_smem);
+    router_gemm_chains<false>(acc, w32, wld, xT1, xld, H, rg_smem);
 #pragma unroll
   for (int i = 0; i < 4; i++) {
     const int t = t0 + 4 * ty + i;
@@ -1778,8 +1784,10 @@ int launch_forward(const ForwardArgs &a, cudaStream_t stream, cudaEvent_t *ev,
       return !(e && e[0] == '0');
     }();
     const bool x8 = wide && x8_on;
+    // every router form but the 32-chain wide one reads the input once per value
+    const bool doubled = wide && !x8;
     launch_pdl(transpose_x_kernel, dim3((a.H + 31) / 32, xld / 32), dim3(256), 0, stream, router_x,
-               router_x_bf16 ? 1 : 0, a.T, a.H, xld, a.xT, tiny, x8 ? 1 : 0);
+               router_x_bf16 ? 1 : 0, a.T, a.H, xld, a.xT, tiny, doubled ? 0 : 1);
     launches++;
 #define DM_ROUTER_TILED(KERNEL, G, EXPERTS, THREADS, SMEM)                                     \
   {                                                                                          \
