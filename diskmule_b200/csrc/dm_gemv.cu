@@ -587,9 +587,12 @@ __device__ __forceinline__ float act_fn(const ForwardArgs &a, int expert, float 
 // [16q, 16q + 16) and [16q + 64, 16q + 80) of each row's 128 quant bytes; the MMA's K
 // order is a permutation of the block's columns (the same one in A and B): MMA c of a
 // piece uses the lane's bytes 2c and 2c + 1, their low nibbles as k = 2q, 2q + 1 and
-// their high nibbles as k = 2q + 8, 2q + 9. A lane's 12 16-byte loads of a block (two
-// rows, header and two quant pieces, gate and up) are all issued before any use. The
-// per-block partial sums of a row are added in block order (deterministic).
+// their high nibbles as k = 2q + 8, 2q + 9. Every 128-byte line of the warp's blocks is
+// first requested into L1 (no registers held by bytes in flight); the lane's six 16-byte
+// loads per matrix and block (two rows: header and two quant pieces) then find them there.
+// The x fragments of a block are built once by the whole warp (shared memory), and the min
+// terms dmin * sum_j m_j X_j run one row per lane. The partial sums of a row are added in
+// a fixed order (deterministic).
 // ---------------------------------------------------------------------------
 
 constexpr int kMmaMaxWarps = 8;
