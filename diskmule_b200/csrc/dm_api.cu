@@ -1033,6 +1033,7 @@ namespace dmi {
 dm::ForwardArgs fill_args(dm_moe_layer *L, const void *x, float *y, int32_t tokens) {
   const dm_moe_desc &d = L->desc;
   dm::ForwardArgs a = L->args;
+  a.balanced_items = 0;  // choose_plans turns it on for the tensor-core kernels
   a.family = d.family;
   a.T = tokens;
   a.H = d.hidden;
@@ -1110,6 +1111,13 @@ void choose_plans(dm_moe_layer *L, dm::ForwardArgs &a, Plans &P) {
       P.tcp.max_items = std::min(pairs, (pairs + P.tcp.nt - 1) / P.tcp.nt + P.plan.max_active);
       a.chunk = P.tcp.nt;
       P.tp = &P.tcp;
+      // the tensor-core kernels take an item's first position and token count from the
+      // item itself, so an expert's tokens may be split evenly over its items
+      static const int balanced = [] {
+        const char *e = getenv("DISKMULE_CUDA_BALANCED_ITEMS");
+        return e && e[0] == '0' ? 0 : 1;
+      }();
+      a.balanced_items = balanced;
     }
   }
 }

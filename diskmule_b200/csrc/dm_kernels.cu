@@ -1110,9 +1110,18 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(ForwardArgs 
       a.offsets[e] = s_count;
       if (e < EB) flags[e] = s_count;
       if (count > 0) a.active[s_active] = e;
-      for (int j = 0; j < items; j++)
-        a.items[s_items + j] = make_int4(e, j * a.chunk, s_count + j * a.chunk,
-                                         min(a.chunk, count - j * a.chunk));
+      if (a.balanced_items && items > 1) {
+        // items of base or base + 1 tokens, the larger ones first
+        const int base = count / items, rem = count - base * items;
+        for (int j = 0; j < items; j++) {
+          const int first = j * base + min(j, rem);
+          a.items[s_items + j] = make_int4(e, first, s_count + first, base + (j < rem ? 1 : 0));
+        }
+      } else {
+        for (int j = 0; j < items; j++)
+          a.items[s_items + j] = make_int4(e, j * a.chunk, s_count + j * a.chunk,
+                                           min(a.chunk, count - j * a.chunk));
+      }
     }
     if (e == 0) {
       a.offsets[E + 1] = tot_count;

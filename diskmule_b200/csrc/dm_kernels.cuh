@@ -73,6 +73,9 @@ struct ForwardArgs {
   // `ret`); null everywhere else
   float **ydest;
   EpReturnMap ret;
+  // Work items of an expert with more than `chunk` tokens split its tokens evenly
+  // (dispatch_kernel) instead of `chunk`-token items and a remainder.
+  int balanced_items;
 };
 
 // Row stride (elements) of the transposed router [H][ld]: E1 rounded up to 8 so
